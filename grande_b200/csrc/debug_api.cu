@@ -1,0 +1,76 @@
+// Kernel-level entry points for the parity tests: each takes host buffers,
+// runs one kernel on `device` and copies the result back. They allocate their
+// own device memory per call; the engine never uses them.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include "capi_util.h"
+#include "gemm.cuh"
+#include "omg_b200.h"
+
+using namespace omg;
+
+namespace {
+
+struct DevBuf {
+  void* p = nullptr;
+  ~DevBuf() {
+    if (p) cudaFree(p);
+  }
+  bool alloc(size_t n) { return cudaMalloc(&p, n ? n : 16) == cudaSuccess; }
+};
+
+}  // namespace
+
+extern "C" int omg_debug_gemm(int device, const uint16_t* x_f16, int m, int k, int lda,
+                              const uint16_t* w_f16, int w_rows, int n_out, int epi, int bn,
+                              int splits, void* out, int ldo) {
+  return guarded([&]() -> int {
+    CUDA_TRY(cudaSetDevice(device));
+    gemm_setup_device();
+    if (bn == 0) {
+      int sms = 148;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+      gemm_pick(n_out, k, sms, &bn, &splits);
+    }
+    DevBuf dx, dw, dout, dstat;
+    const size_t xb = static_cast<size_t>(m) * lda * 2;
+    const size_t wb = static_cast<size_t>(w_rows) * k * 2;
+    const bool f32 = epi == kEpiF32;
+    if (!dx.alloc(xb) || !dw.alloc(wb) || !dstat.alloc(4)) return set_error("cudaMalloc failed");
+    CUDA_TRY(cudaMemcpy(dx.p, x_f16, xb, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(dw.p, w_f16, wb, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemset(dstat.p, 0, 4));
+    GemmPlan plan;
+    char err[256];
+    if (!gemm_plan(&plan, dx.p, m, lda, dw.p, w_rows, n_out, k, epi, bn, splits, err, sizeof err))
+      return set_error(err);
+    const int sp = f32 ? plan.s.splits : 1;
+    const size_t slab = static_cast<size_t>(m) * ldo;
+    const size_t ob = slab * sp * (f32 ? 4 : 2);
+    if (!dout.alloc(ob)) return set_error("cudaMalloc failed");
+    CUDA_TRY(cudaMemset(dout.p, 0, ob));
+    gemm_run(plan, m, dout.p, ldo, slab, static_cast<uint32_t*>(dstat.p), 0);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaDeviceSynchronize());
+    uint32_t st = 0;
+    CUDA_TRY(cudaMemcpy(&st, dstat.p, 4, cudaMemcpyDeviceToHost));
+    if (st) return set_error("gemm kernel reported device status %u", st);
+    if (f32 && sp > 1) {
+      std::vector<float> h(slab * sp);
+      CUDA_TRY(cudaMemcpy(h.data(), dout.p, ob, cudaMemcpyDeviceToHost));
+      float* o = static_cast<float*>(out);
+      for (size_t i = 0; i < slab; ++i) {
+        float s = h[i];
+        for (int z = 1; z < sp; ++z) s += h[z * slab + i];
+        o[i] = s;
+      }
+    } else {
+      CUDA_TRY(cudaMemcpy(out, dout.p, ob, cudaMemcpyDeviceToHost));
+    }
+    return 0;
+  });
+}

@@ -1,0 +1,403 @@
+// tcgen05 GEMM: TMA-fed, single-thread-issued UMMA with the accumulator in
+// tensor memory, warp-specialised (1 TMA warp, 1 MMA warp, 4 epilogue warps).
+//
+// Tile: 128 rows x BN (128 or 256) x 64 K per stage, 128-byte swizzled K-major
+// operands in shared memory, a 4- or 6-stage mbarrier ring. One output tile
+// per CTA; split-K slabs along grid.z for the narrow f32 projections so the
+// grid covers the 148 SMs.
+#include "gemm.cuh"
+#include "ptx.cuh"
+#include <cudaTypedefs.h>
+#include <cstdio>
+#include <cstring>
+
+namespace omg {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+
+struct GemmArgs {
+  int m;             // valid rows
+  int n_out;         // valid output columns
+  int kb_total;      // 64-wide K blocks
+  int kb_per_split;  // K blocks per grid.z slab
+  void* out;
+  int ldo;           // output row stride in elements
+  size_t split_stride;
+  uint32_t* status;
+};
+
+template <int BN>
+struct Cfg {
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr uint32_t TMEM_COLS = BN;
+};
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  // Gemma's tanh GELU with the argument clamped to +-15 (matmul_gated.wgsl:126-134).
+  float z = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+  z = fminf(fmaxf(z, -15.0f), 15.0f);
+  return 0.5f * x * (1.0f + tanhf(z));
+}
+
+__device__ __forceinline__ float erf_as(float x) {
+  // Abramowitz & Stegun 7.1.26, the erf the reference's ModernBERT GeGLU
+  // uses (matmul_gated.wgsl:114-124).
+  const float s = x < 0.f ? -1.f : (x > 0.f ? 1.f : 0.f);
+  const float a = fabsf(x);
+  const float t = 1.0f / (1.0f + 0.3275911f * a);
+  const float y =
+      1.0f -
+      (((((1.061405429f * t - 1.453152027f) * t) + 1.421413741f) * t - 0.284496736f) * t +
+       0.254829592f) *
+          t * expf(-a * a);
+  return s * y;
+}
+
+__device__ __forceinline__ float gelu_erf(float x) {
+  return 0.5f * x * (1.0f + erf_as(x * 0.7071067811865476f));
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
+                GemmArgs g) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + C::STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + C::STAGES * C::B_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* accum = empty + C::STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_tile = blockIdx.x;
+  const int m_tile = blockIdx.y;
+  const int split = blockIdx.z;
+  const int kb0 = split * g.kb_per_split;
+  const int kb1 = min(g.kb_total, kb0 + g.kb_per_split);
+  const int nkb = kb1 - kb0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tma);
+    prefetch_tmap(&tmb);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % C::STAGES;
+        const uint32_t ph = (i / C::STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, g.status)) break;
+        mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+        const int kx = (kb0 + i) * BK;
+        tma_load_2d(sa + s * C::A_BYTES, &tma, &full[s], kx, m_tile * BM);
+        tma_load_2d(sb + s * C::B_BYTES, &tmb, &full[s], kx, n_tile * BN);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(BM, BN);
+      bool ok = true;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % C::STAGES;
+        const uint32_t ph = (i / C::STAGES) & 1;
+        if (!mbar_wait(&full[s], ph, abort_flag, g.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t da = sw128_desc(sa + s * C::A_BYTES);
+        const uint64_t db = sw128_desc(sb + s * C::B_BYTES);
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+      }
+      if (ok) umma_commit(accum);
+    }
+  } else {
+    // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +32, one row per thread.
+    const int q = warp & 3;
+    int ok = 0;
+    if (lane == 0) ok = mbar_wait(accum, 0, abort_flag, g.status) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    __syncwarp();
+    tc_fence_after();
+    if (ok) {
+      const int row = m_tile * BM + q * 32 + lane;
+      const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16);
+      if constexpr (EPI == kEpiF32) {
+        float* obase = static_cast<float*>(g.out) + split * g.split_stride +
+                       static_cast<size_t>(row) * g.ldo;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(tbase + c * 32, v);
+          const int col0 = n_tile * BN + c * 32;
+          if (row < g.m && col0 < g.n_out) {
+            float* o = obase + col0;
+            if (col0 + 32 <= g.n_out) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+              #pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < g.n_out) o[j] = v[j];
+            }
+          }
+        }
+      } else if constexpr (EPI == kEpiF16) {
+        __half* obase = static_cast<__half*>(g.out) + static_cast<size_t>(row) * g.ldo;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(tbase + c * 32, v);
+          const int col0 = n_tile * BN + c * 32;
+          if (row < g.m && col0 < g.n_out) {
+            __half* o = obase + col0;
+            if (col0 + 32 <= g.n_out) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                uint4 pk;
+                __half2 h0 = __floats2half2_rn(v[j], v[j + 1]);
+                __half2 h1 = __floats2half2_rn(v[j + 2], v[j + 3]);
+                __half2 h2 = __floats2half2_rn(v[j + 4], v[j + 5]);
+                __half2 h3 = __floats2half2_rn(v[j + 6], v[j + 7]);
+                pk.x = *reinterpret_cast<uint32_t*>(&h0);
+                pk.y = *reinterpret_cast<uint32_t*>(&h1);
+                pk.z = *reinterpret_cast<uint32_t*>(&h2);
+                pk.w = *reinterpret_cast<uint32_t*>(&h3);
+                *reinterpret_cast<uint4*>(o + j) = pk;
+              }
+            } else {
+              #pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < g.n_out) o[j] = __float2half_rn(v[j]);
+            }
+          }
+        }
+      } else {
+        // GeGLU: TMEM columns 0..127 hold the gate products, 128..255 the up
+        // products of the same 128 output columns.
+        static_assert(BN == 256, "GeGLU tiles pair 128 gate rows with 128 up rows");
+        __half* obase = static_cast<__half*>(g.out) + static_cast<size_t>(row) * g.ldo;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float gv[32], uv[32];
+          tmem_ld32(tbase + c * 32, gv);
+          tmem_ld32(tbase + 128 + c * 32, uv);
+          const int col0 = n_tile * 128 + c * 32;
+          if (row < g.m && col0 < g.n_out) {
+            float hv[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float a = (EPI == kEpiGeGluTanh) ? gelu_tanh(gv[j]) : gelu_erf(gv[j]);
+              hv[j] = a * uv[j];
+            }
+            __half* o = obase + col0;
+            if (col0 + 32 <= g.n_out) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                uint4 pk;
+                __half2 h0 = __floats2half2_rn(hv[j], hv[j + 1]);
+                __half2 h1 = __floats2half2_rn(hv[j + 2], hv[j + 3]);
+                __half2 h2 = __floats2half2_rn(hv[j + 4], hv[j + 5]);
+                __half2 h3 = __floats2half2_rn(hv[j + 6], hv[j + 7]);
+                pk.x = *reinterpret_cast<uint32_t*>(&h0);
+                pk.y = *reinterpret_cast<uint32_t*>(&h1);
+                pk.z = *reinterpret_cast<uint32_t*>(&h2);
+                pk.w = *reinterpret_cast<uint32_t*>(&h3);
+                *reinterpret_cast<uint4*>(o + j) = pk;
+              }
+            } else {
+              #pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < g.n_out) o[j] = __float2half_rn(hv[j]);
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+bool make_tmap_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
+                  uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, char* err,
+                  size_t errlen) {
+  auto fn = encode_fn();
+  if (!fn) {
+    snprintf(err, errlen, "cuTensorMapEncodeTiled is not available from the driver");
+    return false;
+  }
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    snprintf(err, errlen, "cuTensorMapEncodeTiled failed (%d) for [%llu x %llu] stride %llu", (int)r,
+             (unsigned long long)outer, (unsigned long long)inner, (unsigned long long)row_bytes);
+    return false;
+  }
+  return true;
+}
+
+template <int BN, int EPI>
+void set_smem_attr() {
+  cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       Cfg<BN>::SMEM);
+}
+
+template <int BN, int EPI>
+void launch(const GemmPlan& p, const GemmArgs& a, int m_tiles, cudaStream_t stream) {
+  dim3 grid(p.s.n_tiles, m_tiles, p.s.splits);
+  gemm_kernel<BN, EPI><<<grid, 192, Cfg<BN>::SMEM, stream>>>(p.a, p.b, a);
+}
+
+}  // namespace
+
+void gemm_setup_device() {
+  set_smem_attr<128, kEpiF32>();
+  set_smem_attr<256, kEpiF32>();
+  set_smem_attr<128, kEpiF16>();
+  set_smem_attr<256, kEpiF16>();
+  set_smem_attr<256, kEpiGeGluTanh>();
+  set_smem_attr<256, kEpiGeGluErf>();
+}
+
+void gemm_pick(int n, int k, int num_sms, int* bn, int* splits) {
+  (void)num_sms;
+  const int t256 = (n + 255) / 256;
+  const int t128 = (n + 127) / 128;
+  const int kb = (k + BK - 1) / BK;
+  if (t256 >= 32) {
+    *bn = 256;
+    *splits = 1;
+    return;
+  }
+  *bn = 128;
+  // Narrow outputs: split K in two (deterministic: the consumer adds the two
+  // slabs in a fixed order) once each half still has >= 16 K blocks.
+  *splits = (t128 <= 24 && kb >= 32) ? 2 : 1;
+}
+
+bool gemm_plan(GemmPlan* p, const void* a, int a_rows_cap, int lda, const void* w, int w_rows,
+               int n_out, int k, int epi, int bn, int splits, char* err, size_t errlen) {
+  memset(p, 0, sizeof(*p));
+  if (k % 8 != 0 || lda % 8 != 0) {
+    snprintf(err, errlen, "gemm: K %d and lda %d must be multiples of 8", k, lda);
+    return false;
+  }
+  if (epi == kEpiGeGluTanh || epi == kEpiGeGluErf) {
+    bn = 256;
+    splits = 1;
+  }
+  if (epi == kEpiF16) splits = 1;
+  if (bn != 128 && bn != 256) {
+    snprintf(err, errlen, "gemm: BN %d", bn);
+    return false;
+  }
+  const int kb = (k + BK - 1) / BK;
+  if (splits < 1 || splits > kb) splits = 1;
+  // Every slab must own at least one K block.
+  while (splits > 1 && (splits - 1) * ((kb + splits - 1) / splits) >= kb) --splits;
+  p->rows_cap = a_rows_cap;
+  p->s.n_out = n_out;
+  p->s.k = k;
+  p->s.bn = bn;
+  p->s.splits = splits;
+  p->s.epi = epi;
+  if (epi == kEpiGeGluTanh || epi == kEpiGeGluErf)
+    p->s.n_tiles = (n_out + 127) / 128;
+  else
+    p->s.n_tiles = (n_out + bn - 1) / bn;
+  if (!make_tmap_2d(&p->a, a, k, a_rows_cap, static_cast<uint64_t>(lda) * 2, BK, BM, err, errlen))
+    return false;
+  if (!make_tmap_2d(&p->b, w, k, w_rows, static_cast<uint64_t>(k) * 2, BK, bn, err, errlen))
+    return false;
+  return true;
+}
+
+void gemm_run(const GemmPlan& p, int m, void* out, int ldo, size_t split_stride, uint32_t* status,
+              cudaStream_t stream) {
+  if (m <= 0) return;
+  GemmArgs a;
+  a.m = m;
+  a.n_out = p.s.n_out;
+  a.kb_total = (p.s.k + BK - 1) / BK;
+  a.kb_per_split = (a.kb_total + p.s.splits - 1) / p.s.splits;
+  a.out = out;
+  a.ldo = ldo;
+  a.split_stride = split_stride;
+  a.status = status;
+  const int m_tiles = (m + BM - 1) / BM;
+  switch (p.s.epi) {
+    case kEpiF32:
+      if (p.s.bn == 256)
+        launch<256, kEpiF32>(p, a, m_tiles, stream);
+      else
+        launch<128, kEpiF32>(p, a, m_tiles, stream);
+      break;
+    case kEpiF16:
+      if (p.s.bn == 256)
+        launch<256, kEpiF16>(p, a, m_tiles, stream);
+      else
+        launch<128, kEpiF16>(p, a, m_tiles, stream);
+      break;
+    case kEpiGeGluTanh:
+      launch<256, kEpiGeGluTanh>(p, a, m_tiles, stream);
+      break;
+    case kEpiGeGluErf:
+      launch<256, kEpiGeGluErf>(p, a, m_tiles, stream);
+      break;
+  }
+}
+
+}  // namespace omg

@@ -1,0 +1,60 @@
+// Dense f16 GEMM on the 5th-generation tensor cores: Y = X * W^T with X
+// [M, K] and W [N, K] both row-major f16 (K-major for the MMA), f32
+// accumulation in tensor memory. This is the linear layer of the decoder and
+// the encoder (reference: crates/omg-wgpu/src/shaders/matmul.wgsl:1-9 and
+// matmul_gated.wgsl:1-7 — X rounded to f16, the dequantized weight rounded to
+// f16, f32 accumulate; here the weight is dequantized once at load into the
+// exact f16 values the reference produces per use).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace omg {
+
+// What the epilogue does with the f32 accumulator tile.
+enum GemmEpilogue : int {
+  kEpiF32 = 0,        // store f32 rows (split-K partial `blockIdx.z` into its own slab)
+  kEpiGeGluTanh = 1,  // W rows interleaved [gate 128 | up 128]: store f16 gelu_tanh(g) * u
+  kEpiGeGluErf = 2,   // same with the exact (erf) GELU
+  kEpiF16 = 3,        // store f16 rows
+};
+
+struct GemmShape {
+  int n_out;     // valid output columns (N, or the GeGLU width)
+  int k;         // reduction length (multiple of 8)
+  int bn;        // MMA N tile: 128 or 256 (always 256 for GeGLU)
+  int splits;    // split-K factor (f32 epilogue only)
+  int epi;       // GemmEpilogue
+  int n_tiles;   // grid.x
+};
+
+// Tensor maps and launch shape of one (activation buffer, weight) pair,
+// built once when the engine wires its layers.
+struct GemmPlan {
+  CUtensorMap a;  // activations [rows_cap, K] f16, box 64 x 128
+  CUtensorMap b;  // weights [N_rows, K] f16, box 64 x bn
+  GemmShape s;
+  int rows_cap;
+};
+
+// Build the plan. `a_rows_cap` bounds the activation rows the tensor map
+// covers (the workspace capacity); `w_rows` is the weight's row count as
+// stored (for GeGLU: 2 x padded width).
+bool gemm_plan(GemmPlan* p, const void* a, int a_rows_cap, int lda, const void* w, int w_rows,
+               int n_out, int k, int epi, int bn, int splits, char* err, size_t errlen);
+
+// Launch over `m` rows. f32 epilogue: `out` is [splits][m_stride][ldo] f32
+// (slab z at out + z * split_stride). f16 epilogues: [m][ldo] f16.
+void gemm_run(const GemmPlan& p, int m, void* out, int ldo, size_t split_stride,
+              uint32_t* status, cudaStream_t stream);
+
+// Set the kernels' shared-memory limits on the current device (once per
+// device, before the first launch).
+void gemm_setup_device();
+
+// Pick (bn, splits) for an f32-output GEMM of this shape on this GPU. Depends
+// only on (N, K), never on M, so a row's result is the same in every pass.
+void gemm_pick(int n, int k, int num_sms, int* bn, int* splits);
+
+}  // namespace omg

@@ -1,0 +1,550 @@
+/*
+ * omg_oracle.c — TEST INFRASTRUCTURE ONLY (see omg_oracle.h).
+ *
+ * Plain C restatement of the reference's CPU code for the omg-wgpu forward
+ * pass. Built with -ffp-contract=off so a*b+c rounds twice, as Rust does.
+ * The one liberty taken: dot products accumulate in 8 interleaved partial
+ * sums (added in a fixed order) instead of one running sum, so the compiler
+ * can vectorise them; that reassociates f32 additions only.
+ */
+#include "omg_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* ---- f16 ----------------------------------------------------------------- */
+
+uint16_t oracle_f32_to_f16(float v) {
+  uint32_t x;
+  memcpy(&x, &v, 4);
+  const uint32_t sign = (x >> 16) & 0x8000u;
+  const uint32_t exp = (x >> 23) & 0xffu;
+  const uint32_t man = x & 0x7fffffu;
+  if (exp == 0xffu) {
+    if (man) return (uint16_t)(sign | 0x7e00u | (man >> 13));
+    return (uint16_t)(sign | 0x7c00u);
+  }
+  const int e = (int)exp - 127 + 15;
+  if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+  if (e <= 0) {
+    /* Subnormal half: m * 2^-24 with m = (1.man) * 2^(exp - 126). */
+    const int shift = 126 - (int)exp;
+    if (shift > 25) return (uint16_t)sign;
+    const uint64_t full = (uint64_t)(man | 0x800000u);
+    uint64_t m = full >> shift;
+    const uint64_t rem = full & ((1ull << shift) - 1ull);
+    const uint64_t half = 1ull << (shift - 1);
+    if (rem > half || (rem == half && (m & 1ull))) m++;
+    return (uint16_t)(sign | (uint32_t)m);
+  }
+  uint32_t h = sign | ((uint32_t)e << 10) | (man >> 13);
+  const uint32_t rem = man & 0x1fffu;
+  if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h++;
+  return (uint16_t)h;
+}
+
+float oracle_f16_to_f32(uint16_t h) {
+  const uint32_t sign = ((uint32_t)h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1fu;
+  uint32_t man = h & 0x3ffu;
+  uint32_t x;
+  if (exp == 0x1fu) {
+    x = sign | 0x7f800000u | (man << 13);
+  } else if (exp == 0) {
+    if (man == 0) {
+      x = sign;
+    } else {
+      int e = -1;
+      do {
+        e++;
+        man <<= 1;
+      } while (!(man & 0x400u));
+      man &= 0x3ffu;
+      x = sign | ((uint32_t)(127 - 15 - e) << 23) | (man << 13);
+    }
+  } else {
+    x = sign | ((exp - 15 + 127) << 23) | (man << 13);
+  }
+  float v;
+  memcpy(&v, &x, 4);
+  return v;
+}
+
+void oracle_f32_to_f16_n(const float* in, size_t n, uint16_t* out) {
+  for (size_t i = 0; i < n; ++i) out[i] = oracle_f32_to_f16(in[i]);
+}
+
+void oracle_f16_to_f32_n(const uint16_t* in, size_t n, float* out) {
+  for (size_t i = 0; i < n; ++i) out[i] = oracle_f16_to_f32(in[i]);
+}
+
+static float round_f16(float v) { return oracle_f16_to_f32(oracle_f32_to_f16(v)); }
+
+/* ---- xorshift (tests/reference.rs:17-26) ---------------------------------- */
+
+void oracle_rng_values(uint64_t* state, float* out, size_t n, float scale) {
+  uint64_t s = *state;
+  for (size_t i = 0; i < n; ++i) {
+    s ^= s << 13;
+    s ^= s >> 7;
+    s ^= s << 17;
+    const float u = ((float)(s >> 40) / (float)(1ull << 24)) * 2.0f - 1.0f;
+    out[i] = u * scale;
+  }
+  *state = s;
+}
+
+/* ---- quantizers (model.rs:409-466) --------------------------------------- */
+
+static void put_f16(uint8_t* p, float v) {
+  const uint16_t h = oracle_f32_to_f16(v);
+  p[0] = (uint8_t)(h & 0xff);
+  p[1] = (uint8_t)(h >> 8);
+}
+
+static float get_f16(const uint8_t* p) {
+  return oracle_f16_to_f32((uint16_t)(p[0] | ((uint16_t)p[1] << 8)));
+}
+
+int oracle_quantize_q8(const float* v, size_t n, uint8_t* codes, uint8_t* scales) {
+  if (n % 32) return -1;
+  for (size_t b = 0; b < n / 32; ++b) {
+    const float* blk = v + 32 * b;
+    float amax = 0.0f;
+    for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(blk[j]));
+    const float d = amax / 127.0f;
+    const float id = d != 0.0f ? 1.0f / d : 0.0f;
+    put_f16(scales + 2 * b, d);
+    for (int j = 0; j < 32; ++j) {
+      float q = roundf(blk[j] * id);
+      if (q < -127.0f) q = -127.0f;
+      if (q > 127.0f) q = 127.0f;
+      codes[32 * b + j] = (uint8_t)(int8_t)q;
+    }
+  }
+  return 0;
+}
+
+static int clamp_trunc(float x) {
+  /* Rust `as i32` (truncation, saturating), then clamp(0, 15). */
+  int q;
+  if (!(x == x)) q = 0;
+  else if (x >= 2147483647.0f) q = 2147483647;
+  else if (x <= -2147483648.0f) q = (-2147483647 - 1);
+  else q = (int)x;
+  if (q < 0) q = 0;
+  if (q > 15) q = 15;
+  return q;
+}
+
+int oracle_quantize_q4(const float* v, size_t n, uint8_t* codes, uint8_t* scales) {
+  if (n % 32) return -1;
+  for (size_t b = 0; b < n / 32; ++b) {
+    const float* blk = v + 32 * b;
+    float max = 0.0f, amax = 0.0f;
+    for (int j = 0; j < 32; ++j) {
+      if (fabsf(blk[j]) > amax) {
+        amax = fabsf(blk[j]);
+        max = blk[j];
+      }
+    }
+    const float d = max / -8.0f;
+    const float id = d != 0.0f ? 1.0f / d : 0.0f;
+    put_f16(scales + 2 * b, d);
+    for (int j = 0; j < 16; ++j) {
+      const int lo = clamp_trunc(blk[j] * id + 8.5f);
+      const int hi = clamp_trunc(blk[j + 16] * id + 8.5f);
+      codes[16 * b + j] = (uint8_t)(lo | (hi << 4));
+    }
+  }
+  return 0;
+}
+
+int oracle_dequant(int dtype, const uint8_t* codes, const uint8_t* scales, size_t n, float* out) {
+  for (size_t i = 0; i < n; ++i) {
+    if (dtype == 0) {
+      out[i] = get_f16(codes + 2 * i);
+    } else if (dtype == 1) {
+      const float d = get_f16(scales + 2 * (i / 32));
+      out[i] = (float)(int8_t)codes[i] * d;
+    } else if (dtype == 2) {
+      const size_t b = i / 32, j = i % 32;
+      const float d = get_f16(scales + 2 * b);
+      const uint8_t byte = codes[b * 16 + j % 16];
+      const uint8_t q = j < 16 ? (byte & 0xf) : (byte >> 4);
+      out[i] = ((float)q - 8.0f) * d;
+    } else {
+      return -1;
+    }
+  }
+  return 0;
+}
+
+/* ---- forward helpers (tests/reference.rs:141-172) ------------------------- */
+
+static float dot8(const float* a, const float* b, int n) {
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  int i = 0;
+  for (; i + 8 <= n; i += 8)
+    for (int j = 0; j < 8; ++j) acc[j] += a[i + j] * b[i + j];
+  float s = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+  for (; i < n; ++i) s += a[i] * b[i];
+  return s;
+}
+
+/* reference.rs:141-148 */
+static void rmsnorm(const float* x, int n, const float* w, float eps, float offset, float* out) {
+  float ms = 0.0f;
+  for (int i = 0; i < n; ++i) ms += x[i] * x[i];
+  ms /= (float)n;
+  const float inv = 1.0f / sqrtf(ms + eps);
+  for (int i = 0; i < n; ++i) out[i] = x[i] * inv * (w ? offset + w[i] : 1.0f);
+}
+
+/* reference.rs:151-157 for every row of X [t, k]: Y [t, n] = X W^T. */
+static void linear_rows(const float* x, int t, int k, const float* w, int n, int mode, float* y,
+                        int threads) {
+  const float* xs = x;
+  const float* ws = w;
+  float* xr = NULL;
+  float* wr = NULL;
+  if (mode == ORACLE_KERNEL) {
+    xr = (float*)malloc(sizeof(float) * (size_t)t * k);
+    wr = (float*)malloc(sizeof(float) * (size_t)n * k);
+    for (size_t i = 0; i < (size_t)t * k; ++i) xr[i] = round_f16(x[i]);
+    for (size_t i = 0; i < (size_t)n * k; ++i) wr[i] = round_f16(w[i]);
+    xs = xr;
+    ws = wr;
+  }
+#pragma omp parallel for schedule(static) num_threads(threads)
+  for (int r = 0; r < n; ++r)
+    for (int i = 0; i < t; ++i) y[(size_t)i * n + r] = dot8(xs + (size_t)i * k, ws + (size_t)r * k, k);
+  free(xr);
+  free(wr);
+}
+
+/* reference.rs:159-168 */
+static void rope(float* v, int len, int pos, float theta, int rope_dims) {
+  const int half = len / 2;
+  for (int i = 0; i < rope_dims / 2; ++i) {
+    const float ang = (float)pos * powf(theta, -(float)i / (float)half);
+    const float s = sinf(ang), c = cosf(ang);
+    const float a = v[i], b = v[i + half];
+    v[i] = a * c - b * s;
+    v[i + half] = b * c + a * s;
+  }
+}
+
+/* reference.rs:170-172 */
+static float gelu(float x) {
+  return 0.5f * x * (1.0f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x)));
+}
+
+int oracle_visible(int32_t qp, int32_t qs, int32_t kp, int32_t ks, int window) {
+  const int same_group = ((ks ^ qs) >> 12) == 0;
+  return same_group && ((ks & 0xfff) == 0 || ks == qs) && kp <= qp &&
+         (window == 0 || (uint32_t)(qp - kp) < (uint32_t)window);
+}
+
+/* ---- the forward (tests/reference.rs:175-349) ----------------------------- */
+
+typedef struct {
+  const float *attn_norm, *qkv, *q_norm, *k_norm, *o, *post_attn_norm, *ffn_norm, *gate, *up,
+      *down, *post_ffn_norm, *pl_gate, *pl_proj, *pl_norm;
+  float out_scale;
+} layer_w;
+
+int oracle_forward(const oracle_config* cfg, const float* const* tensors, size_t n_tensors,
+                   const uint32_t* ids, const int32_t* pos, const int32_t* seq, size_t t_,
+                   int mode, int threads, float* hidden) {
+  const int d = cfg->d, L = cfg->layers, heads = cfg->heads, kvh = cfg->kv_heads;
+  const int pl = cfg->per_layer_dim;
+  const int t = (int)t_;
+  if (threads <= 0) {
+#ifdef _OPENMP
+    threads = omp_get_max_threads();
+#else
+    threads = 1;
+#endif
+  }
+  /* Catalogue order of Config::tensors (model.rs:277-314). */
+  size_t ti = 0;
+#define NEXT() (ti < n_tensors ? tensors[ti++] : NULL)
+  const float* embed = NEXT();
+  const float* final_norm = NEXT();
+  const float* pl_model_proj = NULL;
+  const float* pl_proj_norm = NULL;
+  if (pl > 0) {
+    pl_model_proj = NEXT();
+    pl_proj_norm = NEXT();
+  }
+  layer_w* lw = (layer_w*)calloc((size_t)L, sizeof(layer_w));
+  for (int l = 0; l < L; ++l) {
+    const int has_kv = cfg->kv_source[l] == l;
+    lw[l].attn_norm = NEXT();
+    lw[l].qkv = NEXT();
+    lw[l].q_norm = NEXT();
+    lw[l].k_norm = has_kv ? NEXT() : NULL;
+    lw[l].o = NEXT();
+    lw[l].post_attn_norm = NEXT();
+    lw[l].ffn_norm = NEXT();
+    lw[l].gate = NEXT();
+    lw[l].up = NEXT();
+    lw[l].down = NEXT();
+    lw[l].post_ffn_norm = NEXT();
+    lw[l].out_scale = 1.0f;
+    if (pl > 0) {
+      lw[l].pl_gate = NEXT();
+      lw[l].pl_proj = NEXT();
+      lw[l].pl_norm = NEXT();
+      const float* os = NEXT();
+      lw[l].out_scale = os ? os[0] : 1.0f;
+    }
+  }
+  const float* pl_table = pl > 0 ? NEXT() : NULL;
+#undef NEXT
+  if (ti != n_tensors || !embed || !final_norm) {
+    free(lw);
+    return -1;
+  }
+  for (int i = 0; i < t; ++i)
+    if ((int)ids[i] >= cfg->vocab) {
+      free(lw);
+      return -2;
+    }
+
+  int max_hd = 0, max_ff = 0, max_qkv = 0;
+  for (int l = 0; l < L; ++l) {
+    if (cfg->head_dim[l] > max_hd) max_hd = cfg->head_dim[l];
+    if (cfg->ff[l] > max_ff) max_ff = cfg->ff[l];
+    const int w = (cfg->kv_source[l] == l ? heads + 2 * kvh : heads) * cfg->head_dim[l];
+    if (w > max_qkv) max_qkv = w;
+  }
+  const size_t T = (size_t)t;
+  float* x = (float*)malloc(sizeof(float) * T * d);
+  float* h = (float*)malloc(sizeof(float) * T * d);
+  float* qkv = (float*)malloc(sizeof(float) * T * max_qkv);
+  float* q = (float*)malloc(sizeof(float) * T * heads * max_hd);
+  float* attn = (float*)malloc(sizeof(float) * T * heads * max_hd);
+  float* a = (float*)malloc(sizeof(float) * T * d);
+  float* gt = (float*)malloc(sizeof(float) * T * max_ff);
+  float* u = (float*)malloc(sizeof(float) * T * max_ff);
+  float* big = (float*)malloc(sizeof(float) * T * (max_ff > d ? max_ff : d));
+  float** kv_k = (float**)calloc((size_t)L, sizeof(float*));
+  float** kv_v = (float**)calloc((size_t)L, sizeof(float*));
+  float* pli = pl > 0 ? (float*)malloc(sizeof(float) * T * pl * L) : NULL;
+
+  /* Embedding times sqrt(d) (reference.rs:183-191). */
+  const float sd = sqrtf((float)d);
+  for (int i = 0; i < t; ++i)
+    for (int k = 0; k < d; ++k) x[(size_t)i * d + k] = embed[(size_t)ids[i] * d + k] * sd;
+
+  /* Per-layer inputs (reference.rs:193-222). */
+  if (pl > 0) {
+    float* p = (float*)malloc(sizeof(float) * T * pl * L);
+    linear_rows(x, t, d, pl_model_proj, pl * L, mode, p, threads);
+    float* sl = (float*)malloc(sizeof(float) * pl);
+    float* nn = (float*)malloc(sizeof(float) * pl);
+    for (int i = 0; i < t; ++i)
+      for (int l = 0; l < L; ++l) {
+        for (int j = 0; j < pl; ++j) sl[j] = p[(size_t)i * pl * L + l * pl + j] / sd;
+        rmsnorm(sl, pl, pl_proj_norm, cfg->eps, cfg->norm_offset, nn);
+        for (int j = 0; j < pl; ++j) {
+          const float e =
+              pl_table[(size_t)ids[i] * pl * L + l * pl + j] * sqrtf((float)pl);
+          pli[(size_t)i * pl * L + l * pl + j] = (nn[j] + e) / sqrtf(2.0f);
+        }
+      }
+    free(p);
+    free(sl);
+    free(nn);
+  }
+
+  for (int li = 0; li < L; ++li) {
+    const layer_w* W = &lw[li];
+    const int hd = cfg->head_dim[li];
+    const int sliding = cfg->sliding[li];
+    const float theta = sliding ? cfg->theta_local : cfg->theta_global;
+    const int has_kv = cfg->kv_source[li] == li;
+    const int hpg = heads / kvh;
+    const int qkv_w = (has_kv ? heads + 2 * kvh : heads) * hd;
+
+    for (int i = 0; i < t; ++i)
+      rmsnorm(x + (size_t)i * d, d, W->attn_norm, cfg->eps, cfg->norm_offset, h + (size_t)i * d);
+    linear_rows(h, t, d, W->qkv, qkv_w, mode, qkv, threads);
+    if (has_kv) {
+      kv_k[li] = (float*)malloc(sizeof(float) * T * kvh * hd);
+      kv_v[li] = (float*)malloc(sizeof(float) * T * kvh * hd);
+    }
+#pragma omp parallel for schedule(static) num_threads(threads)
+    for (int i = 0; i < t; ++i) {
+      const float* row = qkv + (size_t)i * qkv_w;
+      float tmp[1024];
+      for (int hh = 0; hh < heads; ++hh) {
+        rmsnorm(row + hh * hd, hd, W->q_norm, cfg->eps, cfg->norm_offset, tmp);
+        rope(tmp, hd, pos[i], theta, cfg->rope_dims[li]);
+        for (int dd = 0; dd < hd; ++dd)
+          q[(size_t)i * heads * hd + hh * hd + dd] = tmp[dd] * cfg->query_scale;
+      }
+      if (has_kv) {
+        for (int gh = 0; gh < kvh; ++gh) {
+          rmsnorm(row + (heads + gh) * hd, hd, W->k_norm, cfg->eps, cfg->norm_offset, tmp);
+          rope(tmp, hd, pos[i], theta, cfg->rope_dims[li]);
+          memcpy(kv_k[li] + (size_t)i * kvh * hd + gh * hd, tmp, sizeof(float) * hd);
+          const float* vv = row + (heads + kvh + gh) * hd;
+          float* vo = kv_v[li] + (size_t)i * kvh * hd + gh * hd;
+          if (cfg->v_norm)
+            rmsnorm(vv, hd, NULL, cfg->eps, 0.0f, vo);
+          else
+            memcpy(vo, vv, sizeof(float) * hd);
+        }
+      }
+    }
+    const float* K = kv_k[cfg->kv_source[li]];
+    const float* V = kv_v[cfg->kv_source[li]];
+    const int window = sliding ? cfg->window : 0;
+#pragma omp parallel for schedule(dynamic, 4) num_threads(threads)
+    for (int i = 0; i < t; ++i) {
+      float* sc = (float*)malloc(sizeof(float) * T);
+      int* idx = (int*)malloc(sizeof(int) * T);
+      float qh[1024], kj[1024];
+      float* out = attn + (size_t)i * heads * hd;
+      for (int k = 0; k < heads * hd; ++k) out[k] = 0.0f;
+      for (int hh = 0; hh < heads; ++hh) {
+        const int gh = hh / hpg;
+        for (int dd = 0; dd < hd; ++dd) {
+          const float v = q[(size_t)i * heads * hd + hh * hd + dd];
+          qh[dd] = mode == ORACLE_KERNEL ? round_f16(v) : v;
+        }
+        int n = 0;
+        for (int j = 0; j < t; ++j) {
+          if (!oracle_visible(pos[i], seq[i], pos[j], seq[j], window)) continue;
+          const float* kr = K + (size_t)j * kvh * hd + gh * hd;
+          if (mode == ORACLE_KERNEL) {
+            for (int dd = 0; dd < hd; ++dd) kj[dd] = round_f16(kr[dd]);
+            sc[n] = dot8(qh, kj, hd);
+          } else {
+            sc[n] = dot8(qh, kr, hd);
+          }
+          idx[n++] = j;
+        }
+        float m = -3.402823466e38f; /* f32::MIN */
+        for (int s = 0; s < n; ++s) m = fmaxf(m, sc[s]);
+        float lsum = 0.0f;
+        for (int s = 0; s < n; ++s) lsum += expf(sc[s] - m);
+        for (int s = 0; s < n; ++s) {
+          float p;
+          if (mode == ORACLE_KERNEL)
+            p = round_f16(expf(sc[s] - m)) / lsum;
+          else
+            p = expf(sc[s] - m) / lsum;
+          const float* vr = V + (size_t)idx[s] * kvh * hd + gh * hd;
+          for (int dd = 0; dd < hd; ++dd) {
+            const float vv = mode == ORACLE_KERNEL ? round_f16(vr[dd]) : vr[dd];
+            out[hh * hd + dd] += p * vv;
+          }
+        }
+      }
+      free(sc);
+      free(idx);
+    }
+    /* x += post_attn_norm(attn o^T) (reference.rs:286-296) */
+    linear_rows(attn, t, heads * hd, W->o, d, mode, a, threads);
+    for (int i = 0; i < t; ++i) {
+      float* xi = x + (size_t)i * d;
+      rmsnorm(a + (size_t)i * d, d, W->post_attn_norm, cfg->eps, cfg->norm_offset, big);
+      for (int dd = 0; dd < d; ++dd) xi[dd] += big[dd];
+      rmsnorm(xi, d, W->ffn_norm, cfg->eps, cfg->norm_offset, h + (size_t)i * d);
+    }
+    /* GeGLU (reference.rs:297-300) */
+    const int ff = cfg->ff[li];
+    linear_rows(h, t, d, W->gate, ff, mode, gt, threads);
+    linear_rows(h, t, d, W->up, ff, mode, u, threads);
+    for (size_t k = 0; k < T * ff; ++k) big[k] = gelu(gt[k]) * u[k];
+    linear_rows(big, t, ff, W->down, d, mode, a, threads);
+    for (int i = 0; i < t; ++i) {
+      float* xi = x + (size_t)i * d;
+      float tmp[8192];
+      rmsnorm(a + (size_t)i * d, d, W->post_ffn_norm, cfg->eps, cfg->norm_offset, tmp);
+      for (int dd = 0; dd < d; ++dd) xi[dd] += tmp[dd];
+    }
+    float scale = 1.0f;
+    if (pl > 0) {
+      /* reference.rs:310-330 */
+      float* gate = (float*)malloc(sizeof(float) * T * pl);
+      float* gated = (float*)malloc(sizeof(float) * T * pl);
+      linear_rows(x, t, d, W->pl_gate, pl, mode, gate, threads);
+      for (int i = 0; i < t; ++i)
+        for (int j = 0; j < pl; ++j)
+          gated[(size_t)i * pl + j] =
+              gelu(gate[(size_t)i * pl + j]) * pli[(size_t)i * pl * L + li * pl + j];
+      linear_rows(gated, t, pl, W->pl_proj, d, mode, a, threads);
+      for (int i = 0; i < t; ++i) {
+        float tmp[8192];
+        rmsnorm(a + (size_t)i * d, d, W->pl_norm, cfg->eps, cfg->norm_offset, tmp);
+        for (int dd = 0; dd < d; ++dd) x[(size_t)i * d + dd] += tmp[dd];
+      }
+      scale = W->out_scale;
+      free(gate);
+      free(gated);
+    }
+    for (size_t k = 0; k < T * d; ++k) x[k] *= scale;
+  }
+  for (int i = 0; i < t; ++i)
+    rmsnorm(x + (size_t)i * d, d, final_norm, cfg->eps, cfg->norm_offset, hidden + (size_t)i * d);
+
+  for (int l = 0; l < L; ++l) {
+    free(kv_k[l]);
+    free(kv_v[l]);
+  }
+  free(kv_k);
+  free(kv_v);
+  free(x);
+  free(h);
+  free(qkv);
+  free(q);
+  free(attn);
+  free(a);
+  free(gt);
+  free(u);
+  free(big);
+  free(pli);
+  free(lw);
+  return 0;
+}
+
+/* ---- logits and readout --------------------------------------------------- */
+
+void oracle_logits(const float* hidden, const float* embed, int vocab, int d, float softcap,
+                   float* out) {
+  for (int v = 0; v < vocab; ++v) {
+    float z = 0.0f;
+    for (int i = 0; i < d; ++i) z += hidden[i] * embed[(size_t)v * d + i];
+    out[v] = softcap > 0.0f ? softcap * tanhf(z / softcap) : z;
+  }
+}
+
+void oracle_softmax(const float* z, size_t n, float temperature, double* out) {
+  const double t = (double)(temperature > 1e-6f ? temperature : 1e-6f);
+  float m = -INFINITY;
+  for (size_t i = 0; i < n; ++i) m = fmaxf(m, z[i]);
+  double s = 0.0;
+  for (size_t i = 0; i < n; ++i) {
+    out[i] = exp(((double)z[i] - (double)m) / t);
+    s += out[i];
+  }
+  for (size_t i = 0; i < n; ++i) out[i] /= s;
+}
+
+double oracle_log_sum_exp(const float* z, size_t n) {
+  float m = -INFINITY;
+  for (size_t i = 0; i < n; ++i) m = fmaxf(m, z[i]);
+  double s = 0.0;
+  for (size_t i = 0; i < n; ++i) s += exp((double)z[i] - (double)m);
+  return (double)m + log(s);
+}

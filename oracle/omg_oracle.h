@@ -1,0 +1,105 @@
+/*
+ * omg_oracle — TEST INFRASTRUCTURE ONLY.
+ *
+ * A CPU restatement, in plain C, of the reference's own CPU algorithms for the
+ * omg-wgpu forward pass (github.com/bokuweb/omg, crates/omg-wgpu). It is the
+ * checker the parity tests compare the CUDA engine against. Only tests/,
+ * __graft_entry__.smoke() and bench.py's cpu_baseline leg may load it; the
+ * product (grande_b200) never links, imports or calls it.
+ *
+ * Each function cites the reference file:line it restates. Pinning: the
+ * quantizers are checked byte-for-byte against gguf-py 0.19's Q8_0 / Q4_0
+ * quantizers as repacked by the reference's tools/export_wgpu_gguf.py, the
+ * visibility rule against the reference's python/omg_train/model.py
+ * branch_mask, and the decoder forward against transformers 5.5's Gemma 3
+ * text model driven the way python/omg_train/model.py:67-80 drives it
+ * (fixtures in tests/golden/, made by tests/golden/make_golden.py).
+ */
+#ifndef OMG_ORACLE_H
+#define OMG_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* IEEE half <-> float, round to nearest even (the `half` crate's rules). */
+uint16_t oracle_f32_to_f16(float v);
+float oracle_f16_to_f32(uint16_t h);
+
+/* Element-wise batch versions of the two conversions above. */
+void oracle_f32_to_f16_n(const float* in, size_t n, uint16_t* out);
+void oracle_f16_to_f32_n(const uint16_t* in, size_t n, float* out);
+
+/* tests/reference.rs:17-26: xorshift64, uniform in [-1, 1). Fills n values
+ * times `scale`, advancing *state. */
+void oracle_rng_values(uint64_t* state, float* out, size_t n, float scale);
+
+/* model.rs:409-427 (Q8_0) and model.rs:431-466 (Q4_0). n is a multiple of 32;
+ * codes get n (Q8) or n/2 (Q4) bytes, scales n/32 little-endian f16. */
+int oracle_quantize_q8(const float* v, size_t n, uint8_t* codes, uint8_t* scales);
+int oracle_quantize_q4(const float* v, size_t n, uint8_t* codes, uint8_t* scales);
+
+/* model.rs:508-525 QTensor::get for every element. dtype 0 f16 (codes are
+ * little-endian f16), 1 Q8, 2 Q4. */
+int oracle_dequant(int dtype, const uint8_t* codes, const uint8_t* scales, size_t n, float* out);
+
+/* Model description (model.rs:28-63). Per-layer arrays have `layers`
+ * entries. */
+typedef struct {
+  int vocab, d, layers, heads, kv_heads;
+  const int* head_dim;
+  const int* ff;
+  const int* sliding;
+  const int* kv_source;
+  const int* rope_dims;
+  float eps;
+  int window;
+  float theta_global, theta_local, query_scale, norm_offset;
+  int v_norm;
+  int per_layer_dim;
+  float softcap;
+} oracle_config;
+
+/* Rounding modes of oracle_forward. */
+enum {
+  ORACLE_EXACT = 0,   /* tests/reference.rs as written: all f32 */
+  ORACLE_KERNEL = 1   /* the kernels' rounding points: linear inputs and weights
+                         to f16 (matmul.wgsl:1-9), Q/K/V to f16 in attention
+                         (attention.wgsl:80-92,110-117), and, as the CUDA
+                         attention's P.V MMA does, probabilities to f16 */
+};
+
+/* tests/reference.rs:175-349, the plain forward over a packed sequence,
+ * with the shader's visibility rule for grouped sequence ids
+ * (attention.wgsl:70-76; engine.rs:21-24 SEQ_GROUP_SHIFT = 12).
+ *
+ * `tensors` holds dequantized f32 values of every catalogued tensor in the
+ * order of Config::tensors (model.rs:277-314), followed by the per-layer
+ * token table when per_layer_dim > 0. Writes the final-norm hidden state of
+ * every token: hidden[t * d]. threads <= 0 uses all cores. */
+int oracle_forward(const oracle_config* cfg, const float* const* tensors, size_t n_tensors,
+                   const uint32_t* ids, const int32_t* pos, const int32_t* seq, size_t t,
+                   int mode, int threads, float* hidden);
+
+/* The block-causal visibility rule (attention.wgsl:70-76): 1 if a query at
+ * (qp, qs) sees a key at (kp, ks) on a layer with this window (0 = global). */
+int oracle_visible(int32_t qp, int32_t qs, int32_t kp, int32_t ks, int window);
+
+/* tests/reference.rs:581-590 + engine.rs:1901-1906: logits of one hidden row
+ * against the (dequantized) embedding, then softcap if > 0. */
+void oracle_logits(const float* hidden, const float* embed, int vocab, int d, float softcap,
+                   float* out);
+
+/* crates/omg-core/src/math.rs:5-17: softmax of z / temperature and
+ * log-sum-exp, both in f64. */
+void oracle_softmax(const float* z, size_t n, float temperature, double* out);
+double oracle_log_sum_exp(const float* z, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OMG_ORACLE_H */

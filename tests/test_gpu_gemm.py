@@ -1,0 +1,105 @@
+"""The tcgen05 GEMM against an fp32 reference of the same op, rounded the way
+the reference's matmul kernels round (X and W to f16, f32 accumulate:
+crates/omg-wgpu/shaders/matmul.wgsl:1-9, tests/matmul.rs:187-192,221).
+
+Shapes are the reference's odd ones (partial row / column tiles,
+tests/matmul.rs:273-290) plus the BASELINE configs' projection shapes.
+Tolerance 2e-3 relative to max(|expected|, 1), as tests/matmul.rs:232.
+"""
+import numpy as np
+import pytest
+
+from grande_b200 import _lib as L
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+
+
+def gelu_tanh(x):
+    z = np.clip(0.7978845608028654 * (x + 0.044715 * x ** 3), -15, 15)
+    return 0.5 * x * (1.0 + np.tanh(z))
+
+
+def run_gemm(device, x16, w16, n_out, epi, bn=0, splits=1):
+    m, k = x16.shape
+    f32 = epi == 0
+    ldo = n_out if f32 else n_out
+    ldo = (ldo + 7) // 8 * 8
+    out = np.zeros((m, ldo), dtype=np.float32 if f32 else np.float16)
+    L.check(L.lib().omg_debug_gemm(
+        device, L.ptr(x16.view(np.uint16), L.C.c_uint16), m, k, k,
+        L.ptr(np.ascontiguousarray(w16).view(np.uint16), L.C.c_uint16), w16.shape[0], n_out,
+        epi, bn, splits, out.ctypes.data_as(L.C.c_void_p), ldo))
+    return out[:, :n_out].astype(np.float32)
+
+
+def interleave_gate_up(wg, wu):
+    n, k = wg.shape
+    npad = (n + 127) // 128 * 128
+    out = np.zeros((2 * npad, k), dtype=wg.dtype)
+    for b in range(npad // 128):
+        g = wg[128 * b:128 * b + 128]
+        u = wu[128 * b:128 * b + 128]
+        out[256 * b:256 * b + len(g)] = g
+        out[256 * b + 128:256 * b + 128 + len(u)] = u
+    return out
+
+
+def rel_err(got, exp):
+    return float(np.max(np.abs(got - exp) / np.maximum(np.abs(exp), 1.0)))
+
+
+@pytest.mark.parametrize("m,n,k", [(23, 96, 64), (130, 200, 96), (64, 128, 32), (300, 520, 256)])
+@pytest.mark.parametrize("bn", [128, 256])
+def test_matmul_odd_shapes(device, m, n, k, bn):
+    rng = np.random.default_rng(m * n * k + bn)
+    x16 = (rng.uniform(-1, 1, (m, k)) * 4).astype(np.float16)
+    w16 = rng.uniform(-1, 1, (n, k)).astype(np.float16)
+    exp = x16.astype(np.float64) @ w16.astype(np.float64).T
+    got = run_gemm(device, x16, w16, n, 0, bn=bn, splits=1)
+    assert rel_err(got, exp) < TOL
+
+
+@pytest.mark.parametrize("m,n,k", [(23, 96, 64), (70, 100, 160), (200, 300, 128)])
+def test_gated_odd_shapes(device, m, n, k):
+    rng = np.random.default_rng(m + n + k)
+    x16 = rng.uniform(-1, 1, (m, k)).astype(np.float16)
+    wg = rng.uniform(-1, 1, (n, k)).astype(np.float16)
+    wu = rng.uniform(-1, 1, (n, k)).astype(np.float16)
+    w = interleave_gate_up(wg, wu)
+    xd = x16.astype(np.float64)
+    gate = xd @ wg.astype(np.float64).T
+    up = xd @ wu.astype(np.float64).T
+    exp = gelu_tanh(gate) * up
+    got = run_gemm(device, x16, w, n, 1)
+    # the f16 output rounding adds up to 2^-11 relative
+    assert rel_err(got, exp) < TOL + 1e-3
+
+
+@pytest.mark.parametrize("m,n,k,splits", [
+    (788, 3072, 2048, 1),   # E2B qkv
+    (788, 2048, 2048, 2),   # E2B o, split-K
+    (788, 2048, 8192, 2),   # E2B down, split-K
+    (150, 1536, 640, 1),    # 270M qkv
+])
+def test_matmul_config_shapes(device, m, n, k, splits):
+    rng = np.random.default_rng(n + k)
+    x16 = rng.standard_normal((m, k)).astype(np.float16)
+    w16 = (rng.standard_normal((n, k)) * 0.02).astype(np.float16)
+    exp = x16.astype(np.float32) @ w16.astype(np.float32).T
+    got = run_gemm(device, x16, w16, n, 0, bn=128, splits=splits)
+    assert rel_err(got, exp) < TOL
+
+
+def test_gated_config_shape(device):
+    m, n, k = 788, 8192, 2048
+    rng = np.random.default_rng(7)
+    x16 = rng.standard_normal((m, k)).astype(np.float16)
+    wg = (rng.standard_normal((n, k)) * 0.02).astype(np.float16)
+    wu = (rng.standard_normal((n, k)) * 0.02).astype(np.float16)
+    w = interleave_gate_up(wg, wu)
+    xf = x16.astype(np.float32)
+    exp = gelu_tanh(xf @ wg.astype(np.float32).T) * (xf @ wu.astype(np.float32).T)
+    got = run_gemm(device, x16, w, n, 1)
+    assert rel_err(got, exp) < TOL + 1e-3

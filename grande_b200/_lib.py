@@ -44,10 +44,60 @@ class GroupC(C.Structure):
     ]
 
 
-# name -> (restype, argtypes)
+class EngineInfo(C.Structure):
+    _fields_ = [
+        ("d", C.c_int), ("vocab", C.c_int), ("layers", C.c_int), ("embed_dtype", C.c_int),
+        ("per_layer_dim", C.c_int), ("device", C.c_int), ("capacity", C.c_size_t),
+        ("max_rows", C.c_size_t), ("bos", C.c_uint32),
+    ]
+
+
+vp = C.c_void_p
+pp = C.POINTER(C.c_void_p)
+cs = C.c_char_p
+sz = C.c_size_t
+GroupP = C.POINTER(GroupC)
+BranchP = C.POINTER(Branch)
+
+# name -> (restype, argtypes); every function of include/omg_b200.h.
 PROTOTYPES: dict[str, tuple] = {
     "omg_last_error": (C.c_char_p, []),
     "omg_version": (C.c_char_p, []),
+    "omg_device_count": (C.c_int, []),
+    "omg_config_check": (C.c_int, [cs, C.c_char_p, sz]),
+    "omg_config_tensors": (C.c_int, [cs, C.c_char_p, sz, szp]),
+    "omg_builder_new": (C.c_int, [cs, C.c_int, pp]),
+    "omg_builder_push": (C.c_int, [vp, cs, C.c_int, i64p, C.c_int, vp, sz, vp, sz]),
+    "omg_builder_set_per_layer_table": (C.c_int, [vp, C.c_int, i64p, C.c_int, vp, sz, vp, sz]),
+    "omg_builder_missing": (C.c_int, [vp, C.c_char_p, sz, szp]),
+    "omg_builder_finish": (C.c_int, [vp, sz, sz, pp]),
+    "omg_builder_free": (None, [vp]),
+    "omg_engine_evaluate_groups": (C.c_int, [vp, GroupP, sz, C.c_int, f32p, sz, i32p]),
+    "omg_engine_evaluate": (C.c_int, [vp, u32p, sz, BranchP, sz, C.c_int, f32p, sz]),
+    "omg_engine_evaluate_rows": (C.c_int, [vp, u32p, sz, BranchP, sz, C.c_int, vp, sz, f32p, sz]),
+    "omg_engine_warmup": (C.c_int, [vp]),
+    "omg_engine_prefix_source": (C.c_int, [vp]),
+    "omg_engine_is_resident": (C.c_int, [vp, u32p, sz]),
+    "omg_engine_evict_resident": (None, [vp]),
+    "omg_engine_set_state_cache": (C.c_int, [vp, sz, cs, cs]),
+    "omg_engine_save_state": (C.c_int, [vp, u32p, sz, pp]),
+    "omg_engine_restore_state": (C.c_int, [vp, vp]),
+    "omg_engine_gather_per_layer": (C.c_int, [vp, u32p, sz, u8p, sz]),
+    "omg_engine_get_info": (C.c_int, [vp, C.POINTER(EngineInfo)]),
+    "omg_engine_time_forward": (C.c_int, [vp, GroupP, sz, C.c_int, C.c_int, C.c_int, f32p,
+                                          C.POINTER(C.c_int)]),
+    "omg_engine_record_event": (C.c_int, [vp, C.c_int]),
+    "omg_engine_elapsed_ms": (C.c_int, [vp, C.c_int, C.c_int, f32p]),
+    "omg_engine_destroy": (None, [vp]),
+    "omg_state_byte_len": (sz, [vp]),
+    "omg_state_to_bytes": (C.c_int, [vp, cs, u8p, sz, szp]),
+    "omg_state_from_bytes": (C.c_int, [u8p, sz, cs, pp]),
+    "omg_state_prefix": (C.c_int, [vp, u32p, sz, szp]),
+    "omg_state_free": (None, [vp]),
+    "omg_state_key": (C.c_uint64, [cs, u32p, sz]),
+    "omg_quantize": (C.c_int, [C.c_int, f32p, sz, u8p, u8p]),
+    "omg_dequantize": (C.c_int, [C.c_int, u8p, u8p, sz, f32p]),
+    "omg_synth_normal": (C.c_int, [C.c_uint64, cs, C.c_float, C.c_float, f32p, sz]),
     "omg_debug_gemm": (
         C.c_int,
         [C.c_int, u16p, C.c_int, C.c_int, C.c_int, u16p, C.c_int, C.c_int, C.c_int, C.c_int,

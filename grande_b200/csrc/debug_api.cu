@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "capi_util.h"
+#include "attention.cuh"
 #include "gemm.cuh"
 #include "omg_b200.h"
 
@@ -71,6 +72,55 @@ extern "C" int omg_debug_gemm(int device, const uint16_t* x_f16, int m, int k, i
     } else {
       CUDA_TRY(cudaMemcpy(out, dout.p, ob, cudaMemcpyDeviceToHost));
     }
+    return 0;
+  });
+}
+
+// Block-causal attention on host buffers: q [t, heads * hd] f16 (cache rows
+// base..base+t), kv [rows, 2 * kv_heads * hd] f16, meta 4 ints per cache row
+// (pos, seq, row_lo, row_hi), out [t, heads * hd] f16.
+extern "C" int omg_debug_attention(int device, const uint16_t* q, const uint16_t* kv,
+                                   const int32_t* meta, int t, int base, int heads, int kv_heads,
+                                   int hd, int window, uint16_t* out) {
+  return guarded([&]() -> int {
+    CUDA_TRY(cudaSetDevice(device));
+    omg::attention_setup_device();
+    const int rows = base + t;
+    const int rows_pad = (rows + 63) / 64 * 64;
+    DevBuf dq, dkv, dm, dout;
+    const size_t qb = static_cast<size_t>(t) * heads * hd * 2;
+    const size_t kvb = static_cast<size_t>(rows_pad) * 2 * kv_heads * hd * 2;
+    if (!dq.alloc(qb) || !dkv.alloc(kvb) || !dm.alloc(static_cast<size_t>(rows_pad) * 16) ||
+        !dout.alloc(qb))
+      return set_error("cudaMalloc failed");
+    CUDA_TRY(cudaMemset(dkv.p, 0, kvb));
+    CUDA_TRY(cudaMemcpy(dq.p, q, qb, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(dkv.p, kv, static_cast<size_t>(rows) * 2 * kv_heads * hd * 2,
+                        cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(dm.p, meta, static_cast<size_t>(rows) * 16, cudaMemcpyHostToDevice));
+    std::vector<int2> ctas;
+    omg::attention_schedule(reinterpret_cast<const omg::TokMeta*>(meta) + base, t,
+                            heads / kv_heads, &ctas);
+    DevBuf dc;
+    if (!dc.alloc(ctas.size() * sizeof(int2))) return set_error("cudaMalloc failed");
+    CUDA_TRY(cudaMemcpy(dc.p, ctas.data(), ctas.size() * sizeof(int2), cudaMemcpyHostToDevice));
+    omg::AttnArgs a{};
+    a.ctas = static_cast<const int2*>(dc.p);
+    a.n_ctas = static_cast<int>(ctas.size());
+    a.q = static_cast<const __half*>(dq.p);
+    a.kv = static_cast<const __half*>(dkv.p);
+    a.meta = static_cast<const omg::TokMeta*>(dm.p);
+    a.out = static_cast<__half*>(dout.p);
+    a.t = t;
+    a.base = base;
+    a.heads = heads;
+    a.kv_heads = kv_heads;
+    a.hd = hd;
+    a.window = window;
+    omg::launch_attention(a, 0);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaDeviceSynchronize());
+    CUDA_TRY(cudaMemcpy(out, dout.p, qb, cudaMemcpyDeviceToHost));
     return 0;
   });
 }

@@ -1,0 +1,977 @@
+// The decoder engine (see engine.h). Reference: crates/omg-wgpu/src/engine.rs.
+#include "engine.h"
+
+#include <sys/stat.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <sstream>
+
+#include "attention.cuh"
+#include "capi_util.h"
+
+namespace omg {
+
+// ---- buffers ----------------------------------------------------------------
+
+void DevBuffer::alloc(size_t n, bool zero) {
+  release();
+  bytes = n ? n : 16;
+  CUDA_TRY(cudaMalloc(&p, bytes));
+  if (zero) CUDA_TRY(cudaMemset(p, 0, bytes));
+}
+
+void DevBuffer::release() {
+  if (p) cudaFree(p);
+  p = nullptr;
+  bytes = 0;
+}
+
+void PinnedBuffer::alloc(size_t n) {
+  if (p) cudaFreeHost(p);
+  bytes = n ? n : 16;
+  CUDA_TRY(cudaMallocHost(&p, bytes));
+}
+
+PinnedBuffer::~PinnedBuffer() {
+  if (p) cudaFreeHost(p);
+}
+
+float HostTensor::get(size_t i) const {
+  if (dtype == 0) return f16_to_f32(static_cast<uint16_t>(data[2 * i] | (data[2 * i + 1] << 8)));
+  // Decode the 32-element block holding element i (model.rs:508-525).
+  float blk[32];
+  const size_t b = i / 32;
+  dequantize(dtype, data.data() + (dtype == 1 ? b * 32 : b * 16), scales.data() + 2 * b, 32, blk);
+  return blk[i % 32];
+}
+
+// ---- SavedState (engine.rs:503-580) ----------------------------------------
+
+size_t SavedState::byte_len() const {
+  size_t n = prefix.size() * 4;
+  for (const auto& l : layers) n += l.bytes.size();
+  return n;
+}
+
+static void put_u32(std::vector<uint8_t>& out, uint32_t v) {
+  for (int i = 0; i < 4; ++i) out.push_back(static_cast<uint8_t>(v >> (8 * i)));
+}
+
+std::vector<uint8_t> SavedState::to_bytes(const std::string& model_id) const {
+  std::vector<uint8_t> out;
+  out.reserve(byte_len() + 64 + model_id.size());
+  const char magic[6] = {'G', 'R', 'W', 'S', '1', '\0'};
+  out.insert(out.end(), magic, magic + 6);
+  put_u32(out, static_cast<uint32_t>(model_id.size()));
+  out.insert(out.end(), model_id.begin(), model_id.end());
+  put_u32(out, static_cast<uint32_t>(prefix.size()));
+  for (uint32_t t : prefix) put_u32(out, t);
+  put_u32(out, static_cast<uint32_t>(layers.size()));
+  for (const auto& l : layers) {
+    put_u32(out, static_cast<uint32_t>(l.layer));
+    put_u32(out, static_cast<uint32_t>(l.row0));
+    put_u32(out, static_cast<uint32_t>(l.bytes.size()));
+    out.insert(out.end(), l.bytes.begin(), l.bytes.end());
+  }
+  return out;
+}
+
+SavedState SavedState::from_bytes(const uint8_t* b, size_t n, const std::string& model_id) {
+  size_t at = 0;
+  auto take = [&](size_t k) -> const uint8_t* {
+    if (at + k > n || at + k < at) fail("state file truncated");
+    const uint8_t* p = b + at;
+    at += k;
+    return p;
+  };
+  auto u32 = [&]() -> size_t {
+    const uint8_t* p = take(4);
+    return static_cast<size_t>(p[0]) | (static_cast<size_t>(p[1]) << 8) |
+           (static_cast<size_t>(p[2]) << 16) | (static_cast<size_t>(p[3]) << 24);
+  };
+  const uint8_t* magic = take(6);
+  if (std::memcmp(magic, "GRWS1\0", 6) != 0) fail("not a omg wgpu state file");
+  const size_t idn = u32();
+  const uint8_t* id = take(idn);
+  if (idn != model_id.size() || std::memcmp(id, model_id.data(), idn) != 0)
+    fail("state file is for a different model");
+  SavedState s;
+  const size_t np = u32();
+  const uint8_t* pp = take(np * 4);
+  s.prefix.resize(np);
+  for (size_t i = 0; i < np; ++i)
+    s.prefix[i] = static_cast<uint32_t>(pp[4 * i]) | (static_cast<uint32_t>(pp[4 * i + 1]) << 8) |
+                  (static_cast<uint32_t>(pp[4 * i + 2]) << 16) |
+                  (static_cast<uint32_t>(pp[4 * i + 3]) << 24);
+  const size_t nl = u32();
+  for (size_t i = 0; i < nl; ++i) {
+    Layer l;
+    l.layer = static_cast<int>(u32());
+    l.row0 = static_cast<int>(u32());
+    const size_t len = u32();
+    const uint8_t* d = take(len);
+    l.bytes.assign(d, d + len);
+    s.layers.push_back(std::move(l));
+  }
+  return s;
+}
+
+std::optional<SavedState> StateCache::get(const std::vector<uint32_t>& prefix) {
+  for (size_t i = 0; i < entries.size(); ++i) {
+    if (entries[i].prefix == prefix) {
+      SavedState s = std::move(entries[i]);
+      entries.erase(entries.begin() + static_cast<long>(i));
+      entries.push_back(s);
+      return s;
+    }
+  }
+  return std::nullopt;
+}
+
+void StateCache::put(SavedState s) {
+  const size_t len = s.byte_len();
+  if (len > budget) return;
+  for (size_t i = 0; i < entries.size(); ++i)
+    if (entries[i].prefix == s.prefix) {
+      used -= entries[i].byte_len();
+      entries.erase(entries.begin() + static_cast<long>(i));
+      break;
+    }
+  while (used + len > budget && !entries.empty()) {
+    used -= entries.front().byte_len();
+    entries.erase(entries.begin());
+  }
+  used += len;
+  entries.push_back(std::move(s));
+}
+
+uint64_t state_key(const std::string& model_id, const uint32_t* prefix, size_t n) {
+  uint64_t h = 0xcbf29ce484222325ull;
+  auto eat = [&](uint8_t b) {
+    h ^= b;
+    h *= 0x00000100000001b3ull;
+  };
+  for (char c : model_id) eat(static_cast<uint8_t>(c));
+  eat(0);
+  for (size_t i = 0; i < n; ++i)
+    for (int k = 0; k < 4; ++k) eat(static_cast<uint8_t>(prefix[i] >> (8 * k)));
+  return h;
+}
+
+// ---- builder (engine.rs:845-952) --------------------------------------------
+
+static std::string shape_str(const std::vector<int64_t>& s) {
+  std::string o = "[";
+  for (size_t i = 0; i < s.size(); ++i) o += (i ? ", " : "") + std::to_string(s[i]);
+  return o + "]";
+}
+
+EngineBuilder::EngineBuilder(Config cfg, int device) : cfg_(std::move(cfg)), device_(device) {
+  cfg_.validate();
+  int n = 0;
+  CUDA_TRY(cudaGetDeviceCount(&n));
+  if (device < 0 || device >= n) fail("CUDA device %d not present (%d visible)", device, n);
+  CUDA_TRY(cudaSetDevice(device_));
+  int major = 0, minor = 0;
+  CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device_));
+  CUDA_TRY(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device_));
+  if (major != 10 || minor != 0)
+    fail("device %d is sm_%d%d; this library is built for sm_100a (B200)", device, major, minor);
+  CUDA_TRY(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+  for (const auto& s : cfg_.tensors()) expected_[s.name] = s.shape;
+}
+
+EngineBuilder::~EngineBuilder() {
+  if (stream_) cudaStreamDestroy(stream_);
+}
+
+std::vector<std::string> EngineBuilder::missing() const {
+  std::vector<std::string> v;
+  for (const auto& kv : expected_)
+    if (!pushed_.count(kv.first)) v.push_back(kv.first);
+  std::sort(v.begin(), v.end());
+  return v;
+}
+
+static bool ends_with(const std::string& s, const char* suf) {
+  const size_t n = std::strlen(suf);
+  return s.size() >= n && s.compare(s.size() - n, n, suf) == 0;
+}
+
+void EngineBuilder::push(const std::string& name, const HostTensor& t) {
+  CUDA_TRY(cudaSetDevice(device_));
+  auto it = expected_.find(name);
+  if (it == expected_.end()) fail("unexpected tensor %s", name.c_str());
+  if (t.shape != it->second)
+    fail("%s: shape %s, expected %s", name.c_str(), shape_str(t.shape).c_str(),
+         shape_str(it->second).c_str());
+  const size_t n = t.numel();
+  if (t.dtype < 0 || t.dtype > 2) fail("%s: unsupported dtype %d", name.c_str(), t.dtype);
+  // QTensor::from_raw's payload checks (model.rs:484-505).
+  if (t.data.size() != payload_bytes(t.dtype, n))
+    fail("%s: %zu payload bytes, expected %zu", name.c_str(), t.data.size(),
+         payload_bytes(t.dtype, n));
+  const size_t want_scales = t.dtype == 0 ? 0 : n / 32 * 2;
+  if (t.scales.size() != want_scales)
+    fail("%s: %zu scale bytes, expected %zu", name.c_str(), t.scales.size(), want_scales);
+  if (ends_with(name, "out_scale")) {
+    scalars_[name] = t.get(0);
+    pushed_[name] = true;
+    return;
+  }
+  if (t.shape.size() == 1 && t.dtype != 0) fail("%s: 1-D tensors must be f16", name.c_str());
+  if (t.shape.size() == 2 && t.shape[1] % 32 != 0)
+    fail("%s: inner dimension %lld is not a multiple of 32", name.c_str(),
+         static_cast<long long>(t.shape[1]));
+  if (t.shape.size() == 1) {
+    std::vector<float> f(n);
+    dequantize(0, t.data.data(), nullptr, n, f.data());
+    DevBuffer b;
+    b.alloc(n * 4, false);
+    CUDA_TRY(cudaMemcpy(b.p, f.data(), n * 4, cudaMemcpyHostToDevice));
+    norms_[name] = std::move(b);
+    pushed_[name] = true;
+    return;
+  }
+  if (name == "embed") {
+    embed_.dtype = t.dtype;
+    embed_.codes.alloc(t.data.size(), false);
+    CUDA_TRY(cudaMemcpy(embed_.codes.p, t.data.data(), t.data.size(), cudaMemcpyHostToDevice));
+    embed_.scales.alloc(std::max<size_t>(t.scales.size(), 16), true);
+    if (!t.scales.empty())
+      CUDA_TRY(cudaMemcpy(embed_.scales.p, t.scales.data(), t.scales.size(),
+                          cudaMemcpyHostToDevice));
+    pushed_[name] = true;
+    return;
+  }
+  // A linear: dequantize into its f16 layout (bit-exact QTensor::get rounded
+  // to f16, what weight.wgsl's dq*_pair decoders produce per use).
+  const int rows = static_cast<int>(t.shape[0]), k = static_cast<int>(t.shape[1]);
+  DevBuffer codes, scales;
+  codes.alloc(t.data.size(), false);
+  CUDA_TRY(cudaMemcpy(codes.p, t.data.data(), t.data.size(), cudaMemcpyHostToDevice));
+  if (!t.scales.empty()) {
+    scales.alloc(t.scales.size(), false);
+    CUDA_TRY(cudaMemcpy(scales.p, t.scales.data(), t.scales.size(), cudaMemcpyHostToDevice));
+  }
+  std::string key = name;
+  int remap = 0;
+  size_t out_rows = static_cast<size_t>(rows);
+  if (ends_with(name, ".gate") || ends_with(name, ".up")) {
+    key = name.substr(0, name.rfind('.')) + ".gate_up";
+    remap = ends_with(name, ".gate") ? 1 : 2;
+    out_rows = static_cast<size_t>((rows + 127) / 128) * 256;
+  }
+  auto lit = lin_.find(key);
+  if (lit == lin_.end()) {
+    DevBuffer b;
+    b.alloc(out_rows * k * 2, remap != 0);
+    lit = lin_.emplace(key, std::move(b)).first;
+  }
+  launch_dequant_f16(t.dtype, codes.p, scales.p, rows, k, remap, lit->second.as<__half>(), stream_);
+  CUDA_TRY(cudaGetLastError());
+  CUDA_TRY(cudaStreamSynchronize(stream_));
+  pushed_[name] = true;
+}
+
+void EngineBuilder::set_per_layer_table(HostTensor t) {
+  const std::vector<int64_t> want = {cfg_.vocab,
+                                     static_cast<int64_t>(cfg_.per_layer_dim) * cfg_.layers};
+  if (t.shape != want)
+    fail("per-layer table: shape %s, expected %s", shape_str(t.shape).c_str(),
+         shape_str(want).c_str());
+  per_layer_table_ = std::move(t);
+}
+
+std::unique_ptr<Engine> EngineBuilder::finish(size_t capacity, size_t max_rows) {
+  const auto miss = missing();
+  if (!miss.empty()) {
+    std::string e;
+    for (size_t i = 0; i < std::min<size_t>(4, miss.size()); ++i) e += (i ? ", " : "") + miss[i];
+    fail("%zu tensors missing, e.g. %s", miss.size(), e.c_str());
+  }
+  if (capacity == 0) fail("capacity must be positive");
+  return std::unique_ptr<Engine>(new Engine(std::move(*this), capacity, max_rows));
+}
+
+// ---- engine ------------------------------------------------------------------
+
+Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
+    : config(b.cfg_), capacity(capacity_), max_rows(max_rows_), device_(b.device_) {
+  CUDA_TRY(cudaSetDevice(device_));
+  CUDA_TRY(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device_));
+  stream_ = b.stream_;
+  b.stream_ = nullptr;
+  lin_ = std::move(b.lin_);
+  norms_ = std::move(b.norms_);
+  embed_.dtype = b.embed_.dtype;
+  embed_.codes = std::move(b.embed_.codes);
+  embed_.scales = std::move(b.embed_.scales);
+  per_layer_table_ = std::move(b.per_layer_table_);
+  gemm_setup_device();
+  attention_setup_device();
+
+  const Config& c = config;
+  const int d = c.d, L = c.layers, P = c.per_layer_dim;
+  for (int l = 0; l < L; ++l) {
+    max_qkv_ = std::max(max_qkv_, c.qkv_width(l));
+    max_ff_ = std::max(max_ff_, c.ff[l]);
+  }
+  max_attn_ = c.heads * c.max_head_dim();
+  // Cache rows rounded up to whole 64-key tiles: the attention kernel may
+  // stage a tile that ends past the last used row.
+  cap_rows_ = (capacity + 63) / 64 * 64;
+  const size_t C = capacity;
+  const size_t Cpad = cap_rows_;
+  const int S = 2;  // split-K slabs the f32 GEMM outputs may use
+
+  // Workspace. Zero-initialised, so rows a kernel reads but no pass has
+  // written (padding, stale tile tails) are finite.
+  ids_.alloc(Cpad * 4);
+  meta_.alloc(Cpad * sizeof(TokMeta));
+  row_map_.alloc(Cpad * 4);
+  x_.alloc(Cpad * d * 4);
+  h16_.alloc(Cpad * d * 2);
+  qkv_.alloc(S * Cpad * max_qkv_ * 4);
+  q16_.alloc(Cpad * max_attn_ * 2);
+  attn16_.alloc(Cpad * max_attn_ * 2);
+  a32_.alloc(S * Cpad * d * 4);
+  act16_.alloc(Cpad * std::max(max_ff_, P) * 2);
+  rows_.alloc(std::max<size_t>(max_rows, 1) * d * 4);
+  logits_.alloc(std::max<size_t>(max_rows, 1) * c.vocab * 4);
+  status_.alloc(16);
+  if (P > 0) {
+    x16_.alloc(Cpad * d * 2);
+    pl_rows16_.alloc(Cpad * P * L * 2);
+    pli_.alloc(Cpad * P * L * 4);
+    plp_.alloc(Cpad * std::max(P * L, d) * 4);
+  }
+  kv_.resize(L);
+  for (int l = 0; l < L; ++l)
+    if (c.has_kv(l)) kv_[l].alloc(Cpad * 2 * c.kv_heads * c.head_dim[l] * 2);
+  attn_ctas_.alloc(Cpad * sizeof(int2));
+  h_attn_ctas_.alloc(Cpad * sizeof(int2));
+  h_ids_.alloc(Cpad * 4);
+  h_meta_.alloc(Cpad * sizeof(TokMeta));
+  h_row_map_.alloc(Cpad * 4);
+  h_out_.alloc(std::max<size_t>(max_rows, 1) * std::max(c.vocab, d) * 4);
+  h_status_.alloc(16);
+  for (auto& e : events_) CUDA_TRY(cudaEventCreate(&e));
+
+  auto norm = [&](const std::string& n) -> const float* { return norms_.at(n).as<float>(); };
+  auto lin = [&](const std::string& n) -> const __half* { return lin_.at(n).as<__half>(); };
+  final_norm_ = norm("final_norm");
+  char err[512];
+  auto plan = [&](GemmPlan* p, const void* a, int lda, const __half* w, int w_rows, int n_out,
+                  int k, int epi, const char* what, int l) {
+    int bn = 256, splits = 1;
+    if (epi == kEpiF32) gemm_pick(n_out, k, num_sms_, &bn, &splits);
+    if (!gemm_plan(p, a, static_cast<int>(C), lda, w, w_rows, n_out, k, epi, bn,
+                   std::min(splits, S), err, sizeof err))
+      fail("layer %d %s: %s", l, what, err);
+  };
+  layers_.resize(L);
+  for (int l = 0; l < L; ++l) {
+    Layer& ly = layers_[l];
+    auto n = [&](const char* s) { return "blk." + std::to_string(l) + "." + s; };
+    ly.hd = c.head_dim[l];
+    ly.ff = c.ff[l];
+    ly.qkv_w = c.qkv_width(l);
+    ly.sliding = c.sliding[l];
+    ly.has_kv = c.has_kv(l);
+    ly.kv_src = c.kv_source[l];
+    ly.attn_norm = norm(n("attn_norm"));
+    ly.q_norm = norm(n("q_norm"));
+    ly.k_norm = ly.has_kv ? norm(n("k_norm")) : nullptr;
+    ly.post_attn_norm = norm(n("post_attn_norm"));
+    ly.ffn_norm = norm(n("ffn_norm"));
+    ly.post_ffn_norm = norm(n("post_ffn_norm"));
+    ly.next_norm = l + 1 == L ? final_norm_ : norm("blk." + std::to_string(l + 1) + ".attn_norm");
+    auto sc = b.scalars_.find(n("out_scale"));
+    ly.out_scale = sc == b.scalars_.end() ? 1.f : sc->second;
+    ly.w_qkv = lin(n("qkv"));
+    ly.w_o = lin(n("o"));
+    ly.w_gu = lin(n("gate_up"));
+    ly.w_down = lin(n("down"));
+    const int attn_w = c.heads * ly.hd;
+    plan(&ly.qkv, h16_.p, d, ly.w_qkv, ly.qkv_w, ly.qkv_w, d, kEpiF32, "qkv", l);
+    plan(&ly.o, attn16_.p, attn_w, ly.w_o, d, d, attn_w, kEpiF32, "o", l);
+    plan(&ly.gate_up, h16_.p, d, ly.w_gu, (ly.ff + 127) / 128 * 256, ly.ff, d, kEpiGeGluTanh,
+         "gate_up", l);
+    plan(&ly.down, act16_.p, ly.ff, ly.w_down, d, d, ly.ff, kEpiF32, "down", l);
+    if (P > 0) {
+      ly.pl_norm = norm(n("pl_norm"));
+      plan(&ly.pl_gate, x16_.p, d, lin(n("pl_gate")), P, P, d, kEpiF32, "pl_gate", l);
+      plan(&ly.pl_proj, act16_.p, P, lin(n("pl_proj")), d, d, P, kEpiF32, "pl_proj", l);
+    }
+  }
+  if (P > 0) plan(&pl_model_proj_, x16_.p, d, lin("pl_model_proj"), P * L, P * L, d, kEpiF32,
+                  "pl_model_proj", -1);
+  CUDA_TRY(cudaStreamSynchronize(stream_));
+}
+
+Engine::~Engine() {
+  cudaSetDevice(device_);
+  if (stream_) cudaStreamSynchronize(stream_);
+  for (auto& e : events_)
+    if (e) cudaEventDestroy(e);
+  if (stream_) cudaStreamDestroy(stream_);
+}
+
+std::optional<PrefixSource> Engine::prefix_source() const {
+  std::lock_guard<std::mutex> g(mu_);
+  return last_source_;
+}
+
+bool Engine::is_resident(const uint32_t* prefix, size_t n) const {
+  std::lock_guard<std::mutex> g(mu_);
+  return n > 0 && resident_ && resident_->size() == n &&
+         std::equal(resident_->begin(), resident_->end(), prefix);
+}
+
+void Engine::evict_resident() {
+  std::lock_guard<std::mutex> g(mu_);
+  resident_.reset();
+}
+
+void Engine::set_state_cache(size_t bytes, const std::string& dir, const std::string& model_id) {
+  std::lock_guard<std::mutex> g(mu_);
+  states_ = StateCache{};
+  states_.budget = bytes;
+  state_dir_ = dir;
+  model_id_ = model_id;
+}
+
+std::vector<uint8_t> Engine::gather_per_layer(const uint32_t* ids, size_t n) const {
+  if (!per_layer_table_) fail("this model needs per-layer embedding rows; none loaded");
+  const HostTensor& t = *per_layer_table_;
+  const size_t width = static_cast<size_t>(t.shape[1]);
+  std::vector<uint8_t> out(n * width * 2);
+  std::vector<float> row(width);
+  for (size_t i = 0; i < n; ++i) {
+    const size_t r = ids[i];
+    if (t.dtype == 0) {
+      std::memcpy(out.data() + i * width * 2, t.data.data() + r * width * 2, width * 2);
+      continue;
+    }
+    const size_t bpr = width / 32;
+    dequantize(t.dtype, t.data.data() + r * bpr * (t.dtype == 1 ? 32 : 16),
+               t.scales.data() + r * bpr * 2, width, row.data());
+    for (size_t j = 0; j < width; ++j) {
+      const uint16_t h = f32_to_f16(row[j]);
+      out[i * width * 2 + 2 * j] = static_cast<uint8_t>(h & 0xff);
+      out[i * width * 2 + 2 * j + 1] = static_cast<uint8_t>(h >> 8);
+    }
+  }
+  return out;
+}
+
+// engine.rs:1467-1477
+std::pair<size_t, std::optional<PrefixSource>> Engine::admit(const GroupIn* groups, size_t n) {
+  for (size_t i = 0; i < n; ++i)
+    if (is_resident(groups[i].prefix, groups[i].n_prefix))
+      return {i, PrefixSource::Resident};
+  for (size_t i = 0; i < n; ++i) {
+    auto src = restore_from_cache(groups[i].prefix, groups[i].n_prefix);
+    if (src) return {i, src};
+  }
+  return {0, std::nullopt};
+}
+
+// engine.rs:1492-1583: layout order (first, then the rest), per-token
+// metadata, wanted rows, and the request checks with the reference's
+// messages.
+Engine::Packing Engine::pack(const GroupIn* groups, size_t n, size_t first,
+                             bool resident_first) const {
+  Packing p;
+  size_t total = 0;
+  for (size_t i = 0; i < n; ++i) total += groups[i].tokens();
+  if (total > capacity) fail("%zu tokens exceed the engine capacity %zu", total, capacity);
+  if (total == 0) fail("empty request");
+  const size_t p0 = groups[first].n_prefix;
+  p.base = resident_first ? p0 : 0;
+  p.t = total - p.base;
+  p.ids.reserve(p.t);
+  p.meta.reserve(p.t);
+  // Flat output offsets: groups in call order, branches, want slots.
+  std::vector<size_t> group_off(n + 1, 0);
+  for (size_t i = 0; i < n; ++i) group_off[i + 1] = group_off[i] + groups[i].rows();
+  std::vector<size_t> order;
+  order.push_back(first);
+  for (size_t i = 0; i < n; ++i)
+    if (i != first) order.push_back(i);
+  struct Want {
+    size_t out_row, ws_row;
+  };
+  std::vector<Want> wanted;
+  for (size_t k = 0; k < order.size(); ++k) {
+    const size_t gi = order[k];
+    const GroupIn& g = groups[gi];
+    if (g.n_branches >= (1u << 12))
+      fail("%zu branches in one group; the engine addresses at most %u", g.n_branches,
+           (1u << 12) - 1);
+    const int seq_hi = static_cast<int>(k) << 12;
+    const size_t row_lo = k == 0 ? 0 : p.base + p.ids.size();
+    if (!(k == 0 && p.base > 0)) {
+      p.decoded.emplace_back(gi, p.base + p.ids.size());
+      for (size_t i = 0; i < g.n_prefix; ++i) {
+        const size_t row = p.base + p.ids.size();
+        p.meta.push_back({static_cast<int>(i), seq_hi, static_cast<int>(row_lo),
+                          static_cast<int>(row + 1)});
+        p.ids.push_back(static_cast<int32_t>(g.prefix[i]));
+      }
+    }
+    size_t out_row = group_off[gi];
+    for (size_t bi = 0; bi < g.n_branches; ++bi) {
+      const BranchIn& br = g.branches[bi];
+      const size_t start = p.ids.size();
+      for (size_t j = 0; j < br.n_tokens; ++j) {
+        const size_t row = p.base + p.ids.size();
+        p.meta.push_back({static_cast<int>(g.n_prefix + j), seq_hi | static_cast<int>(bi + 1),
+                          static_cast<int>(row_lo), static_cast<int>(row + 1)});
+        p.ids.push_back(br.tokens[j]);
+      }
+      for (size_t s = 0; s < br.n_want; ++s) {
+        if (br.want[s] >= br.n_tokens)
+          fail("branch %zu: wanted position %zu past its %zu tokens", bi, br.want[s],
+               br.n_tokens);
+        wanted.push_back({out_row++, start + br.want[s]});
+      }
+    }
+  }
+  if (wanted.size() > max_rows)
+    fail("%zu rows requested, engine reads back at most %zu", wanted.size(), max_rows);
+  for (int32_t id : p.ids)
+    if (id < 0 || id >= config.vocab)
+      fail("token id %u outside the vocabulary of %d", static_cast<uint32_t>(id), config.vocab);
+  // Several wanted slots may name the same token; the device writes each
+  // token's row once (to its first slot) and the host copies duplicates.
+  p.row_map.assign(p.t, -1);
+  p.out_index.resize(wanted.size());
+  p.nwanted = 0;
+  std::vector<int32_t> dev_row_of_ws(p.t, -1);
+  for (size_t w = 0; w < wanted.size(); ++w) {
+    const size_t ws = wanted[w].ws_row;
+    if (dev_row_of_ws[ws] < 0) {
+      dev_row_of_ws[ws] = static_cast<int32_t>(p.nwanted++);
+      p.row_map[ws] = dev_row_of_ws[ws];
+    }
+    // out_index[device row order] is filled below
+  }
+  attention_schedule(p.meta.data(), static_cast<int>(p.t), config.heads / config.kv_heads,
+                     &p.attn_ctas);
+  // out_index[w] = device row of wanted slot w, paired with its flat out row.
+  p.out_index.clear();
+  for (const auto& w : wanted) {
+    p.out_index.push_back(static_cast<size_t>(dev_row_of_ws[w.ws_row]));
+    p.out_index.push_back(w.out_row);
+  }
+  return p;
+}
+
+void Engine::upload(const Packing& p, const uint8_t* per_layer_rows, size_t rows_bytes) {
+  std::memcpy(h_ids_.p, p.ids.data(), p.t * 4);
+  std::memcpy(h_meta_.p, p.meta.data(), p.t * sizeof(TokMeta));
+  std::memcpy(h_row_map_.p, p.row_map.data(), p.t * 4);
+  CUDA_TRY(cudaMemcpyAsync(ids_.p, h_ids_.p, p.t * 4, cudaMemcpyHostToDevice, stream_));
+  CUDA_TRY(cudaMemcpyAsync(meta_.as<TokMeta>() + p.base, h_meta_.p, p.t * sizeof(TokMeta),
+                           cudaMemcpyHostToDevice, stream_));
+  CUDA_TRY(cudaMemcpyAsync(row_map_.p, h_row_map_.p, p.t * 4, cudaMemcpyHostToDevice, stream_));
+  std::memcpy(h_attn_ctas_.p, p.attn_ctas.data(), p.attn_ctas.size() * sizeof(int2));
+  CUDA_TRY(cudaMemcpyAsync(attn_ctas_.p, h_attn_ctas_.p, p.attn_ctas.size() * sizeof(int2),
+                           cudaMemcpyHostToDevice, stream_));
+  const int P = config.per_layer_dim;
+  if (P > 0) {
+    if (!per_layer_rows) fail("per-layer embedding rows required");
+    const size_t row_bytes = static_cast<size_t>(P) * config.layers * 2;
+    const size_t total = p.base + p.t;
+    const uint8_t* src = per_layer_rows;
+    if (rows_bytes == total * row_bytes)
+      src = per_layer_rows + p.base * row_bytes;
+    else if (rows_bytes != p.t * row_bytes)
+      fail("per-layer rows: %zu bytes, expected %zu (or %zu with the prefix)", rows_bytes,
+           p.t * row_bytes, total * row_bytes);
+    CUDA_TRY(cudaMemcpyAsync(pl_rows16_.p, src, p.t * row_bytes, cudaMemcpyHostToDevice, stream_));
+  }
+}
+
+// The whole network for one pass, launched on the engine's stream
+// (engine.rs:1610-1759 records the same plan). Returns the number of kernel
+// launches.
+int Engine::launch_forward(const Packing& p, Want want) {
+  const Config& c = config;
+  const int t = static_cast<int>(p.t);
+  const int d = c.d, L = c.layers, P = c.per_layer_dim;
+  const size_t C = capacity;
+  const size_t slab_a = cap_rows_ * d;
+  const size_t slab_qkv = cap_rows_ * max_qkv_;
+  uint32_t* status = status_.as<uint32_t>();
+  int launches = 0;
+  CUDA_TRY(cudaMemsetAsync(status, 0, 4, stream_));
+  (void)C;
+
+  launch_embed_norm(embed_.dtype, ids_.as<int>(), t, embed_.codes.p, embed_.scales.p, d,
+                    std::sqrt(static_cast<float>(d)), layers_[0].attn_norm, c.eps, c.norm_offset,
+                    x_.as<float>(), P > 0 ? x16_.as<__half>() : nullptr, h16_.as<__half>(), d,
+                    stream_);
+  ++launches;
+  if (P > 0) {
+    gemm_run(pl_model_proj_, t, plp_.p, P * L, 0, status, stream_);
+    launch_pl_combine(plp_.as<float>(), t, P, L, norms_.at("pl_proj_norm").as<float>(),
+                      pl_rows16_.as<__half>(), c.eps, c.norm_offset,
+                      1.0f / std::sqrt(static_cast<float>(d)), std::sqrt(static_cast<float>(P)),
+                      1.0f / std::sqrt(2.0f), pli_.as<float>(), stream_);
+    launches += 2;
+  }
+  for (int li = 0; li < L; ++li) {
+    const Layer& ly = layers_[li];
+    const bool last = li + 1 == L;
+    // QKV projection.
+    gemm_run(ly.qkv, t, qkv_.p, ly.qkv_w, slab_qkv, status, stream_);
+    // q/k norm + RoPE, K/V into the cache.
+    QkArgs qa{};
+    qa.qkv = qkv_.as<float>();
+    qa.q_stride = ly.qkv_w;
+    qa.splits = ly.qkv.s.splits;
+    qa.split_stride = slab_qkv;
+    qa.t = t;
+    qa.heads = c.heads;
+    qa.kv_heads = c.kv_heads;
+    qa.hd = ly.hd;
+    qa.has_kv = ly.has_kv;
+    qa.v_norm = c.v_norm;
+    qa.rope_dims = c.rope_dims[li];
+    qa.theta = ly.sliding ? c.theta_local : c.theta_global;
+    qa.q_scale = c.query_scale;
+    qa.eps = c.eps;
+    qa.offset = c.norm_offset;
+    qa.qn = ly.q_norm;
+    qa.kn = ly.k_norm;
+    qa.meta = meta_.as<TokMeta>();
+    qa.base = static_cast<int>(p.base);
+    qa.q16 = q16_.as<__half>();
+    qa.kv = ly.has_kv ? kv_[li].as<__half>() : nullptr;
+    launch_qk_prep(qa, stream_);
+    // Block-causal attention over the cache.
+    AttnArgs aa{};
+    aa.q = q16_.as<__half>();
+    aa.kv = kv_[ly.kv_src].as<__half>();
+    aa.meta = meta_.as<TokMeta>();
+    aa.out = attn16_.as<__half>();
+    aa.ctas = attn_ctas_.as<int2>();
+    aa.n_ctas = static_cast<int>(p.attn_ctas.size());
+    aa.t = t;
+    aa.base = static_cast<int>(p.base);
+    aa.heads = c.heads;
+    aa.kv_heads = c.kv_heads;
+    aa.hd = ly.hd;
+    aa.window = ly.sliding ? c.window : 0;
+    launch_attention(aa, stream_);
+    // Output projection, then x += norm(a); h = ffn_norm(x).
+    gemm_run(ly.o, t, a32_.p, d, slab_a, status, stream_);
+    launch_residual_norm(a32_.as<float>(), ly.o.s.splits, slab_a, d, t, d, ly.post_attn_norm,
+                         c.eps, c.norm_offset, 1.0f, x_.as<float>(), nullptr, ly.ffn_norm,
+                         h16_.as<__half>(), d, nullptr, nullptr, stream_);
+    // GeGLU and down projection.
+    gemm_run(ly.gate_up, t, act16_.p, ly.ff, 0, status, stream_);
+    gemm_run(ly.down, t, a32_.p, d, slab_a, status, stream_);
+    launches += 7;
+    const int* rmap = last ? row_map_.as<int>() : nullptr;
+    float* rows = last ? rows_.as<float>() : nullptr;
+    __half* hnext = last ? nullptr : h16_.as<__half>();
+    if (P == 0) {
+      launch_residual_norm(a32_.as<float>(), ly.down.s.splits, slab_a, d, t, d, ly.post_ffn_norm,
+                           c.eps, c.norm_offset, ly.out_scale, x_.as<float>(), nullptr,
+                           ly.next_norm, hnext, d, rmap, rows, stream_);
+      ++launches;
+    } else {
+      // Per-layer input chain (engine.rs:1733-1749).
+      launch_residual_norm(a32_.as<float>(), ly.down.s.splits, slab_a, d, t, d, ly.post_ffn_norm,
+                           c.eps, c.norm_offset, 1.0f, x_.as<float>(), x16_.as<__half>(),
+                           nullptr, nullptr, d, nullptr, nullptr, stream_);
+      gemm_run(ly.pl_gate, t, plp_.p, P, 0, status, stream_);
+      launch_pl_gate(plp_.as<float>(), pli_.as<float>(), t, P, L, li, act16_.as<__half>(),
+                     stream_);
+      gemm_run(ly.pl_proj, t, a32_.p, d, slab_a, status, stream_);
+      launch_residual_norm(a32_.as<float>(), ly.pl_proj.s.splits, slab_a, d, t, d, ly.pl_norm,
+                           c.eps, c.norm_offset, ly.out_scale, x_.as<float>(), nullptr,
+                           ly.next_norm, hnext, d, rmap, rows, stream_);
+      launches += 5;
+    }
+  }
+  if (want == Want::Logits) {
+    launch_logits(embed_.dtype, rows_.as<float>(), static_cast<int>(p.nwanted), embed_.codes.p,
+                  embed_.scales.p, c.vocab, d, c.softcap, logits_.as<float>(), num_sms_, stream_);
+    ++launches;
+  }
+  CUDA_TRY(cudaGetLastError());
+  return launches;
+}
+
+void Engine::check_status() {
+  const uint32_t st = *h_status_.as<uint32_t>();
+  if (st != 0)
+    fail("a kernel gave up waiting (device status %u); the pass was abandoned", st);
+}
+
+void Engine::run(const GroupIn* groups, size_t n, size_t first,
+                 std::optional<PrefixSource> source, Want want, const uint8_t* per_layer_rows,
+                 size_t rows_bytes, float* out, size_t out_floats, int32_t* sources) {
+  CUDA_TRY(cudaSetDevice(device_));
+  Packing p = pack(groups, n, first, source.has_value());
+  const size_t width = want == Want::Hidden ? config.d : config.vocab;
+  size_t total_rows = 0;
+  for (size_t i = 0; i < n; ++i) total_rows += groups[i].rows();
+  if (out_floats < total_rows * width)
+    fail("output buffer holds %zu floats, the request returns %zu", out_floats,
+         total_rows * width);
+  upload(p, per_layer_rows, rows_bytes);
+  launch_forward(p, want);
+  const float* src = want == Want::Logits ? logits_.as<float>() : rows_.as<float>();
+  if (p.nwanted)
+    CUDA_TRY(cudaMemcpyAsync(h_out_.p, src, p.nwanted * width * 4, cudaMemcpyDeviceToHost,
+                             stream_));
+  CUDA_TRY(cudaMemcpyAsync(h_status_.p, status_.p, 4, cudaMemcpyDeviceToHost, stream_));
+  CUDA_TRY(cudaStreamSynchronize(stream_));
+  check_status();
+  const float* h = h_out_.as<float>();
+  for (size_t i = 0; i + 1 < p.out_index.size(); i += 2)
+    std::memcpy(out + p.out_index[i + 1] * width, h + p.out_index[i] * width, width * 4);
+  {
+    std::lock_guard<std::mutex> g(mu_);
+    resident_ = std::vector<uint32_t>(groups[first].prefix,
+                                      groups[first].prefix + groups[first].n_prefix);
+  }
+  for (const auto& dec : p.decoded)
+    remember(groups[dec.first].prefix, groups[dec.first].n_prefix, dec.second);
+  if (sources) {
+    for (size_t i = 0; i < n; ++i) sources[i] = static_cast<int32_t>(PrefixSource::Decoded);
+    sources[first] = static_cast<int32_t>(source.value_or(PrefixSource::Decoded));
+  }
+  std::lock_guard<std::mutex> g(mu_);
+  last_source_ = source.value_or(PrefixSource::Decoded);
+}
+
+void Engine::evaluate_groups(const GroupIn* groups, size_t n, Want want, float* out,
+                             size_t out_floats, int32_t* sources) {
+  if (n == 0) fail("empty request");
+  auto [first, source] = admit(groups, n);
+  std::vector<uint8_t> rows;
+  if (config.per_layer_dim > 0) {
+    std::vector<uint32_t> ids;
+    std::vector<size_t> order{first};
+    for (size_t i = 0; i < n; ++i)
+      if (i != first) order.push_back(i);
+    for (size_t gi : order) {
+      const GroupIn& g = groups[gi];
+      if (!(gi == first && source)) ids.insert(ids.end(), g.prefix, g.prefix + g.n_prefix);
+      for (size_t b = 0; b < g.n_branches; ++b)
+        for (size_t j = 0; j < g.branches[b].n_tokens; ++j)
+          ids.push_back(static_cast<uint32_t>(g.branches[b].tokens[j]));
+    }
+    for (uint32_t id : ids)
+      if (id >= static_cast<uint32_t>(config.vocab))
+        fail("token id %u outside the vocabulary of %d", id, config.vocab);
+    rows = gather_per_layer(ids.data(), ids.size());
+  }
+  run(groups, n, first, source, want, rows.empty() ? nullptr : rows.data(), rows.size(), out,
+      out_floats, sources);
+}
+
+void Engine::evaluate_rows(const GroupIn& g, Want want, const uint8_t* per_layer_rows,
+                           size_t rows_bytes, float* out, size_t out_floats) {
+  auto [first, source] = admit(&g, 1);
+  run(&g, 1, first, source, want, per_layer_rows, rows_bytes, out, out_floats, nullptr);
+}
+
+// engine.rs:1341-1352: a two-token request so the first real one does not
+// pay for first-touch costs.
+void Engine::warmup() {
+  const int32_t tok = 0;
+  const size_t want0 = 0;
+  BranchIn b{&tok, 1, &want0, 1};
+  const uint32_t bos = config.bos;
+  GroupIn g{&bos, 1, &b, 1};
+  std::vector<float> out(config.vocab);
+  std::vector<uint8_t> rows;
+  if (config.per_layer_dim > 0)
+    rows.assign(2 * static_cast<size_t>(config.per_layer_dim) * config.layers * 2, 0);
+  evaluate_rows(g, Want::Logits, rows.empty() ? nullptr : rows.data(), rows.size(), out.data(),
+                out.size());
+}
+
+std::pair<size_t, size_t> Engine::state_rows(int l, size_t p) const {
+  if (config.sliding[l] && config.window > 0)
+    return {p > static_cast<size_t>(config.window) ? p - config.window : 0, p};
+  return {0, p};
+}
+
+SavedState Engine::save_state(const uint32_t* prefix, size_t n) {
+  return save_state_at(prefix, n, 0);
+}
+
+SavedState Engine::save_state_at(const uint32_t* prefix, size_t n, size_t row0) {
+  CUDA_TRY(cudaSetDevice(device_));
+  SavedState s;
+  s.prefix.assign(prefix, prefix + n);
+  for (int l = 0; l < config.layers; ++l) {
+    if (!config.has_kv(l)) continue;
+    auto [r0, r1] = state_rows(l, n);
+    const size_t row_bytes = static_cast<size_t>(2) * config.kv_heads * config.head_dim[l] * 2;
+    SavedState::Layer ly;
+    ly.layer = l;
+    ly.row0 = static_cast<int>(r0);
+    ly.bytes.resize((r1 - r0) * row_bytes);
+    if (!ly.bytes.empty())
+      CUDA_TRY(cudaMemcpyAsync(ly.bytes.data(), kv_[l].as<uint8_t>() + (row0 + r0) * row_bytes,
+                               ly.bytes.size(), cudaMemcpyDeviceToHost, stream_));
+    s.layers.push_back(std::move(ly));
+  }
+  CUDA_TRY(cudaStreamSynchronize(stream_));
+  return s;
+}
+
+void Engine::restore_state(const SavedState& s) {
+  CUDA_TRY(cudaSetDevice(device_));
+  const size_t p = s.prefix.size();
+  if (p > capacity) fail("state of %zu tokens exceeds the engine capacity %zu", p, capacity);
+  for (const auto& ly : s.layers) {
+    if (ly.layer < 0 || ly.layer >= config.layers || !config.has_kv(ly.layer))
+      fail("state has K/V for layer %d, which owns none", ly.layer);
+    const size_t row = static_cast<size_t>(2) * config.kv_heads * config.head_dim[ly.layer];
+    auto [r0, r1] = state_rows(ly.layer, p);
+    if (static_cast<size_t>(ly.row0) != r0 || ly.bytes.size() != (r1 - r0) * row * 2)
+      fail("state layer %d: %zu bytes at row %d, expected %zu at %zu", ly.layer, ly.bytes.size(),
+           ly.row0, (r1 - r0) * row * 2, r0);
+  }
+  for (const auto& ly : s.layers) {
+    const size_t row_bytes = static_cast<size_t>(2) * config.kv_heads * config.head_dim[ly.layer] * 2;
+    if (!ly.bytes.empty())
+      CUDA_TRY(cudaMemcpyAsync(kv_[ly.layer].as<uint8_t>() + ly.row0 * row_bytes, ly.bytes.data(),
+                               ly.bytes.size(), cudaMemcpyHostToDevice, stream_));
+  }
+  std::vector<TokMeta> meta(p);
+  for (size_t i = 0; i < p; ++i)
+    meta[i] = {static_cast<int>(i), 0, 0, static_cast<int>(i + 1)};
+  if (p)
+    CUDA_TRY(cudaMemcpyAsync(meta_.p, meta.data(), p * sizeof(TokMeta), cudaMemcpyHostToDevice,
+                             stream_));
+  CUDA_TRY(cudaStreamSynchronize(stream_));
+  std::lock_guard<std::mutex> g(mu_);
+  resident_ = s.prefix;
+}
+
+std::string Engine::state_path(const uint32_t* prefix, size_t n) const {
+  if (state_dir_.empty()) return "";
+  char name[32];
+  snprintf(name, sizeof name, "%016llx.state",
+           static_cast<unsigned long long>(state_key(model_id_, prefix, n)));
+  return state_dir_ + "/" + name;
+}
+
+// engine.rs:2096-2120: RAM first, then the state directory (promoted).
+std::optional<PrefixSource> Engine::restore_from_cache(const uint32_t* prefix, size_t n) {
+  bool on;
+  {
+    std::lock_guard<std::mutex> g(mu_);
+    on = states_.budget > 0 || !state_dir_.empty();
+  }
+  if (n == 0 || !on) return std::nullopt;
+  std::optional<SavedState> ram;
+  {
+    std::lock_guard<std::mutex> g(mu_);
+    ram = states_.get(std::vector<uint32_t>(prefix, prefix + n));
+  }
+  if (ram) {
+    try {
+      restore_state(*ram);
+      return PrefixSource::Ram;
+    } catch (const Error&) {
+      return std::nullopt;
+    }
+  }
+  const std::string path = state_path(prefix, n);
+  if (path.empty()) return std::nullopt;
+  std::ifstream f(path, std::ios::binary);
+  if (!f) return std::nullopt;
+  std::vector<uint8_t> bytes((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+  try {
+    SavedState s = SavedState::from_bytes(bytes.data(), bytes.size(), model_id_);
+    if (s.prefix.size() != n || !std::equal(s.prefix.begin(), s.prefix.end(), prefix))
+      return std::nullopt;
+    restore_state(s);
+    std::lock_guard<std::mutex> g(mu_);
+    states_.put(std::move(s));
+    return PrefixSource::Disk;
+  } catch (const Error&) {
+    return std::nullopt;
+  }
+}
+
+void Engine::remember(const uint32_t* prefix, size_t n, size_t row0) {
+  bool on;
+  {
+    std::lock_guard<std::mutex> g(mu_);
+    on = states_.budget > 0 || !state_dir_.empty();
+  }
+  if (n == 0 || !on) return;
+  SavedState s = save_state_at(prefix, n, row0);
+  const std::string path = state_path(prefix, n);
+  if (!path.empty()) {
+    mkdir(state_dir_.c_str(), 0755);
+    std::ofstream f(path, std::ios::binary);
+    const auto bytes = s.to_bytes(model_id_);
+    f.write(reinterpret_cast<const char*>(bytes.data()), static_cast<std::streamsize>(bytes.size()));
+    if (!f) fail("writing %s", path.c_str());
+  }
+  std::lock_guard<std::mutex> g(mu_);
+  states_.put(std::move(s));
+}
+
+float Engine::time_forward(const GroupIn* groups, size_t n, Want want, bool resident, int iters,
+                           int* launches) {
+  CUDA_TRY(cudaSetDevice(device_));
+  if (resident && !is_resident(groups[0].prefix, groups[0].n_prefix))
+    fail("time_forward: the first group's prefix is not resident");
+  Packing p = pack(groups, n, 0, resident);
+  std::vector<uint8_t> rows;
+  if (config.per_layer_dim > 0) rows = gather_per_layer(reinterpret_cast<const uint32_t*>(p.ids.data()), p.ids.size());
+  upload(p, rows.empty() ? nullptr : rows.data(), rows.size());
+  CUDA_TRY(cudaStreamSynchronize(stream_));
+  int nl = 0;
+  CUDA_TRY(cudaEventRecord(events_[6], stream_));
+  for (int i = 0; i < iters; ++i) nl = launch_forward(p, want);
+  CUDA_TRY(cudaEventRecord(events_[7], stream_));
+  CUDA_TRY(cudaMemcpyAsync(h_status_.p, status_.p, 4, cudaMemcpyDeviceToHost, stream_));
+  CUDA_TRY(cudaStreamSynchronize(stream_));
+  check_status();
+  float ms = 0;
+  CUDA_TRY(cudaEventElapsedTime(&ms, events_[6], events_[7]));
+  if (launches) *launches = nl;
+  if (!resident) {
+    // The timed passes decoded groups[0]'s prefix into rows 0..P.
+    std::lock_guard<std::mutex> g(mu_);
+    resident_ = std::vector<uint32_t>(groups[0].prefix, groups[0].prefix + groups[0].n_prefix);
+  }
+  return ms;
+}
+
+void Engine::record_event(int slot) {
+  if (slot < 0 || slot >= 6) fail("event slot %d out of range", slot);
+  CUDA_TRY(cudaSetDevice(device_));
+  CUDA_TRY(cudaEventRecord(events_[slot], stream_));
+}
+
+float Engine::elapsed_ms(int a, int b) {
+  if (a < 0 || a >= 6 || b < 0 || b >= 6) fail("event slot out of range");
+  CUDA_TRY(cudaEventSynchronize(events_[b]));
+  float ms = 0;
+  CUDA_TRY(cudaEventElapsedTime(&ms, events_[a], events_[b]));
+  return ms;
+}
+
+}  // namespace omg

@@ -1,0 +1,271 @@
+// The decoder engine: crates/omg-wgpu/src/engine.rs re-designed for one B200.
+//
+// Weights and a token-capacity-sized workspace live in HBM for the life of
+// the engine. A request (one or more groups of prefix + branches) is packed
+// into one block-causal pass exactly as engine.rs:1492-1571 packs it, the
+// whole network is launched on the engine's stream, and only the wanted rows
+// come back. The prefix of the first group stays resident (its K/V rows are
+// kept), and decoded prefixes can be kept in a RAM / file state cache.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <optional>
+#include <string>
+#include <vector>
+
+#include "gemm.cuh"
+#include "kernels.cuh"
+#include "model.h"
+
+namespace omg {
+
+enum class PrefixSource : int { Resident = 0, Ram = 1, Disk = 2, Decoded = 3 };
+enum class Want : int { Logits = 0, Hidden = 1 };
+
+// A tensor as pushed (model.rs:376-384 QTensor).
+struct HostTensor {
+  int dtype = 0;
+  std::vector<int64_t> shape;
+  std::vector<uint8_t> data, scales;
+  size_t numel() const {
+    size_t n = 1;
+    for (auto s : shape) n *= static_cast<size_t>(s);
+    return n;
+  }
+  float get(size_t i) const;
+};
+
+// omg_core::BranchTokens (backend.rs:26-30) and engine.rs Group (:29-32).
+struct BranchIn {
+  const int32_t* tokens;
+  size_t n_tokens;
+  const size_t* want;
+  size_t n_want;
+};
+struct GroupIn {
+  const uint32_t* prefix;
+  size_t n_prefix;
+  const BranchIn* branches;
+  size_t n_branches;
+  size_t tokens() const {
+    size_t n = n_prefix;
+    for (size_t b = 0; b < n_branches; ++b) n += branches[b].n_tokens;
+    return n;
+  }
+  size_t rows() const {
+    size_t n = 0;
+    for (size_t b = 0; b < n_branches; ++b) n += branches[b].n_want;
+    return n;
+  }
+};
+
+// engine.rs:503-580: a prefix's K/V rows as f16 per layer that owns K/V;
+// sliding layers keep only the last `window` rows.
+struct SavedState {
+  std::vector<uint32_t> prefix;
+  struct Layer {
+    int layer = 0;
+    int row0 = 0;
+    std::vector<uint8_t> bytes;  // f16 LE rows of [kv_heads * hd K | kv_heads * hd V]
+  };
+  std::vector<Layer> layers;
+
+  size_t byte_len() const;
+  std::vector<uint8_t> to_bytes(const std::string& model_id) const;
+  static SavedState from_bytes(const uint8_t* b, size_t n, const std::string& model_id);
+};
+
+// engine.rs:584-620: LRU of saved states keyed by the exact prefix, most
+// recently used last.
+struct StateCache {
+  size_t budget = 0, used = 0;
+  std::vector<SavedState> entries;
+  std::optional<SavedState> get(const std::vector<uint32_t>& prefix);
+  void put(SavedState s);
+};
+
+// engine.rs:625-641: FNV-1a of (model id, 0, prefix LE bytes).
+uint64_t state_key(const std::string& model_id, const uint32_t* prefix, size_t n);
+
+struct DevBuffer {
+  void* p = nullptr;
+  size_t bytes = 0;
+  DevBuffer() = default;
+  DevBuffer(const DevBuffer&) = delete;
+  DevBuffer& operator=(const DevBuffer&) = delete;
+  DevBuffer(DevBuffer&& o) noexcept : p(o.p), bytes(o.bytes) { o.p = nullptr; o.bytes = 0; }
+  DevBuffer& operator=(DevBuffer&& o) noexcept {
+    if (this != &o) {
+      release();
+      p = o.p; bytes = o.bytes;
+      o.p = nullptr; o.bytes = 0;
+    }
+    return *this;
+  }
+  ~DevBuffer() { release(); }
+  void alloc(size_t n, bool zero = true);
+  void release();
+  template <class T> T* as() const { return static_cast<T*>(p); }
+};
+
+struct PinnedBuffer {
+  void* p = nullptr;
+  size_t bytes = 0;
+  PinnedBuffer() = default;
+  PinnedBuffer(const PinnedBuffer&) = delete;
+  PinnedBuffer& operator=(const PinnedBuffer&) = delete;
+  ~PinnedBuffer();
+  void alloc(size_t n);
+  template <class T> T* as() const { return static_cast<T*>(p); }
+};
+
+class Engine;
+
+// engine.rs:805-1334 EngineBuilder: receives the weights one tensor at a
+// time (dequantizing each linear straight into its f16 device layout) and
+// allocates the workspace in finish().
+class EngineBuilder {
+ public:
+  EngineBuilder(Config cfg, int device);
+  ~EngineBuilder();
+  const Config& config() const { return cfg_; }
+  std::vector<std::string> missing() const;
+  void push(const std::string& name, const HostTensor& t);
+  void set_per_layer_table(HostTensor t);
+  std::unique_ptr<Engine> finish(size_t capacity, size_t max_rows);
+
+ private:
+  friend class Engine;
+  struct Packed {
+    int dtype = 0;
+    DevBuffer codes, scales;
+  };
+  Config cfg_;
+  int device_;
+  cudaStream_t stream_ = nullptr;
+  std::map<std::string, std::vector<int64_t>> expected_;
+  std::map<std::string, bool> pushed_;
+  std::map<std::string, DevBuffer> lin_;    // f16 dequantized linears (gate+up interleaved as "blk.N.gate_up")
+  std::map<std::string, DevBuffer> norms_;  // f32 norm weights
+  std::map<std::string, float> scalars_;
+  Packed embed_;
+  std::optional<HostTensor> per_layer_table_;
+};
+
+class Engine {
+ public:
+  ~Engine();
+  const Config config;
+  const size_t capacity;
+  const size_t max_rows;
+
+  // engine.rs:1404-1444. `out` gets the wanted rows in (group, branch, want)
+  // order, `width` floats each (vocab for logits, d for hidden);
+  // `sources[g]` the PrefixSource of each group (-1 none).
+  void evaluate_groups(const GroupIn* groups, size_t n, Want want, float* out, size_t out_floats,
+                       int32_t* sources);
+  // engine.rs:1449-1463: caller-gathered per-layer rows (f16 LE).
+  void evaluate_rows(const GroupIn& g, Want want, const uint8_t* per_layer_rows,
+                     size_t rows_bytes, float* out, size_t out_floats);
+  void warmup();
+  std::optional<PrefixSource> prefix_source() const;
+  bool is_resident(const uint32_t* prefix, size_t n) const;
+  void evict_resident();
+  void set_state_cache(size_t bytes, const std::string& dir, const std::string& model_id);
+  SavedState save_state(const uint32_t* prefix, size_t n);
+  void restore_state(const SavedState& s);
+  int embed_dtype() const { return embed_.dtype; }
+  cudaStream_t stream() const { return stream_; }
+  int device() const { return device_; }
+
+  // Device-resident timing: pack `groups` once (no state cache), upload it,
+  // then launch the forward `iters` times on the stream between two CUDA
+  // events; returns the total milliseconds. With `resident`, the first
+  // group's prefix must be resident and only the branches run (config 3).
+  // Kernel launches per pass go to *launches.
+  float time_forward(const GroupIn* groups, size_t n, Want want, bool resident, int iters,
+                     int* launches);
+  // Events on the engine's stream for end-to-end timing around API calls.
+  void record_event(int slot);
+  float elapsed_ms(int a, int b);
+  // Gather per-layer table rows for ids (engine.rs:1370-1381), f16 LE.
+  std::vector<uint8_t> gather_per_layer(const uint32_t* ids, size_t n) const;
+
+ private:
+  friend class EngineBuilder;
+  Engine(EngineBuilder&& b, size_t capacity, size_t max_rows);
+
+  struct Layer {
+    GemmPlan qkv, o, gate_up, down, pl_gate, pl_proj;
+    const __half *w_qkv = nullptr, *w_o = nullptr, *w_gu = nullptr, *w_down = nullptr;
+    const float *attn_norm, *q_norm, *k_norm, *post_attn_norm, *ffn_norm, *post_ffn_norm;
+    const float *pl_norm = nullptr;
+    const float* next_norm;  // the norm that reads the stream after this layer
+    float out_scale = 1.f;
+    int hd, ff, qkv_w;
+    bool sliding, has_kv;
+    int kv_src;
+  };
+
+  struct Packing {
+    std::vector<int32_t> ids;
+    std::vector<TokMeta> meta;
+    std::vector<int32_t> row_map;
+    // (group, branch, slot) -> flat output row
+    std::vector<size_t> out_index;
+    std::vector<std::pair<size_t, size_t>> decoded;  // (group, cache row of its prefix)
+    std::vector<int2> attn_ctas;                     // attention CTA runs
+    size_t t = 0, base = 0, nwanted = 0;
+  };
+
+  std::pair<size_t, std::optional<PrefixSource>> admit(const GroupIn* groups, size_t n);
+  Packing pack(const GroupIn* groups, size_t n, size_t first, bool resident_first) const;
+  void upload(const Packing& p, const uint8_t* per_layer_rows, size_t rows_bytes);
+  int launch_forward(const Packing& p, Want want);
+  void run(const GroupIn* groups, size_t n, size_t first, std::optional<PrefixSource> source,
+           Want want, const uint8_t* per_layer_rows, size_t rows_bytes, float* out,
+           size_t out_floats, int32_t* sources);
+  void check_status();
+  std::pair<size_t, size_t> state_rows(int l, size_t p) const;
+  SavedState save_state_at(const uint32_t* prefix, size_t n, size_t row0);
+  std::optional<PrefixSource> restore_from_cache(const uint32_t* prefix, size_t n);
+  void remember(const uint32_t* prefix, size_t n, size_t row0);
+  std::string state_path(const uint32_t* prefix, size_t n) const;
+
+  int device_;
+  int num_sms_ = 148;
+  cudaStream_t stream_ = nullptr;
+  std::map<std::string, DevBuffer> lin_, norms_;
+  EngineBuilder::Packed embed_;
+  std::optional<HostTensor> per_layer_table_;
+  std::vector<Layer> layers_;
+  const float* final_norm_ = nullptr;
+  int gemm_splits_max_ = 2;
+  int max_qkv_ = 0, max_attn_ = 0, max_ff_ = 0;
+
+  // Workspace.
+  DevBuffer attn_ctas_;
+  PinnedBuffer h_attn_ctas_;
+  DevBuffer ids_, meta_, row_map_, x_, x16_, h16_, qkv_, q16_, attn16_, a32_, act16_, rows_,
+      logits_, status_, pl_rows16_, pli_, plp_;
+  std::vector<DevBuffer> kv_;  // per layer that owns K/V: [cap_rows, 2 * kv_heads * hd] f16
+  size_t cap_rows_ = 0;
+  PinnedBuffer h_ids_, h_meta_, h_row_map_, h_out_, h_status_;
+  GemmPlan pl_model_proj_;
+  DevBuffer w_pl_model_proj_;
+
+  mutable std::mutex mu_;
+  std::optional<std::vector<uint32_t>> resident_;
+  std::optional<PrefixSource> last_source_;
+  StateCache states_;
+  std::string state_dir_;
+  std::string model_id_ = "wgpu";
+  cudaEvent_t events_[8] = {};
+};
+
+}  // namespace omg

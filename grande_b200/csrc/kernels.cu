@@ -1,0 +1,530 @@
+// Row kernels of the decoder pass (see kernels.cuh). Reference shaders:
+// crates/omg-wgpu/src/shaders/{weight,embed,rmsnorm,qk_prep,logits}.wgsl.
+#include "kernels.cuh"
+#include "ptx.cuh"
+
+namespace omg {
+
+namespace {
+
+__device__ __forceinline__ float half_bits_to_float(uint16_t b) {
+  return __half2float(__ushort_as_half(b));
+}
+
+// ---- weight dequantization --------------------------------------------------
+
+__device__ __forceinline__ int remap_row(int r, int mode) {
+  if (mode == 1) return (r / 128) * 256 + (r % 128);
+  if (mode == 2) return (r / 128) * 256 + 128 + (r % 128);
+  return r;
+}
+
+__global__ void dequant_f16_kernel(int dtype, const uint8_t* __restrict__ codes,
+                                   const uint8_t* __restrict__ scales, int rows, int k, int remap,
+                                   __half* __restrict__ out) {
+  const size_t nblk = static_cast<size_t>(rows) * (k / 32);
+  for (size_t b = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; b < nblk;
+       b += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(b / (k / 32));
+    const int c = static_cast<int>(b % (k / 32)) * 32;
+    __half* o = out + static_cast<size_t>(remap_row(r, remap)) * k + c;
+    __align__(16) __half v[32];
+    if (dtype == kF16) {
+      const uint4* src = reinterpret_cast<const uint4*>(codes + b * 64);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) reinterpret_cast<uint4*>(v)[i] = src[i];
+    } else {
+      const uint16_t sb = static_cast<uint16_t>(scales[2 * b]) |
+                          (static_cast<uint16_t>(scales[2 * b + 1]) << 8);
+      const float d = half_bits_to_float(sb);
+      if (dtype == kQ8) {
+        __align__(16) int8_t q[32];
+        reinterpret_cast<uint4*>(q)[0] = reinterpret_cast<const uint4*>(codes + b * 32)[0];
+        reinterpret_cast<uint4*>(q)[1] = reinterpret_cast<const uint4*>(codes + b * 32)[1];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __float2half_rn(static_cast<float>(q[j]) * d);
+      } else {
+        __align__(16) uint8_t q[16];
+        reinterpret_cast<uint4*>(q)[0] = reinterpret_cast<const uint4*>(codes + b * 16)[0];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          v[j] = __float2half_rn((static_cast<float>(q[j] & 0xf) - 8.0f) * d);
+          v[j + 16] = __float2half_rn((static_cast<float>(q[j] >> 4) - 8.0f) * d);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) reinterpret_cast<uint4*>(o)[i] = reinterpret_cast<uint4*>(v)[i];
+  }
+}
+
+// Dequantized 32-element block `b` of a row-major table (f32, exact as
+// QTensor::get).
+template <int DT>
+__device__ __forceinline__ void load_block_f32(const uint8_t* codes, const uint8_t* scales,
+                                               size_t b, float (&v)[32]) {
+  if constexpr (DT == kF16) {
+    __align__(16) uint16_t h[32];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      reinterpret_cast<uint4*>(h)[i] = reinterpret_cast<const uint4*>(codes + b * 64)[i];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = half_bits_to_float(h[j]);
+  } else {
+    const uint16_t sb =
+        static_cast<uint16_t>(scales[2 * b]) | (static_cast<uint16_t>(scales[2 * b + 1]) << 8);
+    const float d = half_bits_to_float(sb);
+    if constexpr (DT == kQ8) {
+      __align__(16) int8_t q[32];
+      reinterpret_cast<uint4*>(q)[0] = reinterpret_cast<const uint4*>(codes + b * 32)[0];
+      reinterpret_cast<uint4*>(q)[1] = reinterpret_cast<const uint4*>(codes + b * 32)[1];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = static_cast<float>(q[j]) * d;
+    } else {
+      __align__(16) uint8_t q[16];
+      reinterpret_cast<uint4*>(q)[0] = reinterpret_cast<const uint4*>(codes + b * 16)[0];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        v[j] = (static_cast<float>(q[j] & 0xf) - 8.0f) * d;
+        v[j + 16] = (static_cast<float>(q[j] >> 4) - 8.0f) * d;
+      }
+    }
+  }
+}
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) s += red[i];
+  return s;
+}
+
+// ---- embedding + first norm ------------------------------------------------
+
+template <int DT>
+__global__ void __launch_bounds__(128) embed_norm_kernel(const int* __restrict__ ids, int t,
+                                                         const uint8_t* __restrict__ codes,
+                                                         const uint8_t* __restrict__ scales,
+                                                         int d, float scale,
+                                                         const float* __restrict__ w, float eps,
+                                                         float offset, float* __restrict__ x,
+                                                         __half* __restrict__ x16,
+                                                         __half* __restrict__ h16, int ldh) {
+  __shared__ float red[4];
+  const int row = blockIdx.x;
+  if (row >= t) return;
+  const size_t id = static_cast<size_t>(ids[row]);
+  float* xr = x + static_cast<size_t>(row) * d;
+  const int nb = d / 32;
+  float ss = 0.f;
+  for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+    float v[32];
+    load_block_f32<DT>(codes, scales, id * nb + b, v);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      v[j] = v[j] * scale;
+      ss += v[j] * v[j];
+    }
+#pragma unroll
+    for (int j = 0; j < 32; j += 4)
+      *reinterpret_cast<float4*>(xr + b * 32 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    if (x16) {
+      __half* xh = x16 + static_cast<size_t>(row) * d + b * 32;
+#pragma unroll
+      for (int j = 0; j < 32; j += 2)
+        *reinterpret_cast<__half2*>(xh + j) = __floats2half2_rn(v[j], v[j + 1]);
+    }
+  }
+  const float inv = rsqrtf(block_sum<128>(ss, red) / static_cast<float>(d) + eps);
+  __half* hr = h16 + static_cast<size_t>(row) * ldh;
+  for (int i = threadIdx.x * 4; i < d; i += blockDim.x * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(xr + i);
+    const float4 ww = *reinterpret_cast<const float4*>(w + i);
+    __half2 a = __floats2half2_rn(v.x * inv * (offset + ww.x), v.y * inv * (offset + ww.y));
+    __half2 b = __floats2half2_rn(v.z * inv * (offset + ww.z), v.w * inv * (offset + ww.w));
+    uint2 pk;
+    pk.x = *reinterpret_cast<uint32_t*>(&a);
+    pk.y = *reinterpret_cast<uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(hr + i) = pk;
+  }
+}
+
+// ---- residual-stream norms -------------------------------------------------
+
+constexpr int kNormThreads = 256;
+constexpr int kNormVec = 8;  // float4 per thread: d <= 8192
+
+__global__ void __launch_bounds__(kNormThreads) residual_norm_kernel(
+    const float* __restrict__ a, int splits, size_t split_stride, int lda, int t, int d,
+    const float* __restrict__ w1, float eps, float offset, float out_scale, float* __restrict__ x,
+    __half* __restrict__ x16, const float* __restrict__ w2, __half* __restrict__ h16, int ldh,
+    const int* __restrict__ row_map, float* __restrict__ rows_out) {
+  __shared__ float red[kNormThreads / 32];
+  const int row = blockIdx.x;
+  if (row >= t) return;
+  const float* ar = a + static_cast<size_t>(row) * lda;
+  float* xr = x + static_cast<size_t>(row) * d;
+  float4 y[kNormVec];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {
+    const int i = (threadIdx.x + j * kNormThreads) * 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < d) {
+      v = *reinterpret_cast<const float4*>(ar + i);
+      for (int z = 1; z < splits; ++z) {
+        const float4 u = *reinterpret_cast<const float4*>(ar + z * split_stride + i);
+        v.x += u.x;
+        v.y += u.y;
+        v.z += u.z;
+        v.w += u.w;
+      }
+    }
+    y[j] = v;
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  const float inv1 = rsqrtf(block_sum<kNormThreads>(ss, red) / static_cast<float>(d) + eps);
+  float ss2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {
+    const int i = (threadIdx.x + j * kNormThreads) * 4;
+    if (i < d) {
+      const float4 ww = *reinterpret_cast<const float4*>(w1 + i);
+      const float4 xo = *reinterpret_cast<const float4*>(xr + i);
+      float4 v = y[j];
+      v.x = (v.x * inv1 * (offset + ww.x) + xo.x) * out_scale;
+      v.y = (v.y * inv1 * (offset + ww.y) + xo.y) * out_scale;
+      v.z = (v.z * inv1 * (offset + ww.z) + xo.z) * out_scale;
+      v.w = (v.w * inv1 * (offset + ww.w) + xo.w) * out_scale;
+      *reinterpret_cast<float4*>(xr + i) = v;
+      if (x16) {
+        __half2 p = __floats2half2_rn(v.x, v.y);
+        __half2 q = __floats2half2_rn(v.z, v.w);
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&p);
+        pk.y = *reinterpret_cast<uint32_t*>(&q);
+        *reinterpret_cast<uint2*>(x16 + static_cast<size_t>(row) * d + i) = pk;
+      }
+      y[j] = v;
+      ss2 += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+  }
+  if (w2 == nullptr) return;
+  const float inv2 = rsqrtf(block_sum<kNormThreads>(ss2, red) / static_cast<float>(d) + eps);
+  const int out_row = row_map ? row_map[row] : -1;
+  __half* hr = h16 ? h16 + static_cast<size_t>(row) * ldh : nullptr;
+  float* orow = out_row >= 0 ? rows_out + static_cast<size_t>(out_row) * d : nullptr;
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {
+    const int i = (threadIdx.x + j * kNormThreads) * 4;
+    if (i < d) {
+      const float4 ww = *reinterpret_cast<const float4*>(w2 + i);
+      float4 v = y[j];
+      v.x = v.x * inv2 * (offset + ww.x);
+      v.y = v.y * inv2 * (offset + ww.y);
+      v.z = v.z * inv2 * (offset + ww.z);
+      v.w = v.w * inv2 * (offset + ww.w);
+      if (hr) {
+        __half2 p = __floats2half2_rn(v.x, v.y);
+        __half2 q = __floats2half2_rn(v.z, v.w);
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&p);
+        pk.y = *reinterpret_cast<uint32_t*>(&q);
+        *reinterpret_cast<uint2*>(hr + i) = pk;
+      }
+      if (orow) *reinterpret_cast<float4*>(orow + i) = v;
+    }
+  }
+}
+
+// ---- q / k norm, RoPE, K/V cache write (qk_prep.wgsl) ----------------------
+
+template <int HD>
+__global__ void __launch_bounds__(128) qk_prep_kernel(QkArgs g) {
+  constexpr int E = HD / 64;  // elements per lane in each half of the head
+  constexpr int HALF = HD / 2;
+  const int tok = blockIdx.x;
+  if (tok >= g.t) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int crow = g.base + tok;
+  const float pos = static_cast<float>(g.meta[crow].pos);
+  const float* row = g.qkv + static_cast<size_t>(tok) * g.q_stride;
+  const int n_heads = g.heads + (g.has_kv ? 2 * g.kv_heads : 0);
+  __half* kvrow = g.kv ? g.kv + static_cast<size_t>(crow) * 2 * g.kv_heads * HD : nullptr;
+  for (int h = warp; h < n_heads; h += 4) {
+    float a[E], b[E];
+    const int off = h * HD + lane * E;
+#pragma unroll
+    for (int e = 0; e < E; e += 4) {
+      float4 u = *reinterpret_cast<const float4*>(row + off + e);
+      float4 v = *reinterpret_cast<const float4*>(row + off + HALF + e);
+      for (int z = 1; z < g.splits; ++z) {
+        const float4 u2 = *reinterpret_cast<const float4*>(row + z * g.split_stride + off + e);
+        const float4 v2 =
+            *reinterpret_cast<const float4*>(row + z * g.split_stride + off + HALF + e);
+        u.x += u2.x; u.y += u2.y; u.z += u2.z; u.w += u2.w;
+        v.x += v2.x; v.y += v2.y; v.z += v2.z; v.w += v2.w;
+      }
+      a[e] = u.x; a[e + 1] = u.y; a[e + 2] = u.z; a[e + 3] = u.w;
+      b[e] = v.x; b[e + 1] = v.y; b[e + 2] = v.z; b[e + 3] = v.w;
+    }
+    const bool is_q = h < g.heads;
+    const bool is_v = h >= g.heads + g.kv_heads;
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) ss += a[e] * a[e] + b[e] * b[e];
+    ss = warp_sum(ss);
+    if (is_v) {
+      const float inv = g.v_norm ? rsqrtf(ss / static_cast<float>(HD) + g.eps) : 1.0f;
+      __half* o = kvrow + (g.kv_heads + (h - g.heads - g.kv_heads)) * HD + lane * E;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        o[e] = __float2half_rn(a[e] * inv);
+        o[HALF + e] = __float2half_rn(b[e] * inv);
+      }
+      continue;
+    }
+    const float inv = rsqrtf(ss / static_cast<float>(HD) + g.eps);
+    const float* wn = is_q ? g.qn : g.kn;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const int dd = lane * E + e;
+      float y1 = a[e] * inv * (g.offset + wn[dd]);
+      float y2 = b[e] * inv * (g.offset + wn[dd + HALF]);
+      if (dd < g.rope_dims / 2) {
+        const float ang = pos * powf(g.theta, -static_cast<float>(dd) / static_cast<float>(HALF));
+        float sn, cs;
+        sincosf(ang, &sn, &cs);
+        const float r1 = y1 * cs - y2 * sn;
+        const float r2 = y2 * cs + y1 * sn;
+        y1 = r1;
+        y2 = r2;
+      }
+      a[e] = y1;
+      b[e] = y2;
+    }
+    if (is_q) {
+      __half* o = g.q16 + static_cast<size_t>(tok) * g.heads * HD + h * HD + lane * E;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        o[e] = __float2half_rn(a[e] * g.q_scale);
+        o[HALF + e] = __float2half_rn(b[e] * g.q_scale);
+      }
+    } else {
+      __half* o = kvrow + (h - g.heads) * HD + lane * E;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        o[e] = __float2half_rn(a[e]);
+        o[HALF + e] = __float2half_rn(b[e]);
+      }
+    }
+  }
+}
+
+// ---- Gemma 4 per-layer inputs (pl_combine.wgsl, pl_gate.wgsl) -------------
+
+__global__ void __launch_bounds__(128) pl_combine_kernel(const float* __restrict__ proj, int t,
+                                                         int P, int layers,
+                                                         const float* __restrict__ w,
+                                                         const __half* __restrict__ emb,
+                                                         float eps, float offset,
+                                                         float proj_scale, float emb_scale,
+                                                         float out_scale, float* __restrict__ out) {
+  __shared__ float red[4];
+  const int layer = blockIdx.x, tok = blockIdx.y;
+  if (layer >= layers || tok >= t) return;
+  const size_t base = (static_cast<size_t>(tok) * layers + layer) * P;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    const float v = proj[base + i] * proj_scale;
+    ss += v * v;
+  }
+  const float inv = rsqrtf(block_sum<128>(ss, red) / static_cast<float>(P) + eps);
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    const float n = proj[base + i] * proj_scale * inv * (offset + w[i]);
+    const float e = __half2float(emb[base + i]);
+    out[base + i] = (n + e * emb_scale) * out_scale;
+  }
+}
+
+__global__ void pl_gate_kernel(const float* __restrict__ g, const float* __restrict__ pli, int t,
+                               int P, int layers, int layer, __half* __restrict__ out16) {
+  const size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+  if (i >= static_cast<size_t>(t) * P) return;
+  const size_t tok = i / P, c = i % P;
+  const float x = g[i];
+  float z = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+  z = fminf(fmaxf(z, -15.0f), 15.0f);
+  const float gl = 0.5f * x * (1.0f + tanhf(z));
+  out16[i] = __float2half_rn(gl * pli[(tok * layers + layer) * P + c]);
+}
+
+// ---- logits at readout rows (logits.wgsl) ----------------------------------
+
+template <int DT>
+__global__ void __launch_bounds__(256) logits_kernel(const float* __restrict__ rows, int nrows,
+                                                     int chunk, const uint8_t* __restrict__ codes,
+                                                     const uint8_t* __restrict__ scales,
+                                                     int vocab, int d, float softcap,
+                                                     float* __restrict__ out) {
+  extern __shared__ float xs[];  // [chunk][d]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  const int nb = d / 32;
+  for (int r0 = 0; r0 < nrows; r0 += chunk) {
+    const int nr = min(chunk, nrows - r0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nr * d; i += blockDim.x) xs[i] = rows[static_cast<size_t>(r0) * d + i];
+    __syncthreads();
+    for (int v = blockIdx.x * nwarps + warp; v < vocab; v += gridDim.x * nwarps) {
+      float acc[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) acc[r] = 0.f;
+      // 8 blocks of 32 per step, 4 lanes per block.
+      for (int b0 = 0; b0 < nb; b0 += 8) {
+        const int b = b0 + (lane >> 2);
+        const int w = lane & 3;
+        if (b >= nb) continue;
+        const size_t gb = static_cast<size_t>(v) * nb + b;
+        float e[8];
+        int c0, c1;  // element offsets of the two groups of 4 within the block
+        if constexpr (DT == kQ4) {
+          const uint16_t sb = static_cast<uint16_t>(scales[2 * gb]) |
+                              (static_cast<uint16_t>(scales[2 * gb + 1]) << 8);
+          const float dq = half_bits_to_float(sb);
+          const uint32_t q = *reinterpret_cast<const uint32_t*>(codes + gb * 16 + 4 * w);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            e[j] = (static_cast<float>((q >> (8 * j)) & 0xf) - 8.0f) * dq;
+            e[4 + j] = (static_cast<float>((q >> (8 * j + 4)) & 0xf) - 8.0f) * dq;
+          }
+          c0 = 4 * w;
+          c1 = 16 + 4 * w;
+        } else if constexpr (DT == kQ8) {
+          const uint16_t sb = static_cast<uint16_t>(scales[2 * gb]) |
+                              (static_cast<uint16_t>(scales[2 * gb + 1]) << 8);
+          const float dq = half_bits_to_float(sb);
+          const uint2 q = *reinterpret_cast<const uint2*>(codes + gb * 32 + 8 * w);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            e[j] = static_cast<float>(static_cast<int8_t>((q.x >> (8 * j)) & 0xff)) * dq;
+            e[4 + j] = static_cast<float>(static_cast<int8_t>((q.y >> (8 * j)) & 0xff)) * dq;
+          }
+          c0 = 8 * w;
+          c1 = 8 * w + 4;
+        } else {
+          const uint4 q = *reinterpret_cast<const uint4*>(codes + gb * 64 + 16 * w);
+          const uint16_t* hq = reinterpret_cast<const uint16_t*>(&q);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) e[j] = half_bits_to_float(hq[j]);
+          c0 = 8 * w;
+          c1 = 8 * w + 4;
+        }
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          if (r < nr) {
+            const float* xr = xs + r * d + b * 32;
+            const float4 x0 = *reinterpret_cast<const float4*>(xr + c0);
+            const float4 x1 = *reinterpret_cast<const float4*>(xr + c1);
+            acc[r] += e[0] * x0.x + e[1] * x0.y + e[2] * x0.z + e[3] * x0.w + e[4] * x1.x +
+                      e[5] * x1.y + e[6] * x1.z + e[7] * x1.w;
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        if (r < nr) {
+          float z = warp_sum(acc[r]);
+          if (lane == 0) {
+            if (softcap > 0.f) z = softcap * tanhf(z / softcap);
+            out[static_cast<size_t>(r0 + r) * vocab + v] = z;
+          }
+        }
+      }
+    }
+  }
+}
+
+}  // namespace
+
+void launch_dequant_f16(int dtype, const void* codes, const void* scales, int rows, int k,
+                        int remap, __half* out, cudaStream_t s) {
+  const size_t nblk = static_cast<size_t>(rows) * (k / 32);
+  const int threads = 256;
+  const int grid = static_cast<int>(std::min<size_t>((nblk + threads - 1) / threads, 148 * 16));
+  dequant_f16_kernel<<<grid, threads, 0, s>>>(dtype, static_cast<const uint8_t*>(codes),
+                                              static_cast<const uint8_t*>(scales), rows, k, remap,
+                                              out);
+}
+
+void launch_embed_norm(int dtype, const int* ids, int t, const void* codes, const void* scales,
+                       int d, float scale, const float* w, float eps, float offset, float* x,
+                       __half* x16, __half* h16, int ldh, cudaStream_t s) {
+  const auto* c = static_cast<const uint8_t*>(codes);
+  const auto* sc = static_cast<const uint8_t*>(scales);
+  if (dtype == kQ4)
+    embed_norm_kernel<kQ4><<<t, 128, 0, s>>>(ids, t, c, sc, d, scale, w, eps, offset, x, x16, h16, ldh);
+  else if (dtype == kQ8)
+    embed_norm_kernel<kQ8><<<t, 128, 0, s>>>(ids, t, c, sc, d, scale, w, eps, offset, x, x16, h16, ldh);
+  else
+    embed_norm_kernel<kF16><<<t, 128, 0, s>>>(ids, t, c, sc, d, scale, w, eps, offset, x, x16, h16, ldh);
+}
+
+void launch_residual_norm(const float* a, int splits, size_t split_stride, int lda, int t, int d,
+                          const float* w1, float eps, float offset, float out_scale, float* x,
+                          __half* x16, const float* w2, __half* h16, int ldh,
+                          const int* row_map, float* rows_out, cudaStream_t s) {
+  residual_norm_kernel<<<t, kNormThreads, 0, s>>>(a, splits, split_stride, lda, t, d, w1, eps,
+                                                  offset, out_scale, x, x16, w2, h16, ldh,
+                                                  row_map, rows_out);
+}
+
+void launch_pl_combine(const float* proj, int t, int P, int layers, const float* w,
+                       const __half* emb, float eps, float offset, float proj_scale,
+                       float emb_scale, float out_scale, float* out, cudaStream_t s) {
+  dim3 grid(layers, t);
+  pl_combine_kernel<<<grid, 128, 0, s>>>(proj, t, P, layers, w, emb, eps, offset, proj_scale,
+                                         emb_scale, out_scale, out);
+}
+
+void launch_pl_gate(const float* g, const float* pli, int t, int P, int layers, int layer,
+                    __half* out16, cudaStream_t s) {
+  const size_t n = static_cast<size_t>(t) * P;
+  pl_gate_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(g, pli, t, P, layers,
+                                                                         layer, out16);
+}
+
+void launch_qk_prep(const QkArgs& a, cudaStream_t s) {
+  if (a.hd == 512)
+    qk_prep_kernel<512><<<a.t, 128, 0, s>>>(a);
+  else
+    qk_prep_kernel<256><<<a.t, 128, 0, s>>>(a);
+}
+
+void launch_logits(int dtype, const float* rows, int nrows, const void* codes, const void* scales,
+                   int vocab, int d, float softcap, float* out, int num_sms, cudaStream_t s) {
+  if (nrows <= 0) return;
+  int chunk = std::max(1, std::min(8, (96 * 1024) / (d * 4)));
+  const size_t smem = static_cast<size_t>(chunk) * d * 4;
+  const auto* c = static_cast<const uint8_t*>(codes);
+  const auto* sc = static_cast<const uint8_t*>(scales);
+  const int grid = num_sms * 2;
+  if (dtype == kQ4) {
+    cudaFuncSetAttribute(logits_kernel<kQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+    logits_kernel<kQ4><<<grid, 256, smem, s>>>(rows, nrows, chunk, c, sc, vocab, d, softcap, out);
+  } else if (dtype == kQ8) {
+    cudaFuncSetAttribute(logits_kernel<kQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+    logits_kernel<kQ8><<<grid, 256, smem, s>>>(rows, nrows, chunk, c, sc, vocab, d, softcap, out);
+  } else {
+    cudaFuncSetAttribute(logits_kernel<kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+    logits_kernel<kF16><<<grid, 256, smem, s>>>(rows, nrows, chunk, c, sc, vocab, d, softcap, out);
+  }
+}
+
+}  // namespace omg

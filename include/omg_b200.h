@@ -1,12 +1,15 @@
 /*
  * omg_b200: C ABI of the B200 engine for the omg decision forward pass.
  *
- * This is the boundary a host-language shim binds (the reference's Rust
- * `omg_wgpu` crate would wrap it as an `extern "C"` block; see
- * INTEGRATION.md). Every entry point takes plain pointers and sizes, returns
+ * This is the boundary a host-language shim binds: the reference's Rust
+ * `omg_wgpu` crate would wrap it in an `extern "C"` block and keep its own
+ * API (EngineBuilder / Engine / SavedState / WgpuBackend) on top; see
+ * INTEGRATION.md. Every entry point takes plain pointers and sizes, returns
  * 0 on success and -1 on error, and leaves a message for omg_last_error()
  * (thread-local, valid until the next call on the same thread). Outputs are
- * caller-allocated; nothing is written to them on error.
+ * caller-allocated; nothing is written to them on error. Calls on one engine
+ * must not overlap (the reference's Engine is driven from one thread too);
+ * engines on different devices may be driven from different threads.
  *
  * Each declaration names the reference interface it replaces, as
  * `path:line` within github.com/bokuweb/omg.
@@ -22,7 +25,9 @@ extern "C" {
 #endif
 
 /* Weight storage types, numbered as model::Dtype::code
- * (crates/omg-wgpu/src/model.rs:357-363). */
+ * (crates/omg-wgpu/src/model.rs:357-363). Quantized tensors are 32-element
+ * blocks with the codes in one buffer and the f16 block scales in another
+ * (model.rs:330-337). */
 enum { OMG_DTYPE_F16 = 0, OMG_DTYPE_Q8 = 1, OMG_DTYPE_Q4 = 2 };
 
 /* omg_core::Want (crates/omg-core/src/backend.rs:15-20). */
@@ -38,14 +43,197 @@ enum {
   OMG_SOURCE_DECODED = 3
 };
 
-/* GEMM epilogues exposed to the kernel tests (gemm.cuh GemmEpilogue). */
+/* GEMM epilogues exposed to the kernel tests. */
 enum { OMG_EPI_F32 = 0, OMG_EPI_GEGLU_TANH = 1, OMG_EPI_GEGLU_ERF = 2, OMG_EPI_F16 = 3 };
+
+typedef struct omg_builder omg_builder;
+typedef struct omg_engine omg_engine;
+typedef struct omg_state omg_state;
+
+/* omg_core::BranchTokens (crates/omg-core/src/backend.rs:26-30): one
+ * question branch, its token ids and the branch-relative positions whose
+ * rows are wanted, ascending. */
+typedef struct {
+  const int32_t* tokens;
+  size_t n_tokens;
+  const size_t* want;
+  size_t n_want;
+} omg_branch;
+
+/* omg_wgpu::Group (crates/omg-wgpu/src/engine.rs:26-38): a prefix and the
+ * branches that continue from it. */
+typedef struct {
+  const uint32_t* prefix;
+  size_t n_prefix;
+  const omg_branch* branches;
+  size_t n_branches;
+} omg_group;
+
+typedef struct {
+  int d;             /* Config::d (n_embd, backend.rs:130) */
+  int vocab;         /* Config::vocab (n_vocab, backend.rs:132) */
+  int layers;
+  int embed_dtype;   /* Engine::embed_dtype (engine.rs:2163-2166) */
+  int per_layer_dim; /* Config::per_layer_dim */
+  int device;
+  size_t capacity;   /* Engine::capacity (engine.rs:454) */
+  size_t max_rows;   /* Engine::max_rows (engine.rs:456) */
+  uint32_t bos;      /* Config::bos (backend.rs:128) */
+} omg_engine_info;
 
 /* The message of the last failed call on this thread ("" if none). */
 const char* omg_last_error(void);
 
 /* Library version string. */
 const char* omg_version(void);
+
+/* Number of visible CUDA devices (0 when none). */
+int omg_device_count(void);
+
+/* ---- model configuration -------------------------------------------------- */
+
+/* Config::from_json + Config::validate (model.rs:66-254). Writes a one-line
+ * summary into `summary` (may be NULL). */
+int omg_config_check(const char* config_json, char* summary, size_t cap);
+
+/* Config::tensors (model.rs:277-314): "name d0,d1\n" per catalogued tensor,
+ * in catalogue order. *needed gets the buffer size required. */
+int omg_config_tensors(const char* config_json, char* buf, size_t cap, size_t* needed);
+
+/* ---- EngineBuilder (crates/omg-wgpu/src/engine.rs:805-1334) -------------- */
+
+/* EngineBuilder::new (engine.rs:845-869) on CUDA device `device`. */
+int omg_builder_new(const char* config_json, int device, omg_builder** out);
+
+/* EngineBuilder::push (engine.rs:888-933) of a QTensor (model.rs:376-384):
+ * payload bytes and, for Q8/Q4, the f16 block scales. */
+int omg_builder_push(omg_builder* b, const char* name, int dtype, const int64_t* shape, int ndim,
+                     const void* data, size_t nbytes, const void* scales, size_t scales_nbytes);
+
+/* EngineBuilder::set_per_layer_table (engine.rs:938-949). */
+int omg_builder_set_per_layer_table(omg_builder* b, int dtype, const int64_t* shape, int ndim,
+                                    const void* data, size_t nbytes, const void* scales,
+                                    size_t scales_nbytes);
+
+/* EngineBuilder::missing (engine.rs:874-885): newline-separated names. */
+int omg_builder_missing(omg_builder* b, char* buf, size_t cap, size_t* needed);
+
+/* EngineBuilder::finish (engine.rs:952-1334). Consumes the builder (it is
+ * freed whether or not this succeeds). */
+int omg_builder_finish(omg_builder* b, size_t capacity, size_t max_rows, omg_engine** out);
+
+/* Free a builder that was not finished. */
+void omg_builder_free(omg_builder* b);
+
+/* ---- Engine (crates/omg-wgpu/src/engine.rs:449-2171) --------------------- */
+
+/* Engine::evaluate_groups (engine.rs:1404-1444): every group in one pass.
+ * `out` receives the wanted rows in (group, branch, want) order, each row
+ * `vocab` floats (OMG_WANT_LOGITS, softcapped as engine.rs:1901-1906) or `d`
+ * floats (OMG_WANT_HIDDEN, the final-norm hidden state). prefix_sources
+ * (may be NULL) gets one OMG_SOURCE_* per group. */
+int omg_engine_evaluate_groups(omg_engine* e, const omg_group* groups, size_t n_groups, int want,
+                               float* out, size_t out_floats, int32_t* prefix_sources);
+
+/* Engine::evaluate (engine.rs:1386-1398): one group. */
+int omg_engine_evaluate(omg_engine* e, const uint32_t* prefix, size_t n_prefix,
+                        const omg_branch* branches, size_t n_branches, int want, float* out,
+                        size_t out_floats);
+
+/* Engine::evaluate_rows (engine.rs:1449-1463): per-layer embedding rows
+ * supplied by the caller (f16 LE, [tokens][layers x P], with or without the
+ * prefix rows). */
+int omg_engine_evaluate_rows(omg_engine* e, const uint32_t* prefix, size_t n_prefix,
+                             const omg_branch* branches, size_t n_branches, int want,
+                             const void* per_layer_rows, size_t rows_bytes, float* out,
+                             size_t out_floats);
+
+/* Engine::warmup (engine.rs:1341-1352). */
+int omg_engine_warmup(omg_engine* e);
+
+/* Engine::prefix_source (engine.rs:2153-2156): OMG_SOURCE_* of the last pass. */
+int omg_engine_prefix_source(omg_engine* e);
+
+/* Engine::is_resident (engine.rs:2146-2150): 1 or 0. */
+int omg_engine_is_resident(omg_engine* e, const uint32_t* prefix, size_t n);
+
+/* Engine::evict_resident (engine.rs:2158-2161). */
+void omg_engine_evict_resident(omg_engine* e);
+
+/* Engine::set_state_cache (engine.rs:1945-1955): RAM LRU of `bytes` and,
+ * when `dir` is non-empty, one GRWS1 file per state in it. */
+int omg_engine_set_state_cache(omg_engine* e, size_t bytes, const char* dir,
+                               const char* model_id);
+
+/* Engine::save_state (engine.rs:1977-1981): the resident prefix's K/V rows as
+ * f16. Free the state with omg_state_free. */
+int omg_engine_save_state(omg_engine* e, const uint32_t* prefix, size_t n, omg_state** out);
+
+/* Engine::restore_state (engine.rs:2051-2092): the prefix becomes resident. */
+int omg_engine_restore_state(omg_engine* e, const omg_state* s);
+
+/* Engine::gather_per_layer (engine.rs:1370-1381) with the engine's table:
+ * f16 LE rows for `ids`, n * layers * P * 2 bytes. */
+int omg_engine_gather_per_layer(omg_engine* e, const uint32_t* ids, size_t n, uint8_t* out,
+                                size_t cap);
+
+/* Config / capacity of the engine (the pub fields of engine.rs:449-457). */
+int omg_engine_get_info(omg_engine* e, omg_engine_info* info);
+
+/* Timing hook for benchmarks (no reference counterpart; the reference's
+ * OMG_WGPU_PROFILE timestamps, engine.rs:643-726, serve the same purpose):
+ * upload the request once, then launch the full forward `iters` times on the
+ * engine's stream between two CUDA events. `resident` = 1 runs only the
+ * branches over the resident first prefix. *ms gets the total time,
+ * *launches the kernel launches of one pass. */
+int omg_engine_time_forward(omg_engine* e, const omg_group* groups, size_t n_groups, int want,
+                            int resident, int iters, float* ms, int* launches);
+
+/* CUDA events on the engine's stream (slots 0..5) for end-to-end timing of
+ * API calls: record, then the elapsed milliseconds between two slots. */
+int omg_engine_record_event(omg_engine* e, int slot);
+int omg_engine_elapsed_ms(omg_engine* e, int a, int b, float* ms);
+
+/* Drop the engine and everything it holds on the device. */
+void omg_engine_destroy(omg_engine* e);
+
+/* ---- SavedState (crates/omg-wgpu/src/engine.rs:503-580) ------------------ */
+
+/* SavedState::byte_len (engine.rs:510-512). */
+size_t omg_state_byte_len(const omg_state* s);
+
+/* SavedState::to_bytes (engine.rs:516-534): the GRWS1 file image. With
+ * buf == NULL only *needed is set. */
+int omg_state_to_bytes(const omg_state* s, const char* model_id, uint8_t* buf, size_t cap,
+                       size_t* needed);
+
+/* SavedState::from_bytes (engine.rs:536-579). */
+int omg_state_from_bytes(const uint8_t* bytes, size_t n, const char* model_id, omg_state** out);
+
+/* The state's prefix tokens (*n gets the count). */
+int omg_state_prefix(const omg_state* s, uint32_t* buf, size_t cap, size_t* n);
+
+void omg_state_free(omg_state* s);
+
+/* state_key (engine.rs:625-641): FNV-1a of (model id, prefix), the on-disk
+ * state file name. */
+uint64_t omg_state_key(const char* model_id, const uint32_t* prefix, size_t n);
+
+/* ---- tensors (crates/omg-wgpu/src/model.rs:395-525) ---------------------- */
+
+/* QTensor::from_f32 / quantize_q8 / quantize_q4 (model.rs:395-466): codes
+ * get 2n (f16), n (Q8) or n/2 (Q4) bytes, scales n/16 bytes. */
+int omg_quantize(int dtype, const float* values, size_t n, uint8_t* codes, uint8_t* scales);
+
+/* QTensor::get over every element (model.rs:508-525). */
+int omg_dequantize(int dtype, const uint8_t* codes, const uint8_t* scales, size_t n, float* out);
+
+/* Seeded N(mean, std) values for synthetic checkpoints (no reference
+ * counterpart: the reference's tests draw uniform values,
+ * crates/omg-wgpu/tests/reference.rs:17-38; this uses the same xorshift64
+ * seeded with FNV-1a(name) ^ seed, through Box-Muller). */
+int omg_synth_normal(uint64_t seed, const char* name, float mean, float stddev, float* out,
+                     size_t n);
 
 /* ---- kernel-level entry points (parity tests) ------------------------------
  * Host buffers in and out; each call allocates its own device memory.

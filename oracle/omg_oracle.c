@@ -438,11 +438,7 @@ int oracle_forward(const oracle_config* cfg, const float* const* tensors, size_t
         float lsum = 0.0f;
         for (int s = 0; s < n; ++s) lsum += expf(sc[s] - m);
         for (int s = 0; s < n; ++s) {
-          float p;
-          if (mode == ORACLE_KERNEL)
-            p = round_f16(expf(sc[s] - m)) / lsum;
-          else
-            p = expf(sc[s] - m) / lsum;
+          const float p = expf(sc[s] - m) / lsum;
           const float* vr = V + (size_t)idx[s] * kvh * hd + gh * hd;
           for (int dd = 0; dd < hd; ++dd) {
             const float vv = mode == ORACLE_KERNEL ? round_f16(vr[dd]) : vr[dd];

@@ -68,8 +68,7 @@ enum {
   ORACLE_EXACT = 0,   /* tests/reference.rs as written: all f32 */
   ORACLE_KERNEL = 1   /* the kernels' rounding points: linear inputs and weights
                          to f16 (matmul.wgsl:1-9), Q/K/V to f16 in attention
-                         (attention.wgsl:80-92,110-117), and, as the CUDA
-                         attention's P.V MMA does, probabilities to f16 */
+                         (attention.wgsl:80-92,110-117) */
 };
 
 /* tests/reference.rs:175-349, the plain forward over a packed sequence,

@@ -86,6 +86,10 @@ PROTOTYPES: dict[str, tuple] = {
     "omg_engine_get_info": (C.c_int, [vp, C.POINTER(EngineInfo)]),
     "omg_engine_time_forward": (C.c_int, [vp, GroupP, sz, C.c_int, C.c_int, C.c_int, f32p,
                                           C.POINTER(C.c_int)]),
+    "omg_engine_profile_forward": (C.c_int, [vp, GroupP, sz, C.c_int, C.c_int, C.c_int,
+                                             C.c_char_p, sz, szp]),
+    "omg_debug_attention": (C.c_int, [C.c_int, u16p, u16p, i32p, C.c_int, C.c_int, C.c_int,
+                                      C.c_int, C.c_int, C.c_int, u16p]),
     "omg_engine_record_event": (C.c_int, [vp, C.c_int]),
     "omg_engine_elapsed_ms": (C.c_int, [vp, C.c_int, C.c_int, f32p]),
     "omg_engine_destroy": (None, [vp]),

@@ -279,6 +279,17 @@ int omg_engine_time_forward(omg_engine* e, const omg_group* groups, size_t n_gro
   });
 }
 
+int omg_engine_profile_forward(omg_engine* e, const omg_group* groups, size_t n_groups, int want,
+                               int resident, int iters, char* json, size_t cap, size_t* needed) {
+  return guarded([&] {
+    auto gs = to_groups(groups, n_groups);
+    if (gs.empty()) fail("empty request");
+    const std::string js =
+        eng(e).profile_forward(gs.data(), gs.size(), want_of(want), resident != 0, iters);
+    return copy_out(js, json, cap, needed);
+  });
+}
+
 int omg_engine_record_event(omg_engine* e, int slot) {
   return guarded([&] {
     eng(e).record_event(slot);

@@ -417,6 +417,7 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
 Engine::~Engine() {
   cudaSetDevice(device_);
   if (stream_) cudaStreamSynchronize(stream_);
+  for (auto e : prof_events_) cudaEventDestroy(e);
   for (auto& e : events_)
     if (e) cudaEventDestroy(e);
   if (stream_) cudaStreamDestroy(stream_);
@@ -606,31 +607,36 @@ int Engine::launch_forward(const Packing& p, Want want) {
   const Config& c = config;
   const int t = static_cast<int>(p.t);
   const int d = c.d, L = c.layers, P = c.per_layer_dim;
-  const size_t C = capacity;
   const size_t slab_a = cap_rows_ * d;
   const size_t slab_qkv = cap_rows_ * max_qkv_;
   uint32_t* status = status_.as<uint32_t>();
   int launches = 0;
+  // `k(name)` names the launch that follows (profiling) and counts it.
+  auto k = [&](const char* name) {
+    ++launches;
+    if (profiling_) prof_mark(name);
+  };
   CUDA_TRY(cudaMemsetAsync(status, 0, 4, stream_));
-  (void)C;
 
+  k("embed_norm");
   launch_embed_norm(embed_.dtype, ids_.as<int>(), t, embed_.codes.p, embed_.scales.p, d,
                     std::sqrt(static_cast<float>(d)), layers_[0].attn_norm, c.eps, c.norm_offset,
                     x_.as<float>(), P > 0 ? x16_.as<__half>() : nullptr, h16_.as<__half>(), d,
                     stream_);
-  ++launches;
   if (P > 0) {
+    k("gemm_pl_model_proj");
     gemm_run(pl_model_proj_, t, plp_.p, P * L, 0, status, stream_);
+    k("pl_combine");
     launch_pl_combine(plp_.as<float>(), t, P, L, norms_.at("pl_proj_norm").as<float>(),
                       pl_rows16_.as<__half>(), c.eps, c.norm_offset,
                       1.0f / std::sqrt(static_cast<float>(d)), std::sqrt(static_cast<float>(P)),
                       1.0f / std::sqrt(2.0f), pli_.as<float>(), stream_);
-    launches += 2;
   }
   for (int li = 0; li < L; ++li) {
     const Layer& ly = layers_[li];
     const bool last = li + 1 == L;
     // QKV projection.
+    k("gemm_qkv");
     gemm_run(ly.qkv, t, qkv_.p, ly.qkv_w, slab_qkv, status, stream_);
     // q/k norm + RoPE, K/V into the cache.
     QkArgs qa{};
@@ -655,6 +661,7 @@ int Engine::launch_forward(const Packing& p, Want want) {
     qa.base = static_cast<int>(p.base);
     qa.q16 = q16_.as<__half>();
     qa.kv = ly.has_kv ? kv_[li].as<__half>() : nullptr;
+    k("qk_prep");
     launch_qk_prep(qa, stream_);
     // Block-causal attention over the cache.
     AttnArgs aa{};
@@ -670,46 +677,114 @@ int Engine::launch_forward(const Packing& p, Want want) {
     aa.kv_heads = c.kv_heads;
     aa.hd = ly.hd;
     aa.window = ly.sliding ? c.window : 0;
+    k("attention");
     launch_attention(aa, stream_);
     // Output projection, then x += norm(a); h = ffn_norm(x).
+    k("gemm_o");
     gemm_run(ly.o, t, a32_.p, d, slab_a, status, stream_);
+    k("residual_norm");
     launch_residual_norm(a32_.as<float>(), ly.o.s.splits, slab_a, d, t, d, ly.post_attn_norm,
                          c.eps, c.norm_offset, 1.0f, x_.as<float>(), nullptr, ly.ffn_norm,
                          h16_.as<__half>(), d, nullptr, nullptr, stream_);
     // GeGLU and down projection.
+    k("gemm_gate_up");
     gemm_run(ly.gate_up, t, act16_.p, ly.ff, 0, status, stream_);
+    k("gemm_down");
     gemm_run(ly.down, t, a32_.p, d, slab_a, status, stream_);
-    launches += 7;
     const int* rmap = last ? row_map_.as<int>() : nullptr;
     float* rows = last ? rows_.as<float>() : nullptr;
     __half* hnext = last ? nullptr : h16_.as<__half>();
     if (P == 0) {
+      k("residual_norm");
       launch_residual_norm(a32_.as<float>(), ly.down.s.splits, slab_a, d, t, d, ly.post_ffn_norm,
                            c.eps, c.norm_offset, ly.out_scale, x_.as<float>(), nullptr,
                            ly.next_norm, hnext, d, rmap, rows, stream_);
-      ++launches;
     } else {
       // Per-layer input chain (engine.rs:1733-1749).
+      k("residual_norm");
       launch_residual_norm(a32_.as<float>(), ly.down.s.splits, slab_a, d, t, d, ly.post_ffn_norm,
                            c.eps, c.norm_offset, 1.0f, x_.as<float>(), x16_.as<__half>(),
                            nullptr, nullptr, d, nullptr, nullptr, stream_);
+      k("gemm_pl_gate");
       gemm_run(ly.pl_gate, t, plp_.p, P, 0, status, stream_);
+      k("pl_gate");
       launch_pl_gate(plp_.as<float>(), pli_.as<float>(), t, P, L, li, act16_.as<__half>(),
                      stream_);
+      k("gemm_pl_proj");
       gemm_run(ly.pl_proj, t, a32_.p, d, slab_a, status, stream_);
+      k("residual_norm");
       launch_residual_norm(a32_.as<float>(), ly.pl_proj.s.splits, slab_a, d, t, d, ly.pl_norm,
                            c.eps, c.norm_offset, ly.out_scale, x_.as<float>(), nullptr,
                            ly.next_norm, hnext, d, rmap, rows, stream_);
-      launches += 5;
     }
   }
   if (want == Want::Logits) {
+    k("logits");
     launch_logits(embed_.dtype, rows_.as<float>(), static_cast<int>(p.nwanted), embed_.codes.p,
                   embed_.scales.p, c.vocab, d, c.softcap, logits_.as<float>(), num_sms_, stream_);
-    ++launches;
   }
+  if (profiling_) prof_mark(nullptr);
   CUDA_TRY(cudaGetLastError());
   return launches;
+}
+
+void Engine::prof_mark(const char* name) {
+  if (prof_used_ == prof_events_.size()) {
+    cudaEvent_t e;
+    CUDA_TRY(cudaEventCreate(&e));
+    prof_events_.push_back(e);
+    prof_names_.push_back(nullptr);
+  }
+  CUDA_TRY(cudaEventRecord(prof_events_[prof_used_], stream_));
+  prof_names_[prof_used_] = name;
+  ++prof_used_;
+}
+
+std::string Engine::profile_forward(const GroupIn* groups, size_t n, Want want, bool resident,
+                                    int iters) {
+  CUDA_TRY(cudaSetDevice(device_));
+  if (resident && !is_resident(groups[0].prefix, groups[0].n_prefix))
+    fail("profile_forward: the first group's prefix is not resident");
+  Packing p = pack(groups, n, 0, resident);
+  std::vector<uint8_t> rows;
+  if (config.per_layer_dim > 0)
+    rows = gather_per_layer(reinterpret_cast<const uint32_t*>(p.ids.data()), p.ids.size());
+  upload(p, rows.empty() ? nullptr : rows.data(), rows.size());
+  profiling_ = true;
+  prof_used_ = 0;
+  for (int i = 0; i < iters; ++i) launch_forward(p, want);
+  profiling_ = false;
+  CUDA_TRY(cudaMemcpyAsync(h_status_.p, status_.p, 4, cudaMemcpyDeviceToHost, stream_));
+  CUDA_TRY(cudaStreamSynchronize(stream_));
+  check_status();
+  // name -> (launches, total ms), in first-seen order.
+  std::vector<std::pair<std::string, std::pair<int, double>>> acc;
+  for (size_t i = 0; i + 1 < prof_used_; ++i) {
+    if (!prof_names_[i]) continue;
+    float ms = 0;
+    CUDA_TRY(cudaEventElapsedTime(&ms, prof_events_[i], prof_events_[i + 1]));
+    auto it = std::find_if(acc.begin(), acc.end(),
+                           [&](const auto& e) { return e.first == prof_names_[i]; });
+    if (it == acc.end()) {
+      acc.push_back({prof_names_[i], {0, 0.0}});
+      it = acc.end() - 1;
+    }
+    it->second.first += 1;
+    it->second.second += ms;
+  }
+  std::string js = "{";
+  for (size_t i = 0; i < acc.size(); ++i) {
+    char buf[160];
+    snprintf(buf, sizeof buf, "%s\"%s\": [%d, %.6f]", i ? ", " : "", acc[i].first.c_str(),
+             acc[i].second.first, acc[i].second.second);
+    js += buf;
+  }
+  js += "}";
+  if (!resident) {
+    std::lock_guard<std::mutex> g(mu_);
+    resident_ = std::vector<uint32_t>(groups[0].prefix, groups[0].prefix + groups[0].n_prefix);
+  }
+  return js;
 }
 
 void Engine::check_status() {

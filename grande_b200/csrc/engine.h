@@ -190,6 +190,11 @@ class Engine {
   // Kernel launches per pass go to *launches.
   float time_forward(const GroupIn* groups, size_t n, Want want, bool resident, int iters,
                      int* launches);
+  // Per-kernel device time of `iters` passes (CUDA events between launches on
+  // the stream, the role of the reference's OMG_WGPU_PROFILE timestamps,
+  // engine.rs:643-726): JSON {"kernel": [launches, total_ms], ...}.
+  std::string profile_forward(const GroupIn* groups, size_t n, Want want, bool resident,
+                              int iters);
   // Events on the engine's stream for end-to-end timing around API calls.
   void record_event(int slot);
   float elapsed_ms(int a, int b);
@@ -231,6 +236,11 @@ class Engine {
            Want want, const uint8_t* per_layer_rows, size_t rows_bytes, float* out,
            size_t out_floats, int32_t* sources);
   void check_status();
+  void prof_mark(const char* name);
+  bool profiling_ = false;
+  std::vector<cudaEvent_t> prof_events_;
+  std::vector<const char*> prof_names_;
+  size_t prof_used_ = 0;
   std::pair<size_t, size_t> state_rows(int l, size_t p) const;
   SavedState save_state_at(const uint32_t* prefix, size_t n, size_t row0);
   std::optional<PrefixSource> restore_from_cache(const uint32_t* prefix, size_t n);

@@ -348,6 +348,16 @@ class Engine:
                                             C.byref(launches)))
         return ms.value, launches.value
 
+    def profile_forward(self, groups: Sequence[Group], want: Want, iters: int,
+                        resident: bool = False) -> dict:
+        """Per-kernel device time: {name: (launches, total_ms)}."""
+        req = _Branches(groups)
+        need = C.c_size_t(0)
+        buf = C.create_string_buffer(8192)
+        check(lib().omg_engine_profile_forward(self._h, req.groups, len(groups), int(want),
+                                               int(resident), iters, buf, 8192, C.byref(need)))
+        return {k: tuple(v) for k, v in json.loads(buf.value.decode()).items()}
+
     def record_event(self, slot: int):
         check(lib().omg_engine_record_event(self._h, slot))
 

@@ -189,6 +189,13 @@ int omg_engine_get_info(omg_engine* e, omg_engine_info* info);
 int omg_engine_time_forward(omg_engine* e, const omg_group* groups, size_t n_groups, int want,
                             int resident, int iters, float* ms, int* launches);
 
+/* Per-kernel device time of `iters` full passes of the request (the role of
+ * the reference's OMG_WGPU_PROFILE per-dispatch timestamps,
+ * engine.rs:643-726 and :1778-1795): CUDA events between launches on the
+ * engine's stream. Writes JSON {"kernel": [launches, total_ms], ...}. */
+int omg_engine_profile_forward(omg_engine* e, const omg_group* groups, size_t n_groups, int want,
+                               int resident, int iters, char* json, size_t cap, size_t* needed);
+
 /* CUDA events on the engine's stream (slots 0..5) for end-to-end timing of
  * API calls: record, then the elapsed milliseconds between two slots. */
 int omg_engine_record_event(omg_engine* e, int slot);
@@ -248,6 +255,15 @@ int omg_synth_normal(uint64_t seed, const char* name, float mean, float stddev, 
  * matmul_gated.wgsl:1-7 (the tests of crates/omg-wgpu/tests/matmul.rs:201-290). */
 int omg_debug_gemm(int device, const uint16_t* x_f16, int m, int k, int lda, const uint16_t* w_f16,
                    int w_rows, int n_out, int epi, int bn, int splits, void* out, int ldo);
+
+/* Block-causal GQA attention (replaces crates/omg-wgpu/src/shaders/attention.wgsl:1-35):
+ * q [t, heads * hd] f16 for cache rows base..base+t, kv [base + t, 2 * kv_heads * hd]
+ * f16 (K heads then V heads per row), meta 4 ints per cache row (position,
+ * sequence id, first key row of its group, own row + 1; engine.rs:1519-1571),
+ * window 0 = global. Writes out [t, heads * hd] f16. */
+int omg_debug_attention(int device, const uint16_t* q, const uint16_t* kv, const int32_t* meta,
+                        int t, int base, int heads, int kv_heads, int hd, int window,
+                        uint16_t* out);
 
 #ifdef __cplusplus
 }

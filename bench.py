@@ -54,6 +54,8 @@ def args_():
     ap.add_argument("--profile-iters", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-layers", type=int, default=2)
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the layer count (small cases for ncu captures only)")
     return ap.parse_args()
 
 
@@ -214,6 +216,9 @@ def run_b200(a, dist: Dist):
     from grande_b200 import synth
     from grande_b200.engine import Want
     shape = synth.CONFIGS[a.config]
+    if a.layers:
+        import dataclasses
+        shape = dataclasses.replace(shape, layers=a.layers)
     resident = a.config.endswith("resident")
     cap = shape.tokens() + 64
     t_build = time.perf_counter()

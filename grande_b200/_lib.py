@@ -90,6 +90,8 @@ PROTOTYPES: dict[str, tuple] = {
                                              C.c_char_p, sz, szp]),
     "omg_debug_attention": (C.c_int, [C.c_int, u16p, u16p, i32p, C.c_int, C.c_int, C.c_int,
                                       C.c_int, C.c_int, C.c_int, u16p]),
+    "omg_gemm_splitk_noalloc": (C.c_int, [C.c_int, vp, C.c_int, C.c_int, C.c_int, vp, C.c_int,
+                                          C.c_int, vp, C.c_int, vp]),
     "omg_engine_record_event": (C.c_int, [vp, C.c_int]),
     "omg_engine_elapsed_ms": (C.c_int, [vp, C.c_int, C.c_int, f32p]),
     "omg_engine_destroy": (None, [vp]),

@@ -265,6 +265,23 @@ int omg_debug_attention(int device, const uint16_t* q, const uint16_t* kv, const
                         int t, int base, int heads, int kv_heads, int hd, int window,
                         uint16_t* out);
 
+/* ---- allocation-free entry point -------------------------------------------
+ * No counterpart in the reference. For callers that own every device buffer
+ * and cannot let a library allocate (their own memory pool, or code where an
+ * allocation would synchronise the device): Y = X * W^T with split-K on the
+ * tcgen05 GEMM, all pointers device memory of the caller — X [m, k] f16
+ * (row stride lda), W [n, k] f16, out [m, ldo] f32 — `stream` a cudaStream_t
+ * or NULL. The partial slabs and the status word live in a file-scope
+ * __device__ array of 32 MiB (held on every GPU that loads the library), so
+ * splits * m * round_up(n, 4) * 4 bytes must fit in 32 MiB - 256; larger
+ * problems are rejected with an error. Calls that overlap on the GPU share
+ * that array and race. The first call on a device looks the array up and
+ * sets kernel attributes: make it before any stream capture there. Returns
+ * after the work has finished (the status word is checked). */
+int omg_gemm_splitk_noalloc(int device, const void* x_f16, int m, int k, int lda,
+                            const void* w_f16, int n, int splits, float* out, int ldo,
+                            void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -109,6 +109,7 @@ PROTOTYPES: dict[str, tuple] = {
         [C.c_int, u16p, C.c_int, C.c_int, C.c_int, u16p, C.c_int, C.c_int, C.c_int, C.c_int,
          C.c_int, C.c_void_p, C.c_int],
     ),
+    "omg_debug_gemm_time": (C.c_int, [C.c_int] * 8 + [f32p]),
 }
 
 

@@ -20,6 +20,11 @@ struct AttnArgs {
   __half* out;          // [t, heads * hd]
   const int2* ctas;     // per CTA: first workspace token, token count (attention_schedule)
   int n_ctas;
+  // Key-range splits (head_dim 256): partials [nsplit][t][heads][256] f32 and
+  // (max, sum) [nsplit][t][heads], merged by a second kernel when nsplit > 1.
+  int nsplit;
+  float* part_o;
+  float2* part_ml;
   int t, base, heads, kv_heads, hd, window;
 };
 
@@ -27,6 +32,15 @@ struct AttnArgs {
 // runs of at most 64 / (heads per KV head) tokens that never cross a request
 // group (groups differ in row_lo).
 void attention_schedule(const TokMeta* meta, int t, int hpg, std::vector<int2>* out);
+
+// Most key-range splits per query tile (sizes the partial buffers).
+constexpr int kAttnMaxSplits = 16;
+
+// Splits for a pass (`meta` the workspace tokens' metadata, `ctas` from
+// attention_schedule): enough that every query tile's visible key tiles come
+// in chunks of >= 4 tiles, at most kAttnMaxSplits. 1 = no split.
+int attention_splits(const TokMeta* meta, int t, int base, int hpg,
+                     const std::vector<int2>& ctas, int hd);
 
 // Dynamic shared memory the attention kernels need (set once per device).
 void attention_setup_device();

@@ -104,7 +104,16 @@ extern "C" int omg_debug_attention(int device, const uint16_t* q, const uint16_t
     DevBuf dc;
     if (!dc.alloc(ctas.size() * sizeof(int2))) return set_error("cudaMalloc failed");
     CUDA_TRY(cudaMemcpy(dc.p, ctas.data(), ctas.size() * sizeof(int2), cudaMemcpyHostToDevice));
+    const int nsplit = omg::attention_splits(reinterpret_cast<const omg::TokMeta*>(meta) + base, t,
+                                             base, heads / kv_heads, ctas, hd);
+    DevBuf dpo, dpm;
+    if (!dpo.alloc(static_cast<size_t>(nsplit) * t * heads * 256 * 4) ||
+        !dpm.alloc(static_cast<size_t>(nsplit) * t * heads * 8))
+      return set_error("cudaMalloc failed");
     omg::AttnArgs a{};
+    a.nsplit = nsplit;
+    a.part_o = static_cast<float*>(dpo.p);
+    a.part_ml = static_cast<float2*>(dpm.p);
     a.ctas = static_cast<const int2*>(dc.p);
     a.n_ctas = static_cast<int>(ctas.size());
     a.q = static_cast<const __half*>(dq.p);
@@ -121,6 +130,54 @@ extern "C" int omg_debug_attention(int device, const uint16_t* q, const uint16_t
     CUDA_TRY(cudaGetLastError());
     CUDA_TRY(cudaDeviceSynchronize());
     CUDA_TRY(cudaMemcpy(out, dout.p, qb, cudaMemcpyDeviceToHost));
+    return 0;
+  });
+}
+
+// Time `iters` launches of the GEMM on device-resident random operands
+// (m x k activations, n x k weights, f16) with CUDA events; *ms gets the
+// average per launch. For the kernel sweeps behind profiles/.
+extern "C" int omg_debug_gemm_time(int device, int m, int n, int k, int epi, int bn, int splits,
+                                   int iters, float* ms) {
+  return guarded([&]() -> int {
+    CUDA_TRY(cudaSetDevice(device));
+    gemm_setup_device();
+    if (bn == 0) {
+      int sms = 148;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+      gemm_pick(n, k, sms, &bn, &splits);
+    }
+    const bool gated = epi == kEpiGeGluTanh || epi == kEpiGeGluErf;
+    const int w_rows = gated ? (n + 127) / 128 * 256 : n;
+    DevBuf dx, dw, dout, dstat;
+    if (!dx.alloc(static_cast<size_t>(m) * k * 2) || !dw.alloc(static_cast<size_t>(w_rows) * k * 2) ||
+        !dout.alloc(static_cast<size_t>(m) * n * 4 * std::max(splits, 1)) || !dstat.alloc(4))
+      return set_error("cudaMalloc failed");
+    CUDA_TRY(cudaMemset(dx.p, 0x3c, static_cast<size_t>(m) * k * 2));   // 1.0-ish halves
+    CUDA_TRY(cudaMemset(dw.p, 0x20, static_cast<size_t>(w_rows) * k * 2));
+    CUDA_TRY(cudaMemset(dstat.p, 0, 4));
+    GemmPlan plan;
+    char err[256];
+    if (!gemm_plan(&plan, dx.p, m, k, dw.p, w_rows, n, k, epi, bn, splits, err, sizeof err))
+      return set_error(err);
+    cudaEvent_t a, b;
+    CUDA_TRY(cudaEventCreate(&a));
+    CUDA_TRY(cudaEventCreate(&b));
+    for (int i = 0; i < 3; ++i)
+      gemm_run(plan, m, dout.p, n, static_cast<size_t>(m) * n, static_cast<uint32_t*>(dstat.p), 0);
+    CUDA_TRY(cudaEventRecord(a, 0));
+    for (int i = 0; i < iters; ++i)
+      gemm_run(plan, m, dout.p, n, static_cast<size_t>(m) * n, static_cast<uint32_t*>(dstat.p), 0);
+    CUDA_TRY(cudaEventRecord(b, 0));
+    CUDA_TRY(cudaEventSynchronize(b));
+    float t = 0;
+    CUDA_TRY(cudaEventElapsedTime(&t, a, b));
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    uint32_t st = 0;
+    CUDA_TRY(cudaMemcpy(&st, dstat.p, 4, cudaMemcpyDeviceToHost));
+    if (st) return set_error("gemm kernel reported device status %u", st);
+    *ms = t / iters;
     return 0;
   });
 }

@@ -354,6 +354,8 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
   for (int l = 0; l < L; ++l)
     if (c.has_kv(l)) kv_[l].alloc(Cpad * 2 * c.kv_heads * c.head_dim[l] * 2);
   attn_ctas_.alloc(Cpad * sizeof(int2));
+  attn_part_o_.alloc(static_cast<size_t>(kAttnMaxSplits) * Cpad * c.heads * 256 * 4, false);
+  attn_part_ml_.alloc(static_cast<size_t>(kAttnMaxSplits) * Cpad * c.heads * sizeof(float2), false);
   h_attn_ctas_.alloc(Cpad * sizeof(int2));
   h_ids_.alloc(Cpad * 4);
   h_meta_.alloc(Cpad * sizeof(TokMeta));
@@ -565,6 +567,8 @@ Engine::Packing Engine::pack(const GroupIn* groups, size_t n, size_t first,
   }
   attention_schedule(p.meta.data(), static_cast<int>(p.t), config.heads / config.kv_heads,
                      &p.attn_ctas);
+  p.attn_nsplit = attention_splits(p.meta.data(), static_cast<int>(p.t), static_cast<int>(p.base),
+                                   config.heads / config.kv_heads, p.attn_ctas, 256);
   // out_index[w] = device row of wanted slot w, paired with its flat out row.
   p.out_index.clear();
   for (const auto& w : wanted) {
@@ -671,6 +675,9 @@ int Engine::launch_forward(const Packing& p, Want want) {
     aa.out = attn16_.as<__half>();
     aa.ctas = attn_ctas_.as<int2>();
     aa.n_ctas = static_cast<int>(p.attn_ctas.size());
+    aa.nsplit = ly.hd == 256 ? p.attn_nsplit : 1;
+    aa.part_o = attn_part_o_.as<float>();
+    aa.part_ml = attn_part_ml_.as<float2>();
     aa.t = t;
     aa.base = static_cast<int>(p.base);
     aa.heads = c.heads;
@@ -679,6 +686,7 @@ int Engine::launch_forward(const Packing& p, Want want) {
     aa.window = ly.sliding ? c.window : 0;
     k("attention");
     launch_attention(aa, stream_);
+    if (aa.nsplit > 1) ++launches;  // the split merge, timed under "attention"
     // Output projection, then x += norm(a); h = ffn_norm(x).
     k("gemm_o");
     gemm_run(ly.o, t, a32_.p, d, slab_a, status, stream_);

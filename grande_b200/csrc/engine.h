@@ -225,6 +225,7 @@ class Engine {
     std::vector<size_t> out_index;
     std::vector<std::pair<size_t, size_t>> decoded;  // (group, cache row of its prefix)
     std::vector<int2> attn_ctas;                     // attention CTA runs
+    int attn_nsplit = 1;                             // key-range splits (head_dim 256)
     size_t t = 0, base = 0, nwanted = 0;
   };
 
@@ -259,7 +260,7 @@ class Engine {
   int max_qkv_ = 0, max_attn_ = 0, max_ff_ = 0;
 
   // Workspace.
-  DevBuffer attn_ctas_;
+  DevBuffer attn_ctas_, attn_part_o_, attn_part_ml_;
   PinnedBuffer h_attn_ctas_;
   DevBuffer ids_, meta_, row_map_, x_, x16_, h16_, qkv_, q16_, attn16_, a32_, act16_, rows_,
       logits_, status_, pl_rows16_, pli_, plp_;

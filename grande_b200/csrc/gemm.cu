@@ -22,7 +22,8 @@ struct GemmArgs {
   int m;             // valid rows
   int n_out;         // valid output columns
   int kb_total;      // 64-wide K blocks
-  int kb_per_split;  // K blocks per grid.z slab
+  int kb_per_split;  // K blocks per split-K slab
+  int m_tiles, n_tiles, splits;
   void* out;
   int ldo;           // output row stride in elements
   size_t split_stride;
@@ -36,7 +37,8 @@ struct Cfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
-  static constexpr uint32_t TMEM_COLS = BN;
+  // Two accumulators: the epilogue drains one while the MMAs fill the other.
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
 };
 
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -64,6 +66,32 @@ __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.0f + erf_as(x * 0.7071067811865476f));
 }
 
+__device__ __forceinline__ void store_f16x32(__half* o, const float (&v)[32], int col0, int n_out) {
+  if (col0 + 32 <= n_out) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      uint4 pk;
+      __half2 h0 = __floats2half2_rn(v[j], v[j + 1]);
+      __half2 h1 = __floats2half2_rn(v[j + 2], v[j + 3]);
+      __half2 h2 = __floats2half2_rn(v[j + 4], v[j + 5]);
+      __half2 h3 = __floats2half2_rn(v[j + 6], v[j + 7]);
+      pk.x = *reinterpret_cast<uint32_t*>(&h0);
+      pk.y = *reinterpret_cast<uint32_t*>(&h1);
+      pk.z = *reinterpret_cast<uint32_t*>(&h2);
+      pk.w = *reinterpret_cast<uint32_t*>(&h3);
+      *reinterpret_cast<uint4*>(o + j) = pk;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < n_out) o[j] = __float2half_rn(v[j]);
+  }
+}
+
+// Persistent: CTA b handles tiles b, b + gridDim.x, ... Tile t is
+// (m = t % m_tiles, n = (t / m_tiles) % n_tiles, split = t / (m_tiles * n_tiles)):
+// the CTAs running at once share few weight tiles, which stay in L2 while
+// every M tile of them is computed.
 template <int BN, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
@@ -76,25 +104,24 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sb = smem + C::STAGES * C::A_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(sb + C::STAGES * C::B_BYTES);
   uint64_t* empty = full + C::STAGES;
-  uint64_t* accum = empty + C::STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* tfull = empty + C::STAGES;   // [2] accumulator ready
+  uint64_t* tempty = tfull + 2;          // [2] accumulator drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n_tile = blockIdx.x;
-  const int m_tile = blockIdx.y;
-  const int split = blockIdx.z;
-  const int kb0 = split * g.kb_per_split;
-  const int kb1 = min(g.kb_total, kb0 + g.kb_per_split);
-  const int nkb = kb1 - kb0;
+  const int total = g.m_tiles * g.n_tiles * g.splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&tma);
@@ -108,49 +135,77 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % C::STAGES;
-        const uint32_t ph = (i / C::STAGES) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, g.status)) break;
-        mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-        const int kx = (kb0 + i) * BK;
-        tma_load_2d(sa + s * C::A_BYTES, &tma, &full[s], kx, m_tile * BM);
-        tma_load_2d(sb + s * C::B_BYTES, &tmb, &full[s], kx, n_tile * BN);
+      int it = 0;
+      for (int tile = blockIdx.x; tile < total && !*abort_flag; tile += gridDim.x) {
+        const int m_tile = tile % g.m_tiles;
+        const int n_tile = (tile / g.m_tiles) % g.n_tiles;
+        const int split = tile / (g.m_tiles * g.n_tiles);
+        const int kb0 = split * g.kb_per_split;
+        const int kb1 = min(g.kb_total, kb0 + g.kb_per_split);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, g.status)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+          tma_load_2d(sa + s * C::A_BYTES, &tma, &full[s], kb * BK, m_tile * BM);
+          tma_load_2d(sb + s * C::B_BYTES, &tmb, &full[s], kb * BK, n_tile * BN);
+        }
+        if (!ok) break;
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16_f32(BM, BN);
-      bool ok = true;
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % C::STAGES;
-        const uint32_t ph = (i / C::STAGES) & 1;
-        if (!mbar_wait(&full[s], ph, abort_flag, g.status)) {
-          ok = false;
-          break;
-        }
+      int it = 0, local = 0;
+      for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++local) {
+        const int split = tile / (g.m_tiles * g.n_tiles);
+        const int kb0 = split * g.kb_per_split;
+        const int kb1 = min(g.kb_total, kb0 + g.kb_per_split);
+        const int b = local & 1;
+        if (!mbar_wait(&tempty[b], ((local >> 1) & 1) ^ 1, abort_flag, g.status)) break;
         tc_fence_after();
-        const uint64_t da = sw128_desc(sa + s * C::A_BYTES);
-        const uint64_t db = sw128_desc(sb + s * C::B_BYTES);
+        const uint32_t d = tmem + static_cast<uint32_t>(b * BN);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort_flag, g.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = sw128_desc(sa + s * C::A_BYTES);
+          const uint64_t db = sw128_desc(sb + s * C::B_BYTES);
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k) {
-          umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16(d, da + 2 * k, db + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
         }
-        umma_commit(&empty[s]);
+        if (!ok) break;
+        umma_commit(&tfull[b]);
       }
-      if (ok) umma_commit(accum);
     }
   } else {
     // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +32, one row per thread.
     const int q = warp & 3;
-    int ok = 0;
-    if (lane == 0) ok = mbar_wait(accum, 0, abort_flag, g.status) ? 1 : 0;
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    __syncwarp();
-    tc_fence_after();
-    if (ok) {
+    int local = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++local) {
+      const int m_tile = tile % g.m_tiles;
+      const int n_tile = (tile / g.m_tiles) % g.n_tiles;
+      const int split = tile / (g.m_tiles * g.n_tiles);
+      const int b = local & 1;
+      int ok = 0;
+      if (lane == 0) ok = mbar_wait(&tfull[b], (local >> 1) & 1, abort_flag, g.status) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
       const int row = m_tile * BM + q * 32 + lane;
-      const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16);
+      const uint32_t tbase =
+          tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BN);
       if constexpr (EPI == kEpiF32) {
         float* obase = static_cast<float*>(g.out) + split * g.split_stride +
                        static_cast<size_t>(row) * g.ldo;
@@ -166,7 +221,7 @@ __global__ void __launch_bounds__(192, 1)
               for (int j = 0; j < 32; j += 4)
                 *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
             } else {
-              #pragma unroll
+#pragma unroll
               for (int j = 0; j < 32; ++j)
                 if (col0 + j < g.n_out) o[j] = v[j];
             }
@@ -179,32 +234,11 @@ __global__ void __launch_bounds__(192, 1)
           float v[32];
           tmem_ld32(tbase + c * 32, v);
           const int col0 = n_tile * BN + c * 32;
-          if (row < g.m && col0 < g.n_out) {
-            __half* o = obase + col0;
-            if (col0 + 32 <= g.n_out) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 8) {
-                uint4 pk;
-                __half2 h0 = __floats2half2_rn(v[j], v[j + 1]);
-                __half2 h1 = __floats2half2_rn(v[j + 2], v[j + 3]);
-                __half2 h2 = __floats2half2_rn(v[j + 4], v[j + 5]);
-                __half2 h3 = __floats2half2_rn(v[j + 6], v[j + 7]);
-                pk.x = *reinterpret_cast<uint32_t*>(&h0);
-                pk.y = *reinterpret_cast<uint32_t*>(&h1);
-                pk.z = *reinterpret_cast<uint32_t*>(&h2);
-                pk.w = *reinterpret_cast<uint32_t*>(&h3);
-                *reinterpret_cast<uint4*>(o + j) = pk;
-              }
-            } else {
-              #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < g.n_out) o[j] = __float2half_rn(v[j]);
-            }
-          }
+          if (row < g.m && col0 < g.n_out) store_f16x32(obase + col0, v, col0, g.n_out);
         }
       } else {
-        // GeGLU: TMEM columns 0..127 hold the gate products, 128..255 the up
-        // products of the same 128 output columns.
+        // GeGLU: accumulator columns 0..127 hold the gate products, 128..255
+        // the up products of the same 128 output columns.
         static_assert(BN == 256, "GeGLU tiles pair 128 gate rows with 128 up rows");
         __half* obase = static_cast<__half*>(g.out) + static_cast<size_t>(row) * g.ldo;
 #pragma unroll 1
@@ -214,35 +248,17 @@ __global__ void __launch_bounds__(192, 1)
           tmem_ld32(tbase + 128 + c * 32, uv);
           const int col0 = n_tile * 128 + c * 32;
           if (row < g.m && col0 < g.n_out) {
-            float hv[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float a = (EPI == kEpiGeGluTanh) ? gelu_tanh(gv[j]) : gelu_erf(gv[j]);
-              hv[j] = a * uv[j];
-            }
-            __half* o = obase + col0;
-            if (col0 + 32 <= g.n_out) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 8) {
-                uint4 pk;
-                __half2 h0 = __floats2half2_rn(hv[j], hv[j + 1]);
-                __half2 h1 = __floats2half2_rn(hv[j + 2], hv[j + 3]);
-                __half2 h2 = __floats2half2_rn(hv[j + 4], hv[j + 5]);
-                __half2 h3 = __floats2half2_rn(hv[j + 6], hv[j + 7]);
-                pk.x = *reinterpret_cast<uint32_t*>(&h0);
-                pk.y = *reinterpret_cast<uint32_t*>(&h1);
-                pk.z = *reinterpret_cast<uint32_t*>(&h2);
-                pk.w = *reinterpret_cast<uint32_t*>(&h3);
-                *reinterpret_cast<uint4*>(o + j) = pk;
-              }
-            } else {
-              #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < g.n_out) o[j] = __float2half_rn(hv[j]);
-            }
+            for (int j = 0; j < 32; ++j)
+              gv[j] = ((EPI == kEpiGeGluTanh) ? gelu_tanh(gv[j]) : gelu_erf(gv[j])) * uv[j];
+            store_f16x32(obase + col0, gv, col0, g.n_out);
           }
         }
       }
+      // This warp is done with accumulator b.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
     }
   }
   tc_fence_before();
@@ -296,8 +312,9 @@ void set_smem_attr() {
 }
 
 template <int BN, int EPI>
-void launch(const GemmPlan& p, const GemmArgs& a, int m_tiles, cudaStream_t stream) {
-  dim3 grid(p.s.n_tiles, m_tiles, p.s.splits);
+void launch(const GemmPlan& p, const GemmArgs& a, cudaStream_t stream) {
+  const int total = a.m_tiles * a.n_tiles * a.splits;
+  const int grid = total < p.num_sms ? total : p.num_sms;
   gemm_kernel<BN, EPI><<<grid, 192, Cfg<BN>::SMEM, stream>>>(p.a, p.b, a);
 }
 
@@ -313,19 +330,28 @@ void gemm_setup_device() {
 }
 
 void gemm_pick(int n, int k, int num_sms, int* bn, int* splits) {
-  (void)num_sms;
-  const int t256 = (n + 255) / 256;
-  const int t128 = (n + 127) / 128;
+  // BN 256 moves half the operand bytes per FLOP of BN 128 and measured
+  // faster at every projection shape (1.46 vs 1.02 PFLOP/s at 8192^3). Split
+  // K into s slabs (the consumer adds them in a fixed order) when that cuts
+  // the rounds of tiles per SM: cost ~ ceil(tiles * s / SMs) / s, for a
+  // nominal 7 row tiles (a ~900-token pass). The choice depends on (N, K)
+  // only, so a row's result never depends on how many rows share its pass.
   const int kb = (k + BK - 1) / BK;
-  if (t256 >= 32) {
-    *bn = 256;
-    *splits = 1;
-    return;
+  *bn = n <= 128 ? 128 : 256;
+  const int tiles = 7 * ((n + *bn - 1) / *bn);
+  const int sms = num_sms > 0 ? num_sms : 148;
+  int best = 1;
+  double best_cost = 1e30;
+  for (int s = 1; s <= 2; ++s) {
+    if (kb < 16 * s) break;  // keep >= 16 K blocks per slab
+    const int rounds = (tiles * s + sms - 1) / sms;
+    const double cost = static_cast<double>(rounds) / s + (s > 1 ? 0.05 : 0.0);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = s;
+    }
   }
-  *bn = 128;
-  // Narrow outputs: split K in two (deterministic: the consumer adds the two
-  // slabs in a fixed order) once each half still has >= 16 K blocks.
-  *splits = (t128 <= 24 && kb >= 32) ? 2 : 1;
+  *splits = best;
 }
 
 bool gemm_plan(GemmPlan* p, const void* a, int a_rows_cap, int lda, const void* w, int w_rows,
@@ -349,6 +375,10 @@ bool gemm_plan(GemmPlan* p, const void* a, int a_rows_cap, int lda, const void* 
   // Every slab must own at least one K block.
   while (splits > 1 && (splits - 1) * ((kb + splits - 1) / splits) >= kb) --splits;
   p->rows_cap = a_rows_cap;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  p->num_sms = 148;
+  cudaDeviceGetAttribute(&p->num_sms, cudaDevAttrMultiProcessorCount, dev);
   p->s.n_out = n_out;
   p->s.k = k;
   p->s.bn = bn;
@@ -377,25 +407,27 @@ void gemm_run(const GemmPlan& p, int m, void* out, int ldo, size_t split_stride,
   a.ldo = ldo;
   a.split_stride = split_stride;
   a.status = status;
-  const int m_tiles = (m + BM - 1) / BM;
+  a.m_tiles = (m + BM - 1) / BM;
+  a.n_tiles = p.s.n_tiles;
+  a.splits = p.s.splits;
   switch (p.s.epi) {
     case kEpiF32:
       if (p.s.bn == 256)
-        launch<256, kEpiF32>(p, a, m_tiles, stream);
+        launch<256, kEpiF32>(p, a, stream);
       else
-        launch<128, kEpiF32>(p, a, m_tiles, stream);
+        launch<128, kEpiF32>(p, a, stream);
       break;
     case kEpiF16:
       if (p.s.bn == 256)
-        launch<256, kEpiF16>(p, a, m_tiles, stream);
+        launch<256, kEpiF16>(p, a, stream);
       else
-        launch<128, kEpiF16>(p, a, m_tiles, stream);
+        launch<128, kEpiF16>(p, a, stream);
       break;
     case kEpiGeGluTanh:
-      launch<256, kEpiGeGluTanh>(p, a, m_tiles, stream);
+      launch<256, kEpiGeGluTanh>(p, a, stream);
       break;
     case kEpiGeGluErf:
-      launch<256, kEpiGeGluErf>(p, a, m_tiles, stream);
+      launch<256, kEpiGeGluErf>(p, a, stream);
       break;
   }
 }

@@ -36,6 +36,7 @@ struct GemmPlan {
   CUtensorMap b;  // weights [N_rows, K] f16, box 64 x bn
   GemmShape s;
   int rows_cap;
+  int num_sms;  // persistent grid size (CTAs = min(tiles, SMs))
 };
 
 // Build the plan. `a_rows_cap` bounds the activation rows the tensor map

@@ -254,6 +254,14 @@ __global__ void __launch_bounds__(128) qk_prep_kernel(QkArgs g) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int crow = g.base + tok;
   const float pos = static_cast<float>(g.meta[crow].pos);
+  // The token's RoPE rotation, shared by all its q and k heads:
+  // angle = pos * theta^(-dd / (HD/2)) (qk_prep.wgsl:52-64).
+  __shared__ float rope_c[HALF], rope_s[HALF];
+  for (int dd = threadIdx.x; dd < g.rope_dims / 2; dd += blockDim.x) {
+    const float ang = pos * powf(g.theta, -static_cast<float>(dd) / static_cast<float>(HALF));
+    sincosf(ang, &rope_s[dd], &rope_c[dd]);
+  }
+  __syncthreads();
   const float* row = g.qkv + static_cast<size_t>(tok) * g.q_stride;
   const int n_heads = g.heads + (g.has_kv ? 2 * g.kv_heads : 0);
   __half* kvrow = g.kv ? g.kv + static_cast<size_t>(crow) * 2 * g.kv_heads * HD : nullptr;
@@ -298,9 +306,7 @@ __global__ void __launch_bounds__(128) qk_prep_kernel(QkArgs g) {
       float y1 = a[e] * inv * (g.offset + wn[dd]);
       float y2 = b[e] * inv * (g.offset + wn[dd + HALF]);
       if (dd < g.rope_dims / 2) {
-        const float ang = pos * powf(g.theta, -static_cast<float>(dd) / static_cast<float>(HALF));
-        float sn, cs;
-        sincosf(ang, &sn, &cs);
+        const float cs = rope_c[dd], sn = rope_s[dd];
         const float r1 = y1 * cs - y2 * sn;
         const float r2 = y2 * cs + y1 * sn;
         y1 = r1;

@@ -265,6 +265,14 @@ int omg_debug_attention(int device, const uint16_t* q, const uint16_t* kv, const
                         int t, int base, int heads, int kv_heads, int hd, int window,
                         uint16_t* out);
 
+/* Kernel timing for tile sweeps (no reference counterpart; the reference
+ * times dispatches with timestamp queries, crates/omg-wgpu/src/engine.rs:643-726):
+ * `iters` launches of the GEMM on device-resident operands of the given shape
+ * (bn = 0 picks the engine's tiling), CUDA events around them; *ms gets the
+ * average per launch. */
+int omg_debug_gemm_time(int device, int m, int n, int k, int epi, int bn, int splits, int iters,
+                        float* ms);
+
 /* ---- allocation-free entry point -------------------------------------------
  * No counterpart in the reference. For callers that own every device buffer
  * and cannot let a library allocate (their own memory pool, or code where an

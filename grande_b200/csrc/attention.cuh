@@ -5,6 +5,7 @@
 // layers. Q, K and V are f16, scores and the online softmax f32.
 #pragma once
 #include <cuda_fp16.h>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <vector>
@@ -13,6 +14,17 @@
 
 namespace omg {
 
+// attention.wgsl:70-76 (groups: engine.rs SEQ_GROUP_SHIFT = 12): a query at
+// (qp, qs) sees a key at (kp, ks) of its own request group that is a prefix
+// key or in its own branch, at or before its position, within the window.
+__host__ __device__ inline bool attn_visible(int qp, int qs, int kp, int ks, int window) {
+  const bool same_group = ((ks ^ qs) >> 12) == 0;
+  return same_group && ((ks & 0xfff) == 0 || ks == qs) && kp <= qp &&
+         (window == 0 || static_cast<unsigned>(qp - kp) < static_cast<unsigned>(window));
+}
+
+// ---- head_dim 512: mma.sync kernel ------------------------------------------
+
 struct AttnArgs {
   const __half* q;      // [t, heads * hd]: workspace rows 0..t = cache rows base..base+t
   const __half* kv;     // [rows, 2 * kv_heads * hd]: K heads then V heads per cache row
@@ -20,11 +32,6 @@ struct AttnArgs {
   __half* out;          // [t, heads * hd]
   const int2* ctas;     // per CTA: first workspace token, token count (attention_schedule)
   int n_ctas;
-  // Key-range splits (head_dim 256): partials [nsplit][t][heads][256] f32 and
-  // (max, sum) [nsplit][t][heads], merged by a second kernel when nsplit > 1.
-  int nsplit;
-  float* part_o;
-  float2* part_ml;
   int t, base, heads, kv_heads, hd, window;
 };
 
@@ -33,18 +40,77 @@ struct AttnArgs {
 // group (groups differ in row_lo).
 void attention_schedule(const TokMeta* meta, int t, int hpg, std::vector<int2>* out);
 
-// Most key-range splits per query tile (sizes the partial buffers).
-constexpr int kAttnMaxSplits = 16;
+void launch_attention(const AttnArgs& a, cudaStream_t s);
 
-// Splits for a pass (`meta` the workspace tokens' metadata, `ctas` from
-// attention_schedule): enough that every query tile's visible key tiles come
-// in chunks of >= 4 tiles, at most kAttnMaxSplits. 1 = no split.
-int attention_splits(const TokMeta* meta, int t, int base, int hpg,
-                     const std::vector<int2>& ctas, int hd);
+// ---- head_dim 256: tensor-core (tcgen05) kernel -----------------------------
+//
+// A work item is one run of query tokens of one request group (up to
+// 128 / heads-per-KV-head tokens, so 128 query rows: the tokens x the query
+// heads sharing one KV head) against one 128-key tile of that group's cache
+// rows. Tiles sit on a grid anchored at the group's first cache row, so a
+// token meets its keys in the same tiles whatever else shares the pass. A run
+// whose keys span one tile writes its output directly; otherwise each item
+// writes an unnormalised partial (sum p.v, max, sum p) and
+// launch_attention_tc merges a row's partials in tile order.
+
+constexpr int kAttnTileRows = 128;  // query rows per item
+constexpr int kAttnTileKeys = 128;  // keys per item
+
+struct AttnItem {
+  int tok0, ntok;  // workspace tokens of the run
+  int key0;        // first cache row of the key tile
+  int slot;        // partial slot, or -1: the run's only item writes the output
+};
+
+struct AttnRun {
+  int tok0, ntok;      // workspace tokens
+  int slot0, nslots;   // its items' partial slots (consecutive, in tile order)
+};
+
+struct AttnTcArgs {
+  const int4* vis;         // per workspace token: visible cache rows [x, y) U [z, w), no window
+  const TokMeta* meta;     // cache-row order
+  const AttnItem* items;
+  const AttnRun* runs;     // runs with more than one item
+  int n_items, n_runs;
+  float* part_o;           // [slot][kv_heads][128 rows][256] f32
+  float2* part_ml;         // [slot][kv_heads][128 rows] (max, sum)
+  __half* out;             // [t, heads * 256] f16
+  uint32_t* status;        // device status word (bounded waits)
+  int t, base, heads, kv_heads, hpg, window;
+};
+
+// Per workspace token (metadata `meta_ws` = cache rows base..base+t) the
+// cache rows it may see before any window: its group's prefix rows up to
+// itself (prefix tokens) or all of them (branch tokens), and its own branch's
+// rows up to itself. Derived from the packing's metadata alone.
+void attention_intervals(const TokMeta* meta_ws, int t, int base, std::vector<int4>* vis);
+
+// Check attention_intervals against attn_visible for every (query, key)
+// pair; `meta_all` covers cache rows 0..base+t. Returns false on the first
+// disagreement (a packing the interval form does not describe).
+bool attention_check_intervals(const TokMeta* meta_all, int t, int base, const int4* vis,
+                               int window);
+
+// Items and multi-item runs of a pass for one window (0 = global). Returns
+// the number of partial slots used.
+int attention_items(const TokMeta* meta_ws, const int4* vis, int t, int base, int hpg, int window,
+                    std::vector<AttnItem>* items, std::vector<AttnRun>* runs);
+
+// Tensor maps of the tensor-core kernel: q16 [t_cap][heads * 256] f16 and one
+// layer's K/V cache [rows_cap][2 * kv_heads * 256] f16.
+bool attention_tc_map_q(CUtensorMap* m, const void* q16, int t_cap, int heads, int kv_heads,
+                        char* err, size_t errlen);
+bool attention_tc_map_kv(CUtensorMap* m, const void* kv, int rows_cap, int kv_heads, char* err,
+                         size_t errlen);
+
+// The items, then (when any run has several) the merge of their partials.
+// Returns the number of kernel launches.
+int launch_attention_tc(const CUtensorMap& tq, const CUtensorMap& tkv, const AttnTcArgs& a,
+                        cudaStream_t s);
 
 // Dynamic shared memory the attention kernels need (set once per device).
 void attention_setup_device();
-
-void launch_attention(const AttnArgs& a, cudaStream_t s);
+void attention_tc_setup_device();
 
 }  // namespace omg

@@ -4,6 +4,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <algorithm>
 #include <cstring>
 #include <vector>
 
@@ -98,22 +99,67 @@ extern "C" int omg_debug_attention(int device, const uint16_t* q, const uint16_t
     CUDA_TRY(cudaMemcpy(dkv.p, kv, static_cast<size_t>(rows) * 2 * kv_heads * hd * 2,
                         cudaMemcpyHostToDevice));
     CUDA_TRY(cudaMemcpy(dm.p, meta, static_cast<size_t>(rows) * 16, cudaMemcpyHostToDevice));
+    const omg::TokMeta* hm = reinterpret_cast<const omg::TokMeta*>(meta);
+    if (hd == 256) {
+      // Tensor-core path: the engine's schedule, with the interval form of
+      // the visibility rule checked against the rule itself on every pair.
+      std::vector<int4> vis;
+      omg::attention_intervals(hm + base, t, base, &vis);
+      if (!omg::attention_check_intervals(hm, t, base, vis.data(), window))
+        return set_error("attention: the packing's visibility is not two intervals per token");
+      std::vector<omg::AttnItem> items;
+      std::vector<omg::AttnRun> runs;
+      const int slots =
+          omg::attention_items(hm + base, vis.data(), t, base, heads / kv_heads, window, &items, &runs);
+      DevBuf dv, di, dr, dpo, dpm, dst;
+      const size_t prow = static_cast<size_t>(std::max(slots, 1)) * kv_heads * omg::kAttnTileRows;
+      if (!dv.alloc(vis.size() * sizeof(int4)) || !di.alloc(items.size() * sizeof(omg::AttnItem)) ||
+          !dr.alloc(runs.size() * sizeof(omg::AttnRun)) || !dpo.alloc(prow * 256 * 4) ||
+          !dpm.alloc(prow * 8) || !dst.alloc(4))
+        return set_error("cudaMalloc failed");
+      CUDA_TRY(cudaMemcpy(dv.p, vis.data(), vis.size() * sizeof(int4), cudaMemcpyHostToDevice));
+      CUDA_TRY(cudaMemcpy(di.p, items.data(), items.size() * sizeof(omg::AttnItem),
+                          cudaMemcpyHostToDevice));
+      CUDA_TRY(cudaMemcpy(dr.p, runs.data(), runs.size() * sizeof(omg::AttnRun),
+                          cudaMemcpyHostToDevice));
+      CUDA_TRY(cudaMemset(dst.p, 0, 4));
+      CUtensorMap tq, tkv;
+      char err[256];
+      if (!omg::attention_tc_map_q(&tq, dq.p, t, heads, kv_heads, err, sizeof err) ||
+          !omg::attention_tc_map_kv(&tkv, dkv.p, rows_pad, kv_heads, err, sizeof err))
+        return set_error("%s", err);
+      omg::AttnTcArgs a{};
+      a.vis = static_cast<const int4*>(dv.p);
+      a.meta = static_cast<const omg::TokMeta*>(dm.p);
+      a.items = static_cast<const omg::AttnItem*>(di.p);
+      a.runs = static_cast<const omg::AttnRun*>(dr.p);
+      a.n_items = static_cast<int>(items.size());
+      a.n_runs = static_cast<int>(runs.size());
+      a.part_o = static_cast<float*>(dpo.p);
+      a.part_ml = static_cast<float2*>(dpm.p);
+      a.out = static_cast<__half*>(dout.p);
+      a.status = static_cast<uint32_t*>(dst.p);
+      a.t = t;
+      a.base = base;
+      a.heads = heads;
+      a.kv_heads = kv_heads;
+      a.hpg = heads / kv_heads;
+      a.window = window;
+      omg::launch_attention_tc(tq, tkv, a, 0);
+      CUDA_TRY(cudaGetLastError());
+      CUDA_TRY(cudaDeviceSynchronize());
+      uint32_t st = 0;
+      CUDA_TRY(cudaMemcpy(&st, dst.p, 4, cudaMemcpyDeviceToHost));
+      if (st) return set_error("attention kernel reported device status %u", st);
+      CUDA_TRY(cudaMemcpy(out, dout.p, qb, cudaMemcpyDeviceToHost));
+      return 0;
+    }
     std::vector<int2> ctas;
-    omg::attention_schedule(reinterpret_cast<const omg::TokMeta*>(meta) + base, t,
-                            heads / kv_heads, &ctas);
+    omg::attention_schedule(hm + base, t, heads / kv_heads, &ctas);
     DevBuf dc;
     if (!dc.alloc(ctas.size() * sizeof(int2))) return set_error("cudaMalloc failed");
     CUDA_TRY(cudaMemcpy(dc.p, ctas.data(), ctas.size() * sizeof(int2), cudaMemcpyHostToDevice));
-    const int nsplit = omg::attention_splits(reinterpret_cast<const omg::TokMeta*>(meta) + base, t,
-                                             base, heads / kv_heads, ctas, hd);
-    DevBuf dpo, dpm;
-    if (!dpo.alloc(static_cast<size_t>(nsplit) * t * heads * 256 * 4) ||
-        !dpm.alloc(static_cast<size_t>(nsplit) * t * heads * 8))
-      return set_error("cudaMalloc failed");
     omg::AttnArgs a{};
-    a.nsplit = nsplit;
-    a.part_o = static_cast<float*>(dpo.p);
-    a.part_ml = static_cast<float2*>(dpm.p);
     a.ctas = static_cast<const int2*>(dc.p);
     a.n_ctas = static_cast<int>(ctas.size());
     a.q = static_cast<const __half*>(dq.p);

@@ -18,6 +18,7 @@
 #include <string>
 #include <vector>
 
+#include "attention.cuh"
 #include "gemm.cuh"
 #include "kernels.cuh"
 #include "model.h"
@@ -224,8 +225,15 @@ class Engine {
     // (group, branch, slot) -> flat output row
     std::vector<size_t> out_index;
     std::vector<std::pair<size_t, size_t>> decoded;  // (group, cache row of its prefix)
-    std::vector<int2> attn_ctas;                     // attention CTA runs
-    int attn_nsplit = 1;                             // key-range splits (head_dim 256)
+    std::vector<int2> attn_ctas;                     // attention CTA runs (head_dim 512)
+    // Tensor-core attention schedule (head_dim 256): per-token visible rows,
+    // then items and multi-item runs for sliding [0] and global [1] layers,
+    // staged as one block: vis | items[0] | runs[0] | items[1] | runs[1].
+    std::vector<int4> attn_vis;
+    std::vector<AttnItem> attn_items[2];
+    std::vector<AttnRun> attn_runs[2];
+    int attn_slots = 0;
+    size_t attn_off[5] = {}, attn_bytes = 0;
     size_t t = 0, base = 0, nwanted = 0;
   };
 
@@ -260,8 +268,11 @@ class Engine {
   int max_qkv_ = 0, max_attn_ = 0, max_ff_ = 0;
 
   // Workspace.
-  DevBuffer attn_ctas_, attn_part_o_, attn_part_ml_;
-  PinnedBuffer h_attn_ctas_;
+  DevBuffer attn_ctas_, attn_part_o_, attn_part_ml_, attn_sched_;
+  PinnedBuffer h_attn_ctas_, h_attn_sched_;
+  int attn_slots_cap_ = 0;
+  CUtensorMap attn_tq_;
+  std::vector<CUtensorMap> attn_tkv_;  // per layer owning head_dim-256 K/V
   DevBuffer ids_, meta_, row_map_, x_, x16_, h16_, qkv_, q16_, attn16_, a32_, act16_, rows_,
       logits_, status_, pl_rows16_, pli_, plp_;
   std::vector<DevBuffer> kv_;  // per layer that owns K/V: [cap_rows, 2 * kv_heads * hd] f16

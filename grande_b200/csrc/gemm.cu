@@ -13,6 +13,9 @@
 
 namespace omg {
 
+bool make_tmap_f16(CUtensorMap* m, const void* base, int rank, const uint64_t* dims,
+                   const uint64_t* strides, const uint32_t* box, char* err, size_t errlen);
+
 namespace {
 
 constexpr int BM = 128;
@@ -285,24 +288,10 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 bool make_tmap_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
                   uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, char* err,
                   size_t errlen) {
-  auto fn = encode_fn();
-  if (!fn) {
-    snprintf(err, errlen, "cuTensorMapEncodeTiled is not available from the driver");
-    return false;
-  }
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {row_bytes};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t es[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
-                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    snprintf(err, errlen, "cuTensorMapEncodeTiled failed (%d) for [%llu x %llu] stride %llu", (int)r,
-             (unsigned long long)outer, (unsigned long long)inner, (unsigned long long)row_bytes);
-    return false;
-  }
-  return true;
+  const uint64_t dims[2] = {inner, outer};
+  const uint64_t strides[1] = {row_bytes};
+  const uint32_t box[2] = {box_inner, box_outer};
+  return make_tmap_f16(m, base, 2, dims, strides, box, err, errlen);
 }
 
 template <int BN, int EPI>
@@ -319,6 +308,34 @@ void launch(const GemmPlan& p, const GemmArgs& a, cudaStream_t stream) {
 }
 
 }  // namespace
+
+bool make_tmap_f16(CUtensorMap* m, const void* base, int rank, const uint64_t* dims,
+                   const uint64_t* strides, const uint32_t* box, char* err, size_t errlen) {
+  auto fn = encode_fn();
+  if (!fn) {
+    snprintf(err, errlen, "cuTensorMapEncodeTiled is not available from the driver");
+    return false;
+  }
+  cuuint64_t d[5], st[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+    if (i + 1 < rank) st[i] = strides[i];
+  }
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, static_cast<cuuint32_t>(rank),
+                  const_cast<void*>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    snprintf(err, errlen, "cuTensorMapEncodeTiled failed (%d) for a rank-%d map, dims [%llu x %llu]",
+             static_cast<int>(r), rank, static_cast<unsigned long long>(dims[0]),
+             static_cast<unsigned long long>(dims[rank - 1]));
+    return false;
+  }
+  return true;
+}
 
 void gemm_setup_device() {
   set_smem_attr<128, kEpiF32>();

@@ -50,6 +50,12 @@ bool gemm_plan(GemmPlan* p, const void* a, int a_rows_cap, int lda, const void* 
 void gemm_run(const GemmPlan& p, int m, void* out, int ldo, size_t split_stride,
               uint32_t* status, cudaStream_t stream);
 
+// Encode a TMA tensor map over f16 data with the 128-byte swizzle: `rank`
+// dimensions innermost first, byte strides of dimensions 1..rank-1, box
+// extents per dimension (the innermost box must be 64 elements = 128 bytes).
+bool make_tmap_f16(CUtensorMap* m, const void* base, int rank, const uint64_t* dims,
+                   const uint64_t* strides, const uint32_t* box, char* err, size_t errlen);
+
 // Set the kernels' shared-memory limits on the current device (once per
 // device, before the first launch).
 void gemm_setup_device();

@@ -100,6 +100,26 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, ui
       : "memory");
 }
 
+// 4-D TMA tile load, coordinates innermost first.
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* tmap, uint64_t* bar, int x,
+                                            int y, int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
+// Programmatic dependent launch: wait until the grids this one depends on
+// have completed and their writes are visible (a no-op when the launch had no
+// such dependency), and let the next grid in the stream start launching.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
@@ -165,6 +185,40 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 consecutive f32 columns of this thread's TMEM lane, without the wait:
+// issue several, then call tmem_ld_wait() once before using any of them.
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor for an MN-major operand staged by TMA with
+// the 128-byte swizzle: 64 MN-elements (128 bytes) per row, consecutive K
+// rows 128 bytes apart in 8-row (1024-byte) atoms, the next 64 MN-elements
+// `mn_stride` bytes further on (leading byte offset); the next 8 K rows are
+// one atom (1024 bytes) further (stride byte offset).
+__device__ __forceinline__ uint64_t sw128_mn_desc(const void* smem, uint32_t mn_stride) {
+  const uint64_t addr = smem_u32(smem);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;
+  d |= static_cast<uint64_t>((mn_stride >> 4) & 0x3FFF) << 16;
+  d |= (1024ull >> 4) << 32;
+  d |= 1ull << 46;
+  d |= 2ull << 61;
+  return d;
+}
+
 // Shared-memory matrix descriptor for a K-major tile written by TMA with the
 // 128-byte swizzle: rows of 128 bytes, 8-row atoms 1024 bytes apart. The
 // tile base must be 1024-byte aligned; advancing along K inside the atom is
@@ -186,6 +240,11 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
          | (0u << 7) | (0u << 10)                    // A, B format f16
          | (static_cast<uint32_t>(N >> 3) << 17)     // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
+}
+
+// The same with B MN-major (B stored [K][N], N contiguous).
+__host__ __device__ constexpr uint32_t idesc_f16_f32_bmn(int M, int N) {
+  return idesc_f16_f32(M, N) | (1u << 16);
 }
 
 // ---- small numeric helpers -----------------------------------------------

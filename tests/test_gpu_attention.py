@@ -115,3 +115,53 @@ def test_attention_layout_invariance(device, hd, window):
         pad_kv = np.concatenate([np.zeros((lead, 2 * kvh * hd), np.float16), kv])
         got = run_attention(device, pad_q, pad_kv, meta, lead + n, 0, heads, kvh, hd, window)[lead:]
         assert np.array_equal(got, ref), (lead, float(np.abs(got - ref).max()))
+
+
+@pytest.mark.parametrize("window", [0, 512, 100])
+def test_attention_e2b_packing(device, window):
+    """A 500-token state with 12 branches of 24 (the E2B request) at GQA 8/2:
+    runs span several 128-key tiles, so their partials are merged."""
+    rng = np.random.default_rng(window + 11)
+    heads, kvh, hd = 8, 2, 256
+    meta = layout([(500, [24] * 12)])
+    rows = len(meta)
+    q, kv = make_inputs(rng, rows, heads, kvh, hd, 1.0 / np.sqrt(np.sqrt(hd)))
+    got = run_attention(device, q, kv, meta, rows, 0, heads, kvh, hd, window)
+    exp = reference(q, kv, meta, rows, 0, heads, kvh, hd, window)
+    assert np.abs(got - exp).max() < 2e-3 * max(np.abs(exp).max(), 1.0)
+
+
+@pytest.mark.parametrize("hd", [256, 512])
+@pytest.mark.parametrize("window", [0, 60])
+def test_attention_resident_equals_cold(device, hd, window):
+    """Branch rows computed with the prefix resident (queries = branch rows
+    only) equal, bit for bit, the same rows of a cold pass over prefix and
+    branches (tests/reference.rs:432-480 asserts this on the engine)."""
+    rng = np.random.default_rng(hd + window + 3)
+    heads, kvh = 8, 2
+    prefix = 300
+    meta = layout([(prefix, [24, 17, 40])])
+    rows = len(meta)
+    q, kv = make_inputs(rng, rows, heads, kvh, hd, 1.0)
+    cold = run_attention(device, q, kv, meta, rows, 0, heads, kvh, hd, window)
+    warm = run_attention(device, q[prefix:], kv, meta, rows - prefix, prefix, heads, kvh, hd,
+                         window)
+    assert np.array_equal(cold[prefix:], warm), float(np.abs(cold[prefix:] - warm).max())
+
+
+def test_attention_layout_invariance_long(device):
+    """A group spanning several key tiles behind other rows of another group:
+    its rows are bit-identical wherever it sits."""
+    rng = np.random.default_rng(77)
+    heads, kvh, hd = 8, 2, 256
+    grp = [(260, [31, 12])]
+    base_meta = layout(grp)
+    n = len(base_meta)
+    q, kv = make_inputs(rng, n, heads, kvh, hd, 1.0)
+    ref = run_attention(device, q, kv, base_meta, n, 0, heads, kvh, hd, 0)
+    for lead in (3, 130):
+        meta = layout(grp, lead)
+        pad_q = np.concatenate([np.ones((lead, heads * hd), np.float16), q])
+        pad_kv = np.concatenate([np.ones((lead, 2 * kvh * hd), np.float16), kv])
+        got = run_attention(device, pad_q, pad_kv, meta, lead + n, 0, heads, kvh, hd, 0)[lead:]
+        assert np.array_equal(got, ref), (lead, float(np.abs(got - ref).max()))

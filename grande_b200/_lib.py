@@ -52,6 +52,16 @@ class EngineInfo(C.Structure):
     ]
 
 
+class LayaSeqC(C.Structure):
+    _fields_ = [
+        ("ids", u32p),
+        ("n_ids", C.c_size_t),
+        ("markers", szp),
+        ("n_markers", C.c_size_t),
+        ("qtype", C.c_int),
+    ]
+
+
 vp = C.c_void_p
 pp = C.POINTER(C.c_void_p)
 cs = C.c_char_p
@@ -110,6 +120,24 @@ PROTOTYPES: dict[str, tuple] = {
          C.c_int, C.c_void_p, C.c_int],
     ),
     "omg_debug_gemm_time": (C.c_int, [C.c_int] * 8 + [f32p]),
+    "omg_laya_config_check": (C.c_int, [cs, C.c_char_p, sz]),
+    "omg_laya_config_tensors": (C.c_int, [cs, C.c_char_p, sz, szp]),
+    "omg_laya_builder_new": (C.c_int, [cs, C.c_int, pp]),
+    "omg_laya_builder_push": (C.c_int, [vp, cs, C.c_int, i64p, C.c_int, vp, sz, vp, sz]),
+    "omg_laya_builder_missing": (C.c_int, [vp, C.c_char_p, sz, szp]),
+    "omg_laya_builder_finish": (C.c_int, [vp, sz, sz, pp]),
+    "omg_laya_builder_free": (None, [vp]),
+    "omg_laya_warmup": (C.c_int, [vp]),
+    "omg_laya_hidden": (C.c_int, [vp, C.POINTER(LayaSeqC), sz, f32p, sz]),
+    "omg_laya_evaluate": (C.c_int, [vp, C.POINTER(LayaSeqC), sz, f32p, sz, f32p]),
+    "omg_laya_probabilities": (C.c_int, [vp, C.c_int, f32p, sz, C.POINTER(C.c_double)]),
+    "omg_laya_time_forward": (C.c_int, [vp, C.POINTER(LayaSeqC), sz, C.c_int, f32p,
+                                        C.POINTER(C.c_int)]),
+    "omg_laya_profile_forward": (C.c_int, [vp, C.POINTER(LayaSeqC), sz, C.c_int, C.c_char_p, sz,
+                                           szp]),
+    "omg_laya_record_event": (C.c_int, [vp, C.c_int]),
+    "omg_laya_elapsed_ms": (C.c_int, [vp, C.c_int, C.c_int, f32p]),
+    "omg_laya_destroy": (None, [vp]),
 }
 
 

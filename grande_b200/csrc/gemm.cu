@@ -31,6 +31,7 @@ struct GemmArgs {
   int ldo;           // output row stride in elements
   size_t split_stride;
   uint32_t* status;
+  GemmEpi epi;
 };
 
 template <int BN>
@@ -239,6 +240,95 @@ __global__ void __launch_bounds__(192, 1)
           const int col0 = n_tile * BN + c * 32;
           if (row < g.m && col0 < g.n_out) store_f16x32(obase + col0, v, col0, g.n_out);
         }
+      } else if constexpr (EPI == kEpiRopeF16) {
+        // 64-dim heads: columns c and c + 32 of a head form a rotation pair.
+        __half* obase = static_cast<__half*>(g.out) + static_cast<size_t>(row) * g.ldo;
+        const int p = row < g.m ? g.epi.pos[row] : 0;
+        const float2* rt = g.epi.rope + static_cast<size_t>(p) * 32;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; c += 2) {
+          float lo[32], hi[32];
+          tmem_ld32(tbase + c * 32, lo);
+          tmem_ld32(tbase + (c + 1) * 32, hi);
+          const int col0 = n_tile * BN + c * 32;
+          if (row < g.m && col0 < g.n_out) {
+            if (col0 < 2 * g.epi.q_cols) {
+              const float sc = col0 < g.epi.q_cols ? g.epi.q_scale : 1.0f;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float2 cs = rt[j];
+                const float a = lo[j], b = hi[j];
+                lo[j] = (a * cs.x - b * cs.y) * sc;
+                hi[j] = (b * cs.x + a * cs.y) * sc;
+              }
+            }
+            store_f16x32(obase + col0, lo, col0, g.n_out);
+            store_f16x32(obase + col0 + 32, hi, col0 + 32, g.n_out);
+          }
+        }
+      } else if constexpr (EPI == kEpiBiasF16 || EPI == kEpiBiasReluF16) {
+        __half* obase = static_cast<__half*>(g.out) + static_cast<size_t>(row) * g.ldo;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(tbase + c * 32, v);
+          const int col0 = n_tile * BN + c * 32;
+          if (row < g.m && col0 < g.n_out) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float b = col0 + j < g.n_out ? g.epi.bias[col0 + j] : 0.f;
+              v[j] += b;
+              if constexpr (EPI == kEpiBiasReluF16) v[j] = fmaxf(v[j], 0.f);
+            }
+            store_f16x32(obase + col0, v, col0, g.n_out);
+          }
+        }
+      } else if constexpr (EPI == kEpiResidF32) {
+        // Each output element belongs to one tile (no split-K), so the
+        // read-modify-write of the residual row is race-free.
+        float* obase = static_cast<float*>(g.out) + static_cast<size_t>(row) * g.ldo;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(tbase + c * 32, v);
+          const int col0 = n_tile * BN + c * 32;
+          if (row < g.m && col0 < g.n_out) {
+            float* o = obase + col0;
+            const float* bp = g.epi.bias ? g.epi.bias + col0 : nullptr;
+            if (col0 + 32 <= g.n_out) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                float4 x = *reinterpret_cast<const float4*>(o + j);
+                float4 b = bp ? *reinterpret_cast<const float4*>(bp + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+                if (g.epi.bias_first) {
+                  x.x = (v[j] + b.x) + x.x;
+                  x.y = (v[j + 1] + b.y) + x.y;
+                  x.z = (v[j + 2] + b.z) + x.z;
+                  x.w = (v[j + 3] + b.w) + x.w;
+                } else {
+                  x.x = x.x + v[j];
+                  x.y = x.y + v[j + 1];
+                  x.z = x.z + v[j + 2];
+                  x.w = x.w + v[j + 3];
+                  if (bp) {
+                    x.x += b.x;
+                    x.y += b.y;
+                    x.z += b.z;
+                    x.w += b.w;
+                  }
+                }
+                *reinterpret_cast<float4*>(o + j) = x;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < g.n_out) {
+                  const float b = bp ? bp[j] : 0.f;
+                  o[j] = g.epi.bias_first ? (v[j] + b) + o[j] : (bp ? (o[j] + v[j]) + b : o[j] + v[j]);
+                }
+            }
+          }
+        }
       } else {
         // GeGLU: accumulator columns 0..127 hold the gate products, 128..255
         // the up products of the same 128 output columns.
@@ -344,6 +434,14 @@ void gemm_setup_device() {
   set_smem_attr<256, kEpiF16>();
   set_smem_attr<256, kEpiGeGluTanh>();
   set_smem_attr<256, kEpiGeGluErf>();
+  set_smem_attr<128, kEpiRopeF16>();
+  set_smem_attr<256, kEpiRopeF16>();
+  set_smem_attr<128, kEpiBiasF16>();
+  set_smem_attr<256, kEpiBiasF16>();
+  set_smem_attr<128, kEpiBiasReluF16>();
+  set_smem_attr<256, kEpiBiasReluF16>();
+  set_smem_attr<128, kEpiResidF32>();
+  set_smem_attr<256, kEpiResidF32>();
 }
 
 void gemm_pick(int n, int k, int num_sms, int* bn, int* splits) {
@@ -382,7 +480,7 @@ bool gemm_plan(GemmPlan* p, const void* a, int a_rows_cap, int lda, const void* 
     bn = 256;
     splits = 1;
   }
-  if (epi == kEpiF16) splits = 1;
+  if (epi != kEpiF32) splits = 1;
   if (bn != 128 && bn != 256) {
     snprintf(err, errlen, "gemm: BN %d", bn);
     return false;
@@ -445,6 +543,45 @@ void gemm_run(const GemmPlan& p, int m, void* out, int ldo, size_t split_stride,
       break;
     case kEpiGeGluErf:
       launch<256, kEpiGeGluErf>(p, a, stream);
+      break;
+    default:
+      break;
+  }
+}
+
+void gemm_run_epi(const GemmPlan& p, int m, void* out, int ldo, const GemmEpi& epi,
+                  uint32_t* status, cudaStream_t stream) {
+  if (m <= 0) return;
+  GemmArgs a;
+  a.m = m;
+  a.n_out = p.s.n_out;
+  a.kb_total = (p.s.k + BK - 1) / BK;
+  a.kb_per_split = a.kb_total;
+  a.out = out;
+  a.ldo = ldo;
+  a.split_stride = 0;
+  a.status = status;
+  a.m_tiles = (m + BM - 1) / BM;
+  a.n_tiles = p.s.n_tiles;
+  a.splits = 1;
+  a.epi = epi;
+  const bool wide = p.s.bn == 256;
+  switch (p.s.epi) {
+    case kEpiRopeF16:
+      wide ? launch<256, kEpiRopeF16>(p, a, stream) : launch<128, kEpiRopeF16>(p, a, stream);
+      break;
+    case kEpiBiasF16:
+      wide ? launch<256, kEpiBiasF16>(p, a, stream) : launch<128, kEpiBiasF16>(p, a, stream);
+      break;
+    case kEpiBiasReluF16:
+      wide ? launch<256, kEpiBiasReluF16>(p, a, stream)
+           : launch<128, kEpiBiasReluF16>(p, a, stream);
+      break;
+    case kEpiResidF32:
+      wide ? launch<256, kEpiResidF32>(p, a, stream) : launch<128, kEpiResidF32>(p, a, stream);
+      break;
+    default:
+      gemm_run(p, m, out, ldo, 0, status, stream);
       break;
   }
 }

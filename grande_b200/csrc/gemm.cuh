@@ -18,6 +18,23 @@ enum GemmEpilogue : int {
   kEpiGeGluTanh = 1,  // W rows interleaved [gate 128 | up 128]: store f16 gelu_tanh(g) * u
   kEpiGeGluErf = 2,   // same with the exact (erf) GELU
   kEpiF16 = 3,        // store f16 rows
+  // Encoder epilogues (GemmEpi carries their operands):
+  kEpiRopeF16 = 4,      // fused [q | k | v] projection: rotate q and k heads at the row's
+                        // position (rope_bi.wgsl), q times q_scale, store f16
+  kEpiBiasF16 = 5,      // store f16(acc + bias)
+  kEpiBiasReluF16 = 6,  // store f16(max(acc + bias, 0))
+  kEpiResidF32 = 7,     // residual update in place: x = (x + acc) + bias, or
+                        // (acc + bias) + x with bias_first
+};
+
+// Operands of the encoder epilogues.
+struct GemmEpi {
+  const float* bias = nullptr;   // per output column, f32
+  const float2* rope = nullptr;  // [position][hd / 2] (cos, sin)
+  const int* pos = nullptr;      // per row: its position (the rope table row)
+  float q_scale = 1.f;
+  int q_cols = 0;                // columns [0, q_cols) are q heads, [q_cols, 2 q_cols) k heads
+  int bias_first = 0;
 };
 
 struct GemmShape {
@@ -49,6 +66,12 @@ bool gemm_plan(GemmPlan* p, const void* a, int a_rows_cap, int lda, const void* 
 // (slab z at out + z * split_stride). f16 epilogues: [m][ldo] f16.
 void gemm_run(const GemmPlan& p, int m, void* out, int ldo, size_t split_stride,
               uint32_t* status, cudaStream_t stream);
+
+// The same for the encoder epilogues (kEpiRopeF16 .. kEpiResidF32; no
+// split-K). kEpiRopeF16 needs 64-dim heads (one 64-column pair of 32-column
+// halves per head).
+void gemm_run_epi(const GemmPlan& p, int m, void* out, int ldo, const GemmEpi& epi,
+                  uint32_t* status, cudaStream_t stream);
 
 // Encode a TMA tensor map over f16 data with the 128-byte swizzle: `rank`
 // dimensions innermost first, byte strides of dimensions 1..rank-1, box

@@ -2,14 +2,11 @@
 // crates/omg-wgpu/src/shaders/{weight,embed,rmsnorm,qk_prep,logits}.wgsl.
 #include "kernels.cuh"
 #include "ptx.cuh"
+#include "quant.cuh"
 
 namespace omg {
 
 namespace {
-
-__device__ __forceinline__ float half_bits_to_float(uint16_t b) {
-  return __half2float(__ushort_as_half(b));
-}
 
 // ---- weight dequantization --------------------------------------------------
 
@@ -55,40 +52,6 @@ __global__ void dequant_f16_kernel(int dtype, const uint8_t* __restrict__ codes,
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) reinterpret_cast<uint4*>(o)[i] = reinterpret_cast<uint4*>(v)[i];
-  }
-}
-
-// Dequantized 32-element block `b` of a row-major table (f32, exact as
-// QTensor::get).
-template <int DT>
-__device__ __forceinline__ void load_block_f32(const uint8_t* codes, const uint8_t* scales,
-                                               size_t b, float (&v)[32]) {
-  if constexpr (DT == kF16) {
-    __align__(16) uint16_t h[32];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      reinterpret_cast<uint4*>(h)[i] = reinterpret_cast<const uint4*>(codes + b * 64)[i];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = half_bits_to_float(h[j]);
-  } else {
-    const uint16_t sb =
-        static_cast<uint16_t>(scales[2 * b]) | (static_cast<uint16_t>(scales[2 * b + 1]) << 8);
-    const float d = half_bits_to_float(sb);
-    if constexpr (DT == kQ8) {
-      __align__(16) int8_t q[32];
-      reinterpret_cast<uint4*>(q)[0] = reinterpret_cast<const uint4*>(codes + b * 32)[0];
-      reinterpret_cast<uint4*>(q)[1] = reinterpret_cast<const uint4*>(codes + b * 32)[1];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = static_cast<float>(q[j]) * d;
-    } else {
-      __align__(16) uint8_t q[16];
-      reinterpret_cast<uint4*>(q)[0] = reinterpret_cast<const uint4*>(codes + b * 16)[0];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        v[j] = (static_cast<float>(q[j] & 0xf) - 8.0f) * d;
-        v[j + 16] = (static_cast<float>(q[j] >> 4) - 8.0f) * d;
-      }
-    }
   }
 }
 

@@ -1,0 +1,475 @@
+// Row kernels and the tensor-core bidirectional attention of the Laya /
+// ModernBERT encoder (see laya_kernels.cuh). Reference shaders:
+// crates/omg-wgpu/src/shaders/{embed,layernorm,rope_bi,attention_bi}.wgsl.
+#include <algorithm>
+#include <cstdio>
+
+#include "gemm.cuh"
+#include "laya_kernels.cuh"
+#include "ptx.cuh"
+#include "quant.cuh"
+
+namespace omg {
+
+namespace {
+
+// ---- RoPE table ---------------------------------------------------------------
+
+__global__ void rope_table_kernel(float theta, int hd, int n_pos, float2* tab) {
+  const int half = hd / 2;
+  const int n = n_pos * half;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int p = i / half, k = i % half;
+    // rope_bi.wgsl:28: angle = pos * pow(theta, -f32(2 d) / f32(HD)).
+    const float angle = static_cast<float>(p) * powf(theta, -static_cast<float>(2 * k) /
+                                                                static_cast<float>(hd));
+    tab[i] = make_float2(cosf(angle), sinf(angle));
+  }
+}
+
+// ---- LayerNorm helpers ---------------------------------------------------------
+
+constexpr int kLnMaxVec = 16;  // float4 per lane: d <= 2048
+
+// Mean, then the variance around it (layernorm.wgsl:51-61), of a row held as
+// float4s by one warp (lane l owns float4 l + 32 k, k < nv).
+__device__ __forceinline__ void ln_stats(const float4 (&v)[kLnMaxVec], int nv, int d, float eps,
+                                         float* mean, float* inv) {
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < kLnMaxVec; ++k)
+    if (k < nv) s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+  const float m = warp_sum(s) / static_cast<float>(d);
+  float q = 0.f;
+#pragma unroll
+  for (int k = 0; k < kLnMaxVec; ++k)
+    if (k < nv) {
+      const float a = v[k].x - m, b = v[k].y - m, c = v[k].z - m, e = v[k].w - m;
+      q += (a * a + b * b) + (c * c + e * e);
+    }
+  *mean = m;
+  *inv = rsqrtf(warp_sum(q) / static_cast<float>(d) + eps);
+}
+
+__device__ __forceinline__ float4 ln_apply(float4 v, float mean, float inv, float4 w, float4 b) {
+  return make_float4((v.x - mean) * inv * w.x + b.x, (v.y - mean) * inv * w.y + b.y,
+                     (v.z - mean) * inv * w.z + b.z, (v.w - mean) * inv * w.w + b.w);
+}
+
+__device__ __forceinline__ void store_h4(__half* p, float4 v) {
+  const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+  uint2 pk;
+  pk.x = *reinterpret_cast<const uint32_t*>(&a);
+  pk.y = *reinterpret_cast<const uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = pk;
+}
+
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+// One warp per row, 8 rows per CTA.
+__global__ void __launch_bounds__(256) laya_ln_kernel(LayaLnArgs a) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= a.t) return;
+  const int nv = a.d / 128;
+  float* xr = a.x + static_cast<size_t>(row) * a.d;
+  float4 v[kLnMaxVec];
+#pragma unroll
+  for (int k = 0; k < kLnMaxVec; ++k)
+    if (k < nv) v[k] = ld4(xr + (lane + 32 * k) * 4);
+  float mean, inv;
+  ln_stats(v, nv, a.d, a.eps, &mean, &inv);
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  __half* hr = a.h16 ? a.h16 + static_cast<size_t>(row) * a.d : nullptr;
+  if (!a.in_place) {
+#pragma unroll
+    for (int k = 0; k < kLnMaxVec; ++k)
+      if (k < nv) {
+        const int c = (lane + 32 * k) * 4;
+        store_h4(hr + c, ln_apply(v[k], mean, inv, ld4(a.w1 + c), a.b1 ? ld4(a.b1 + c) : zero));
+      }
+    return;
+  }
+  const float* te = a.type_emb ? a.type_emb + static_cast<size_t>(a.qtype[row]) * a.d : nullptr;
+#pragma unroll
+  for (int k = 0; k < kLnMaxVec; ++k)
+    if (k < nv) {
+      const int c = (lane + 32 * k) * 4;
+      float4 y = ln_apply(v[k], mean, inv, ld4(a.w1 + c), a.b1 ? ld4(a.b1 + c) : zero);
+      if (te) {
+        // embed.wgsl with residual = 1: the type row is added after the norm.
+        const float4 e = ld4(te + c);
+        y.x += e.x;
+        y.y += e.y;
+        y.z += e.z;
+        y.w += e.w;
+      }
+      v[k] = y;
+      *reinterpret_cast<float4*>(xr + c) = y;
+    }
+  if (!a.w2) return;
+  ln_stats(v, nv, a.d, a.eps, &mean, &inv);
+#pragma unroll
+  for (int k = 0; k < kLnMaxVec; ++k)
+    if (k < nv) {
+      const int c = (lane + 32 * k) * 4;
+      store_h4(hr + c, ln_apply(v[k], mean, inv, ld4(a.w2 + c), a.b2 ? ld4(a.b2 + c) : zero));
+    }
+}
+
+// embed.wgsl (scale 1) + layernorm.wgsl: one warp per row; lane l dequantizes
+// 32-element blocks l, l + 32, ... into x, then normalises the row.
+template <int DT>
+__global__ void __launch_bounds__(256)
+    laya_embed_ln_kernel(const int* __restrict__ ids, int t, const uint8_t* __restrict__ codes,
+                         const uint8_t* __restrict__ scales, int d, const float* __restrict__ w,
+                         float eps, float* __restrict__ x, __half* __restrict__ h16) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= t) return;
+  const size_t id = static_cast<size_t>(ids[row]);
+  const int nb = d / 32;
+  float* xr = x + static_cast<size_t>(row) * d;
+  for (int b = lane; b < nb; b += 32) {
+    float e[32];
+    load_block_f32<DT>(codes, scales, id * nb + b, e);
+#pragma unroll
+    for (int j = 0; j < 32; j += 4)
+      *reinterpret_cast<float4*>(xr + b * 32 + j) = make_float4(e[j], e[j + 1], e[j + 2], e[j + 3]);
+  }
+  __syncwarp();
+  const int nv = d / 128;
+  float4 v[kLnMaxVec];
+#pragma unroll
+  for (int k = 0; k < kLnMaxVec; ++k)
+    if (k < nv) v[k] = ld4(xr + (lane + 32 * k) * 4);
+  float mean, inv;
+  ln_stats(v, nv, d, eps, &mean, &inv);
+  __half* hr = h16 + static_cast<size_t>(row) * d;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int k = 0; k < kLnMaxVec; ++k)
+    if (k < nv) {
+      const int c = (lane + 32 * k) * 4;
+      const float4 y = ln_apply(v[k], mean, inv, ld4(w + c), zero);
+      *reinterpret_cast<float4*>(xr + c) = y;
+      store_h4(hr + c, y);
+    }
+}
+
+__global__ void laya_gather_kernel(const float* __restrict__ x, int d, const int* __restrict__ map,
+                                   int n, float* __restrict__ rows) {
+  const int r = blockIdx.x;
+  if (r >= n) return;
+  const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(map[r]) * d);
+  float4* dst = reinterpret_cast<float4*>(rows + static_cast<size_t>(r) * d);
+  for (int i = threadIdx.x; i < d / 4; i += blockDim.x) dst[i] = src[i];
+}
+
+// ---- bidirectional attention on the tensor cores ------------------------------
+//
+// One CTA = one item x one head:
+//   warp 0     TMA: Q [128 rows][64 dims] once, then per 128-key tile K and V
+//   warp 1     MMA: S = Q K^T (M 128, N 128, K 64) into TMEM columns 0..127;
+//              after the softmax, O_j = P V (M 128, N 64, K 128) into columns
+//              128..191
+//   warps 2-5  one query row per thread (its TMEM lane): masked max over the
+//              tile, exp, row sum, P (f16) into shared memory; then fold O_j
+//              into the running output in registers; finally out = o / l.
+// Two CTAs fit on an SM (83 KB of shared memory and 256 TMEM columns each),
+// so one CTA's loads overlap the other's math.
+
+constexpr int LA_CHUNK = kLayaTile * 128;  // [128 rows][128 bytes] f16
+constexpr int LA_SMEM = 1024 + 5 * LA_CHUNK + 256;
+constexpr uint32_t LA_TMEM_COLS = 256;
+constexpr uint32_t LA_TMEM_O = 128;
+constexpr float kLog2e = 1.4426950408889634f;
+
+enum { LB_Q = 0, LB_K, LB_V, LB_S, LB_P, LB_O, LB_KFREE, LB_VFREE, LB_N };
+
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          uint32_t* status, int lane) {
+  int ok = 0;
+  if (lane == 0) ok = mbar_wait(bar, parity, abort_flag, status) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+__global__ void __launch_bounds__(192, 2)
+    laya_attention_kernel(const __grid_constant__ CUtensorMap tqkv, LayaAttnArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* qs = sm;
+  uint8_t* ks = qs + LA_CHUNK;
+  uint8_t* vs = ks + LA_CHUNK;
+  uint8_t* ps = vs + LA_CHUNK;  // 2 chunks: keys 0..63, 64..127
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ps + 2 * LA_CHUNK);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + LB_N);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const LayaAttnItem it = g.items[blockIdx.x];
+  const int head = blockIdx.y;
+  const int ntiles = (it.nk + kLayaTile - 1) / kLayaTile;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < LB_N; ++i) mbar_init(&bars[i], i == LB_P ? 4 : 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tqkv);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, LA_TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bars[LB_Q], LA_CHUNK);
+      tma_load_2d(qs, &tqkv, &bars[LB_Q], head * kLayaHd, it.q0);
+      for (int j = 0; j < ntiles; ++j) {
+        const int kt = it.k0 + j * kLayaTile;
+        if (j > 0 && !mbar_wait(&bars[LB_KFREE], (j - 1) & 1, abort_flag, g.status)) break;
+        mbar_arrive_expect_tx(&bars[LB_K], LA_CHUNK);
+        tma_load_2d(ks, &tqkv, &bars[LB_K], g.d + head * kLayaHd, kt);
+        if (j > 0 && !mbar_wait(&bars[LB_VFREE], (j - 1) & 1, abort_flag, g.status)) break;
+        mbar_arrive_expect_tx(&bars[LB_V], LA_CHUNK);
+        tma_load_2d(vs, &tqkv, &bars[LB_V], 2 * g.d + head * kLayaHd, kt);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_f16_f32(128, kLayaTile);
+      constexpr uint32_t idesc_o = idesc_f16_f32_bmn(128, kLayaHd);
+      bool ok = mbar_wait(&bars[LB_Q], 0, abort_flag, g.status);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        if (!mbar_wait(&bars[LB_K], j & 1, abort_flag, g.status)) break;
+        tc_fence_after();
+        const uint64_t da = sw128_desc(qs), db = sw128_desc(ks);
+#pragma unroll
+        for (int k = 0; k < kLayaHd / 16; ++k) umma_f16(tmem, da + 2 * k, db + 2 * k, idesc_s, k);
+        umma_commit(&bars[LB_S]);
+        umma_commit(&bars[LB_KFREE]);
+        if (!mbar_wait(&bars[LB_P], j & 1, abort_flag, g.status) ||
+            !mbar_wait(&bars[LB_V], j & 1, abort_flag, g.status))
+          break;
+        tc_fence_after();
+        // K = 128 keys in 8 steps of 16; P chunk kk / 4 holds keys 64 (kk / 4) ..
+#pragma unroll
+        for (int kk = 0; kk < kLayaTile / 16; ++kk) {
+          const uint64_t pa = sw128_desc(ps + (kk >> 2) * LA_CHUNK) + 2 * (kk & 3);
+          const uint64_t vb = sw128_mn_desc(vs + kk * 2048, LA_CHUNK);
+          umma_f16(tmem + LA_TMEM_O, pa, vb, idesc_o, kk ? 1u : 0u);
+        }
+        umma_commit(&bars[LB_O]);
+        umma_commit(&bars[LB_VFREE]);
+      }
+    }
+  } else {
+    const int q4 = warp & 3;
+    const int r = 32 * q4 + lane;
+    const bool valid = r < it.nq;
+    const int tok = it.q0 + r;
+    int vlo = 0, vhi = 0;
+    if (valid) {
+      const int2 sp = g.span[tok];
+      vlo = sp.x;
+      vhi = sp.y;
+      if (g.window > 0) {
+        vlo = max(vlo, tok - g.window);
+        vhi = min(vhi, tok + g.window + 1);
+      }
+    }
+    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q4) << 16);
+    float o[kLayaHd];
+#pragma unroll
+    for (int i = 0; i < kLayaHd; ++i) o[i] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int kt = it.k0 + j * kLayaTile;
+      int c0 = min(max(vlo - kt, 0), kLayaTile), c1 = min(max(vhi - kt, 0), kLayaTile);
+      if (c1 < c0) c1 = c0;
+      if (!warp_wait(&bars[LB_S], j & 1, abort_flag, g.status, lane)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      // Pass 1: the tile's masked row max.
+      float mt = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < kLayaTile / 32; ++c) {
+        float s[32];
+        tmem_ld32(trow + c * 32, s);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int col = c * 32 + e;
+          if (col >= c0 && col < c1) mt = fmaxf(mt, s[e]);
+        }
+      }
+      const float m_new = fmaxf(m, mt);
+      const float alpha = m_new == -INFINITY ? 1.f : exp2f((m - m_new) * kLog2e);
+      const float mb = m_new == -INFINITY ? 0.f : m_new * kLog2e;
+      // Fold the previous tile's P.V into the running output: the MMA that
+      // made it is done, so its P buffer is free again.
+      if (j > 0) {
+        if (!warp_wait(&bars[LB_O], (j - 1) & 1, abort_flag, g.status, lane)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < kLayaHd / 32; ++c) {
+          float ov[32];
+          tmem_ld32(trow + LA_TMEM_O + c * 32, ov);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[c * 32 + e] = fmaf(o[c * 32 + e], alpha_prev, ov[e]);
+        }
+      }
+      // Pass 2: P = exp(s - m_new) on visible keys, 0 elsewhere, as f16 in
+      // the 128-byte-swizzled K-major layout the MMA reads.
+      float sum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < kLayaTile / 32; ++c) {
+        float s[32];
+        tmem_ld32(trow + c * 32, s);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int col = c * 32 + e;
+          const float p = (col >= c0 && col < c1) ? exp2f(fmaf(s[e], kLog2e, -mb)) : 0.f;
+          s[e] = p;
+          sum += p;
+        }
+#pragma unroll
+        for (int pc = 0; pc < 4; ++pc) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const __half2 h = __floats2half2_rn(s[pc * 8 + 2 * e], s[pc * 8 + 2 * e + 1]);
+            w4[e] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          const int key0 = c * 32 + pc * 8;
+          const int kc = key0 >> 6, pw = (key0 & 63) >> 3;
+          *reinterpret_cast<uint4*>(ps + kc * LA_CHUNK + r * 128 + ((pw ^ (r & 7)) << 4)) =
+              make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+      }
+      l = l * alpha + sum;
+      m = m_new;
+      alpha_prev = alpha;
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[LB_P]);
+    }
+    if (ok && warp_wait(&bars[LB_O], (ntiles - 1) & 1, abort_flag, g.status, lane)) {
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < kLayaHd / 32; ++c) {
+        float ov[32];
+        tmem_ld32(trow + LA_TMEM_O + c * 32, ov);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[c * 32 + e] = fmaf(o[c * 32 + e], alpha_prev, ov[e]);
+      }
+      if (valid) {
+        const float inv = l > 0.f ? 1.0f / l : 0.f;
+        __half* orow = g.out + static_cast<size_t>(tok) * g.d + head * kLayaHd;
+#pragma unroll
+        for (int e = 0; e < kLayaHd; e += 8) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const __half2 h = __floats2half2_rn(o[e + 2 * q] * inv, o[e + 2 * q + 1] * inv);
+            w4[q] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          *reinterpret_cast<uint4*>(orow + e) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, LA_TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+void launch_laya_rope_table(float theta, int hd, int n_pos, float2* tab, cudaStream_t s) {
+  const int n = n_pos * (hd / 2);
+  rope_table_kernel<<<std::max(1, std::min(1024, (n + 255) / 256)), 256, 0, s>>>(theta, hd, n_pos,
+                                                                                  tab);
+}
+
+void launch_laya_embed_ln(int dtype, const int* ids, int t, const void* codes, const void* scales,
+                          int d, const float* w, float eps, float* x, __half* h16,
+                          cudaStream_t s) {
+  if (t <= 0) return;
+  const auto* c = static_cast<const uint8_t*>(codes);
+  const auto* sc = static_cast<const uint8_t*>(scales);
+  const unsigned grid = static_cast<unsigned>((t + 7) / 8);
+  if (dtype == kQ4)
+    laya_embed_ln_kernel<kQ4><<<grid, 256, 0, s>>>(ids, t, c, sc, d, w, eps, x, h16);
+  else if (dtype == kQ8)
+    laya_embed_ln_kernel<kQ8><<<grid, 256, 0, s>>>(ids, t, c, sc, d, w, eps, x, h16);
+  else
+    laya_embed_ln_kernel<kF16><<<grid, 256, 0, s>>>(ids, t, c, sc, d, w, eps, x, h16);
+}
+
+void launch_laya_ln(const LayaLnArgs& a, cudaStream_t s) {
+  if (a.t <= 0) return;
+  laya_ln_kernel<<<static_cast<unsigned>((a.t + 7) / 8), 256, 0, s>>>(a);
+}
+
+void launch_laya_gather(const float* x, int d, const int* row_map, int n, float* rows,
+                        cudaStream_t s) {
+  if (n <= 0) return;
+  laya_gather_kernel<<<n, 128, 0, s>>>(x, d, row_map, n, rows);
+}
+
+void laya_attention_items(const int2* span, int t, int window, std::vector<LayaAttnItem>* items) {
+  items->clear();
+  int i = 0;
+  while (i < t) {
+    // Each sequence gets its own items, with query and key tiles anchored at
+    // its first row: a row meets its keys at the same tile columns whatever
+    // else shares the pass, so its result does not depend on the packing.
+    const int lo = span[i].x, hi = span[i].y;
+    for (int q0 = lo; q0 < hi; q0 += kLayaTile) {
+      const int nq = std::min(kLayaTile, hi - q0);
+      int k0 = lo, k1 = hi;
+      if (window > 0) {
+        // Keep the key grid anchored at lo: start at the tile holding the
+        // first key the chunk sees.
+        const int first = std::max(lo, q0 - window);
+        k0 = lo + (first - lo) / kLayaTile * kLayaTile;
+        k1 = std::min(hi, q0 + nq + window);
+      }
+      items->push_back(LayaAttnItem{q0, nq, k0, k1 - k0});
+    }
+    i = hi;
+  }
+}
+
+bool laya_attention_map(CUtensorMap* m, const void* qkv16, int rows_cap, int d, char* err,
+                        size_t errlen) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(3 * d), static_cast<uint64_t>(rows_cap)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(3 * d) * 2};
+  const uint32_t box[2] = {64, static_cast<uint32_t>(kLayaTile)};
+  return make_tmap_f16(m, qkv16, 2, dims, strides, box, err, errlen);
+}
+
+void launch_laya_attention(const CUtensorMap& tqkv, const LayaAttnArgs& a, cudaStream_t s) {
+  if (a.n_items <= 0) return;
+  dim3 grid(a.n_items, a.heads);
+  laya_attention_kernel<<<grid, 192, LA_SMEM, s>>>(tqkv, a);
+}
+
+void laya_setup_device() {
+  cudaFuncSetAttribute(laya_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LA_SMEM);
+}
+
+}  // namespace omg

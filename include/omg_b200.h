@@ -273,6 +273,84 @@ int omg_debug_attention(int device, const uint16_t* q, const uint16_t* kv, const
 int omg_debug_gemm_time(int device, int m, int n, int k, int epi, int bn, int splits, int iters,
                         float* ms);
 
+/* ---- Laya / ModernBERT encoder (crates/omg-wgpu/src/laya.rs) ---------------
+ * The encoder behind omg_core::Decider (crates/omg-core/src/engine.rs:70-93,
+ * via LayaBackend, crates/omg-wgpu/src/laya/backend.rs:139). */
+
+typedef struct omg_laya_builder omg_laya_builder;
+typedef struct omg_laya_engine omg_laya_engine;
+
+/* laya::Sequence (laya.rs:469-476): one question's token ids, the token
+ * index of each option's [MASK] in option order, and its question type
+ * (0 choice, 1 score, 2 noul). */
+typedef struct {
+  const uint32_t* ids;
+  size_t n_ids;
+  const size_t* markers;
+  size_t n_markers;
+  int qtype;
+} omg_laya_sequence;
+
+/* config_from_export + LayaConfig::from_json / validate (laya.rs:88-230,
+ * 312-323): the exported config.json (encoder config, `laya_agent`,
+ * `laya_tokens`). The reference resolves the special tokens' surface forms
+ * with its tokenizer; the caller passes that map as `laya_special_ids`
+ * ({"[CLS]": id, ...}) in the same object. One-line summary into `summary`. */
+int omg_laya_config_check(const char* config_json, char* summary, size_t cap);
+
+/* LayaConfig::tensors (laya.rs:252-309): "name d0,d1\n" per tensor. */
+int omg_laya_config_tensors(const char* config_json, char* buf, size_t cap, size_t* needed);
+
+/* LayaBuilder::new (laya.rs:623-645) on CUDA device `device`. */
+int omg_laya_builder_new(const char* config_json, int device, omg_laya_builder** out);
+
+/* LayaBuilder::push (laya.rs:662-708). */
+int omg_laya_builder_push(omg_laya_builder* b, const char* name, int dtype, const int64_t* shape,
+                          int ndim, const void* data, size_t nbytes, const void* scales,
+                          size_t scales_nbytes);
+
+/* LayaBuilder::missing (laya.rs:651-660): newline-separated names. */
+int omg_laya_builder_missing(omg_laya_builder* b, char* buf, size_t cap, size_t* needed);
+
+/* LayaBuilder::finish (laya.rs:711-1084): `capacity` packed tokens,
+ * `max_rows` read-back rows (one per sequence plus one per marker).
+ * Consumes the builder. */
+int omg_laya_builder_finish(omg_laya_builder* b, size_t capacity, size_t max_rows,
+                            omg_laya_engine** out);
+
+void omg_laya_builder_free(omg_laya_builder* b);
+
+/* LayaEngine::warmup (laya.rs:1126-1134). */
+int omg_laya_warmup(omg_laya_engine* e);
+
+/* LayaEngine::hidden (laya.rs:1138-1432): per sequence the [CLS] row then
+ * each marker's row, d floats each, in sequence order. */
+int omg_laya_hidden(omg_laya_engine* e, const omg_laya_sequence* seqs, size_t n, float* out_rows,
+                    size_t out_floats);
+
+/* LayaEngine::evaluate (laya.rs:1435-1438) = hidden + the host scorer and
+ * act head (laya.rs:1442-1486): out_logits gets each sequence's option
+ * logits back to back (sum of n_markers floats), out_act (n floats, may be
+ * NULL) the act probability, NaN without an act head. */
+int omg_laya_evaluate(omg_laya_engine* e, const omg_laya_sequence* seqs, size_t n,
+                      float* out_logits, size_t logits_cap, float* out_act);
+
+/* LayaEngine::probabilities (laya.rs:1489-1493). */
+int omg_laya_probabilities(omg_laya_engine* e, int qtype, const float* logits, size_t k,
+                           double* out);
+
+/* Device-resident timing and per-kernel profile (no reference counterpart
+ * beyond OMG_WGPU_PROFILE, engine.rs:643-726): as omg_engine_time_forward /
+ * omg_engine_profile_forward. */
+int omg_laya_time_forward(omg_laya_engine* e, const omg_laya_sequence* seqs, size_t n, int iters,
+                          float* ms, int* launches);
+int omg_laya_profile_forward(omg_laya_engine* e, const omg_laya_sequence* seqs, size_t n,
+                             int iters, char* buf, size_t cap, size_t* needed);
+int omg_laya_record_event(omg_laya_engine* e, int slot);
+int omg_laya_elapsed_ms(omg_laya_engine* e, int a, int b, float* ms);
+
+void omg_laya_destroy(omg_laya_engine* e);
+
 /* ---- allocation-free entry point -------------------------------------------
  * No counterpart in the reference. For callers that own every device buffer
  * and cannot let a library allocate (their own memory pool, or code where an

@@ -544,3 +544,345 @@ double oracle_log_sum_exp(const float* z, size_t n) {
   for (size_t i = 0; i < n; ++i) s += exp((double)z[i] - (double)m);
   return (double)m + log(s);
 }
+
+/* ---- Laya / ModernBERT encoder (crates/omg-wgpu/src/laya.rs) --------------
+ *
+ * The reference has no CPU code for this path; this restates the GPU plan
+ * of LayaEngine::hidden (laya.rs:1263-1345) kernel by kernel: embed.wgsl,
+ * layernorm.wgsl:48-68, rope_bi.wgsl:16-44, attention_bi.wgsl:59-188,
+ * matmul_gated.wgsl:114-134 (erf GELU), bias_act.wgsl:26-40, and the host
+ * scorer / act head of laya.rs:1442-1493. */
+
+/* layernorm.wgsl:48-68: optional residual update x += a (+ rb), then
+ * y = (v - mean) * rsqrt(var + eps) * w (+ b), variance around the mean. */
+static void laya_ln_row(float* x, const float* a, const float* rb, const float* w, const float* b,
+                        int d, float eps, float* out) {
+  if (a) {
+    for (int i = 0; i < d; ++i) {
+      float e = x[i] + a[i];
+      if (rb) e += rb[i];
+      x[i] = e;
+    }
+  }
+  float s = 0.0f;
+  for (int i = 0; i < d; ++i) s += x[i];
+  const float mean = s / (float)d;
+  float q = 0.0f;
+  for (int i = 0; i < d; ++i) {
+    const float c = x[i] - mean;
+    q += c * c;
+  }
+  const float inv = 1.0f / sqrtf(q / (float)d + eps);
+  for (int i = 0; i < d; ++i) {
+    float y = (x[i] - mean) * inv * w[i];
+    if (b) y += b[i];
+    out[i] = y;
+  }
+}
+
+/* matmul_gated.wgsl:114-124 and laya.rs:1526-1539: erf by Abramowitz &
+ * Stegun 7.1.26. */
+static float laya_erf(float x) {
+  const float s = x > 0.0f ? 1.0f : (x < 0.0f ? -1.0f : 0.0f);
+  const float a = fabsf(x);
+  const float t = 1.0f / (1.0f + 0.3275911f * a);
+  const float poly =
+      ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t +
+       0.254829592f) * t;
+  return s * (1.0f - poly * expf(-a * a));
+}
+
+static float laya_gelu_erf(float x) { return 0.5f * x * (1.0f + laya_erf(x * 0.70710678118654752f)); }
+
+/* attention_bi.wgsl:59-188 over the fused [t][q | k | v] rows (stride 3d):
+ * a query sees the keys of its own sequence, within |dpos| <= window on
+ * local layers (window 0 = all). */
+static void laya_attention(const float* qkv, int t, int d, int heads, const int32_t* pos,
+                           const int32_t* seq, int window, int mode, int threads, float* out) {
+  const int hd = d / heads;
+#pragma omp parallel for schedule(dynamic, 4) num_threads(threads)
+  for (int i = 0; i < t; ++i) {
+    float* sc = (float*)malloc(sizeof(float) * (size_t)t);
+    int* idx = (int*)malloc(sizeof(int) * (size_t)t);
+    float qh[1024], kj[1024];
+    for (int hh = 0; hh < heads; ++hh) {
+      const float* qr = qkv + (size_t)i * 3 * d + hh * hd;
+      for (int dd = 0; dd < hd; ++dd) qh[dd] = mode == ORACLE_KERNEL ? round_f16(qr[dd]) : qr[dd];
+      int n = 0;
+      for (int j = 0; j < t; ++j) {
+        if (seq[j] != seq[i]) continue;
+        const int dist = pos[i] > pos[j] ? pos[i] - pos[j] : pos[j] - pos[i];
+        if (window != 0 && dist > window) continue;
+        const float* kr = qkv + (size_t)j * 3 * d + d + hh * hd;
+        for (int dd = 0; dd < hd; ++dd) kj[dd] = mode == ORACLE_KERNEL ? round_f16(kr[dd]) : kr[dd];
+        sc[n] = dot8(qh, kj, hd);
+        idx[n++] = j;
+      }
+      float m = -INFINITY;
+      for (int s = 0; s < n; ++s) m = fmaxf(m, sc[s]);
+      float l = 0.0f;
+      for (int s = 0; s < n; ++s) l += expf(sc[s] - m);
+      float* o = out + (size_t)i * d + hh * hd;
+      for (int dd = 0; dd < hd; ++dd) o[dd] = 0.0f;
+      for (int s = 0; s < n; ++s) {
+        const float p = expf(sc[s] - m) / l;
+        const float* vr = qkv + (size_t)idx[s] * 3 * d + 2 * d + hh * hd;
+        for (int dd = 0; dd < hd; ++dd) {
+          const float vv = mode == ORACLE_KERNEL ? round_f16(vr[dd]) : vr[dd];
+          o[dd] += p * vv;
+        }
+      }
+    }
+    free(sc);
+    free(idx);
+  }
+}
+
+int oracle_laya_hidden(const oracle_laya_config* cfg, const float* const* tensors,
+                       size_t n_tensors, const uint32_t* ids, const int32_t* pos,
+                       const int32_t* seq, const uint32_t* qtype, size_t t_, int mode,
+                       int threads, float* x_out) {
+  const int d = cfg->d, L = cfg->layers, heads = cfg->heads, ff = cfg->ff;
+  const int hd = d / heads;
+  const int t = (int)t_;
+  if (t <= 0 || heads <= 0 || d % heads != 0 || hd > 1024) return -1;
+  if (threads <= 0) {
+#ifdef _OPENMP
+    threads = omp_get_max_threads();
+#else
+    threads = 1;
+#endif
+  }
+  /* Catalogue order of LayaConfig::tensors (laya.rs:265-313). */
+  size_t ti = 0;
+  int missing = 0;
+#define NEXT() (ti < n_tensors && tensors[ti] ? tensors[ti++] : (missing = 1, (const float*)NULL))
+  const float* embed = NEXT();
+  const float* embed_norm = NEXT();
+  const float* final_norm = NEXT();
+  const float* type_emb = cfg->type_emb ? NEXT() : NULL;
+  typedef struct { const float *attn_norm, *qkv, *o, *mlp_norm, *val, *gate, *wo; } enc_w;
+  typedef struct {
+    const float *n1w, *n1b, *in, *in_b, *out, *out_b, *n2w, *n2b, *l1, *l1_b, *l2, *l2_b;
+  } head_w;
+  enc_w* ew = (enc_w*)calloc((size_t)L, sizeof(enc_w));
+  head_w* hw = (head_w*)calloc((size_t)(cfg->head_layers > 0 ? cfg->head_layers : 1), sizeof(head_w));
+  for (int l = 0; l < L; ++l) {
+    ew[l].attn_norm = l > 0 ? NEXT() : NULL;
+    ew[l].qkv = NEXT();
+    ew[l].o = NEXT();
+    ew[l].mlp_norm = NEXT();
+    ew[l].val = NEXT();
+    ew[l].gate = NEXT();
+    ew[l].wo = NEXT();
+  }
+  for (int h = 0; h < cfg->head_layers; ++h) {
+    hw[h].n1w = NEXT(); hw[h].n1b = NEXT();
+    hw[h].in = NEXT(); hw[h].in_b = NEXT();
+    hw[h].out = NEXT(); hw[h].out_b = NEXT();
+    hw[h].n2w = NEXT(); hw[h].n2b = NEXT();
+    hw[h].l1 = NEXT(); hw[h].l1_b = NEXT();
+    hw[h].l2 = NEXT(); hw[h].l2_b = NEXT();
+  }
+#undef NEXT
+  const size_t T = (size_t)t;
+  const int wide = ff > 4 * d ? ff : 4 * d;
+  float* x = x_out;
+  float* h = (float*)malloc(sizeof(float) * T * d);
+  float* qkv = (float*)malloc(sizeof(float) * T * 3 * d);
+  float* attn = (float*)malloc(sizeof(float) * T * d);
+  float* a = (float*)malloc(sizeof(float) * T * d);
+  float* g1 = (float*)malloc(sizeof(float) * T * wide);
+  float* g2 = (float*)malloc(sizeof(float) * T * wide);
+  int rc = 0;
+  if (missing) {
+    rc = -2;
+    goto done;
+  }
+
+  /* embed (scale 1, laya.rs:1264-1268) into h, embed_norm -> x. */
+  for (int i = 0; i < t; ++i) {
+    memcpy(h + (size_t)i * d, embed + (size_t)ids[i] * d, sizeof(float) * d);
+    laya_ln_row(h + (size_t)i * d, NULL, NULL, embed_norm, NULL, d, cfg->eps, x + (size_t)i * d);
+  }
+  for (int l = 0; l < L; ++l) {
+    const enc_w* W = &ew[l];
+    const int sliding = cfg->sliding[l];
+    /* mm_qkv reads x on layer 0 (its norm is the embedding norm), h after. */
+    linear_rows(l > 0 ? h : x, t, d, W->qkv, 3 * d, mode, qkv, threads);
+    /* rope_bi.wgsl: whole-head rotation at the token's position, q * hd^-0.5. */
+    const float theta = sliding ? cfg->theta_local : cfg->theta_global;
+    const float scale = powf((float)hd, -0.5f);
+    for (int i = 0; i < t; ++i)
+      for (int hh = 0; hh < heads; ++hh)
+        for (int dd = 0; dd < hd / 2; ++dd) {
+          const float ang = (float)pos[i] * powf(theta, -(float)(2 * dd) / (float)hd);
+          const float c = cosf(ang), s = sinf(ang);
+          float* q = qkv + (size_t)i * 3 * d + hh * hd;
+          float* k = q + d;
+          const float qa = q[dd], qb = q[dd + hd / 2];
+          q[dd] = (qa * c - qb * s) * scale;
+          q[dd + hd / 2] = (qb * c + qa * s) * scale;
+          const float ka = k[dd], kb = k[dd + hd / 2];
+          k[dd] = ka * c - kb * s;
+          k[dd + hd / 2] = kb * c + ka * s;
+        }
+    laya_attention(qkv, t, d, heads, pos, seq, sliding ? cfg->window : 0, mode, threads, attn);
+    linear_rows(attn, t, d, W->o, d, mode, a, threads);
+    /* add_o_norm: x += a, h = mlp_norm(x). */
+    for (int i = 0; i < t; ++i)
+      laya_ln_row(x + (size_t)i * d, a + (size_t)i * d, NULL, W->mlp_norm, NULL, d, cfg->eps,
+                  h + (size_t)i * d);
+    /* mm_wi: gelu_erf(h Wval^T) * (h Wgate^T). */
+    linear_rows(h, t, d, W->val, ff, mode, g1, threads);
+    linear_rows(h, t, d, W->gate, ff, mode, g2, threads);
+    for (size_t k = 0; k < T * ff; ++k) g1[k] = laya_gelu_erf(g1[k]) * g2[k];
+    linear_rows(g1, t, ff, W->wo, d, mode, a, threads);
+    /* add_wo_norm: x += a, then the next layer's attn_norm into h, or the
+     * final norm over x in place on the last layer. */
+    for (int i = 0; i < t; ++i) {
+      float* xi = x + (size_t)i * d;
+      if (l + 1 < L) {
+        laya_ln_row(xi, a + (size_t)i * d, NULL, ew[l + 1].attn_norm, NULL, d, cfg->eps,
+                    h + (size_t)i * d);
+      } else {
+        float tmp[8192];
+        laya_ln_row(xi, a + (size_t)i * d, NULL, final_norm, NULL, d, cfg->eps, tmp);
+        memcpy(xi, tmp, sizeof(float) * d);
+      }
+    }
+  }
+  /* type_emb (embed.wgsl with residual = 1, scale 1). */
+  if (type_emb)
+    for (int i = 0; i < t; ++i)
+      for (int dd = 0; dd < d; ++dd) x[(size_t)i * d + dd] += type_emb[(size_t)qtype[i] * d + dd];
+  /* Decision-head layers (laya.rs:1316-1345). */
+  for (int hl = 0; hl < cfg->head_layers; ++hl) {
+    const head_w* W = &hw[hl];
+    if (hl == 0)
+      for (int i = 0; i < t; ++i) {
+        float tmp[8192];
+        memcpy(tmp, x + (size_t)i * d, sizeof(float) * d);
+        laya_ln_row(tmp, NULL, NULL, W->n1w, W->n1b, d, cfg->eps, h + (size_t)i * d);
+      }
+    linear_rows(h, t, d, W->in, 3 * d, mode, qkv, threads);
+    for (int i = 0; i < t; ++i)
+      for (int c = 0; c < 3 * d; ++c) qkv[(size_t)i * 3 * d + c] += W->in_b[c];
+    /* No RoPE and no query scale on the head's attention (laya.rs:1322-1327). */
+    laya_attention(qkv, t, d, heads, pos, seq, 0, mode, threads, attn);
+    linear_rows(attn, t, d, W->out, d, mode, a, threads);
+    for (int i = 0; i < t; ++i)
+      laya_ln_row(x + (size_t)i * d, a + (size_t)i * d, W->out_b, W->n2w, W->n2b, d, cfg->eps,
+                  h + (size_t)i * d);
+    linear_rows(h, t, d, W->l1, 4 * d, mode, g1, threads);
+    for (int i = 0; i < t; ++i)
+      for (int c = 0; c < 4 * d; ++c) {
+        const float y = g1[(size_t)i * 4 * d + c] + W->l1_b[c];
+        g1[(size_t)i * 4 * d + c] = y > 0.0f ? y : 0.0f;
+      }
+    linear_rows(g1, t, 4 * d, W->l2, d, mode, a, threads);
+    if (hl + 1 == cfg->head_layers) {
+      /* bias_act.wgsl with residual: x = (a + b) + x. */
+      for (int i = 0; i < t; ++i)
+        for (int c = 0; c < d; ++c) {
+          float* xi = x + (size_t)i * d + c;
+          *xi = (a[(size_t)i * d + c] + W->l2_b[c]) + *xi;
+        }
+    } else {
+      for (int i = 0; i < t; ++i)
+        laya_ln_row(x + (size_t)i * d, a + (size_t)i * d, W->l2_b, hw[hl + 1].n1w, hw[hl + 1].n1b,
+                    d, cfg->eps, h + (size_t)i * d);
+    }
+  }
+done:
+  free(h);
+  free(qkv);
+  free(attn);
+  free(a);
+  free(g1);
+  free(g2);
+  free(ew);
+  free(hw);
+  return rc;
+}
+
+/* laya.rs:1500-1523: host LayerNorm, linear and softmax of the scorer. */
+static void host_ln(const float* x, const float* w, const float* b, int n, float eps, float* out) {
+  float s = 0.0f;
+  for (int i = 0; i < n; ++i) s += x[i];
+  const float mean = s / (float)n;
+  float v = 0.0f;
+  for (int i = 0; i < n; ++i) v += (x[i] - mean) * (x[i] - mean);
+  v /= (float)n;
+  const float inv = 1.0f / sqrtf(v + eps);
+  for (int i = 0; i < n; ++i) out[i] = (x[i] - mean) * inv * w[i] + b[i];
+}
+
+static float host_dot(const float* a, const float* b, int n) {
+  float s = 0.0f;
+  for (int i = 0; i < n; ++i) s += a[i] * b[i];
+  return s;
+}
+
+static void host_softmax(const float* z, int n, float* out) {
+  float m = -INFINITY;
+  for (int i = 0; i < n; ++i) m = fmaxf(m, z[i]);
+  float s = 0.0f;
+  for (int i = 0; i < n; ++i) {
+    out[i] = expf(z[i] - m);
+    s += out[i];
+  }
+  for (int i = 0; i < n; ++i) out[i] /= s;
+}
+
+int oracle_laya_score(const float* rows, int k, int d, float eps, const float* const* w,
+                      int act_hidden, int act_out, float* logits, float* act_prob) {
+  /* w: scorer.norm_w, norm_b, l1, l1_b, l2, l2_b, then act.l1, l1_b, l2, l2_b. */
+  if (k < 1 || d > 8192) return -1;
+  float z[8192], y[8192];
+  for (int o = 0; o < k; ++o) {
+    host_ln(rows + (size_t)(o + 1) * d, w[0], w[1], d, eps, z);
+    for (int r = 0; r < d; ++r) y[r] = laya_gelu_erf(host_dot(w[2] + (size_t)r * d, z, d) + w[3][r]);
+    logits[o] = host_dot(y, w[4], d) + w[5][0];
+  }
+  if (act_out <= 0) return 0;
+  const int kk = k > 2 ? k : 2;
+  float* padded = (float*)malloc(sizeof(float) * (size_t)kk);
+  float* p = (float*)malloc(sizeof(float) * (size_t)kk);
+  for (int i = 0; i < kk; ++i) padded[i] = i < k ? logits[i] : -1e4f;
+  host_softmax(padded, kk, p);
+  float ent = 0.0f;
+  for (int i = 0; i < kk; ++i) ent += p[i] * logf(p[i] > 1e-9f ? p[i] : 1e-9f);
+  ent = -ent / logf((float)kk);
+  /* top1 / top2 of the sorted probabilities. */
+  float top1 = -INFINITY, top2 = -INFINITY;
+  for (int i = 0; i < kk; ++i) {
+    if (p[i] > top1) {
+      top2 = top1;
+      top1 = p[i];
+    } else if (p[i] > top2) {
+      top2 = p[i];
+    }
+  }
+  float* pooled = (float*)malloc(sizeof(float) * (size_t)(d + 4));
+  memcpy(pooled, rows, sizeof(float) * d);
+  pooled[d] = top1;
+  pooled[d + 1] = top1 - top2;
+  pooled[d + 2] = ent;
+  pooled[d + 3] = (float)kk / 255.0f;
+  float* ah = (float*)malloc(sizeof(float) * (size_t)act_hidden);
+  for (int r = 0; r < act_hidden; ++r)
+    ah[r] = laya_gelu_erf(host_dot(w[6] + (size_t)r * (d + 4), pooled, d + 4) + w[7][r]);
+  float* ao = (float*)malloc(sizeof(float) * (size_t)act_out);
+  float* ap = (float*)malloc(sizeof(float) * (size_t)act_out);
+  for (int r = 0; r < act_out; ++r) ao[r] = host_dot(w[8] + (size_t)r * act_hidden, ah, act_hidden) + w[9][r];
+  host_softmax(ao, act_out, ap);
+  *act_prob = ap[0];
+  free(padded);
+  free(p);
+  free(pooled);
+  free(ah);
+  free(ao);
+  free(ap);
+  return 0;
+}

@@ -97,6 +97,40 @@ void oracle_logits(const float* hidden, const float* embed, int vocab, int d, fl
 void oracle_softmax(const float* z, size_t n, float temperature, double* out);
 double oracle_log_sum_exp(const float* z, size_t n);
 
+/* ---- Laya / ModernBERT encoder (crates/omg-wgpu/src/laya.rs) ------------- */
+
+/* LayaConfig (laya.rs:46-83), the fields the forward reads. */
+typedef struct {
+  int vocab, d, layers, heads, ff;
+  const int* sliding; /* per encoder layer: 1 = local attention */
+  int window;         /* inclusive |query pos - key pos| on local layers */
+  float theta_global, theta_local, eps;
+  int head_layers;
+  int type_emb;
+} oracle_laya_config;
+
+/* LayaEngine::hidden's GPU plan (laya.rs:1263-1345) over a packed batch of
+ * sequences: embed -> embed_norm -> per layer [Wqkv, RoPE (q * hd^-0.5),
+ * bidirectional attention, Wo, x += o & mlp_norm, GeGLU(erf), Wo_mlp,
+ * x += wo & next norm] -> x = final_norm(x) + type_emb[qtype] -> decision-head
+ * layers. `tensors` are dequantized f32 in LayaConfig::tensors order
+ * (laya.rs:265-313; trailing host tensors are ignored). pos = index within
+ * the sequence, seq = sequence index. Writes the residual stream x of every
+ * token (the rows the scorer reads): x_out[t * d]. Mode ORACLE_KERNEL rounds
+ * linear inputs and weights to f16 and Q/K/V to f16 in attention
+ * (matmul.wgsl, attention_bi.wgsl:80-90). */
+int oracle_laya_hidden(const oracle_laya_config* cfg, const float* const* tensors,
+                       size_t n_tensors, const uint32_t* ids, const int32_t* pos,
+                       const int32_t* seq, const uint32_t* qtype, size_t t, int mode,
+                       int threads, float* x_out);
+
+/* LayaEngine::score (laya.rs:1442-1493): rows = [CLS] row then k marker
+ * rows (d each). w = scorer.norm_w, scorer.norm_b, scorer.l1, scorer.l1_b,
+ * scorer.l2, scorer.l2_b, act.l1, act.l1_b, act.l2, act.l2_b. Writes k
+ * logits and, when act_out > 0, the act probability. */
+int oracle_laya_score(const float* rows, int k, int d, float eps, const float* const* w,
+                      int act_hidden, int act_out, float* logits, float* act_prob);
+
 #ifdef __cplusplus
 }
 #endif

@@ -38,6 +38,15 @@ class _Cfg(C.Structure):
     ]
 
 
+class _LayaCfg(C.Structure):
+    _fields_ = [
+        ("vocab", C.c_int), ("d", C.c_int), ("layers", C.c_int), ("heads", C.c_int),
+        ("ff", C.c_int), ("sliding", C.POINTER(C.c_int)), ("window", C.c_int),
+        ("theta_global", C.c_float), ("theta_local", C.c_float), ("eps", C.c_float),
+        ("head_layers", C.c_int), ("type_emb", C.c_int),
+    ]
+
+
 def build() -> Path:
     """Compile the oracle with its Makefile (no-op when up to date)."""
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
@@ -66,6 +75,12 @@ def lib():
         _lib.oracle_softmax.argtypes = [fp, C.c_size_t, C.c_float, C.POINTER(C.c_double)]
         _lib.oracle_log_sum_exp.argtypes = [fp, C.c_size_t]
         _lib.oracle_log_sum_exp.restype = C.c_double
+        _lib.oracle_laya_hidden.argtypes = [
+            C.POINTER(_LayaCfg), C.POINTER(fp), C.c_size_t, C.POINTER(C.c_uint32),
+            C.POINTER(C.c_int32), C.POINTER(C.c_int32), C.POINTER(C.c_uint32), C.c_size_t,
+            C.c_int, C.c_int, fp]
+        _lib.oracle_laya_score.argtypes = [fp, C.c_int, C.c_int, C.c_float, C.POINTER(fp),
+                                           C.c_int, C.c_int, fp, fp]
     return _lib
 
 
@@ -272,3 +287,110 @@ def pack_groups(groups):
                 pos.append(len(prefix) + j)
                 seq.append(hi | (bi + 1))
     return np.array(ids, np.uint32), np.array(pos, np.int32), np.array(seq, np.int32)
+
+
+# ---- Laya / ModernBERT encoder (crates/omg-wgpu/src/laya.rs) ------------------
+
+@dataclass
+class OracleLayaConfig:
+    """LayaConfig (laya.rs:46-83), the fields the forward and scorer read."""
+    vocab: int
+    d: int
+    layers: int
+    heads: int
+    ff: int
+    sliding: list
+    window: int = 64
+    theta_global: float = 160000.0
+    theta_local: float = 10000.0
+    eps: float = 1e-5
+    head_layers: int = 2
+    type_emb: bool = True
+    act_hidden: int = 256
+    act_out: int = 0
+    _keep: list = field(default_factory=list, repr=False)
+
+    def tensors(self) -> list[tuple[str, list[int]]]:
+        """LayaConfig::tensors (laya.rs:265-313)."""
+        d, ff = self.d, self.ff
+        v = [("embed", [self.vocab, d]), ("embed_norm", [d]), ("final_norm", [d])]
+        if self.type_emb:
+            v.append(("type_emb", [3, d]))
+        for l in range(self.layers):
+            n = lambda s: f"enc.{l}.{s}"  # noqa: E731
+            if l > 0:
+                v.append((n("attn_norm"), [d]))
+            v += [(n("qkv"), [3 * d, d]), (n("o"), [d, d]), (n("mlp_norm"), [d]),
+                  (n("wi_val"), [ff, d]), (n("wi_gate"), [ff, d]), (n("wo"), [d, ff])]
+        for h in range(self.head_layers):
+            n = lambda s: f"head.{h}.{s}"  # noqa: E731
+            v += [(n("norm1_w"), [d]), (n("norm1_b"), [d]), (n("in_proj"), [3 * d, d]),
+                  (n("in_proj_b"), [3 * d]), (n("out_proj"), [d, d]), (n("out_proj_b"), [d]),
+                  (n("norm2_w"), [d]), (n("norm2_b"), [d]), (n("l1"), [4 * d, d]),
+                  (n("l1_b"), [4 * d]), (n("l2"), [d, 4 * d]), (n("l2_b"), [d])]
+        v += [("scorer.norm_w", [d]), ("scorer.norm_b", [d]), ("scorer.l1", [d, d]),
+              ("scorer.l1_b", [d]), ("scorer.l2", [1, d]), ("scorer.l2_b", [1])]
+        if self.act_out > 0:
+            v += [("act.l1", [self.act_hidden, d + 4]), ("act.l1_b", [self.act_hidden]),
+                  ("act.l2", [self.act_out, self.act_hidden]), ("act.l2_b", [self.act_out])]
+        return v
+
+    def _c(self) -> _LayaCfg:
+        sl = (C.c_int * len(self.sliding))(*[int(s) for s in self.sliding])
+        self._keep = [sl]
+        return _LayaCfg(self.vocab, self.d, self.layers, self.heads, self.ff, sl, self.window,
+                        self.theta_global, self.theta_local, self.eps, self.head_layers,
+                        int(self.type_emb))
+
+
+def laya_pack(seqs):
+    """laya.rs:1161-1189: ids, positions (index in the sequence), sequence
+    index and question type per token of the sequences [(ids, qtype), ...]."""
+    ids, pos, seq, qt = [], [], [], []
+    for si, (toks, qtype) in enumerate(seqs):
+        for i, t in enumerate(toks):
+            ids.append(t)
+            pos.append(i)
+            seq.append(si)
+            qt.append(qtype)
+    return (np.array(ids, np.uint32), np.array(pos, np.int32), np.array(seq, np.int32),
+            np.array(qt, np.uint32))
+
+
+def laya_hidden(cfg: OracleLayaConfig, tensors: list, ids, pos, seq, qtype,
+                mode: int = ORACLE_EXACT, threads: int = 0) -> np.ndarray:
+    """The residual stream x [t, d] after the decision-head layers (the rows
+    LayaEngine::hidden reads back). `tensors` in LayaConfig::tensors order."""
+    arrs = [np.ascontiguousarray(t, dtype=np.float32).ravel() for t in tensors]
+    ptrs = (C.POINTER(C.c_float) * len(arrs))(*[_p(a, C.c_float) for a in arrs])
+    ids = np.ascontiguousarray(ids, dtype=np.uint32)
+    pos = np.ascontiguousarray(pos, dtype=np.int32)
+    seq = np.ascontiguousarray(seq, dtype=np.int32)
+    qtype = np.ascontiguousarray(qtype, dtype=np.uint32)
+    t = ids.size
+    out = np.empty((t, cfg.d), dtype=np.float32)
+    c = cfg._c()
+    rc = lib().oracle_laya_hidden(C.byref(c), ptrs, len(arrs), _p(ids, C.c_uint32),
+                                  _p(pos, C.c_int32), _p(seq, C.c_int32),
+                                  _p(qtype, C.c_uint32), t, mode, threads, _p(out, C.c_float))
+    if rc != 0:
+        raise ValueError(f"oracle_laya_hidden failed ({rc})")
+    return out
+
+
+def laya_score(cfg: OracleLayaConfig, host: dict, rows) -> tuple[np.ndarray, float | None]:
+    """LayaEngine::score (laya.rs:1442-1493) on [CLS] + marker rows."""
+    rows = np.ascontiguousarray(rows, dtype=np.float32)
+    k = rows.shape[0] - 1
+    names = ["scorer.norm_w", "scorer.norm_b", "scorer.l1", "scorer.l1_b", "scorer.l2",
+             "scorer.l2_b", "act.l1", "act.l1_b", "act.l2", "act.l2_b"]
+    arrs = [np.ascontiguousarray(host.get(n, np.zeros(1, np.float32)), dtype=np.float32).ravel()
+            for n in names]
+    ptrs = (C.POINTER(C.c_float) * len(arrs))(*[_p(a, C.c_float) for a in arrs])
+    logits = np.empty(k, np.float32)
+    act = np.zeros(1, np.float32)
+    rc = lib().oracle_laya_score(_p(rows, C.c_float), k, cfg.d, cfg.eps, ptrs, cfg.act_hidden,
+                                 cfg.act_out, _p(logits, C.c_float), _p(act, C.c_float))
+    if rc != 0:
+        raise ValueError("oracle_laya_score failed")
+    return logits, (float(act[0]) if cfg.act_out > 0 else None)

@@ -2,7 +2,7 @@
 """Benchmark of the omg decision forward pass on B200s.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--config e2b-q4|e2b-q4-resident|gemma3-270m-q8|e4b-q4]
+                    [--config e2b-q4|e2b-q4-resident|gemma3-270m-q8|e4b-q4|mmbert-q8]
 
 Metric: questions/s on the E2B-shaped Q4_0 decoder, one
 request = a 500-token state + 12 question branches of 24 tokens evaluated in
@@ -21,6 +21,11 @@ collective on the data path). Rank 0 prints one JSON line.
   events, against MEASURED_PEAKS.json.
 * ``cpu_baseline`` / ``--impl reference``: the reference's CPU forward
   (tests/reference.rs), restated in oracle/, on the host cores.
+
+``--config mmbert-q8`` measures BASELINE.json's encoder configuration instead
+(not the headline metric): 256 sequences of 128 tokens through the Laya /
+mmBERT-shaped encoder and its decision head, the [CLS] and [MASK] rows read
+back, questions/s = sequences/s.
 """
 from __future__ import annotations
 
@@ -325,6 +330,126 @@ def run_b200(a, dist: Dist):
     eng.close()
 
 
+def laya_cpu_sample(shape, seqs: int, seed: int = 0) -> dict:
+    """`seqs` sequences of the encoder shape through oracle/ (the restated
+    GPU plan of laya.rs:1263-1345) with one encoder layer, then one encoder
+    layer + one head layer; per-layer times extrapolated to the full depth
+    and to the whole batch."""
+    import dataclasses
+
+    from grande_b200 import synth
+    from oracle import oracle as O
+    threads = os.cpu_count() or 1
+    reqs = synth.laya_request(shape, seed)[:seqs]
+    ids, pos, seq, qt = O.laya_pack([(r.ids, r.qtype) for r in reqs])
+    times = []
+    for head in (0, 1):
+        ocfg = O.OracleLayaConfig(vocab=shape.vocab, d=shape.d, layers=1, heads=shape.heads,
+                                  ff=shape.ff, sliding=[0], window=64, head_layers=head,
+                                  act_out=shape.act_costs + 1)
+        tensors = []
+        for name, dims in ocfg.tensors():
+            qt_ = synth.laya_tensor(seed, name, dims, shape.dtype)
+            tensors.append(O.dequantize(int(qt_.dtype), qt_.data, qt_.scales, qt_.numel()))
+        t0 = time.perf_counter()
+        O.laya_hidden(ocfg, tensors, ids, pos, seq, qt, O.ORACLE_EXACT, threads)
+        times.append(time.perf_counter() - t0)
+    t_enc, t_head = times[0], max(times[1] - times[0], 0.0)
+    per_batch = (t_enc * shape.layers + t_head * shape.head_layers) * shape.seqs / seqs
+    return {"per_batch_s": per_batch, "threads": threads, "sampled_s": sum(times)}
+
+
+def run_laya(a, dist: Dist):
+    """the encoder over a batch of sequences."""
+    from grande_b200 import synth
+    shape = synth.LAYA_CONFIGS[a.config]
+    if a.layers:
+        import dataclasses
+        shape = dataclasses.replace(shape, layers=a.layers)
+    t_build = time.perf_counter()
+    eng = synth.build_laya_engine(shape, shape.tokens(), shape.rows(), device=dist.local, seed=0)
+    t_build = time.perf_counter() - t_build
+    req = synth.laya_request(shape, seed=1000 + dist.rank)
+    eng.time_forward(req, max(a.warmup, 3))
+    dist.barrier()
+    clocks = Clocks(gpu_index(dist.local))
+    clocks.start()
+    time.sleep(0.25)
+    ms, launches = eng.time_forward(req, a.steps)
+    ms_max = dist.max(ms)
+    dist.barrier()
+    reqs = [synth.laya_request(shape, seed=2000 + dist.rank * 100003 + i) for i in range(4)]
+    for i in range(max(a.warmup, 3)):
+        eng.evaluate(reqs[i % len(reqs)])
+    dist.barrier()
+    lat = []
+    eng.record_event(0)
+    for i in range(a.steps):
+        t0 = time.perf_counter()
+        eng.evaluate(reqs[i % len(reqs)])
+        lat.append((time.perf_counter() - t0) * 1e3)
+    eng.record_event(1)
+    e2e_ms = eng.elapsed_ms(0, 1)
+    e2e_max = dist.max(e2e_ms)
+    dist.barrier()
+    clk = clocks.stop()
+    prof = eng.profile_forward(req, a.profile_iters)
+    t = shape.tokens()
+    wi_launches, wi_ms = prof["gemm_wi"]
+    wi_avg = wi_ms / wi_launches
+    flops_wi = 2.0 * t * shape.d * 2 * shape.ff
+    pk, pk_kind = peaks()
+    peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+    achieved = flops_wi / (wi_avg * 1e-3) / 1e12
+    n = dist.world
+    value = n * shape.seqs * a.steps / (ms_max * 1e-3)
+    e2e_value = n * shape.seqs * a.steps / (e2e_max * 1e-3)
+    out = {
+        "metric": "questions/s/GPU mmBERT-shape Q8_0 encoder (256 seqs x 128 tokens)",
+        "value": round(value, 2), "unit": UNIT, "n_gpus": n, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(ms_max / a.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic: seeded N(0,0.02) weights quantized to Q8_0, uniform token ids",
+        "config": {
+            "workload": f"{shape.name}: {shape.seqs} sequences x {shape.seq_len} tokens, full "
+                        f"bidirectional attention, [CLS] + {shape.markers} [MASK] row(s) per "
+                        f"sequence read back; 1 question per sequence",
+            "model": f"{shape.name} shape, random init ({shape.layers} layers, d {shape.d}, "
+                     f"{shape.heads} heads x 64, GeGLU ff {shape.ff}, vocab {shape.vocab}, "
+                     f"{shape.head_layers} decision-head layers)",
+            "tokens_per_pass": t, "parallelism": f"replicas x{n} (independent batches)",
+            "l2": "activations larger than L2 (32768 x 768 f32 residual stream per pass)",
+        },
+        "p50_latency_ms": round(statistics.median(lat), 3) if lat else None,
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
+                "h2d_bytes_per_step": t * 4 * 4 + 8 * shape.markers * shape.seqs,
+                "d2h_bytes_per_step": shape.rows() * shape.d * 4,
+                "ms_per_step": round(e2e_max / a.steps, 4)},
+        "gpu_launches": launches * a.steps,
+        "roofline": {"kernel": "gemm_wi (tcgen05, fused erf GeGLU)", "bound": "tensor",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": f"{pk_kind} sustained",
+                     "traffic": None, "avg_launch_ms": round(wi_avg, 5),
+                     "flop_per_launch": flops_wi},
+        "kernels_ms_per_pass": {k: round(v[1] / a.profile_iters, 4) for k, v in prof.items()},
+        "clocks": clk,
+        "build_s": round(t_build, 1),
+    }
+    if dist.world == 1 and not a.no_cpu_baseline:
+        cb = laya_cpu_sample(shape, 8)
+        out["cpu_baseline"] = {
+            "value": round(shape.seqs / cb["per_batch_s"], 4), "unit": UNIT,
+            "cores": cb["threads"], "kind": "port",
+            "sample": f"8 of {shape.seqs} sequences through oracle/ (laya.rs:1263-1345 restated "
+                      f"in C with OpenMP), one encoder layer and one head layer, extrapolated "
+                      f"to {shape.layers} + {shape.head_layers} layers and the whole batch; "
+                      f"{cb['sampled_s']:.1f} s sampled",
+        }
+    if dist.rank == 0:
+        print(json.dumps(out), flush=True)
+    eng.close()
+
+
 def read_traffic(config: str):
     """DRAM bytes per launch of the GeGLU GEMM from the committed ncu summary."""
     p = ROOT / "profiles" / f"gemm_gate_up_{config}.txt"
@@ -344,6 +469,8 @@ def run_reference(a, dist: Dist):
     if dist.rank != 0:
         return
     from grande_b200 import synth
+    if a.config in synth.LAYA_CONFIGS:
+        return run_reference_laya(a)
     shape = synth.CONFIGS[a.config]
     # Each step is a bounded sample (a.cpu_sample_layers layers of one request,
     # extrapolated to the full depth) so K steps end within minutes.
@@ -373,12 +500,43 @@ def run_reference(a, dist: Dist):
     print(json.dumps(out), flush=True)
 
 
+def run_reference_laya(a):
+    from grande_b200 import synth
+    shape = synth.LAYA_CONFIGS[a.config]
+    per = []
+    threads = os.cpu_count() or 1
+    for i in range(a.warmup + a.steps):
+        cb = laya_cpu_sample(shape, 8, seed=i)
+        if i >= a.warmup:
+            per.append(cb["per_batch_s"])
+    total = sum(per)
+    value = shape.seqs * len(per) / total
+    out = {
+        "impl": "reference",
+        "metric": "questions/s/GPU mmBERT-shape Q8_0 encoder (256 seqs x 128 tokens)",
+        "value": round(value, 4), "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(total / len(per) * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": f"{shape.name}: {shape.seqs} sequences x {shape.seq_len} tokens"},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": "per step: 8 sequences, one encoder + one head layer through "
+                                   "oracle/, extrapolated to the full depth and batch"},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
 def main():
     a = args_()
     dist = Dist(a.gpus)
     try:
+        from grande_b200 import synth
         if a.impl == "reference":
             run_reference(a, dist)
+        elif a.config in synth.LAYA_CONFIGS:
+            run_laya(a, dist)
         else:
             run_b200(a, dist)
     finally:

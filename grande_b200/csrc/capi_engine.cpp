@@ -326,7 +326,7 @@ uint64_t omg_state_key(const char* model_id, const uint32_t* prefix, size_t n) {
 
 int omg_quantize(int dtype, const float* v, size_t n, uint8_t* codes, uint8_t* scales) {
   return guarded([&] {
-    if (n % 32) fail("%zu values is not a multiple of 32", n);
+    if (dtype != OMG_DTYPE_F16 && n % 32) fail("%zu values is not a multiple of 32", n);
     if (dtype == OMG_DTYPE_Q8)
       quantize_q8(v, n, codes, scales);
     else if (dtype == OMG_DTYPE_Q4)

@@ -285,47 +285,40 @@ __global__ void __launch_bounds__(192, 1)
         }
       } else if constexpr (EPI == kEpiResidF32) {
         // Each output element belongs to one tile (no split-K), so the
-        // read-modify-write of the residual row is race-free.
-        float* obase = static_cast<float*>(g.out) + static_cast<size_t>(row) * g.ldo;
+        // read-modify-write of the residual row is race-free. The bias chunk
+        // is read into registers before the row is touched, so no bias load
+        // waits behind a store to the (possibly aliasing) residual row.
+        float* __restrict__ obase = static_cast<float*>(g.out) + static_cast<size_t>(row) * g.ldo;
+        const float* __restrict__ bias = g.epi.bias;
+        const bool bias_first = g.epi.bias_first != 0;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          tmem_ld32(tbase + c * 32, v);
+          float v[32], b[32];
           const int col0 = n_tile * BN + c * 32;
-          if (row < g.m && col0 < g.n_out) {
-            float* o = obase + col0;
-            const float* bp = g.epi.bias ? g.epi.bias + col0 : nullptr;
-            if (col0 + 32 <= g.n_out) {
 #pragma unroll
-              for (int j = 0; j < 32; j += 4) {
-                float4 x = *reinterpret_cast<const float4*>(o + j);
-                float4 b = bp ? *reinterpret_cast<const float4*>(bp + j) : make_float4(0.f, 0.f, 0.f, 0.f);
-                if (g.epi.bias_first) {
-                  x.x = (v[j] + b.x) + x.x;
-                  x.y = (v[j + 1] + b.y) + x.y;
-                  x.z = (v[j + 2] + b.z) + x.z;
-                  x.w = (v[j + 3] + b.w) + x.w;
-                } else {
-                  x.x = x.x + v[j];
-                  x.y = x.y + v[j + 1];
-                  x.z = x.z + v[j + 2];
-                  x.w = x.w + v[j + 3];
-                  if (bp) {
-                    x.x += b.x;
-                    x.y += b.y;
-                    x.z += b.z;
-                    x.w += b.w;
-                  }
+          for (int j = 0; j < 32; ++j) b[j] = (bias && col0 + j < g.n_out) ? __ldg(bias + col0 + j) : 0.f;
+          tmem_ld32(tbase + c * 32, v);
+          if (row < g.m && col0 < g.n_out) {
+            float* __restrict__ o = obase + col0;
+            if (col0 + 32 <= g.n_out) {
+              float4 xv[8];
+#pragma unroll
+              for (int q = 0; q < 8; ++q) xv[q] = *reinterpret_cast<const float4*>(o + 4 * q);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                float* x = reinterpret_cast<float*>(&xv[q]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int j = 4 * q + e;
+                  x[e] = bias_first ? (v[j] + b[j]) + x[e] : (x[e] + v[j]) + b[j];
                 }
-                *reinterpret_cast<float4*>(o + j) = x;
+                *reinterpret_cast<float4*>(o + 4 * q) = xv[q];
               }
             } else {
 #pragma unroll
               for (int j = 0; j < 32; ++j)
-                if (col0 + j < g.n_out) {
-                  const float b = bp ? bp[j] : 0.f;
-                  o[j] = g.epi.bias_first ? (v[j] + b) + o[j] : (bp ? (o[j] + v[j]) + b : o[j] + v[j]);
-                }
+                if (col0 + j < g.n_out)
+                  o[j] = bias_first ? (v[j] + b[j]) + o[j] : (o[j] + v[j]) + b[j];
             }
           }
         }

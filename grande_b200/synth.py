@@ -118,3 +118,90 @@ def request(shape: Shape, seed: int = 0, state: int | None = None) -> Group:
     branches = [BranchTokens(rng.integers(0, shape.vocab, shape.branch_len).tolist(),
                              [shape.branch_len - 1]) for _ in range(shape.branches)]
     return Group(prefix, branches)
+
+
+# ---- the Laya / mmBERT encoder --------------------------
+
+@dataclass
+class LayaShape:
+    """An encoder configuration: model widths and the batch of sequences."""
+    name: str
+    layers: int
+    d: int
+    heads: int
+    ff: int
+    vocab: int
+    dtype: Dtype
+    head_layers: int
+    act_costs: int
+    seqs: int
+    seq_len: int
+    markers: int        # [MASK] rows read per sequence
+
+    def config(self) -> dict:
+        from .laya import synthetic_config
+        # Full bidirectional attention on every layer (BASELINE.json
+        # configs[4]: window 0 throughout).
+        return synthetic_config(self.vocab, self.d, self.layers, self.heads, self.ff,
+                                head_layers=self.head_layers, act_costs=self.act_costs,
+                                layer_types=["full_attention"] * self.layers)
+
+    def config_json(self) -> str:
+        return json.dumps(self.config())
+
+    def tokens(self) -> int:
+        return self.seqs * self.seq_len
+
+    def rows(self) -> int:
+        return self.seqs * (1 + self.markers)
+
+
+LAYA_CONFIGS = {
+    "mmbert-q8": LayaShape("mmbert-q8", 22, 768, 12, 1152, 56000, Dtype.Q8, 2, 3, 256, 128, 1),
+}
+
+
+def laya_tensor(seed: int, name: str, shape, dtype: Dtype) -> QTensor:
+    """Linears ~N(0, 0.02) quantized to `dtype`; norm weights 1 + N(0, 0.02);
+    biases, the type embedding and the host-side scorer / act head
+    ~N(0, 0.02) in f16."""
+    n = int(np.prod(shape))
+    last = name.rsplit(".", 1)[-1]
+    host = name.startswith("scorer.") or name.startswith("act.")
+    if len(shape) == 1:
+        mean = 0.0 if last.endswith("_b") else 1.0
+        return QTensor.from_f32(shape, normal(seed, name, n, mean, 0.02))
+    v = normal(seed, name, n, 0.0, 0.02)
+    if host or name == "type_emb":
+        return QTensor.from_f32(shape, v)
+    return QTensor._encode(dtype, shape, v)
+
+
+def build_laya_engine(shape: LayaShape, capacity: int, max_rows: int, device: int = 0,
+                      seed: int = 0, threads: int = 8):
+    from .laya import LayaBuilder, config_tensors
+    b = LayaBuilder(shape.config_json(), device)
+    specs = config_tensors(shape.config_json())
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        futs = [(name, ex.submit(laya_tensor, seed, name, dims, shape.dtype))
+                for name, dims in specs]
+        for name, f in futs:
+            b.push(name, f.result())
+    return b.finish(capacity, max_rows)
+
+
+def laya_request(shape: LayaShape, seed: int = 0) -> list:
+    """`shape.seqs` sequences: [CLS], uniform ids, [MASK] markers at seeded
+    positions, [SEP] last; question types cycle 0, 1, 2."""
+    from .laya import Sequence
+    rng = np.random.default_rng(seed)
+    out = []
+    for i in range(shape.seqs):
+        ids = rng.integers(5, shape.vocab, shape.seq_len)
+        ids[0], ids[-1] = 1, 2
+        markers = sorted(rng.choice(np.arange(1, shape.seq_len - 1), shape.markers,
+                                    replace=False).tolist())
+        for m in markers:
+            ids[m] = 3
+        out.append(Sequence(ids.tolist(), markers, i % 3))
+    return out

@@ -229,7 +229,8 @@ uint64_t omg_state_key(const char* model_id, const uint32_t* prefix, size_t n);
 /* ---- tensors (crates/omg-wgpu/src/model.rs:395-525) ---------------------- */
 
 /* QTensor::from_f32 / quantize_q8 / quantize_q4 (model.rs:395-466): codes
- * get 2n (f16), n (Q8) or n/2 (Q4) bytes, scales n/16 bytes. */
+ * get 2n (f16), n (Q8) or n/2 (Q4) bytes, scales n/16 bytes (Q8 / Q4 only,
+ * n a multiple of 32; f16 takes any n and no scales). */
 int omg_quantize(int dtype, const float* values, size_t n, uint8_t* codes, uint8_t* scales);
 
 /* QTensor::get over every element (model.rs:508-525). */

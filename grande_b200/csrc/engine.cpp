@@ -410,7 +410,10 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
     ly.w_gu = lin(n("gate_up"));
     ly.w_down = lin(n("down"));
     const int attn_w = c.heads * ly.hd;
-    plan(&ly.qkv, h16_.p, d, ly.w_qkv, ly.qkv_w, ly.qkv_w, d, kEpiF32, "qkv", l);
+    // 256-dim heads: q/k norm, RoPE and the K/V-cache write ride in the
+    // projection's epilogue (one 256-column tile per head).
+    plan(&ly.qkv, h16_.p, d, ly.w_qkv, ly.qkv_w, ly.qkv_w, d,
+         ly.hd == 256 ? kEpiQkPrep : kEpiF32, "qkv", l);
     plan(&ly.o, attn16_.p, attn_w, ly.w_o, d, d, attn_w, kEpiF32, "o", l);
     plan(&ly.gate_up, h16_.p, d, ly.w_gu, (ly.ff + 127) / 128 * 256, ly.ff, d, kEpiGeGluTanh,
          "gate_up", l);
@@ -423,6 +426,14 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
   }
   if (P > 0) plan(&pl_model_proj_, x16_.p, d, lin("pl_model_proj"), P * L, P * L, d, kEpiF32,
                   "pl_model_proj", -1);
+  // RoPE rotations of every cache position for the two thetas (the fused
+  // QKV epilogue's table).
+  for (int w = 0; w < 2; ++w) {
+    rope_tab_[w].alloc(cap_rows_ * 128 * sizeof(float2), false);
+    launch_rope_table(w == 0 ? c.theta_local : c.theta_global, 128, static_cast<int>(cap_rows_),
+                      rope_tab_[w].as<float2>(), stream_);
+  }
+  CUDA_TRY(cudaGetLastError());
   CUDA_TRY(cudaStreamSynchronize(stream_));
 }
 
@@ -696,34 +707,58 @@ int Engine::launch_forward(const Packing& p, Want want) {
   for (int li = 0; li < L; ++li) {
     const Layer& ly = layers_[li];
     const bool last = li + 1 == L;
-    // QKV projection.
-    k("gemm_qkv");
-    gemm_run(ly.qkv, t, qkv_.p, ly.qkv_w, slab_qkv, status, stream_);
-    // q/k norm + RoPE, K/V into the cache.
-    QkArgs qa{};
-    qa.qkv = qkv_.as<float>();
-    qa.q_stride = ly.qkv_w;
-    qa.splits = ly.qkv.s.splits;
-    qa.split_stride = slab_qkv;
-    qa.t = t;
-    qa.heads = c.heads;
-    qa.kv_heads = c.kv_heads;
-    qa.hd = ly.hd;
-    qa.has_kv = ly.has_kv;
-    qa.v_norm = c.v_norm;
-    qa.rope_dims = c.rope_dims[li];
-    qa.theta = ly.sliding ? c.theta_local : c.theta_global;
-    qa.q_scale = c.query_scale;
-    qa.eps = c.eps;
-    qa.offset = c.norm_offset;
-    qa.qn = ly.q_norm;
-    qa.kn = ly.k_norm;
-    qa.meta = meta_.as<TokMeta>();
-    qa.base = static_cast<int>(p.base);
-    qa.q16 = q16_.as<__half>();
-    qa.kv = ly.has_kv ? kv_[li].as<__half>() : nullptr;
-    k("qk_prep");
-    launch_qk_prep(qa, stream_);
+    if (ly.qkv.s.epi == kEpiQkPrep) {
+      // QKV projection with q/k norm + RoPE, K/V into the cache, in one launch.
+      GemmEpi e{};
+      QkEpi& q = e.qk;
+      q.q16 = q16_.as<__half>();
+      q.kv = ly.has_kv ? kv_[li].as<__half>() : nullptr;
+      q.meta = meta_.as<TokMeta>();
+      q.qn = ly.q_norm;
+      q.kn = ly.k_norm;
+      q.rope = rope_tab_[ly.sliding ? 0 : 1].as<float2>();
+      q.rope_stride = static_cast<int>(cap_rows_);
+      q.base = static_cast<int>(p.base);
+      q.heads = c.heads;
+      q.kv_heads = c.kv_heads;
+      q.rope_dims = c.rope_dims[li];
+      q.v_norm = c.v_norm;
+      q.has_kv = ly.has_kv;
+      q.q_scale = c.query_scale;
+      q.eps = c.eps;
+      q.offset = c.norm_offset;
+      k("gemm_qkv");
+      gemm_run_epi(ly.qkv, t, nullptr, 0, e, status, stream_);
+    } else {
+      // Other head sizes: the projection's f32 output, then qk_prep.
+      k("gemm_qkv");
+      gemm_run(ly.qkv, t, qkv_.p, ly.qkv_w, slab_qkv, status, stream_);
+      // q/k norm + RoPE, K/V into the cache.
+      QkArgs qa{};
+      qa.qkv = qkv_.as<float>();
+      qa.q_stride = ly.qkv_w;
+      qa.splits = ly.qkv.s.splits;
+      qa.split_stride = slab_qkv;
+      qa.t = t;
+      qa.heads = c.heads;
+      qa.kv_heads = c.kv_heads;
+      qa.hd = ly.hd;
+      qa.has_kv = ly.has_kv;
+      qa.v_norm = c.v_norm;
+      qa.rope_dims = c.rope_dims[li];
+      qa.theta = ly.sliding ? c.theta_local : c.theta_global;
+      qa.q_scale = c.query_scale;
+      qa.eps = c.eps;
+      qa.offset = c.norm_offset;
+      qa.qn = ly.q_norm;
+      qa.kn = ly.k_norm;
+      qa.meta = meta_.as<TokMeta>();
+      qa.base = static_cast<int>(p.base);
+      qa.q16 = q16_.as<__half>();
+      qa.kv = ly.has_kv ? kv_[li].as<__half>() : nullptr;
+      k("qk_prep");
+      launch_qk_prep(qa, stream_);
+    }
     // Block-causal attention over the cache.
     if (ly.hd == 256) {
       const int w = ly.sliding ? 0 : 1;

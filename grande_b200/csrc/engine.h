@@ -278,6 +278,7 @@ class Engine {
   std::vector<DevBuffer> kv_;  // per layer that owns K/V: [cap_rows, 2 * kv_heads * hd] f16
   size_t cap_rows_ = 0;
   PinnedBuffer h_ids_, h_meta_, h_row_map_, h_out_, h_status_;
+  DevBuffer rope_tab_[2];  // [cap_rows][128] (cos, sin): local theta, global theta
   GemmPlan pl_model_proj_;
   DevBuffer w_pl_model_proj_;
 

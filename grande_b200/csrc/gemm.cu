@@ -243,8 +243,11 @@ __global__ void __launch_bounds__(192, 1)
       } else if constexpr (EPI == kEpiRopeF16) {
         // 64-dim heads: columns c and c + 32 of a head form a rotation pair.
         __half* obase = static_cast<__half*>(g.out) + static_cast<size_t>(row) * g.ldo;
+        // Table [pair][position]: the rows of a tile are mostly consecutive
+        // positions, so a warp's reads of one pair are contiguous.
         const int p = row < g.m ? g.epi.pos[row] : 0;
-        const float2* rt = g.epi.rope + static_cast<size_t>(p) * 32;
+        const float2* rt = g.epi.rope + p;
+        const size_t rs = static_cast<size_t>(g.epi.rope_stride);
 #pragma unroll 1
         for (int c = 0; c < BN / 32; c += 2) {
           float lo[32], hi[32];
@@ -256,7 +259,7 @@ __global__ void __launch_bounds__(192, 1)
               const float sc = col0 < g.epi.q_cols ? g.epi.q_scale : 1.0f;
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
-                const float2 cs = rt[j];
+                const float2 cs = rt[j * rs];
                 const float a = lo[j], b = hi[j];
                 lo[j] = (a * cs.x - b * cs.y) * sc;
                 hi[j] = (b * cs.x + a * cs.y) * sc;
@@ -321,6 +324,67 @@ __global__ void __launch_bounds__(192, 1)
                   o[j] = bias_first ? (v[j] + b[j]) + o[j] : (o[j] + v[j]) + b[j];
             }
           }
+        }
+      } else if constexpr (EPI == kEpiQkPrep) {
+        // qk_prep.wgsl on the accumulator: this tile is head n_tile of the
+        // row, all 256 of its dims in this thread's TMEM lane.
+        static_assert(BN == 256, "one 256-column tile per head");
+        const QkEpi& q = g.epi.qk;
+        const int h = n_tile;
+        const bool is_q = h < q.heads;
+        const bool is_v = h >= q.heads + q.kv_heads;
+        const bool ok_row = row < g.m;
+        float ss = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          float v[32];
+          tmem_ld32(tbase + c * 32, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) ss = fmaf(v[j], v[j], ss);
+        }
+        const float inv = (is_v && !q.v_norm) ? 1.0f : rsqrtf(ss / 256.0f + q.eps);
+        const int crow = q.base + (ok_row ? row : 0);
+        __half* orow;
+        if (is_q)
+          orow = q.q16 + static_cast<size_t>(ok_row ? row : 0) * q.heads * 256 + h * 256;
+        else
+          orow = q.kv + static_cast<size_t>(crow) * 2 * q.kv_heads * 256 + (h - q.heads) * 256;
+        const float* wn = is_q ? q.qn : q.kn;
+        // Table [pair][position]: consecutive rows read consecutive entries.
+        const float2* rt = q.rope + (ok_row ? q.meta[crow].pos : 0);
+        const size_t rs = static_cast<size_t>(q.rope_stride);
+        const float scale = is_q ? q.q_scale : 1.0f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float a[32], b[32];
+          tmem_ld32(tbase + c * 32, a);
+          tmem_ld32(tbase + (c + 4) * 32, b);
+          if (!ok_row) continue;
+          if (is_v) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              a[j] *= inv;
+              b[j] *= inv;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int dd = c * 32 + j;
+              float y1 = a[j] * inv * (q.offset + wn[dd]);
+              float y2 = b[j] * inv * (q.offset + wn[dd + 128]);
+              if (dd < q.rope_dims / 2) {
+                const float2 cs = rt[dd * rs];
+                const float r1 = y1 * cs.x - y2 * cs.y;
+                const float r2 = y2 * cs.x + y1 * cs.y;
+                y1 = r1;
+                y2 = r2;
+              }
+              a[j] = y1 * scale;
+              b[j] = y2 * scale;
+            }
+          }
+          store_f16x32(orow + c * 32, a, 0, 32);
+          store_f16x32(orow + 128 + c * 32, b, 0, 32);
         }
       } else {
         // GeGLU: accumulator columns 0..127 hold the gate products, 128..255
@@ -435,6 +499,7 @@ void gemm_setup_device() {
   set_smem_attr<256, kEpiBiasReluF16>();
   set_smem_attr<128, kEpiResidF32>();
   set_smem_attr<256, kEpiResidF32>();
+  set_smem_attr<256, kEpiQkPrep>();
 }
 
 void gemm_pick(int n, int k, int num_sms, int* bn, int* splits) {
@@ -469,7 +534,7 @@ bool gemm_plan(GemmPlan* p, const void* a, int a_rows_cap, int lda, const void* 
     snprintf(err, errlen, "gemm: K %d and lda %d must be multiples of 8", k, lda);
     return false;
   }
-  if (epi == kEpiGeGluTanh || epi == kEpiGeGluErf) {
+  if (epi == kEpiGeGluTanh || epi == kEpiGeGluErf || epi == kEpiQkPrep) {
     bn = 256;
     splits = 1;
   }
@@ -572,6 +637,9 @@ void gemm_run_epi(const GemmPlan& p, int m, void* out, int ldo, const GemmEpi& e
       break;
     case kEpiResidF32:
       wide ? launch<256, kEpiResidF32>(p, a, stream) : launch<128, kEpiResidF32>(p, a, stream);
+      break;
+    case kEpiQkPrep:
+      launch<256, kEpiQkPrep>(p, a, stream);
       break;
     default:
       gemm_run(p, m, out, ldo, 0, status, stream);

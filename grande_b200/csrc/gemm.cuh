@@ -7,8 +7,11 @@
 // exact f16 values the reference produces per use).
 #pragma once
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+
+#include "kernels.cuh"
 
 namespace omg {
 
@@ -25,16 +28,36 @@ enum GemmEpilogue : int {
   kEpiBiasReluF16 = 6,  // store f16(max(acc + bias, 0))
   kEpiResidF32 = 7,     // residual update in place: x = (x + acc) + bias, or
                         // (acc + bias) + x with bias_first
+  // Decoder epilogue (GemmEpi::qk):
+  kEpiQkPrep = 8,       // fused [q heads | k heads | v heads] projection with 256-dim heads,
+                        // one 256-column tile per head: qk_prep.wgsl on the accumulator
+};
+
+// Operands of kEpiQkPrep: per row, RMSNorm each q / k head with its norm
+// weights, RoPE the first rope_dims dims, q times q_scale into q16; k and the
+// (optionally RMS-normalised) v heads into the K/V cache at row base + row.
+struct QkEpi {
+  __half* q16 = nullptr;        // [rows][heads * 256]
+  __half* kv = nullptr;         // [cache rows][2 * kv_heads * 256], null without own K/V
+  const TokMeta* meta = nullptr;  // cache-row order
+  const float* qn = nullptr;
+  const float* kn = nullptr;
+  const float2* rope = nullptr;   // [128][rope_stride positions] (cos, sin)
+  int rope_stride = 0;
+  int base = 0, heads = 0, kv_heads = 0, rope_dims = 256, v_norm = 0, has_kv = 0;
+  float q_scale = 1.f, eps = 1e-6f, offset = 0.f;
 };
 
 // Operands of the encoder epilogues.
 struct GemmEpi {
   const float* bias = nullptr;   // per output column, f32
-  const float2* rope = nullptr;  // [position][hd / 2] (cos, sin)
-  const int* pos = nullptr;      // per row: its position (the rope table row)
+  const float2* rope = nullptr;  // [hd / 2][rope_stride positions] (cos, sin)
+  int rope_stride = 0;
+  const int* pos = nullptr;      // per row: its position (the rope table column)
   float q_scale = 1.f;
   int q_cols = 0;                // columns [0, q_cols) are q heads, [q_cols, 2 q_cols) k heads
   int bias_first = 0;
+  QkEpi qk;
 };
 
 struct GemmShape {
@@ -67,8 +90,8 @@ bool gemm_plan(GemmPlan* p, const void* a, int a_rows_cap, int lda, const void* 
 void gemm_run(const GemmPlan& p, int m, void* out, int ldo, size_t split_stride,
               uint32_t* status, cudaStream_t stream);
 
-// The same for the encoder epilogues (kEpiRopeF16 .. kEpiResidF32; no
-// split-K). kEpiRopeF16 needs 64-dim heads (one 64-column pair of 32-column
+// The same for the epilogues that take GemmEpi operands (kEpiRopeF16 ..
+// kEpiQkPrep; no split-K). kEpiRopeF16 needs 64-dim heads (one 64-column pair of 32-column
 // halves per head).
 void gemm_run_epi(const GemmPlan& p, int m, void* out, int ldo, const GemmEpi& epi,
                   uint32_t* status, cudaStream_t stream);

@@ -469,6 +469,31 @@ void launch_pl_gate(const float* g, const float* pli, int t, int P, int layers, 
                                                                          layer, out16);
 }
 
+namespace {
+
+// The RoPE rotation of qk_prep.wgsl:52-64 for every position < n_pos and
+// pair dd < half: angle = pos * theta^(-dd / half), the same float
+// operations qk_prep_kernel performs per token.
+__global__ void rope_table_kernel(float theta, int half, int n_pos, float2* tab) {
+  const int n = n_pos * half;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int dd = i / n_pos, p = i % n_pos;
+    const float ang =
+        static_cast<float>(p) * powf(theta, -static_cast<float>(dd) / static_cast<float>(half));
+    float sn, cs;
+    sincosf(ang, &sn, &cs);
+    tab[i] = make_float2(cs, sn);
+  }
+}
+
+}  // namespace
+
+void launch_rope_table(float theta, int half, int n_pos, float2* tab, cudaStream_t s) {
+  const int n = n_pos * half;
+  rope_table_kernel<<<std::max(1, std::min(2048, (n + 255) / 256)), 256, 0, s>>>(theta, half,
+                                                                                   n_pos, tab);
+}
+
 void launch_qk_prep(const QkArgs& a, cudaStream_t s) {
   if (a.hd == 512)
     qk_prep_kernel<512><<<a.t, 128, 0, s>>>(a);

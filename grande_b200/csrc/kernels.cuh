@@ -76,6 +76,11 @@ struct QkArgs {
 };
 void launch_qk_prep(const QkArgs& a, cudaStream_t s);
 
+// tab[dd * n_pos + pos] = (cos, sin) of qk_prep's RoPE angle
+// pos * theta^(-dd / half) for pos < n_pos: the table the fused QKV GEMM
+// epilogue (gemm.cuh kEpiQkPrep) reads.
+void launch_rope_table(float theta, int half, int n_pos, float2* tab, cudaStream_t s);
+
 // logits.wgsl + the host softcap (engine.rs:1901-1906): out[r, v] =
 // sum_k rows[r, k] * dequant(embed[v, k]) in f32, then cap * tanh(z / cap).
 void launch_logits(int dtype, const float* rows, int nrows, const void* codes, const void* scales,

@@ -594,6 +594,7 @@ int LayaEngine::launch_forward(const Packing& p) {
     const EncLayer& e = enc_[l];
     GemmEpi rope{};
     rope.rope = e.sliding ? rope_local_.as<float2>() : rope_global_.as<float2>();
+    rope.rope_stride = c.max_len;
     rope.pos = pos;
     rope.q_scale = 1.0f / std::sqrt(static_cast<float>(c.head_dim()));
     rope.q_cols = d;

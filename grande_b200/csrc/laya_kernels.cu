@@ -19,7 +19,7 @@ __global__ void rope_table_kernel(float theta, int hd, int n_pos, float2* tab) {
   const int half = hd / 2;
   const int n = n_pos * half;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const int p = i / half, k = i % half;
+    const int k = i / n_pos, p = i % n_pos;
     // rope_bi.wgsl:28: angle = pos * pow(theta, -f32(2 d) / f32(HD)).
     const float angle = static_cast<float>(p) * powf(theta, -static_cast<float>(2 * k) /
                                                                 static_cast<float>(hd));

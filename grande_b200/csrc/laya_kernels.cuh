@@ -14,7 +14,7 @@
 namespace omg {
 
 // rope_bi.wgsl:28-31 for every position < n_pos and pair i < hd / 2:
-// angle = pos * theta^(-2i / hd), tab[pos * hd / 2 + i] = (cos, sin).
+// angle = pos * theta^(-2i / hd), tab[i * n_pos + pos] = (cos, sin).
 void launch_laya_rope_table(float theta, int hd, int n_pos, float2* tab, cudaStream_t s);
 
 // embed.wgsl (scale 1) then layernorm.wgsl (no bias) with `w`:

@@ -166,8 +166,16 @@ class LayaEngine:
         return ms.value, n.value
 
     def profile_forward(self, seqs: Seq[Sequence], iters: int) -> dict:
+        """Per-kernel device time: {name: (launches, total_ms)} (one run of
+        the passes, so one call with a buffer large enough for the report)."""
         req = _Seqs(seqs)
-        return json.loads(_text(lib().omg_laya_profile_forward, self._h, req.arr, req.n, iters))
+        need = C.c_size_t(0)
+        buf = C.create_string_buffer(16384)
+        check(lib().omg_laya_profile_forward(self._h, req.arr, req.n, iters, buf, 16384,
+                                             C.byref(need)))
+        if need.value > 16384:
+            raise OmgError(f"profile report needs {need.value} bytes")
+        return {k: tuple(v) for k, v in json.loads(buf.value.decode()).items()}
 
     def record_event(self, slot: int):
         check(lib().omg_laya_record_event(self._h, slot))

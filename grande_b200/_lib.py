@@ -99,7 +99,7 @@ PROTOTYPES: dict[str, tuple] = {
     "omg_engine_profile_forward": (C.c_int, [vp, GroupP, sz, C.c_int, C.c_int, C.c_int,
                                              C.c_char_p, sz, szp]),
     "omg_debug_attention": (C.c_int, [C.c_int, u16p, u16p, i32p, C.c_int, C.c_int, C.c_int,
-                                      C.c_int, C.c_int, C.c_int, u16p]),
+                                      C.c_int, C.c_int, C.c_int, C.c_int, u16p]),
     "omg_gemm_splitk_noalloc": (C.c_int, [C.c_int, vp, C.c_int, C.c_int, C.c_int, vp, C.c_int,
                                           C.c_int, vp, C.c_int, vp]),
     "omg_engine_record_event": (C.c_int, [vp, C.c_int]),

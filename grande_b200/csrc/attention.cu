@@ -348,7 +348,7 @@ __global__ void __launch_bounds__(AttnCfg<HD>::THREADS, 1) attention_kernel(Attn
 }  // namespace
 
 void attention_setup_device() {
-  attention_tc_setup_device();
+  attention_flash_setup_device();
   cudaFuncSetAttribute(attention_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        AttnCfg<256>::SMEM);
   cudaFuncSetAttribute(attention_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize,

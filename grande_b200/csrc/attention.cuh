@@ -44,39 +44,29 @@ void launch_attention(const AttnArgs& a, cudaStream_t s);
 
 // ---- head_dim 256: tensor-core (tcgen05) kernel -----------------------------
 //
-// A work item is one run of query tokens of one request group (up to
-// 128 / heads-per-KV-head tokens, so 128 query rows: the tokens x the query
-// heads sharing one KV head) against one 128-key tile of that group's cache
-// rows. Tiles sit on a grid anchored at the group's first cache row, so a
-// token meets its keys in the same tiles whatever else shares the pass. A run
-// whose keys span one tile writes its output directly; otherwise each item
-// writes an unnormalised partial (sum p.v, max, sum p) and
-// launch_attention_tc merges a row's partials in tile order.
+// A run is up to 128 / (heads per KV head) consecutive query tokens of one
+// request group: 128 query rows (the tokens x the query heads sharing one KV
+// head). One CTA per (run, KV head) visits, with an online softmax, every
+// 64-key tile that any of its rows sees; tiles sit on a grid anchored at the
+// group's first cache row, so a token meets its keys in the same tiles
+// whatever else shares the pass.
 
-constexpr int kAttnTileRows = 128;  // query rows per item
-constexpr int kAttnTileKeys = 128;  // keys per item
+constexpr int kAttnTileRows = 128;  // query rows per run
+constexpr int kAttnTileKeys = 64;   // keys per tile
 
-struct AttnItem {
-  int tok0, ntok;  // workspace tokens of the run
-  int key0;        // first cache row of the key tile
-  int slot;        // partial slot, or -1: the run's only item writes the output
+struct AttnFlashRun {
+  int tok0, ntok;       // workspace tokens of the run
+  int tile0, ntiles;    // its key tiles: tiles[tile0 .. tile0 + ntiles)
 };
 
-struct AttnRun {
-  int tok0, ntok;      // workspace tokens
-  int slot0, nslots;   // its items' partial slots (consecutive, in tile order)
-};
-
-struct AttnTcArgs {
-  const int4* vis;         // per workspace token: visible cache rows [x, y) U [z, w), no window
-  const TokMeta* meta;     // cache-row order
-  const AttnItem* items;
-  const AttnRun* runs;     // runs with more than one item
-  int n_items, n_runs;
-  float* part_o;           // [slot][kv_heads][128 rows][256] f32
-  float2* part_ml;         // [slot][kv_heads][128 rows] (max, sum)
-  __half* out;             // [t, heads * 256] f16
-  uint32_t* status;        // device status word (bounded waits)
+struct AttnFlashArgs {
+  const int4* vis;       // per workspace token: visible cache rows [x, y) U [z, w), no window
+  const TokMeta* meta;   // cache-row order
+  const AttnFlashRun* runs;
+  const int* tiles;      // first cache row of each key tile
+  int n_runs;
+  __half* out;           // [t, heads * 256] f16
+  uint32_t* status;      // device status word (bounded waits)
   int t, base, heads, kv_heads, hpg, window;
 };
 
@@ -92,25 +82,24 @@ void attention_intervals(const TokMeta* meta_ws, int t, int base, std::vector<in
 bool attention_check_intervals(const TokMeta* meta_all, int t, int base, const int4* vis,
                                int window);
 
-// Items and multi-item runs of a pass for one window (0 = global). Returns
-// the number of partial slots used.
-int attention_items(const TokMeta* meta_ws, const int4* vis, int t, int base, int hpg, int window,
-                    std::vector<AttnItem>* items, std::vector<AttnRun>* runs);
+// Runs of a pass and their key tiles for one window (0 = global).
+void attention_flash_runs(const TokMeta* meta_ws, const int4* vis, int t, int hpg, int window,
+                          std::vector<AttnFlashRun>* runs, std::vector<int>* tiles);
 
 // Tensor maps of the tensor-core kernel: q16 [t_cap][heads * 256] f16 and one
-// layer's K/V cache [rows_cap][2 * kv_heads * 256] f16.
-bool attention_tc_map_q(CUtensorMap* m, const void* q16, int t_cap, int heads, int kv_heads,
-                        char* err, size_t errlen);
-bool attention_tc_map_kv(CUtensorMap* m, const void* kv, int rows_cap, int kv_heads, char* err,
-                         size_t errlen);
+// layer's K/V cache [rows_cap][2 * kv_heads * 256] f16 (64-key boxes).
+bool attention_map_q(CUtensorMap* m, const void* q16, int t_cap, int heads, int kv_heads,
+                     char* err, size_t errlen);
+bool attention_map_kv(CUtensorMap* m, const void* kv, int rows_cap, int kv_heads, char* err,
+                      size_t errlen);
 
-// The items, then (when any run has several) the merge of their partials.
-// Returns the number of kernel launches.
-int launch_attention_tc(const CUtensorMap& tq, const CUtensorMap& tkv, const AttnTcArgs& a,
-                        cudaStream_t s);
+// `p_lo`: also feed what f16 rounding dropped from P (a second P.V product),
+// so P carries ~22 bits instead of f16's 11.
+void launch_attention_flash(const CUtensorMap& tq, const CUtensorMap& tkv,
+                            const AttnFlashArgs& a, bool p_lo, cudaStream_t s);
 
 // Dynamic shared memory the attention kernels need (set once per device).
 void attention_setup_device();
-void attention_tc_setup_device();
+void attention_flash_setup_device();
 
 }  // namespace omg

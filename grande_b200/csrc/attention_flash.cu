@@ -1,0 +1,470 @@
+// Block-causal GQA attention on the 5th-generation tensor cores, head_dim 256
+// (see attention.cuh). Replaces crates/omg-wgpu/src/shaders/attention.wgsl
+// for the decoder's head_dim-256 layers.
+//
+// One CTA = one run (up to 128 query rows: a run's tokens x the query heads of
+// one KV head) against every 64-key tile any of its rows sees, with an online
+// softmax; the output accumulates in tensor memory.
+//
+//   warp 0     TMA: Q (4 x [128 rows][64 dims]) once; K and V tiles
+//              (4 x [64 keys][64 dims] each) into two alternating buffers
+//   warp 1     MMA: S_j = Q K_j^T (M 128, N 64, K 256) into one of two TMEM
+//              score buffers, issued one tile ahead; O += P_j V_j (M 128,
+//              N 256, K 64 keys, V read MN-major as stored)
+//   warps 2-5  one query row per thread (its TMEM lane): mask, tile max,
+//              exp, row sum, P as f16 into shared memory; rescale O in TMEM
+//              when the row's reference max moves; finally out = O / l.
+//
+// Numerics follow attention.wgsl: Q, K, V f16; scores, max, exp and the row
+// sum f32. A row keeps a reference max m and only moves it (rescaling O and
+// l) when a tile's max exceeds it by more than kTau, so P = exp(s - m) stays
+// below e^kTau (well inside f16) and most tiles need no rescale; the ratio
+// O / l is the same softmax. Keys no row of the tile sees contribute exact
+// zeros, so a row's result depends only on its own visible keys and the
+// key grid anchored at its group's first row: a group's rows are the same
+// bits wherever it sits in the pass, and whether its prefix is resident.
+#include <algorithm>
+#include <climits>
+#include <cstdio>
+
+#include "attention.cuh"
+#include "gemm.cuh"
+#include "ptx.cuh"
+
+namespace omg {
+
+namespace {
+
+constexpr int FA_HD = 256;
+constexpr int FA_KEYS = kAttnTileKeys;                  // 64 keys per tile
+constexpr int FA_QCH = 128 * 128;                       // [128 rows][128 bytes]
+constexpr int FA_KVCH = FA_KEYS * 128;                  // [64 keys][128 bytes]
+constexpr int FA_Q_BYTES = 4 * FA_QCH;                  // 128 rows x 256 dims
+constexpr int FA_KV_BYTES = 4 * FA_KVCH;                // 64 keys x 256 dims
+constexpr int FA_P_BYTES = 128 * FA_KEYS * 2;           // [128 rows][64 keys] f16
+constexpr uint32_t FA_TMEM_COLS = 512;
+constexpr uint32_t FA_TMEM_O = 256;                     // O [128 x 256]; S buffers at 0, 64
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kTau = 8.0f;                            // reference-max slack (natural log)
+
+template <bool PLO>
+constexpr int fa_smem() {
+  return 1024 + FA_Q_BYTES + 4 * FA_KV_BYTES + (PLO ? 2 : 1) * FA_P_BYTES + 256;
+}
+
+enum {
+  B_Q = 0, B_K0, B_K1, B_V0, B_V1, B_S0, B_S1, B_P, B_O, B_KF0, B_KF1, B_VF0, B_VF1, B_N
+};
+
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          uint32_t* status, int lane) {
+  int ok = 0;
+  if (lane == 0) ok = mbar_wait(bar, parity, abort_flag, status) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+template <bool PLO>
+__global__ void __launch_bounds__(192, 1)
+    attention_flash_kernel(const __grid_constant__ CUtensorMap tq,
+                           const __grid_constant__ CUtensorMap tkv, AttnFlashArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* qs = sm;
+  auto ks = [&](int b) { return qs + FA_Q_BYTES + b * FA_KV_BYTES; };        // K buffer b
+  auto vs = [&](int b) { return qs + FA_Q_BYTES + (2 + b) * FA_KV_BYTES; };  // V buffer b
+  uint8_t* ps = qs + FA_Q_BYTES + 4 * FA_KV_BYTES;  // P hi, then (PLO) P lo
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ps + (PLO ? 2 : 1) * FA_P_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B_N);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const AttnFlashRun run = g.runs[blockIdx.x];
+  const int kvh = blockIdx.y;
+  const int tok_per_tile = kAttnTileRows / g.hpg;
+  const int* tiles = g.tiles + run.tile0;
+  const int nt = run.ntiles;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < B_N; ++i) mbar_init(&bars[i], i == B_P ? 4 : 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tq);
+    prefetch_tmap(&tkv);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, FA_TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  griddep_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t qbytes = 4u * 64u * 2u * static_cast<uint32_t>(g.hpg * tok_per_tile);
+      mbar_arrive_expect_tx(&bars[B_Q], qbytes);
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        tma_load_4d(qs + c * FA_QCH, &tq, &bars[B_Q], c * 64, 0, kvh, run.tok0);
+      for (int j = 0; j < nt; ++j) {
+        const int b = j & 1, u = j >> 1;
+        if (u > 0 && !mbar_wait(&bars[B_KF0 + b], (u - 1) & 1, abort_flag, g.status)) break;
+        mbar_arrive_expect_tx(&bars[B_K0 + b], FA_KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          tma_load_2d(ks(b) + c * FA_KVCH, &tkv, &bars[B_K0 + b], kvh * FA_HD + c * 64, tiles[j]);
+        if (u > 0 && !mbar_wait(&bars[B_VF0 + b], (u - 1) & 1, abort_flag, g.status)) break;
+        mbar_arrive_expect_tx(&bars[B_V0 + b], FA_KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          tma_load_2d(vs(b) + c * FA_KVCH, &tkv, &bars[B_V0 + b],
+                      (g.kv_heads + kvh) * FA_HD + c * 64, tiles[j]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_f16_f32(128, FA_KEYS);
+      constexpr uint32_t idesc_o = idesc_f16_f32_bmn(128, FA_HD);
+      // S_j = Q K_j^T into score buffer j & 1.
+      auto issue_s = [&](int j) -> bool {
+        const int b = j & 1;
+        if (!mbar_wait(&bars[B_K0 + b], (j >> 1) & 1, abort_flag, g.status)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint64_t da = sw128_desc(qs + c * FA_QCH);
+          const uint64_t db = sw128_desc(ks(b) + c * FA_KVCH);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_f16(tmem + b * FA_KEYS, da + 2 * k, db + 2 * k, idesc_s, (c | k) ? 1u : 0u);
+        }
+        umma_commit(&bars[B_S0 + b]);
+        umma_commit(&bars[B_KF0 + b]);
+        return true;
+      };
+      bool ok = mbar_wait(&bars[B_Q], 0, abort_flag, g.status) && issue_s(0);
+      for (int j = 0; ok && j < nt; ++j) {
+        const int b = j & 1;
+        // S_{j+1} one tile ahead, so the softmax of tile j + 1 overlaps
+        // P_j V_j. Its score buffer held S_{j-1}, which the softmax warps
+        // finished with before P_{j-1} (waited for last iteration).
+        if (j + 1 < nt && !issue_s(j + 1)) break;
+        if (!mbar_wait(&bars[B_P], j & 1, abort_flag, g.status) ||
+            !mbar_wait(&bars[B_V0 + b], (j >> 1) & 1, abort_flag, g.status))
+          break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < FA_KEYS / 16; ++kk) {
+          const uint64_t pa = sw128_desc(ps) + 2 * kk;
+          const uint64_t vb = sw128_mn_desc(vs(b) + kk * 2048, FA_KVCH);
+          umma_f16(tmem + FA_TMEM_O, pa, vb, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        if constexpr (PLO) {
+#pragma unroll
+          for (int kk = 0; kk < FA_KEYS / 16; ++kk) {
+            const uint64_t pa = sw128_desc(ps + FA_P_BYTES) + 2 * kk;
+            const uint64_t vb = sw128_mn_desc(vs(b) + kk * 2048, FA_KVCH);
+            umma_f16(tmem + FA_TMEM_O, pa, vb, idesc_o, 1u);
+          }
+        }
+        umma_commit(&bars[B_O]);
+        umma_commit(&bars[B_VF0 + b]);
+      }
+    }
+  } else {
+    // One query row per thread: TMEM lane r.
+    const int q4 = warp & 3;
+    const int r = 32 * q4 + lane;
+    const int tl = r / g.hpg;
+    const bool valid = tl < run.ntok && tl < tok_per_tile;
+    const int tok = run.tok0 + tl;
+    // This row's visible cache rows: [a0, a1) U [b0, b1).
+    int a0 = 0, a1 = 0, b0 = 0, b1 = 0;
+    if (valid) {
+      const int4 v = g.vis[tok];
+      const int qp = g.meta[g.base + tok].pos;
+      a0 = v.x;
+      a1 = v.y;
+      b0 = v.z;
+      b1 = v.w;
+      if (g.window > 0) {
+        a0 = max(a0, v.x + qp - g.window + 1);
+        b0 = max(b0, v.w - g.window);
+      }
+    }
+    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q4) << 16);
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      const int key0 = tiles[j];
+      int ca0 = min(max(a0 - key0, 0), FA_KEYS), ca1 = min(max(a1 - key0, 0), FA_KEYS);
+      int cb0 = min(max(b0 - key0, 0), FA_KEYS), cb1 = min(max(b1 - key0, 0), FA_KEYS);
+      if (ca1 < ca0) ca1 = ca0;
+      if (cb1 < cb0) cb1 = cb0;
+      if (!warp_wait(&bars[B_S0 + (j & 1)], (j >> 1) & 1, abort_flag, g.status, lane)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[FA_KEYS];
+      {
+        uint32_t raw0[32], raw1[32];
+        tmem_ld32_nowait(trow + (j & 1) * FA_KEYS, raw0);
+        tmem_ld32_nowait(trow + (j & 1) * FA_KEYS + 32, raw1);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          s[c] = __uint_as_float(raw0[c]);
+          s[32 + c] = __uint_as_float(raw1[c]);
+        }
+      }
+      // A tile is usually wholly visible or wholly hidden for a row; mask
+      // element by element only in between. Eight independent partial
+      // maxima and sums keep the one warp per sub-partition issuing.
+      const bool full = (ca0 == 0 && ca1 == FA_KEYS) || (cb0 == 0 && cb1 == FA_KEYS);
+      const bool none = ca0 == ca1 && cb0 == cb1;
+      if (!full && !none) {
+#pragma unroll
+        for (int c = 0; c < FA_KEYS; ++c) {
+          const bool vis = (c >= ca0 && c < ca1) || (c >= cb0 && c < cb1);
+          s[c] = vis ? s[c] : -INFINITY;
+        }
+      }
+      float mt = -INFINITY;
+      if (!none) {
+        float mx[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mx[e] = s[e];
+#pragma unroll
+        for (int c = 8; c < FA_KEYS; ++c) mx[c & 7] = fmaxf(mx[c & 7], s[c]);
+        mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                   fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      }
+      float alpha = 1.f;
+      bool rescale = false;
+      if (mt > m_ref + kTau) {
+        // O holds earlier tiles only when the old reference was finite.
+        rescale = m_ref != -INFINITY;
+        alpha = rescale ? exp2f((m_ref - mt) * kLog2e) : 0.f;
+        m_ref = mt;
+      }
+      float sum = 0.f;
+      if (none || m_ref == -INFINITY) {
+#pragma unroll
+        for (int c = 0; c < FA_KEYS; ++c) s[c] = 0.f;
+      } else {
+        // exp2(-inf) = 0 for the masked keys.
+        const float mb = m_ref * kLog2e;
+        float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < FA_KEYS; ++c) {
+          s[c] = exp2f(fmaf(s[c], kLog2e, -mb));
+          ps[c & 7] += s[c];
+        }
+        sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      }
+      l = l * alpha + sum;
+      // The previous P.V is done: its P buffer is free and O is stable.
+      if (j > 0) {
+        if (!warp_wait(&bars[B_O], (j - 1) & 1, abort_flag, g.status, lane)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      if (__any_sync(0xffffffffu, rescale)) {
+        const float f = rescale ? alpha : 1.0f;
+#pragma unroll 1
+        for (int c = 0; c < FA_HD / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32_nowait(trow + FA_TMEM_O + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+          tmem_st32(trow + FA_TMEM_O + c * 32, o);
+        }
+        tmem_st_wait();
+      }
+      // P (and, with PLO, what f16 missed of it) K-major with the 128-byte
+      // swizzle: 16-byte piece pw holds keys 8 pw .. 8 pw + 7.
+#pragma unroll
+      for (int pw = 0; pw < FA_KEYS / 8; ++pw) {
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float x = s[pw * 8 + 2 * e], y = s[pw * 8 + 2 * e + 1];
+          const __half2 h = __floats2half2_rn(x, y);
+          hi[e] = *reinterpret_cast<const uint32_t*>(&h);
+          if constexpr (PLO) {
+            const float2 hf = __half22float2(h);
+            const __half2 d = __floats2half2_rn(x - hf.x, y - hf.y);
+            lo[e] = *reinterpret_cast<const uint32_t*>(&d);
+          }
+        }
+        const uint32_t off = r * 128 + ((pw ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(ps + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        if constexpr (PLO)
+          *reinterpret_cast<uint4*>(ps + FA_P_BYTES + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[B_P]);
+    }
+    if (ok && warp_wait(&bars[B_O], (nt - 1) & 1, abort_flag, g.status, lane)) {
+      tc_fence_after();
+      const int head = kvh * g.hpg + (r % g.hpg);
+      __half* orow = g.out + (static_cast<size_t>(tok) * g.heads + head) * FA_HD;
+      const float inv = l > 0.f ? 1.0f / l : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < FA_HD / 32; ++c) {
+        float o[32];
+        tmem_ld32(trow + FA_TMEM_O + c * 32, o);
+        if (!valid) continue;
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const __half2 h = __floats2half2_rn(o[e + 2 * q] * inv, o[e + 2 * q + 1] * inv);
+            w4[q] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          *reinterpret_cast<uint4*>(orow + c * 32 + e) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+      }
+    }
+  }
+  griddep_launch();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, FA_TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+void attention_intervals(const TokMeta* m, int t, int base, std::vector<int4>* vis) {
+  vis->resize(static_cast<size_t>(t));
+  for (int i = 0; i < t; ++i) {
+    const int row = base + i;
+    if ((m[i].seq & 0xfff) == 0) {
+      (*vis)[i] = make_int4(m[i].row_lo, row + 1, row + 1, row + 1);
+      continue;
+    }
+    // The branch's first token: scan back while the sequence id holds (a
+    // branch's tokens are contiguous and all in this pass). Its position
+    // is the group's prefix length.
+    int j = i;
+    while (j > 0 && m[j - 1].seq == m[i].seq) --j;
+    const int prefix_len = m[j].pos;
+    (*vis)[i] = make_int4(m[i].row_lo, m[i].row_lo + prefix_len, base + j, row + 1);
+  }
+}
+
+bool attention_check_intervals(const TokMeta* meta_all, int t, int base, const int4* vis,
+                               int window) {
+  for (int i = 0; i < t; ++i) {
+    const TokMeta q = meta_all[base + i];
+    const int4 v = vis[i];
+    int a0 = v.x, b0 = v.z;
+    if (window > 0) {
+      a0 = std::max(a0, v.x + q.pos - window + 1);
+      b0 = std::max(b0, v.w - window);
+    }
+    for (int k = 0; k < base + t; ++k) {
+      const TokMeta kk = meta_all[k];
+      const bool want = attn_visible(q.pos, q.seq, kk.pos, kk.seq, window);
+      const bool got = (k >= a0 && k < v.y) || (k >= b0 && k < v.w);
+      if (want != got) return false;
+    }
+  }
+  return true;
+}
+
+void attention_flash_runs(const TokMeta* m, const int4* vis, int t, int hpg, int window,
+                          std::vector<AttnFlashRun>* runs, std::vector<int>* tiles) {
+  runs->clear();
+  tiles->clear();
+  const int tok_per_tile = kAttnTileRows / hpg;
+  std::vector<int2> ivs;
+  for (int i = 0; i < t;) {
+    int n = 1;
+    while (i + n < t && n < tok_per_tile && m[i + n].row_lo == m[i].row_lo) ++n;
+    const int row_lo = m[i].row_lo;
+    ivs.clear();
+    int lo = INT_MAX, hi = INT_MIN;
+    for (int k = 0; k < n; ++k) {
+      const int4 v = vis[i + k];
+      int a0 = v.x, b0 = v.z;
+      if (window > 0) {
+        a0 = std::max(a0, v.x + m[i + k].pos - window + 1);
+        b0 = std::max(b0, v.w - window);
+      }
+      if (a0 < v.y) ivs.push_back(make_int2(a0, v.y));
+      if (b0 < v.w) ivs.push_back(make_int2(b0, v.w));
+    }
+    for (const int2& iv : ivs) {
+      lo = std::min(lo, iv.x);
+      hi = std::max(hi, iv.y);
+    }
+    const int first = static_cast<int>(tiles->size());
+    if (lo < hi) {
+      // 64-key tiles on the grid anchored at the group's first row; tiles no
+      // row of the run sees are skipped.
+      for (int j = (lo - row_lo) / kAttnTileKeys; row_lo + j * kAttnTileKeys < hi; ++j) {
+        const int k0 = row_lo + j * kAttnTileKeys, k1 = k0 + kAttnTileKeys;
+        bool any = false;
+        for (const int2& iv : ivs) any |= iv.x < k1 && iv.y > k0;
+        if (any) tiles->push_back(k0);
+      }
+    }
+    runs->push_back(AttnFlashRun{i, n, first, static_cast<int>(tiles->size()) - first});
+    i += n;
+  }
+}
+
+bool attention_map_q(CUtensorMap* mp, const void* q16, int t_cap, int heads, int kv_heads,
+                     char* err, size_t errlen) {
+  const int hpg = heads / kv_heads;
+  if (hpg < 1 || hpg > kAttnTileRows || heads % kv_heads != 0) {
+    snprintf(err, errlen, "attention: %d query heads over %d KV heads", heads, kv_heads);
+    return false;
+  }
+  const uint64_t dims[4] = {static_cast<uint64_t>(FA_HD), static_cast<uint64_t>(hpg),
+                            static_cast<uint64_t>(kv_heads), static_cast<uint64_t>(t_cap)};
+  const uint64_t strides[3] = {FA_HD * 2ull, static_cast<uint64_t>(hpg) * FA_HD * 2,
+                               static_cast<uint64_t>(heads) * FA_HD * 2};
+  const uint32_t box[4] = {64, static_cast<uint32_t>(hpg), 1,
+                           static_cast<uint32_t>(kAttnTileRows / hpg)};
+  return make_tmap_f16(mp, q16, 4, dims, strides, box, err, errlen);
+}
+
+bool attention_map_kv(CUtensorMap* mp, const void* kv, int rows_cap, int kv_heads, char* err,
+                      size_t errlen) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(2 * kv_heads * FA_HD),
+                            static_cast<uint64_t>(rows_cap)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(2 * kv_heads * FA_HD) * 2};
+  const uint32_t box[2] = {64, static_cast<uint32_t>(FA_KEYS)};
+  return make_tmap_f16(mp, kv, 2, dims, strides, box, err, errlen);
+}
+
+void attention_flash_setup_device() {
+  cudaFuncSetAttribute(attention_flash_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       fa_smem<true>());
+  cudaFuncSetAttribute(attention_flash_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       fa_smem<false>());
+}
+
+void launch_attention_flash(const CUtensorMap& tq, const CUtensorMap& tkv,
+                            const AttnFlashArgs& a, bool p_lo, cudaStream_t s) {
+  if (a.n_runs <= 0) return;
+  dim3 grid(a.n_runs, a.kv_heads);
+  if (p_lo)
+    attention_flash_kernel<true><<<grid, 192, fa_smem<true>(), s>>>(tq, tkv, a);
+  else
+    attention_flash_kernel<false><<<grid, 192, fa_smem<false>(), s>>>(tq, tkv, a);
+}
+
+}  // namespace omg

@@ -82,7 +82,7 @@ extern "C" int omg_debug_gemm(int device, const uint16_t* x_f16, int m, int k, i
 // (pos, seq, row_lo, row_hi), out [t, heads * hd] f16.
 extern "C" int omg_debug_attention(int device, const uint16_t* q, const uint16_t* kv,
                                    const int32_t* meta, int t, int base, int heads, int kv_heads,
-                                   int hd, int window, uint16_t* out) {
+                                   int hd, int window, int p_lo, uint16_t* out) {
   return guarded([&]() -> int {
     CUDA_TRY(cudaSetDevice(device));
     omg::attention_setup_device();
@@ -107,36 +107,30 @@ extern "C" int omg_debug_attention(int device, const uint16_t* q, const uint16_t
       omg::attention_intervals(hm + base, t, base, &vis);
       if (!omg::attention_check_intervals(hm, t, base, vis.data(), window))
         return set_error("attention: the packing's visibility is not two intervals per token");
-      std::vector<omg::AttnItem> items;
-      std::vector<omg::AttnRun> runs;
-      const int slots =
-          omg::attention_items(hm + base, vis.data(), t, base, heads / kv_heads, window, &items, &runs);
-      DevBuf dv, di, dr, dpo, dpm, dst;
-      const size_t prow = static_cast<size_t>(std::max(slots, 1)) * kv_heads * omg::kAttnTileRows;
-      if (!dv.alloc(vis.size() * sizeof(int4)) || !di.alloc(items.size() * sizeof(omg::AttnItem)) ||
-          !dr.alloc(runs.size() * sizeof(omg::AttnRun)) || !dpo.alloc(prow * 256 * 4) ||
-          !dpm.alloc(prow * 8) || !dst.alloc(4))
+      std::vector<omg::AttnFlashRun> runs;
+      std::vector<int> tiles;
+      omg::attention_flash_runs(hm + base, vis.data(), t, heads / kv_heads, window, &runs, &tiles);
+      DevBuf dv, dr, dti, dst;
+      if (!dv.alloc(vis.size() * sizeof(int4)) ||
+          !dr.alloc(runs.size() * sizeof(omg::AttnFlashRun)) ||
+          !dti.alloc(std::max<size_t>(tiles.size(), 1) * sizeof(int)) || !dst.alloc(4))
         return set_error("cudaMalloc failed");
       CUDA_TRY(cudaMemcpy(dv.p, vis.data(), vis.size() * sizeof(int4), cudaMemcpyHostToDevice));
-      CUDA_TRY(cudaMemcpy(di.p, items.data(), items.size() * sizeof(omg::AttnItem),
+      CUDA_TRY(cudaMemcpy(dr.p, runs.data(), runs.size() * sizeof(omg::AttnFlashRun),
                           cudaMemcpyHostToDevice));
-      CUDA_TRY(cudaMemcpy(dr.p, runs.data(), runs.size() * sizeof(omg::AttnRun),
-                          cudaMemcpyHostToDevice));
+      CUDA_TRY(cudaMemcpy(dti.p, tiles.data(), tiles.size() * sizeof(int), cudaMemcpyHostToDevice));
       CUDA_TRY(cudaMemset(dst.p, 0, 4));
       CUtensorMap tq, tkv;
       char err[256];
-      if (!omg::attention_tc_map_q(&tq, dq.p, t, heads, kv_heads, err, sizeof err) ||
-          !omg::attention_tc_map_kv(&tkv, dkv.p, rows_pad, kv_heads, err, sizeof err))
+      if (!omg::attention_map_q(&tq, dq.p, t, heads, kv_heads, err, sizeof err) ||
+          !omg::attention_map_kv(&tkv, dkv.p, rows_pad, kv_heads, err, sizeof err))
         return set_error("%s", err);
-      omg::AttnTcArgs a{};
+      omg::AttnFlashArgs a{};
       a.vis = static_cast<const int4*>(dv.p);
       a.meta = static_cast<const omg::TokMeta*>(dm.p);
-      a.items = static_cast<const omg::AttnItem*>(di.p);
-      a.runs = static_cast<const omg::AttnRun*>(dr.p);
-      a.n_items = static_cast<int>(items.size());
+      a.runs = static_cast<const omg::AttnFlashRun*>(dr.p);
+      a.tiles = static_cast<const int*>(dti.p);
       a.n_runs = static_cast<int>(runs.size());
-      a.part_o = static_cast<float*>(dpo.p);
-      a.part_ml = static_cast<float2*>(dpm.p);
       a.out = static_cast<__half*>(dout.p);
       a.status = static_cast<uint32_t*>(dst.p);
       a.t = t;
@@ -145,7 +139,7 @@ extern "C" int omg_debug_attention(int device, const uint16_t* q, const uint16_t
       a.kv_heads = kv_heads;
       a.hpg = heads / kv_heads;
       a.window = window;
-      omg::launch_attention_tc(tq, tkv, a, 0);
+      omg::launch_attention_flash(tq, tkv, a, p_lo != 0, 0);
       CUDA_TRY(cudaGetLastError());
       CUDA_TRY(cudaDeviceSynchronize());
       uint32_t st = 0;

@@ -15,6 +15,12 @@
 
 namespace omg {
 
+// The attention's P enters P.V as f16 only (the reference rounds Q, K and V
+// to f16; P's own f16 rounding adds ~2^-12 relative error, below the f16
+// rounding of the attention output that follows). Set to feed P's rounding
+// residue too, for ~22-bit P.
+constexpr bool kAttnPLo = false;
+
 // ---- buffers ----------------------------------------------------------------
 
 void DevBuffer::alloc(size_t n, bool zero) {
@@ -356,13 +362,13 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
   attn_ctas_.alloc(Cpad * sizeof(int2));
   {
     char err[256];
-    if (!attention_tc_map_q(&attn_tq_, q16_.p, static_cast<int>(Cpad), c.heads, c.kv_heads, err,
+    if (!attention_map_q(&attn_tq_, q16_.p, static_cast<int>(Cpad), c.heads, c.kv_heads, err,
                             sizeof err))
       fail("%s", err);
     attn_tkv_.resize(L);
     for (int l = 0; l < L; ++l)
       if (c.has_kv(l) && c.head_dim[l] == 256 &&
-          !attention_tc_map_kv(&attn_tkv_[l], kv_[l].p, static_cast<int>(Cpad), c.kv_heads, err,
+          !attention_map_kv(&attn_tkv_[l], kv_[l].p, static_cast<int>(Cpad), c.kv_heads, err,
                                sizeof err))
         fail("layer %d: %s", l, err);
   }
@@ -592,22 +598,19 @@ Engine::Packing Engine::pack(const GroupIn* groups, size_t n, size_t first,
     const int t = static_cast<int>(p.t), base = static_cast<int>(p.base);
     const int hpg = config.heads / config.kv_heads;
     attention_intervals(p.meta.data(), t, base, &p.attn_vis);
-    p.attn_slots = 0;
     for (int w = 0; w < 2; ++w)
-      p.attn_slots = std::max(
-          p.attn_slots, attention_items(p.meta.data(), p.attn_vis.data(), t, base, hpg,
-                                        w == 0 ? config.window : 0, &p.attn_items[w],
-                                        &p.attn_runs[w]));
+      attention_flash_runs(p.meta.data(), p.attn_vis.data(), t, hpg, w == 0 ? config.window : 0,
+                           &p.attn_runs[w], &p.attn_tiles[w]);
     size_t off = 0;
     auto put = [&](int i, size_t bytes) {
       p.attn_off[i] = off;
       off += (bytes + 255) / 256 * 256;
     };
     put(0, p.attn_vis.size() * sizeof(int4));
-    put(1, p.attn_items[0].size() * sizeof(AttnItem));
-    put(2, p.attn_runs[0].size() * sizeof(AttnRun));
-    put(3, p.attn_items[1].size() * sizeof(AttnItem));
-    put(4, p.attn_runs[1].size() * sizeof(AttnRun));
+    put(1, p.attn_runs[0].size() * sizeof(AttnFlashRun));
+    put(2, p.attn_tiles[0].size() * sizeof(int));
+    put(3, p.attn_runs[1].size() * sizeof(AttnFlashRun));
+    put(4, p.attn_tiles[1].size() * sizeof(int));
     p.attn_bytes = off;
   }
   // out_index[w] = device row of wanted slot w, paired with its flat out row.
@@ -627,30 +630,22 @@ void Engine::upload(const Packing& p, const uint8_t* per_layer_rows, size_t rows
   CUDA_TRY(cudaMemcpyAsync(meta_.as<TokMeta>() + p.base, h_meta_.p, p.t * sizeof(TokMeta),
                            cudaMemcpyHostToDevice, stream_));
   CUDA_TRY(cudaMemcpyAsync(row_map_.p, h_row_map_.p, p.t * 4, cudaMemcpyHostToDevice, stream_));
-  // Tensor-core attention schedule: one staged block; partial buffers grow
-  // to the largest pass seen.
+  // Tensor-core attention schedule: one staged block, grown to the largest
+  // pass seen.
   if (h_attn_sched_.bytes < p.attn_bytes || attn_sched_.bytes < p.attn_bytes) {
     CUDA_TRY(cudaStreamSynchronize(stream_));
     const size_t cap = std::max<size_t>(p.attn_bytes * 2, 1 << 16);
     h_attn_sched_.alloc(cap);
     attn_sched_.alloc(cap, false);
   }
-  if (p.attn_slots > attn_slots_cap_) {
-    CUDA_TRY(cudaStreamSynchronize(stream_));
-    const int slots = std::max(p.attn_slots, 2 * attn_slots_cap_);
-    const size_t rows = static_cast<size_t>(slots) * config.kv_heads * kAttnTileRows;
-    attn_part_o_.alloc(rows * 256 * 4, false);
-    attn_part_ml_.alloc(rows * sizeof(float2), false);
-    attn_slots_cap_ = slots;
-  }
   {
     uint8_t* h = h_attn_sched_.as<uint8_t>();
     std::memcpy(h + p.attn_off[0], p.attn_vis.data(), p.attn_vis.size() * sizeof(int4));
     for (int w = 0; w < 2; ++w) {
-      std::memcpy(h + p.attn_off[1 + 2 * w], p.attn_items[w].data(),
-                  p.attn_items[w].size() * sizeof(AttnItem));
-      std::memcpy(h + p.attn_off[2 + 2 * w], p.attn_runs[w].data(),
-                  p.attn_runs[w].size() * sizeof(AttnRun));
+      std::memcpy(h + p.attn_off[1 + 2 * w], p.attn_runs[w].data(),
+                  p.attn_runs[w].size() * sizeof(AttnFlashRun));
+      std::memcpy(h + p.attn_off[2 + 2 * w], p.attn_tiles[w].data(),
+                  p.attn_tiles[w].size() * sizeof(int));
     }
     CUDA_TRY(cudaMemcpyAsync(attn_sched_.p, h, p.attn_bytes, cudaMemcpyHostToDevice, stream_));
   }
@@ -763,15 +758,12 @@ int Engine::launch_forward(const Packing& p, Want want) {
     if (ly.hd == 256) {
       const int w = ly.sliding ? 0 : 1;
       const uint8_t* sched = attn_sched_.as<uint8_t>();
-      AttnTcArgs ta{};
+      AttnFlashArgs ta{};
       ta.vis = reinterpret_cast<const int4*>(sched + p.attn_off[0]);
       ta.meta = meta_.as<TokMeta>();
-      ta.items = reinterpret_cast<const AttnItem*>(sched + p.attn_off[1 + 2 * w]);
-      ta.runs = reinterpret_cast<const AttnRun*>(sched + p.attn_off[2 + 2 * w]);
-      ta.n_items = static_cast<int>(p.attn_items[w].size());
+      ta.runs = reinterpret_cast<const AttnFlashRun*>(sched + p.attn_off[1 + 2 * w]);
+      ta.tiles = reinterpret_cast<const int*>(sched + p.attn_off[2 + 2 * w]);
       ta.n_runs = static_cast<int>(p.attn_runs[w].size());
-      ta.part_o = attn_part_o_.as<float>();
-      ta.part_ml = attn_part_ml_.as<float2>();
       ta.out = attn16_.as<__half>();
       ta.status = status;
       ta.t = t;
@@ -781,8 +773,7 @@ int Engine::launch_forward(const Packing& p, Want want) {
       ta.hpg = c.heads / c.kv_heads;
       ta.window = ly.sliding ? c.window : 0;
       k("attention");
-      const int n = launch_attention_tc(attn_tq_, attn_tkv_[ly.kv_src], ta, stream_);
-      if (n > 1) ++launches;  // the partial merge, timed under "attention"
+      launch_attention_flash(attn_tq_, attn_tkv_[ly.kv_src], ta, kAttnPLo, stream_);
     } else {
       AttnArgs aa{};
       aa.q = q16_.as<__half>();

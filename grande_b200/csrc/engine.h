@@ -230,9 +230,8 @@ class Engine {
     // then items and multi-item runs for sliding [0] and global [1] layers,
     // staged as one block: vis | items[0] | runs[0] | items[1] | runs[1].
     std::vector<int4> attn_vis;
-    std::vector<AttnItem> attn_items[2];
-    std::vector<AttnRun> attn_runs[2];
-    int attn_slots = 0;
+    std::vector<AttnFlashRun> attn_runs[2];
+    std::vector<int> attn_tiles[2];
     size_t attn_off[5] = {}, attn_bytes = 0;
     size_t t = 0, base = 0, nwanted = 0;
   };
@@ -268,9 +267,8 @@ class Engine {
   int max_qkv_ = 0, max_attn_ = 0, max_ff_ = 0;
 
   // Workspace.
-  DevBuffer attn_ctas_, attn_part_o_, attn_part_ml_, attn_sched_;
+  DevBuffer attn_ctas_, attn_sched_;
   PinnedBuffer h_attn_ctas_, h_attn_sched_;
-  int attn_slots_cap_ = 0;
   CUtensorMap attn_tq_;
   std::vector<CUtensorMap> attn_tkv_;  // per layer owning head_dim-256 K/V
   DevBuffer ids_, meta_, row_map_, x_, x16_, h16_, qkv_, q16_, attn16_, a32_, act16_, rows_,

@@ -296,17 +296,28 @@ __global__ void __launch_bounds__(192, 2)
         break;
       }
       tc_fence_after();
-      // Pass 1: the tile's masked row max.
+      // Pass 1: the tile's masked row max. A 32-key chunk is wholly visible,
+      // wholly hidden or (at the window and sequence edges) split; eight
+      // independent partial maxima keep the warp issuing.
       float mt = -INFINITY;
 #pragma unroll 1
       for (int c = 0; c < kLayaTile / 32; ++c) {
         float s[32];
         tmem_ld32(trow + c * 32, s);
+        const int k0 = c * 32;
+        if (c1 <= k0 || c0 >= k0 + 32) continue;
+        if (c0 > k0 || c1 < k0 + 32) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int col = c * 32 + e;
-          if (col >= c0 && col < c1) mt = fmaxf(mt, s[e]);
+          for (int e = 0; e < 32; ++e)
+            if (k0 + e < c0 || k0 + e >= c1) s[e] = -INFINITY;
         }
+        float mx[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mx[e] = s[e];
+#pragma unroll
+        for (int e = 8; e < 32; ++e) mx[e & 7] = fmaxf(mx[e & 7], s[e]);
+        mt = fmaxf(mt, fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))));
       }
       const float m_new = fmaxf(m, mt);
       const float alpha = m_new == -INFINITY ? 1.f : exp2f((m - m_new) * kLog2e);
@@ -329,17 +340,24 @@ __global__ void __launch_bounds__(192, 2)
       }
       // Pass 2: P = exp(s - m_new) on visible keys, 0 elsewhere, as f16 in
       // the 128-byte-swizzled K-major layout the MMA reads.
-      float sum = 0.f;
+      float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
       for (int c = 0; c < kLayaTile / 32; ++c) {
         float s[32];
         tmem_ld32(trow + c * 32, s);
+        const int k0 = c * 32;
+        if (c1 <= k0 || c0 >= k0 + 32 || m_new == -INFINITY) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int col = c * 32 + e;
-          const float p = (col >= c0 && col < c1) ? exp2f(fmaf(s[e], kLog2e, -mb)) : 0.f;
-          s[e] = p;
-          sum += p;
+          for (int e = 0; e < 32; ++e) s[e] = 0.f;
+        } else {
+          const bool split = c0 > k0 || c1 < k0 + 32;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            float p = exp2f(fmaf(s[e], kLog2e, -mb));
+            if (split && (k0 + e < c0 || k0 + e >= c1)) p = 0.f;
+            s[e] = p;
+            ps8[e & 7] += p;
+          }
         }
 #pragma unroll
         for (int pc = 0; pc < 4; ++pc) {
@@ -355,6 +373,7 @@ __global__ void __launch_bounds__(192, 2)
               make_uint4(w4[0], w4[1], w4[2], w4[3]);
         }
       }
+      const float sum = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       l = l * alpha + sum;
       m = m_new;
       alpha_prev = alpha;

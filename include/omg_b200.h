@@ -261,9 +261,10 @@ int omg_debug_gemm(int device, const uint16_t* x_f16, int m, int k, int lda, con
  * q [t, heads * hd] f16 for cache rows base..base+t, kv [base + t, 2 * kv_heads * hd]
  * f16 (K heads then V heads per row), meta 4 ints per cache row (position,
  * sequence id, first key row of its group, own row + 1; engine.rs:1519-1571),
- * window 0 = global. Writes out [t, heads * hd] f16. */
+ * window 0 = global. p_lo (head_dim 256): also feed P's f16 rounding residue
+ * into P.V. Writes out [t, heads * hd] f16. */
 int omg_debug_attention(int device, const uint16_t* q, const uint16_t* kv, const int32_t* meta,
-                        int t, int base, int heads, int kv_heads, int hd, int window,
+                        int t, int base, int heads, int kv_heads, int hd, int window, int p_lo,
                         uint16_t* out);
 
 /* Kernel timing for tile sweeps (no reference counterpart; the reference

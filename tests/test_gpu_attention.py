@@ -15,11 +15,12 @@ pytestmark = pytest.mark.gpu
 
 
 
-def run_attention(device, q, kv, meta, t, base, heads, kvh, hd, window):
+def run_attention(device, q, kv, meta, t, base, heads, kvh, hd, window, p_lo=False):
     out = np.zeros((t, heads * hd), np.float16)
-    L.check(L.lib().omg_debug_attention(device, L.ptr(q.view(np.uint16), C.c_uint16), L.ptr(kv.view(np.uint16), C.c_uint16),
-               L.ptr(meta, C.c_int32), t, base, heads, kvh, hd, window,
-               L.ptr(out.view(np.uint16), C.c_uint16)))
+    L.check(L.lib().omg_debug_attention(device, L.ptr(q.view(np.uint16), C.c_uint16),
+                                        L.ptr(kv.view(np.uint16), C.c_uint16),
+                                        L.ptr(meta, C.c_int32), t, base, heads, kvh, hd, window,
+                                        int(p_lo), L.ptr(out.view(np.uint16), C.c_uint16)))
     return out.astype(np.float32)
 
 
@@ -118,16 +119,34 @@ def test_attention_layout_invariance(device, hd, window):
 
 
 @pytest.mark.parametrize("window", [0, 512, 100])
-def test_attention_e2b_packing(device, window):
+@pytest.mark.parametrize("p_lo", [False, True])
+def test_attention_e2b_packing(device, window, p_lo):
     """A 500-token state with 12 branches of 24 (the E2B request) at GQA 8/2:
-    runs span several 128-key tiles, so their partials are merged."""
+    runs span many 64-key tiles, with and without P's f16 residue."""
     rng = np.random.default_rng(window + 11)
     heads, kvh, hd = 8, 2, 256
     meta = layout([(500, [24] * 12)])
     rows = len(meta)
     q, kv = make_inputs(rng, rows, heads, kvh, hd, 1.0 / np.sqrt(np.sqrt(hd)))
-    got = run_attention(device, q, kv, meta, rows, 0, heads, kvh, hd, window)
+    got = run_attention(device, q, kv, meta, rows, 0, heads, kvh, hd, window, p_lo)
     exp = reference(q, kv, meta, rows, 0, heads, kvh, hd, window)
+    assert np.abs(got - exp).max() < 2e-3 * max(np.abs(exp).max(), 1.0)
+
+
+def test_attention_peaked_scores_rescale(device):
+    """Scores growing along the keys (each tile's max above the last by more
+    than the reference-max slack) force the output rescale on every tile."""
+    rng = np.random.default_rng(9)
+    heads, kvh, hd = 4, 1, 256
+    meta = layout([(400, [30, 7])])
+    rows = len(meta)
+    q, kv = make_inputs(rng, rows, heads, kvh, hd, 0.2)
+    # Positive queries against K rows that grow with the row index: a 64-key
+    # tile's scores exceed the previous tile's by ~9, more than the slack.
+    kv[:, :hd] = np.repeat(np.linspace(0.0, 3.0, rows)[:, None], hd, 1).astype(np.float16)
+    q[:] = (np.abs(q.astype(np.float32)) * 0.5).astype(np.float16)
+    got = run_attention(device, q, kv, meta, rows, 0, heads, kvh, hd, 0)
+    exp = reference(q, kv, meta, rows, 0, heads, kvh, hd, 0)
     assert np.abs(got - exp).max() < 2e-3 * max(np.abs(exp).max(), 1.0)
 
 

@@ -7,6 +7,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <thread>
 
 #include "capi_util.h"
 #include "json.h"
@@ -671,8 +672,8 @@ void LayaEngine::hidden(const LayaSequence* seqs, size_t n, float* out, size_t o
   std::memcpy(out, h_out_.p, nrows * d * 4);
 }
 
-// laya.rs:1496-1523: the host helpers, sums in index order as Rust's
-// iterator sum.
+// laya.rs:1496-1523: the host helpers (the LayerNorm's sums in index order
+// as Rust's iterator sum; dot products below in eight partial sums).
 static std::vector<float> host_layer_norm(const float* x, const std::vector<float>& w,
                                           const std::vector<float>& b, size_t n, float eps) {
   float s = 0.f;
@@ -687,9 +688,16 @@ static std::vector<float> host_layer_norm(const float* x, const std::vector<floa
   return out;
 }
 
+// Eight interleaved partial sums, added in a fixed order: the loop
+// vectorises, and the result differs from a sequential sum only by f32
+// reassociation.
 static float host_dot(const float* a, const float* b, size_t n) {
-  float s = 0.f;
-  for (size_t i = 0; i < n; ++i) s += a[i] * b[i];
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  size_t i = 0;
+  for (; i + 8 <= n; i += 8)
+    for (int j = 0; j < 8; ++j) acc[j] += a[i + j] * b[i + j];
+  float s = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+  for (; i < n; ++i) s += a[i] * b[i];
   return s;
 }
 
@@ -768,16 +776,26 @@ LayaOutput LayaEngine::score(const float* rows, size_t k) const {
 }
 
 std::vector<LayaOutput> LayaEngine::evaluate(const LayaSequence* seqs, size_t n) {
-  size_t rows = 0;
-  for (size_t i = 0; i < n; ++i) rows += 1 + seqs[i].n_markers;
-  std::vector<float> h(rows * config.d);
+  std::vector<size_t> first(n + 1, 0);
+  for (size_t i = 0; i < n; ++i) first[i + 1] = first[i] + 1 + seqs[i].n_markers;
+  std::vector<float> h(first[n] * config.d);
   hidden(seqs, n, h.data(), h.size());
-  std::vector<LayaOutput> out;
-  out.reserve(n);
-  size_t r = 0;
-  for (size_t i = 0; i < n; ++i) {
-    out.push_back(score(h.data() + r * config.d, seqs[i].n_markers));
-    r += 1 + seqs[i].n_markers;
+  // The host half, sequences split over the host's cores (each sequence's
+  // score is independent and computed the same way on any thread).
+  std::vector<LayaOutput> out(n);
+  const size_t nthreads =
+      std::min<size_t>(std::max(1u, std::thread::hardware_concurrency()), (n + 7) / 8);
+  auto work = [&](size_t w) {
+    for (size_t i = w; i < n; i += nthreads)
+      out[i] = score(h.data() + first[i] * config.d, seqs[i].n_markers);
+  };
+  if (nthreads <= 1) {
+    work(0);
+  } else {
+    std::vector<std::thread> pool;
+    for (size_t w = 1; w < nthreads; ++w) pool.emplace_back(work, w);
+    work(0);
+    for (auto& th : pool) th.join();
   }
   return out;
 }

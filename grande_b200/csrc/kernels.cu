@@ -336,86 +336,105 @@ __global__ void pl_gate_kernel(const float* __restrict__ g, const float* __restr
 
 // ---- logits at readout rows (logits.wgsl) ----------------------------------
 
+// Element k (k % 4 == 0) and the three after it of vocab row v as f32
+// (QTensor::get): Q4 blocks hold elements 0..15 in the low nibbles of their
+// 16 bytes and 16..31 in the high nibbles.
+template <int DT>
+__device__ __forceinline__ float4 load4_f32(const uint8_t* __restrict__ codes,
+                                            const uint8_t* __restrict__ scales, size_t v, int nb,
+                                            int k) {
+  const size_t gb = v * nb + (k >> 5);
+  const int e = k & 31;
+  if constexpr (DT == kF16) {
+    const uint2 q = *reinterpret_cast<const uint2*>(codes + (gb * 32 + e) * 2);
+    const __half2 a = *reinterpret_cast<const __half2*>(&q.x);
+    const __half2 b = *reinterpret_cast<const __half2*>(&q.y);
+    const float2 fa = __half22float2(a), fb = __half22float2(b);
+    return make_float4(fa.x, fa.y, fb.x, fb.y);
+  } else {
+    const uint16_t sb =
+        static_cast<uint16_t>(scales[2 * gb]) | (static_cast<uint16_t>(scales[2 * gb + 1]) << 8);
+    const float dq = half_bits_to_float(sb);
+    if constexpr (DT == kQ8) {
+      const uint32_t q = *reinterpret_cast<const uint32_t*>(codes + gb * 32 + e);
+      return make_float4(static_cast<float>(static_cast<int8_t>(q & 0xff)) * dq,
+                         static_cast<float>(static_cast<int8_t>((q >> 8) & 0xff)) * dq,
+                         static_cast<float>(static_cast<int8_t>((q >> 16) & 0xff)) * dq,
+                         static_cast<float>(static_cast<int8_t>(q >> 24)) * dq);
+    } else {
+      const uint32_t q = *reinterpret_cast<const uint32_t*>(codes + gb * 16 + (e & 15));
+      const int sh = e < 16 ? 0 : 4;
+      return make_float4((static_cast<float>((q >> sh) & 0xf) - 8.0f) * dq,
+                         (static_cast<float>((q >> (8 + sh)) & 0xf) - 8.0f) * dq,
+                         (static_cast<float>((q >> (16 + sh)) & 0xf) - 8.0f) * dq,
+                         (static_cast<float>((q >> (24 + sh)) & 0xf) - 8.0f) * dq);
+    }
+  }
+}
+
+constexpr int kLogitsVocab = 4;   // vocab rows per warp at once
+constexpr int kLogitsRows = 12;   // readout rows per pass over the table
+
+// logits.wgsl in f32: out[r, v] = sum_k rows[r, k] * W[v, k] (+ the host
+// softcap). A warp takes kLogitsVocab vocab rows against up to kLogitsRows
+// readout rows staged in shared memory; lane l owns elements 4 l + 128 i,
+// so each readout float4 it reads from shared memory serves kLogitsVocab
+// rows of the table and a warp's reads are conflict-free. d % 32 == 0.
 template <int DT>
 __global__ void __launch_bounds__(256) logits_kernel(const float* __restrict__ rows, int nrows,
-                                                     int chunk, const uint8_t* __restrict__ codes,
+                                                     const uint8_t* __restrict__ codes,
                                                      const uint8_t* __restrict__ scales,
                                                      int vocab, int d, float softcap,
                                                      float* __restrict__ out) {
-  extern __shared__ float xs[];  // [chunk][d]
+  extern __shared__ float xs[];  // [kLogitsRows][d]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
   const int nb = d / 32;
-  for (int r0 = 0; r0 < nrows; r0 += chunk) {
-    const int nr = min(chunk, nrows - r0);
+  const int steps = (d + 127) / 128;
+  for (int r0 = 0; r0 < nrows; r0 += kLogitsRows) {
+    const int nr = min(kLogitsRows, nrows - r0);
     __syncthreads();
-    for (int i = threadIdx.x; i < nr * d; i += blockDim.x) xs[i] = rows[static_cast<size_t>(r0) * d + i];
+    for (int i = threadIdx.x; i < nr * d; i += blockDim.x)
+      xs[i] = rows[static_cast<size_t>(r0) * d + i];
     __syncthreads();
-    for (int v = blockIdx.x * nwarps + warp; v < vocab; v += gridDim.x * nwarps) {
-      float acc[8];
+    for (int v0 = (blockIdx.x * nwarps + warp) * kLogitsVocab; v0 < vocab;
+         v0 += gridDim.x * nwarps * kLogitsVocab) {
+      float acc[kLogitsVocab][kLogitsRows];
 #pragma unroll
-      for (int r = 0; r < 8; ++r) acc[r] = 0.f;
-      // 8 blocks of 32 per step, 4 lanes per block.
-      for (int b0 = 0; b0 < nb; b0 += 8) {
-        const int b = b0 + (lane >> 2);
-        const int w = lane & 3;
-        if (b >= nb) continue;
-        const size_t gb = static_cast<size_t>(v) * nb + b;
-        float e[8];
-        int c0, c1;  // element offsets of the two groups of 4 within the block
-        if constexpr (DT == kQ4) {
-          const uint16_t sb = static_cast<uint16_t>(scales[2 * gb]) |
-                              (static_cast<uint16_t>(scales[2 * gb + 1]) << 8);
-          const float dq = half_bits_to_float(sb);
-          const uint32_t q = *reinterpret_cast<const uint32_t*>(codes + gb * 16 + 4 * w);
+      for (int u = 0; u < kLogitsVocab; ++u)
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            e[j] = (static_cast<float>((q >> (8 * j)) & 0xf) - 8.0f) * dq;
-            e[4 + j] = (static_cast<float>((q >> (8 * j + 4)) & 0xf) - 8.0f) * dq;
-          }
-          c0 = 4 * w;
-          c1 = 16 + 4 * w;
-        } else if constexpr (DT == kQ8) {
-          const uint16_t sb = static_cast<uint16_t>(scales[2 * gb]) |
-                              (static_cast<uint16_t>(scales[2 * gb + 1]) << 8);
-          const float dq = half_bits_to_float(sb);
-          const uint2 q = *reinterpret_cast<const uint2*>(codes + gb * 32 + 8 * w);
+        for (int r = 0; r < kLogitsRows; ++r) acc[u][r] = 0.f;
+#pragma unroll 2
+      for (int i = 0; i < steps; ++i) {
+        const int k = 4 * lane + 128 * i;
+        if (k >= d) continue;  // d % 32 == 0: the lane's four elements are all in or all out
+        float4 w[kLogitsVocab];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            e[j] = static_cast<float>(static_cast<int8_t>((q.x >> (8 * j)) & 0xff)) * dq;
-            e[4 + j] = static_cast<float>(static_cast<int8_t>((q.y >> (8 * j)) & 0xff)) * dq;
-          }
-          c0 = 8 * w;
-          c1 = 8 * w + 4;
-        } else {
-          const uint4 q = *reinterpret_cast<const uint4*>(codes + gb * 64 + 16 * w);
-          const uint16_t* hq = reinterpret_cast<const uint16_t*>(&q);
+        for (int u = 0; u < kLogitsVocab; ++u)
+          w[u] = v0 + u < vocab ? load4_f32<DT>(codes, scales, static_cast<size_t>(v0 + u), nb, k)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) e[j] = half_bits_to_float(hq[j]);
-          c0 = 8 * w;
-          c1 = 8 * w + 4;
-        }
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
+        for (int r = 0; r < kLogitsRows; ++r) {
           if (r < nr) {
-            const float* xr = xs + r * d + b * 32;
-            const float4 x0 = *reinterpret_cast<const float4*>(xr + c0);
-            const float4 x1 = *reinterpret_cast<const float4*>(xr + c1);
-            acc[r] += e[0] * x0.x + e[1] * x0.y + e[2] * x0.z + e[3] * x0.w + e[4] * x1.x +
-                      e[5] * x1.y + e[6] * x1.z + e[7] * x1.w;
+            const float4 x = *reinterpret_cast<const float4*>(xs + r * d + k);
+#pragma unroll
+            for (int u = 0; u < kLogitsVocab; ++u)
+              acc[u][r] += w[u].x * x.x + w[u].y * x.y + w[u].z * x.z + w[u].w * x.w;
           }
         }
       }
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        if (r < nr) {
-          float z = warp_sum(acc[r]);
-          if (lane == 0) {
-            if (softcap > 0.f) z = softcap * tanhf(z / softcap);
-            out[static_cast<size_t>(r0 + r) * vocab + v] = z;
+      for (int u = 0; u < kLogitsVocab; ++u)
+#pragma unroll
+        for (int r = 0; r < kLogitsRows; ++r) {
+          if (r < nr) {
+            float z = warp_sum(acc[u][r]);
+            if (lane == 0 && v0 + u < vocab) {
+              if (softcap > 0.f) z = softcap * tanhf(z / softcap);
+              out[static_cast<size_t>(r0 + r) * vocab + v0 + u] = z;
+            }
           }
         }
-      }
     }
   }
 }
@@ -504,20 +523,24 @@ void launch_qk_prep(const QkArgs& a, cudaStream_t s) {
 void launch_logits(int dtype, const float* rows, int nrows, const void* codes, const void* scales,
                    int vocab, int d, float softcap, float* out, int num_sms, cudaStream_t s) {
   if (nrows <= 0) return;
-  int chunk = std::max(1, std::min(8, (96 * 1024) / (d * 4)));
-  const size_t smem = static_cast<size_t>(chunk) * d * 4;
+  const size_t smem = static_cast<size_t>(kLogitsRows) * d * 4;
   const auto* c = static_cast<const uint8_t*>(codes);
   const auto* sc = static_cast<const uint8_t*>(scales);
-  const int grid = num_sms * 2;
+  // One sweep of the table: 4 vocab rows per warp, 8 warps per CTA.
+  (void)num_sms;
+  const int grid = (vocab + 31) / 32;
   if (dtype == kQ4) {
-    cudaFuncSetAttribute(logits_kernel<kQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-    logits_kernel<kQ4><<<grid, 256, smem, s>>>(rows, nrows, chunk, c, sc, vocab, d, softcap, out);
+    cudaFuncSetAttribute(logits_kernel<kQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    logits_kernel<kQ4><<<grid, 256, smem, s>>>(rows, nrows, c, sc, vocab, d, softcap, out);
   } else if (dtype == kQ8) {
-    cudaFuncSetAttribute(logits_kernel<kQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-    logits_kernel<kQ8><<<grid, 256, smem, s>>>(rows, nrows, chunk, c, sc, vocab, d, softcap, out);
+    cudaFuncSetAttribute(logits_kernel<kQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    logits_kernel<kQ8><<<grid, 256, smem, s>>>(rows, nrows, c, sc, vocab, d, softcap, out);
   } else {
-    cudaFuncSetAttribute(logits_kernel<kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-    logits_kernel<kF16><<<grid, 256, smem, s>>>(rows, nrows, chunk, c, sc, vocab, d, softcap, out);
+    cudaFuncSetAttribute(logits_kernel<kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    logits_kernel<kF16><<<grid, 256, smem, s>>>(rows, nrows, c, sc, vocab, d, softcap, out);
   }
 }
 

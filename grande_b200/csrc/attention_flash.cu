@@ -29,6 +29,7 @@
 
 #include "attention.cuh"
 #include "gemm.cuh"
+#include "launch.cuh"
 #include "ptx.cuh"
 
 namespace omg {
@@ -98,6 +99,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   griddep_wait();
+  griddep_launch();  // one CTA per (run, KV head): a single wave
 
   if (warp == 0) {
     if (lane == 0) {
@@ -334,7 +336,6 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   }
-  griddep_launch();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -462,9 +463,9 @@ void launch_attention_flash(const CUtensorMap& tq, const CUtensorMap& tkv,
   if (a.n_runs <= 0) return;
   dim3 grid(a.n_runs, a.kv_heads);
   if (p_lo)
-    attention_flash_kernel<true><<<grid, 192, fa_smem<true>(), s>>>(tq, tkv, a);
+    launch_pdl(attention_flash_kernel<true>, grid, dim3(192), fa_smem<true>(), s, tq, tkv, a);
   else
-    attention_flash_kernel<false><<<grid, 192, fa_smem<false>(), s>>>(tq, tkv, a);
+    launch_pdl(attention_flash_kernel<false>, grid, dim3(192), fa_smem<false>(), s, tq, tkv, a);
 }
 
 }  // namespace omg

@@ -6,6 +6,7 @@
 // per CTA; split-K slabs along grid.z for the narrow f32 projections so the
 // grid covers the 148 SMs.
 #include "gemm.cuh"
+#include "launch.cuh"
 #include "ptx.cuh"
 #include <cudaTypedefs.h>
 #include <cstdio>
@@ -136,6 +137,11 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Operands and residual rows come from earlier kernels (programmatic
+  // dependent launch: the prologue above may overlap their tail). The grid
+  // is persistent (one wave), so the next kernel may begin launching now.
+  griddep_wait();
+  griddep_launch();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -451,7 +457,7 @@ template <int BN, int EPI>
 void launch(const GemmPlan& p, const GemmArgs& a, cudaStream_t stream) {
   const int total = a.m_tiles * a.n_tiles * a.splits;
   const int grid = total < p.num_sms ? total : p.num_sms;
-  gemm_kernel<BN, EPI><<<grid, 192, Cfg<BN>::SMEM, stream>>>(p.a, p.b, a);
+  launch_pdl(gemm_kernel<BN, EPI>, dim3(grid), dim3(192), Cfg<BN>::SMEM, stream, p.a, p.b, a);
 }
 
 }  // namespace

@@ -1,6 +1,7 @@
 // Row kernels of the decoder pass (see kernels.cuh). Reference shaders:
 // crates/omg-wgpu/src/shaders/{weight,embed,rmsnorm,qk_prep,logits}.wgsl.
 #include "kernels.cuh"
+#include "launch.cuh"
 #include "ptx.cuh"
 #include "quant.cuh"
 
@@ -79,6 +80,9 @@ __global__ void __launch_bounds__(128) embed_norm_kernel(const int* __restrict__
                                                          float offset, float* __restrict__ x,
                                                          __half* __restrict__ x16,
                                                          __half* __restrict__ h16, int ldh) {
+  griddep_wait();
+  // Let the next kernel start its prologue; its CTAs wait for this grid.
+  griddep_launch();
   __shared__ float red[4];
   const int row = blockIdx.x;
   if (row >= t) return;
@@ -128,6 +132,9 @@ __global__ void __launch_bounds__(kNormThreads) residual_norm_kernel(
     const float* __restrict__ w1, float eps, float offset, float out_scale, float* __restrict__ x,
     __half* __restrict__ x16, const float* __restrict__ w2, __half* __restrict__ h16, int ldh,
     const int* __restrict__ row_map, float* __restrict__ rows_out) {
+  griddep_wait();
+  // Let the next kernel start its prologue; its CTAs wait for this grid.
+  griddep_launch();
   __shared__ float red[kNormThreads / 32];
   const int row = blockIdx.x;
   if (row >= t) return;
@@ -210,6 +217,9 @@ __global__ void __launch_bounds__(kNormThreads) residual_norm_kernel(
 
 template <int HD>
 __global__ void __launch_bounds__(128) qk_prep_kernel(QkArgs g) {
+  griddep_wait();
+  // Let the next kernel start its prologue; its CTAs wait for this grid.
+  griddep_launch();
   constexpr int E = HD / 64;  // elements per lane in each half of the head
   constexpr int HALF = HD / 2;
   const int tok = blockIdx.x;
@@ -305,6 +315,7 @@ __global__ void __launch_bounds__(128) pl_combine_kernel(const float* __restrict
                                                          float eps, float offset,
                                                          float proj_scale, float emb_scale,
                                                          float out_scale, float* __restrict__ out) {
+  griddep_wait();
   __shared__ float red[4];
   const int layer = blockIdx.x, tok = blockIdx.y;
   if (layer >= layers || tok >= t) return;
@@ -324,6 +335,7 @@ __global__ void __launch_bounds__(128) pl_combine_kernel(const float* __restrict
 
 __global__ void pl_gate_kernel(const float* __restrict__ g, const float* __restrict__ pli, int t,
                                int P, int layers, int layer, __half* __restrict__ out16) {
+  griddep_wait();
   const size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
   if (i >= static_cast<size_t>(t) * P) return;
   const size_t tok = i / P, c = i % P;
@@ -386,6 +398,7 @@ __global__ void __launch_bounds__(256) logits_kernel(const float* __restrict__ r
                                                      const uint8_t* __restrict__ scales,
                                                      int vocab, int d, float softcap,
                                                      float* __restrict__ out) {
+  griddep_wait();
   extern __shared__ float xs[];  // [kLogitsRows][d]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
@@ -457,35 +470,37 @@ void launch_embed_norm(int dtype, const int* ids, int t, const void* codes, cons
   const auto* c = static_cast<const uint8_t*>(codes);
   const auto* sc = static_cast<const uint8_t*>(scales);
   if (dtype == kQ4)
-    embed_norm_kernel<kQ4><<<t, 128, 0, s>>>(ids, t, c, sc, d, scale, w, eps, offset, x, x16, h16, ldh);
+    launch_pdl(embed_norm_kernel<kQ4>, dim3(t), dim3(128), 0, s, ids, t, c, sc, d, scale, w, eps, offset,
+               x, x16, h16, ldh);
   else if (dtype == kQ8)
-    embed_norm_kernel<kQ8><<<t, 128, 0, s>>>(ids, t, c, sc, d, scale, w, eps, offset, x, x16, h16, ldh);
+    launch_pdl(embed_norm_kernel<kQ8>, dim3(t), dim3(128), 0, s, ids, t, c, sc, d, scale, w, eps, offset,
+               x, x16, h16, ldh);
   else
-    embed_norm_kernel<kF16><<<t, 128, 0, s>>>(ids, t, c, sc, d, scale, w, eps, offset, x, x16, h16, ldh);
+    launch_pdl(embed_norm_kernel<kF16>, dim3(t), dim3(128), 0, s, ids, t, c, sc, d, scale, w, eps, offset,
+               x, x16, h16, ldh);
 }
 
 void launch_residual_norm(const float* a, int splits, size_t split_stride, int lda, int t, int d,
                           const float* w1, float eps, float offset, float out_scale, float* x,
                           __half* x16, const float* w2, __half* h16, int ldh,
                           const int* row_map, float* rows_out, cudaStream_t s) {
-  residual_norm_kernel<<<t, kNormThreads, 0, s>>>(a, splits, split_stride, lda, t, d, w1, eps,
-                                                  offset, out_scale, x, x16, w2, h16, ldh,
-                                                  row_map, rows_out);
+  launch_pdl(residual_norm_kernel, dim3(t), dim3(kNormThreads), 0, s, a, splits, split_stride, lda,
+             t, d, w1, eps, offset, out_scale, x, x16, w2, h16, ldh, row_map, rows_out);
 }
 
 void launch_pl_combine(const float* proj, int t, int P, int layers, const float* w,
                        const __half* emb, float eps, float offset, float proj_scale,
                        float emb_scale, float out_scale, float* out, cudaStream_t s) {
   dim3 grid(layers, t);
-  pl_combine_kernel<<<grid, 128, 0, s>>>(proj, t, P, layers, w, emb, eps, offset, proj_scale,
-                                         emb_scale, out_scale, out);
+  launch_pdl(pl_combine_kernel, grid, dim3(128), 0, s, proj, t, P, layers, w, emb, eps, offset,
+             proj_scale, emb_scale, out_scale, out);
 }
 
 void launch_pl_gate(const float* g, const float* pli, int t, int P, int layers, int layer,
                     __half* out16, cudaStream_t s) {
   const size_t n = static_cast<size_t>(t) * P;
-  pl_gate_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(g, pli, t, P, layers,
-                                                                         layer, out16);
+  launch_pdl(pl_gate_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, s, g, pli,
+             t, P, layers, layer, out16);
 }
 
 namespace {
@@ -515,9 +530,9 @@ void launch_rope_table(float theta, int half, int n_pos, float2* tab, cudaStream
 
 void launch_qk_prep(const QkArgs& a, cudaStream_t s) {
   if (a.hd == 512)
-    qk_prep_kernel<512><<<a.t, 128, 0, s>>>(a);
+    launch_pdl(qk_prep_kernel<512>, dim3(a.t), dim3(128), 0, s, a);
   else
-    qk_prep_kernel<256><<<a.t, 128, 0, s>>>(a);
+    launch_pdl(qk_prep_kernel<256>, dim3(a.t), dim3(128), 0, s, a);
 }
 
 void launch_logits(int dtype, const float* rows, int nrows, const void* codes, const void* scales,
@@ -532,15 +547,18 @@ void launch_logits(int dtype, const float* rows, int nrows, const void* codes, c
   if (dtype == kQ4) {
     cudaFuncSetAttribute(logits_kernel<kQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(smem));
-    logits_kernel<kQ4><<<grid, 256, smem, s>>>(rows, nrows, c, sc, vocab, d, softcap, out);
+    launch_pdl(logits_kernel<kQ4>, dim3(grid), dim3(256), smem, s, rows, nrows, c, sc, vocab, d, softcap,
+               out);
   } else if (dtype == kQ8) {
     cudaFuncSetAttribute(logits_kernel<kQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(smem));
-    logits_kernel<kQ8><<<grid, 256, smem, s>>>(rows, nrows, c, sc, vocab, d, softcap, out);
+    launch_pdl(logits_kernel<kQ8>, dim3(grid), dim3(256), smem, s, rows, nrows, c, sc, vocab, d, softcap,
+               out);
   } else {
     cudaFuncSetAttribute(logits_kernel<kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(smem));
-    logits_kernel<kF16><<<grid, 256, smem, s>>>(rows, nrows, c, sc, vocab, d, softcap, out);
+    launch_pdl(logits_kernel<kF16>, dim3(grid), dim3(256), smem, s, rows, nrows, c, sc, vocab, d, softcap,
+               out);
   }
 }
 

@@ -6,6 +6,7 @@
 
 #include "gemm.cuh"
 #include "laya_kernels.cuh"
+#include "launch.cuh"
 #include "ptx.cuh"
 #include "quant.cuh"
 
@@ -68,6 +69,7 @@ __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast
 
 // One warp per row, 8 rows per CTA.
 __global__ void __launch_bounds__(256) laya_ln_kernel(LayaLnArgs a) {
+  griddep_wait();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= a.t) return;
@@ -124,6 +126,7 @@ __global__ void __launch_bounds__(256)
     laya_embed_ln_kernel(const int* __restrict__ ids, int t, const uint8_t* __restrict__ codes,
                          const uint8_t* __restrict__ scales, int d, const float* __restrict__ w,
                          float eps, float* __restrict__ x, __half* __restrict__ h16) {
+  griddep_wait();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= t) return;
@@ -159,6 +162,7 @@ __global__ void __launch_bounds__(256)
 
 __global__ void laya_gather_kernel(const float* __restrict__ x, int d, const int* __restrict__ map,
                                    int n, float* __restrict__ rows) {
+  griddep_wait();
   const int r = blockIdx.x;
   if (r >= n) return;
   const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(map[r]) * d);
@@ -223,6 +227,7 @@ __global__ void __launch_bounds__(192, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -407,6 +412,7 @@ __global__ void __launch_bounds__(192, 2)
       }
     }
   }
+  griddep_launch();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -431,22 +437,22 @@ void launch_laya_embed_ln(int dtype, const int* ids, int t, const void* codes, c
   const auto* sc = static_cast<const uint8_t*>(scales);
   const unsigned grid = static_cast<unsigned>((t + 7) / 8);
   if (dtype == kQ4)
-    laya_embed_ln_kernel<kQ4><<<grid, 256, 0, s>>>(ids, t, c, sc, d, w, eps, x, h16);
+    launch_pdl(laya_embed_ln_kernel<kQ4>, dim3(grid), dim3(256), 0, s, ids, t, c, sc, d, w, eps, x, h16);
   else if (dtype == kQ8)
-    laya_embed_ln_kernel<kQ8><<<grid, 256, 0, s>>>(ids, t, c, sc, d, w, eps, x, h16);
+    launch_pdl(laya_embed_ln_kernel<kQ8>, dim3(grid), dim3(256), 0, s, ids, t, c, sc, d, w, eps, x, h16);
   else
-    laya_embed_ln_kernel<kF16><<<grid, 256, 0, s>>>(ids, t, c, sc, d, w, eps, x, h16);
+    launch_pdl(laya_embed_ln_kernel<kF16>, dim3(grid), dim3(256), 0, s, ids, t, c, sc, d, w, eps, x, h16);
 }
 
 void launch_laya_ln(const LayaLnArgs& a, cudaStream_t s) {
   if (a.t <= 0) return;
-  laya_ln_kernel<<<static_cast<unsigned>((a.t + 7) / 8), 256, 0, s>>>(a);
+  launch_pdl(laya_ln_kernel, dim3(static_cast<unsigned>((a.t + 7) / 8)), dim3(256), 0, s, a);
 }
 
 void launch_laya_gather(const float* x, int d, const int* row_map, int n, float* rows,
                         cudaStream_t s) {
   if (n <= 0) return;
-  laya_gather_kernel<<<n, 128, 0, s>>>(x, d, row_map, n, rows);
+  launch_pdl(laya_gather_kernel, dim3(n), dim3(128), 0, s, x, d, row_map, n, rows);
 }
 
 void laya_attention_items(const int2* span, int t, int window, std::vector<LayaAttnItem>* items) {
@@ -484,7 +490,7 @@ bool laya_attention_map(CUtensorMap* m, const void* qkv16, int rows_cap, int d, 
 void launch_laya_attention(const CUtensorMap& tqkv, const LayaAttnArgs& a, cudaStream_t s) {
   if (a.n_items <= 0) return;
   dim3 grid(a.n_items, a.heads);
-  laya_attention_kernel<<<grid, 192, LA_SMEM, s>>>(tqkv, a);
+  launch_pdl(laya_attention_kernel, grid, dim3(192), LA_SMEM, s, tqkv, a);
 }
 
 void laya_setup_device() {

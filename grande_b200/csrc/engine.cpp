@@ -320,6 +320,7 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
   per_layer_table_ = std::move(b.per_layer_table_);
   gemm_setup_device();
   attention_setup_device();
+  logits_setup_device(config.d);
 
   const Config& c = config;
   const int d = c.d, L = c.layers, P = c.per_layer_dim;
@@ -446,6 +447,7 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
 Engine::~Engine() {
   cudaSetDevice(device_);
   if (stream_) cudaStreamSynchronize(stream_);
+  for (auto& g : graphs_) cudaGraphExecDestroy(g.exec);
   for (auto e : prof_events_) cudaEventDestroy(e);
   for (auto& e : events_)
     if (e) cudaEventDestroy(e);
@@ -840,6 +842,68 @@ int Engine::launch_forward(const Packing& p, Want want) {
   return launches;
 }
 
+bool Engine::GraphKey::operator==(const GraphKey& o) const {
+  return t == o.t && base == o.base && nwanted == o.nwanted && ctas == o.ctas &&
+         sched_bytes == o.sched_bytes && want == o.want && sched == o.sched &&
+         std::equal(attn_off, attn_off + 5, o.attn_off) && runs[0] == o.runs[0] &&
+         runs[1] == o.runs[1] && tiles[0] == o.tiles[0] && tiles[1] == o.tiles[1];
+}
+
+Engine::GraphKey Engine::graph_key(const Packing& p, Want want) const {
+  GraphKey k;
+  k.t = p.t;
+  k.base = p.base;
+  k.nwanted = p.nwanted;
+  k.ctas = p.attn_ctas.size();
+  k.sched_bytes = p.attn_bytes;
+  std::copy(p.attn_off, p.attn_off + 5, k.attn_off);
+  for (int w = 0; w < 2; ++w) {
+    k.runs[w] = p.attn_runs[w].size();
+    k.tiles[w] = p.attn_tiles[w].size();
+  }
+  k.want = static_cast<int>(want);
+  k.sched = attn_sched_.p;
+  return k;
+}
+
+int Engine::run_forward(const Packing& p, Want want) {
+  const GraphKey key = graph_key(p, want);
+  ++graph_clock_;
+  for (auto& g : graphs_)
+    if (g.key == key) {
+      g.used = graph_clock_;
+      CUDA_TRY(cudaGraphLaunch(g.exec, stream_));
+      return g.launches;
+    }
+  cudaGraph_t graph = nullptr;
+  CUDA_TRY(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+  int launches = 0;
+  try {
+    launches = launch_forward(p, want);
+  } catch (...) {
+    cudaStreamEndCapture(stream_, &graph);
+    if (graph) cudaGraphDestroy(graph);
+    throw;
+  }
+  CUDA_TRY(cudaStreamEndCapture(stream_, &graph));
+  CachedGraph g;
+  g.key = key;
+  g.launches = launches;
+  g.used = graph_clock_;
+  const cudaError_t e = cudaGraphInstantiate(&g.exec, graph, 0);
+  cudaGraphDestroy(graph);
+  CUDA_TRY(e);
+  if (graphs_.size() >= kMaxGraphs) {
+    auto lru = std::min_element(graphs_.begin(), graphs_.end(),
+                                [](const CachedGraph& a, const CachedGraph& b) { return a.used < b.used; });
+    cudaGraphExecDestroy(lru->exec);
+    graphs_.erase(lru);
+  }
+  graphs_.push_back(g);
+  CUDA_TRY(cudaGraphLaunch(g.exec, stream_));
+  return launches;
+}
+
 void Engine::prof_mark(const char* name) {
   if (prof_used_ == prof_events_.size()) {
     cudaEvent_t e;
@@ -917,7 +981,7 @@ void Engine::run(const GroupIn* groups, size_t n, size_t first,
     fail("output buffer holds %zu floats, the request returns %zu", out_floats,
          total_rows * width);
   upload(p, per_layer_rows, rows_bytes);
-  launch_forward(p, want);
+  run_forward(p, want);
   const float* src = want == Want::Logits ? logits_.as<float>() : rows_.as<float>();
   if (p.nwanted)
     CUDA_TRY(cudaMemcpyAsync(h_out_.p, src, p.nwanted * width * 4, cudaMemcpyDeviceToHost,
@@ -1131,7 +1195,7 @@ float Engine::time_forward(const GroupIn* groups, size_t n, Want want, bool resi
   CUDA_TRY(cudaStreamSynchronize(stream_));
   int nl = 0;
   CUDA_TRY(cudaEventRecord(events_[6], stream_));
-  for (int i = 0; i < iters; ++i) nl = launch_forward(p, want);
+  for (int i = 0; i < iters; ++i) nl = run_forward(p, want);
   CUDA_TRY(cudaEventRecord(events_[7], stream_));
   CUDA_TRY(cudaMemcpyAsync(h_status_.p, status_.p, 4, cudaMemcpyDeviceToHost, stream_));
   CUDA_TRY(cudaStreamSynchronize(stream_));

@@ -236,6 +236,32 @@ class Engine {
     size_t t = 0, base = 0, nwanted = 0;
   };
 
+  // The launch sequence of a pass is fixed by these values (kernel shapes and
+  // the schedule's offsets); everything else it reads lives at fixed device
+  // addresses and is uploaded before each pass.
+  struct GraphKey {
+    size_t t = 0, base = 0, nwanted = 0, ctas = 0, sched_bytes = 0;
+    size_t attn_off[5] = {};
+    size_t runs[2] = {}, tiles[2] = {};
+    int want = 0;
+    const void* sched = nullptr;
+    bool operator==(const GraphKey& o) const;
+  };
+  struct CachedGraph {
+    GraphKey key;
+    cudaGraphExec_t exec = nullptr;
+    int launches = 0;
+    uint64_t used = 0;
+  };
+  GraphKey graph_key(const Packing& p, Want want) const;
+  // launch_forward through a cached CUDA graph of this packing's shape
+  // (captured on first use; a few shapes are kept, least recently used
+  // dropped).
+  int run_forward(const Packing& p, Want want);
+  std::vector<CachedGraph> graphs_;
+  uint64_t graph_clock_ = 0;
+  static constexpr size_t kMaxGraphs = 8;
+
   std::pair<size_t, std::optional<PrefixSource>> admit(const GroupIn* groups, size_t n);
   Packing pack(const GroupIn* groups, size_t n, size_t first, bool resident_first) const;
   void upload(const Packing& p, const uint8_t* per_layer_rows, size_t rows_bytes);

@@ -535,6 +535,13 @@ void launch_qk_prep(const QkArgs& a, cudaStream_t s) {
     launch_pdl(qk_prep_kernel<256>, dim3(a.t), dim3(128), 0, s, a);
 }
 
+void logits_setup_device(int d) {
+  const int smem = kLogitsRows * d * 4;
+  cudaFuncSetAttribute(logits_kernel<kQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaFuncSetAttribute(logits_kernel<kQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaFuncSetAttribute(logits_kernel<kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+}
+
 void launch_logits(int dtype, const float* rows, int nrows, const void* codes, const void* scales,
                    int vocab, int d, float softcap, float* out, int num_sms, cudaStream_t s) {
   if (nrows <= 0) return;
@@ -545,18 +552,12 @@ void launch_logits(int dtype, const float* rows, int nrows, const void* codes, c
   (void)num_sms;
   const int grid = (vocab + 31) / 32;
   if (dtype == kQ4) {
-    cudaFuncSetAttribute(logits_kernel<kQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
     launch_pdl(logits_kernel<kQ4>, dim3(grid), dim3(256), smem, s, rows, nrows, c, sc, vocab, d, softcap,
                out);
   } else if (dtype == kQ8) {
-    cudaFuncSetAttribute(logits_kernel<kQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
     launch_pdl(logits_kernel<kQ8>, dim3(grid), dim3(256), smem, s, rows, nrows, c, sc, vocab, d, softcap,
                out);
   } else {
-    cudaFuncSetAttribute(logits_kernel<kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
     launch_pdl(logits_kernel<kF16>, dim3(grid), dim3(256), smem, s, rows, nrows, c, sc, vocab, d, softcap,
                out);
   }

@@ -83,6 +83,10 @@ void launch_rope_table(float theta, int half, int n_pos, float2* tab, cudaStream
 
 // logits.wgsl + the host softcap (engine.rs:1901-1906): out[r, v] =
 // sum_k rows[r, k] * dequant(embed[v, k]) in f32, then cap * tanh(z / cap).
+// Shared-memory limit of the logits kernel for row width d (once per device
+// and width, before the first launch).
+void logits_setup_device(int d);
+
 void launch_logits(int dtype, const float* rows, int nrows, const void* codes, const void* scales,
                    int vocab, int d, float softcap, float* out, int num_sms, cudaStream_t s);
 

@@ -1,6 +1,6 @@
 // Blackwell (sm_100a) building blocks written as inline PTX: mbarriers with
-// bounded waits, TMA tile loads (no cluster multicast anywhere in this
-// library), tcgen05 tensor-memory allocation, MMA issue, commit and loads.
+// bounded waits, TMA tile loads into this CTA's own shared memory, tcgen05
+// tensor-memory allocation, MMA issue, commit and loads.
 //
 // Every wait in this file gives up after a time limit instead of spinning
 // forever: it records an error code in the caller's device status word and

@@ -41,7 +41,9 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  // Ring + alignment slack + barriers, and 2 KB the epilogue may stage its
+  // per-column constants in (the q / k norm weights of kEpiQkPrep).
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + 2048;
   // Two accumulators: the epilogue drains one while the MMAs fill the other.
   static constexpr uint32_t TMEM_COLS = 2 * BN;
 };
@@ -113,6 +115,7 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* tempty = tfull + 2;          // [2] accumulator drained
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* epi_consts = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -202,6 +205,14 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +32, one row per thread.
     const int q = warp & 3;
+    if constexpr (EPI == kEpiQkPrep) {
+      // The q and k norm weights, staged while the first tile's mainloop runs.
+      for (int i = threadIdx.x - 64; i < 512; i += 128) {
+        const float* src = i < 256 ? g.epi.qk.qn : g.epi.qk.kn;
+        epi_consts[i] = src ? src[i & 255] : 0.f;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+    }
     int local = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++local) {
       const int m_tile = tile % g.m_tiles;
@@ -333,21 +344,25 @@ __global__ void __launch_bounds__(192, 1)
         }
       } else if constexpr (EPI == kEpiQkPrep) {
         // qk_prep.wgsl on the accumulator: this tile is head n_tile of the
-        // row, all 256 of its dims in this thread's TMEM lane.
+        // row, all 256 of its dims in this thread's TMEM lane. Loads are
+        // batched ahead of the math (one thread per row has little else to
+        // hide their latency with): the norm weights come from shared memory,
+        // each 32-pair chunk's RoPE entries are read before they are used.
         static_assert(BN == 256, "one 256-column tile per head");
         const QkEpi& q = g.epi.qk;
         const int h = n_tile;
         const bool is_q = h < q.heads;
         const bool is_v = h >= q.heads + q.kv_heads;
         const bool ok_row = row < g.m;
-        float ss = 0.f;
+        float ssp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
         for (int c = 0; c < 8; ++c) {
           float v[32];
           tmem_ld32(tbase + c * 32, v);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) ss = fmaf(v[j], v[j], ss);
+          for (int j = 0; j < 32; ++j) ssp[j & 7] = fmaf(v[j], v[j], ssp[j & 7]);
         }
+        const float ss = ((ssp[0] + ssp[1]) + (ssp[2] + ssp[3])) + ((ssp[4] + ssp[5]) + (ssp[6] + ssp[7]));
         const float inv = (is_v && !q.v_norm) ? 1.0f : rsqrtf(ss / 256.0f + q.eps);
         const int crow = q.base + (ok_row ? row : 0);
         __half* orow;
@@ -355,14 +370,21 @@ __global__ void __launch_bounds__(192, 1)
           orow = q.q16 + static_cast<size_t>(ok_row ? row : 0) * q.heads * 256 + h * 256;
         else
           orow = q.kv + static_cast<size_t>(crow) * 2 * q.kv_heads * 256 + (h - q.heads) * 256;
-        const float* wn = is_q ? q.qn : q.kn;
+        const float* wn = epi_consts + (is_q ? 0 : 256);
         // Table [pair][position]: consecutive rows read consecutive entries.
         const float2* rt = q.rope + (ok_row ? q.meta[crow].pos : 0);
         const size_t rs = static_cast<size_t>(q.rope_stride);
         const float scale = is_q ? q.q_scale : 1.0f;
+        const int half_rot = q.rope_dims / 2;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           float a[32], b[32];
+          float2 cs[32];
+          const bool rot = !is_v && c * 32 < half_rot;
+          if (rot) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) cs[j] = rt[static_cast<size_t>(c * 32 + j) * rs];
+          }
           tmem_ld32(tbase + c * 32, a);
           tmem_ld32(tbase + (c + 4) * 32, b);
           if (!ok_row) continue;
@@ -378,10 +400,9 @@ __global__ void __launch_bounds__(192, 1)
               const int dd = c * 32 + j;
               float y1 = a[j] * inv * (q.offset + wn[dd]);
               float y2 = b[j] * inv * (q.offset + wn[dd + 128]);
-              if (dd < q.rope_dims / 2) {
-                const float2 cs = rt[dd * rs];
-                const float r1 = y1 * cs.x - y2 * cs.y;
-                const float r2 = y2 * cs.x + y1 * cs.y;
+              if (rot && dd < half_rot) {
+                const float r1 = y1 * cs[j].x - y2 * cs[j].y;
+                const float r2 = y2 * cs[j].x + y1 * cs[j].y;
                 y1 = r1;
                 y2 = r2;
               }

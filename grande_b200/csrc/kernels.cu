@@ -124,9 +124,9 @@ __global__ void __launch_bounds__(128) embed_norm_kernel(const int* __restrict__
 
 // ---- residual-stream norms -------------------------------------------------
 
-constexpr int kNormThreads = 256;
-constexpr int kNormVec = 8;  // float4 per thread: d <= 8192
+constexpr int kNormThreads = 256;  // NV float4 per thread: d <= 1024 NV
 
+template <int NV>
 __global__ void __launch_bounds__(kNormThreads) residual_norm_kernel(
     const float* __restrict__ a, int splits, size_t split_stride, int lda, int t, int d,
     const float* __restrict__ w1, float eps, float offset, float out_scale, float* __restrict__ x,
@@ -140,38 +140,50 @@ __global__ void __launch_bounds__(kNormThreads) residual_norm_kernel(
   if (row >= t) return;
   const float* ar = a + static_cast<size_t>(row) * lda;
   float* xr = x + static_cast<size_t>(row) * d;
-  float4 y[kNormVec];
-  float ss = 0.f;
+  // Every load of the row up front (the slabs, the residual row and both
+  // norms' weights): only the two reductions order the work after them.
+  float4 y[NV], xo[NV], wa[NV], wb[NV];
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-  for (int j = 0; j < kNormVec; ++j) {
+  for (int j = 0; j < NV; ++j) {
     const int i = (threadIdx.x + j * kNormThreads) * 4;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    y[j] = xo[j] = wa[j] = wb[j] = zero;
     if (i < d) {
-      v = *reinterpret_cast<const float4*>(ar + i);
-      for (int z = 1; z < splits; ++z) {
+      y[j] = *reinterpret_cast<const float4*>(ar + i);
+      xo[j] = *reinterpret_cast<const float4*>(xr + i);
+      wa[j] = *reinterpret_cast<const float4*>(w1 + i);
+      if (w2) wb[j] = *reinterpret_cast<const float4*>(w2 + i);
+    }
+  }
+  for (int z = 1; z < splits; ++z) {
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int i = (threadIdx.x + j * kNormThreads) * 4;
+      if (i < d) {
         const float4 u = *reinterpret_cast<const float4*>(ar + z * split_stride + i);
-        v.x += u.x;
-        v.y += u.y;
-        v.z += u.z;
-        v.w += u.w;
+        y[j].x += u.x;
+        y[j].y += u.y;
+        y[j].z += u.z;
+        y[j].w += u.w;
       }
     }
-    y[j] = v;
-    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
   }
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j)
+    ss += y[j].x * y[j].x + y[j].y * y[j].y + y[j].z * y[j].z + y[j].w * y[j].w;
   const float inv1 = rsqrtf(block_sum<kNormThreads>(ss, red) / static_cast<float>(d) + eps);
   float ss2 = 0.f;
 #pragma unroll
-  for (int j = 0; j < kNormVec; ++j) {
+  for (int j = 0; j < NV; ++j) {
     const int i = (threadIdx.x + j * kNormThreads) * 4;
     if (i < d) {
-      const float4 ww = *reinterpret_cast<const float4*>(w1 + i);
-      const float4 xo = *reinterpret_cast<const float4*>(xr + i);
+      const float4 ww = wa[j];
       float4 v = y[j];
-      v.x = (v.x * inv1 * (offset + ww.x) + xo.x) * out_scale;
-      v.y = (v.y * inv1 * (offset + ww.y) + xo.y) * out_scale;
-      v.z = (v.z * inv1 * (offset + ww.z) + xo.z) * out_scale;
-      v.w = (v.w * inv1 * (offset + ww.w) + xo.w) * out_scale;
+      v.x = (v.x * inv1 * (offset + ww.x) + xo[j].x) * out_scale;
+      v.y = (v.y * inv1 * (offset + ww.y) + xo[j].y) * out_scale;
+      v.z = (v.z * inv1 * (offset + ww.z) + xo[j].z) * out_scale;
+      v.w = (v.w * inv1 * (offset + ww.w) + xo[j].w) * out_scale;
       *reinterpret_cast<float4*>(xr + i) = v;
       if (x16) {
         __half2 p = __floats2half2_rn(v.x, v.y);
@@ -191,10 +203,10 @@ __global__ void __launch_bounds__(kNormThreads) residual_norm_kernel(
   __half* hr = h16 ? h16 + static_cast<size_t>(row) * ldh : nullptr;
   float* orow = out_row >= 0 ? rows_out + static_cast<size_t>(out_row) * d : nullptr;
 #pragma unroll
-  for (int j = 0; j < kNormVec; ++j) {
+  for (int j = 0; j < NV; ++j) {
     const int i = (threadIdx.x + j * kNormThreads) * 4;
     if (i < d) {
-      const float4 ww = *reinterpret_cast<const float4*>(w2 + i);
+      const float4 ww = wb[j];
       float4 v = y[j];
       v.x = v.x * inv2 * (offset + ww.x);
       v.y = v.y * inv2 * (offset + ww.y);
@@ -484,8 +496,20 @@ void launch_residual_norm(const float* a, int splits, size_t split_stride, int l
                           const float* w1, float eps, float offset, float out_scale, float* x,
                           __half* x16, const float* w2, __half* h16, int ldh,
                           const int* row_map, float* rows_out, cudaStream_t s) {
-  launch_pdl(residual_norm_kernel, dim3(t), dim3(kNormThreads), 0, s, a, splits, split_stride, lda,
-             t, d, w1, eps, offset, out_scale, x, x16, w2, h16, ldh, row_map, rows_out);
+  if (t <= 0) return;
+#define OMG_NORM(NV)                                                                        \
+  launch_pdl(residual_norm_kernel<NV>, dim3(t), dim3(kNormThreads), 0, s, a, splits,         \
+             split_stride, lda, t, d, w1, eps, offset, out_scale, x, x16, w2, h16, ldh, row_map, \
+             rows_out)
+  if (d <= 1024)
+    OMG_NORM(1);
+  else if (d <= 2048)
+    OMG_NORM(2);
+  else if (d <= 4096)
+    OMG_NORM(4);
+  else
+    OMG_NORM(8);
+#undef OMG_NORM
 }
 
 void launch_pl_combine(const float* proj, int t, int P, int layers, const float* w,

@@ -27,7 +27,13 @@ void DevBuffer::alloc(size_t n, bool zero) {
   release();
   bytes = n ? n : 16;
   CUDA_TRY(cudaMalloc(&p, bytes));
-  if (zero) CUDA_TRY(cudaMemset(p, 0, bytes));
+  if (zero) {
+    // cudaMemset runs on the legacy default stream, which does not order
+    // with the engines' non-blocking streams: wait for it here, or a pass
+    // launched right after could race with the zero fill.
+    CUDA_TRY(cudaMemset(p, 0, bytes));
+    CUDA_TRY(cudaStreamSynchronize(nullptr));
+  }
 }
 
 void DevBuffer::release() {

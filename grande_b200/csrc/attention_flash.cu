@@ -48,14 +48,44 @@ constexpr uint32_t FA_TMEM_O = 256;                     // O [128 x 256]; S buff
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kTau = 8.0f;                            // reference-max slack (natural log)
 
+// P slots: two with f16 P, so the softmax of tile j + 1 writes its P while
+// P_j V_j still runs; one (hi, then lo) with PLO.
+template <bool PLO>
+constexpr int fa_p_slots() {
+  return PLO ? 1 : 2;
+}
+template <bool PLO>
+constexpr int fa_p_slot_bytes() {
+  return (PLO ? 2 : 1) * FA_P_BYTES;
+}
 template <bool PLO>
 constexpr int fa_smem() {
-  return 1024 + FA_Q_BYTES + 4 * FA_KV_BYTES + (PLO ? 2 : 1) * FA_P_BYTES + 256;
+  return 1024 + FA_Q_BYTES + 4 * FA_KV_BYTES + fa_p_slots<PLO>() * fa_p_slot_bytes<PLO>() + 256;
+}
+static_assert(fa_smem<false>() <= 227 * 1024 && fa_smem<true>() <= 227 * 1024,
+              "attention shared memory above the per-CTA limit");
+
+// B_P*: P of the slot written (4 softmax warps arrive); B_O*: the P.V of the
+// tiles of that parity done.
+enum {
+  B_Q = 0, B_K0, B_K1, B_V0, B_V1, B_S0, B_S1, B_P0, B_P1, B_O0, B_O1, B_KF0, B_KF1, B_VF0,
+  B_VF1, B_N
+};
+
+// Bits [a, b) of a 64-bit set, 0 <= a <= b <= 64.
+__device__ __forceinline__ uint64_t key_bits(int a, int b) {
+  const uint64_t below_b = b >= 64 ? ~0ull : (1ull << b) - 1;
+  const uint64_t below_a = a >= 64 ? ~0ull : (1ull << a) - 1;
+  return below_b & ~below_a;
 }
 
-enum {
-  B_Q = 0, B_K0, B_K1, B_V0, B_V1, B_S0, B_S1, B_P, B_O, B_KF0, B_KF1, B_VF0, B_VF1, B_N
-};
+// 2^x on the special-function unit (PTX ex2.approx.ftz.f32; relative error
+// about 2^-22; -inf gives +0 without a special-value path).
+__device__ __forceinline__ float fa_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           uint32_t* status, int lane) {
@@ -75,7 +105,8 @@ __global__ void __launch_bounds__(192, 1)
   auto ks = [&](int b) { return qs + FA_Q_BYTES + b * FA_KV_BYTES; };        // K buffer b
   auto vs = [&](int b) { return qs + FA_Q_BYTES + (2 + b) * FA_KV_BYTES; };  // V buffer b
   uint8_t* ps = qs + FA_Q_BYTES + 4 * FA_KV_BYTES;  // P hi, then (PLO) P lo
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ps + (PLO ? 2 : 1) * FA_P_BYTES);
+  constexpr int NPS = fa_p_slots<PLO>(), PSB = fa_p_slot_bytes<PLO>();
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ps + NPS * PSB);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B_N);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -87,7 +118,7 @@ __global__ void __launch_bounds__(192, 1)
   const int nt = run.ntiles;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < B_N; ++i) mbar_init(&bars[i], i == B_P ? 4 : 1);
+    for (int i = 0; i < B_N; ++i) mbar_init(&bars[i], (i == B_P0 || i == B_P1) ? 4 : 1);
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&tq);
@@ -151,25 +182,29 @@ __global__ void __launch_bounds__(192, 1)
         // P_j V_j. Its score buffer held S_{j-1}, which the softmax warps
         // finished with before P_{j-1} (waited for last iteration).
         if (j + 1 < nt && !issue_s(j + 1)) break;
-        if (!mbar_wait(&bars[B_P], j & 1, abort_flag, g.status) ||
+        // P_j sits in slot j & 1 (the only slot with PLO).
+        const int slot = NPS == 2 ? b : 0;
+        const uint32_t p_par = NPS == 2 ? (j >> 1) & 1 : j & 1;
+        if (!mbar_wait(&bars[B_P0 + slot], p_par, abort_flag, g.status) ||
             !mbar_wait(&bars[B_V0 + b], (j >> 1) & 1, abort_flag, g.status))
           break;
         tc_fence_after();
+        const uint8_t* pj = ps + slot * PSB;
 #pragma unroll
         for (int kk = 0; kk < FA_KEYS / 16; ++kk) {
-          const uint64_t pa = sw128_desc(ps) + 2 * kk;
+          const uint64_t pa = sw128_desc(pj) + 2 * kk;
           const uint64_t vb = sw128_mn_desc(vs(b) + kk * 2048, FA_KVCH);
           umma_f16(tmem + FA_TMEM_O, pa, vb, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
         if constexpr (PLO) {
 #pragma unroll
           for (int kk = 0; kk < FA_KEYS / 16; ++kk) {
-            const uint64_t pa = sw128_desc(ps + FA_P_BYTES) + 2 * kk;
+            const uint64_t pa = sw128_desc(pj + FA_P_BYTES) + 2 * kk;
             const uint64_t vb = sw128_mn_desc(vs(b) + kk * 2048, FA_KVCH);
             umma_f16(tmem + FA_TMEM_O, pa, vb, idesc_o, 1u);
           }
         }
-        umma_commit(&bars[B_O]);
+        umma_commit(&bars[B_O0 + b]);
         umma_commit(&bars[B_VF0 + b]);
       }
     }
@@ -220,20 +255,21 @@ __global__ void __launch_bounds__(192, 1)
           s[32 + c] = __uint_as_float(raw1[c]);
         }
       }
-      // A tile is usually wholly visible or wholly hidden for a row; mask
-      // element by element only in between. Eight independent partial
+      // Mask with the row's visible keys as a 64-bit set: one branch-free
+      // path for rows that see all, some or none of the tile (per-row
+      // branches made the warp run every path). Eight independent partial
       // maxima and sums keep the one warp per sub-partition issuing.
-      const bool full = (ca0 == 0 && ca1 == FA_KEYS) || (cb0 == 0 && cb1 == FA_KEYS);
-      const bool none = ca0 == ca1 && cb0 == cb1;
-      if (!full && !none) {
+      {
+        const uint64_t vis = key_bits(ca0, ca1) | key_bits(cb0, cb1);
+        const uint32_t vlo = static_cast<uint32_t>(vis), vhi = static_cast<uint32_t>(vis >> 32);
 #pragma unroll
         for (int c = 0; c < FA_KEYS; ++c) {
-          const bool vis = (c >= ca0 && c < ca1) || (c >= cb0 && c < cb1);
-          s[c] = vis ? s[c] : -INFINITY;
+          const uint32_t w = c < 32 ? vlo : vhi;
+          s[c] = ((w >> (c & 31)) & 1u) ? s[c] : -INFINITY;
         }
       }
-      float mt = -INFINITY;
-      if (!none) {
+      float mt;
+      {
         float mx[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) mx[e] = s[e];
@@ -247,34 +283,47 @@ __global__ void __launch_bounds__(192, 1)
       if (mt > m_ref + kTau) {
         // O holds earlier tiles only when the old reference was finite.
         rescale = m_ref != -INFINITY;
-        alpha = rescale ? exp2f((m_ref - mt) * kLog2e) : 0.f;
+        alpha = rescale ? fa_exp2((m_ref - mt) * kLog2e) : 0.f;
         m_ref = mt;
       }
       float sum = 0.f;
-      if (none || m_ref == -INFINITY) {
+      if (m_ref == -INFINITY) {
 #pragma unroll
         for (int c = 0; c < FA_KEYS; ++c) s[c] = 0.f;
       } else {
         // exp2(-inf) = 0 for the masked keys.
         const float mb = m_ref * kLog2e;
-        float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        float psum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < FA_KEYS; ++c) {
-          s[c] = exp2f(fmaf(s[c], kLog2e, -mb));
-          ps[c & 7] += s[c];
+          s[c] = fa_exp2(fmaf(s[c], kLog2e, -mb));
+          psum[c & 7] += s[c];
         }
-        sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+        sum = ((psum[0] + psum[1]) + (psum[2] + psum[3])) +
+              ((psum[4] + psum[5]) + (psum[6] + psum[7]));
       }
       l = l * alpha + sum;
-      // The previous P.V is done: its P buffer is free and O is stable.
-      if (j > 0) {
-        if (!warp_wait(&bars[B_O], (j - 1) & 1, abort_flag, g.status, lane)) {
+      // Rescaling O needs P_{j-1} V_{j-1} done; with one P slot, so does
+      // writing P_j. (That barrier's next phase needs P_{j+1}: no parity
+      // alias.)
+      const bool any_rescale = __any_sync(0xffffffffu, rescale);
+      if (j > 0 && (any_rescale || NPS == 1)) {
+        if (!warp_wait(&bars[B_O0 + ((j - 1) & 1)], ((j - 1) >> 1) & 1, abort_flag, g.status,
+                       lane)) {
           ok = false;
           break;
         }
         tc_fence_after();
       }
-      if (__any_sync(0xffffffffu, rescale)) {
+      // With two slots, slot j & 1 is free once P_{j-2} V_{j-2} is done.
+      if (NPS == 2 && j >= 2) {
+        if (!warp_wait(&bars[B_O0 + (j & 1)], ((j - 2) >> 1) & 1, abort_flag, g.status, lane)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      if (any_rescale) {
         const float f = rescale ? alpha : 1.0f;
 #pragma unroll 1
         for (int c = 0; c < FA_HD / 32; ++c) {
@@ -289,6 +338,8 @@ __global__ void __launch_bounds__(192, 1)
       }
       // P (and, with PLO, what f16 missed of it) K-major with the 128-byte
       // swizzle: 16-byte piece pw holds keys 8 pw .. 8 pw + 7.
+      const int slot = NPS == 2 ? (j & 1) : 0;
+      uint8_t* pj = ps + slot * PSB;
 #pragma unroll
       for (int pw = 0; pw < FA_KEYS / 8; ++pw) {
         uint32_t hi[4], lo[4];
@@ -304,34 +355,57 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
         const uint32_t off = r * 128 + ((pw ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(ps + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(pj + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
         if constexpr (PLO)
-          *reinterpret_cast<uint4*>(ps + FA_P_BYTES + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          *reinterpret_cast<uint4*>(pj + FA_P_BYTES + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
       }
       fence_proxy_async();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[B_P]);
+      if (lane == 0) mbar_arrive(&bars[B_P0 + slot]);
     }
-    if (ok && warp_wait(&bars[B_O], (nt - 1) & 1, abort_flag, g.status, lane)) {
+    if (ok && warp_wait(&bars[B_O0 + ((nt - 1) & 1)], ((nt - 1) >> 1) & 1, abort_flag, g.status,
+                        lane)) {
       tc_fence_after();
-      const int head = kvh * g.hpg + (r % g.hpg);
-      __half* orow = g.out + (static_cast<size_t>(tok) * g.heads + head) * FA_HD;
+      // out = O / l as f16, staged in the Q buffer (every S MMA is done):
+      // row r at r * 512 bytes, its 16-byte piece p at slot p ^ (r & 7), so
+      // neither the writes (a row per lane) nor the reads (a row per warp)
+      // conflict. Then each warp stores its 32 rows, 512 contiguous bytes
+      // per instruction.
+      uint8_t* stage = qs;
       const float inv = l > 0.f ? 1.0f / l : 0.f;
 #pragma unroll 1
       for (int c = 0; c < FA_HD / 32; ++c) {
         float o[32];
         tmem_ld32(trow + FA_TMEM_O + c * 32, o);
-        if (!valid) continue;
 #pragma unroll
-        for (int e = 0; e < 32; e += 8) {
+        for (int e = 0; e < 4; ++e) {
           uint32_t w4[4];
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const __half2 h = __floats2half2_rn(o[e + 2 * q] * inv, o[e + 2 * q + 1] * inv);
+            const __half2 h =
+                __floats2half2_rn(o[8 * e + 2 * q] * inv, o[8 * e + 2 * q + 1] * inv);
             w4[q] = *reinterpret_cast<const uint32_t*>(&h);
           }
-          *reinterpret_cast<uint4*>(orow + c * 32 + e) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          const int piece = 4 * c + e;
+          *reinterpret_cast<uint4*>(stage + r * 512 + ((piece ^ (r & 7)) << 4)) =
+              make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+      }
+      __syncwarp();
+      // Row 32 q4 + i is head hh of run token rt (counted along, no division
+      // per row).
+      int rt = (32 * q4) / g.hpg, hh = (32 * q4) % g.hpg;
+      for (int i = 0; i < 32; ++i) {
+        if (rt >= run.ntok || rt >= tok_per_tile) break;  // later rows are past the run too
+        const int row = 32 * q4 + i;
+        const uint4 v = *reinterpret_cast<const uint4*>(stage + row * 512 + ((lane ^ (row & 7)) << 4));
+        __half* orow =
+            g.out + (static_cast<size_t>(run.tok0 + rt) * g.heads + kvh * g.hpg + hh) * FA_HD;
+        *reinterpret_cast<uint4*>(orow + lane * 8) = v;
+        if (++hh == g.hpg) {
+          hh = 0;
+          ++rt;
         }
       }
     }

@@ -41,9 +41,10 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  // Ring + alignment slack + barriers, and 2 KB the epilogue may stage its
-  // per-column constants in (the q / k norm weights of kEpiQkPrep).
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + 2048;
+  // Ring + alignment slack + barriers, 2 KB the epilogue may stage its
+  // per-column constants in (the q / k norm weights of kEpiQkPrep), and a
+  // 4 KB row-staging slot per epilogue warp.
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + 2048 + 4 * 4096;
   // Two accumulators: the epilogue drains one while the MMAs fill the other.
   static constexpr uint32_t TMEM_COLS = 2 * BN;
 };
@@ -93,6 +94,63 @@ __device__ __forceinline__ void store_f16x32(__half* o, const float (&v)[32], in
     for (int j = 0; j < 32; ++j)
       if (col0 + j < n_out) o[j] = __float2half_rn(v[j]);
   }
+}
+
+__device__ __forceinline__ uint4 pack_f16x8(const float* v) {
+  const __half2 h0 = __floats2half2_rn(v[0], v[1]);
+  const __half2 h1 = __floats2half2_rn(v[2], v[3]);
+  const __half2 h2 = __floats2half2_rn(v[4], v[5]);
+  const __half2 h3 = __floats2half2_rn(v[6], v[7]);
+  return make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
+                    *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
+}
+
+__device__ __forceinline__ uint4 pack_f32x4(const float* v) {
+  return make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]),
+                    __float_as_uint(v[3]));
+}
+
+// Row staging for coalesced epilogue stores. Lane i of an epilogue warp owns
+// row i of the warp's 32 rows and 128 bytes of it (eight 16-byte pieces);
+// piece p of row r sits at r * 128 + (p ^ (r & 7)) * 16 of the warp's 4 KB
+// slot, so neither the writes (a row per lane) nor the reads (a row per 8
+// lanes) conflict on banks.
+__device__ __forceinline__ void stage_pieces(uint8_t* slot, int lane, int first, const uint4* pc,
+                                             int n) {
+#pragma unroll
+  for (int i = 0; i < n; ++i)
+    *reinterpret_cast<uint4*>(slot + lane * 128 + (((first + i) ^ (lane & 7)) << 4)) = pc[i];
+}
+
+// Store the staged 32 x 128 bytes: row r to base + r * stride, rows
+// >= nrows skipped; four full 128-byte row segments per instruction.
+__device__ __forceinline__ void flush_rows(uint8_t* slot, int lane, uint8_t* base, size_t stride,
+                                           int nrows) {
+  __syncwarp();
+  const int p = lane & 7;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = 4 * i + (lane >> 3);
+    const uint4 v = *reinterpret_cast<const uint4*>(slot + r * 128 + ((p ^ (r & 7)) << 4));
+    if (r < nrows) *reinterpret_cast<uint4*>(base + r * stride + p * 16) = v;
+  }
+  __syncwarp();
+}
+
+// The same with two destinations: pieces 0-3 of row r (64 bytes) to
+// base_lo + r * stride, pieces 4-7 to base_hi + r * stride.
+__device__ __forceinline__ void flush_rows_split(uint8_t* slot, int lane, uint8_t* base_lo,
+                                                 uint8_t* base_hi, size_t stride, int nrows) {
+  __syncwarp();
+  const int p = lane & 7;
+  uint8_t* base = p < 4 ? base_lo + p * 16 : base_hi + (p - 4) * 16;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = 4 * i + (lane >> 3);
+    const uint4 v = *reinterpret_cast<const uint4*>(slot + r * 128 + ((p ^ (r & 7)) << 4));
+    if (r < nrows) *reinterpret_cast<uint4*>(base + r * stride) = v;
+  }
+  __syncwarp();
 }
 
 // Persistent: CTA b handles tiles b, b + gridDim.x, ... Tile t is
@@ -225,41 +283,64 @@ __global__ void __launch_bounds__(192, 1)
       if (!ok) break;
       tc_fence_after();
       const int row = m_tile * BM + q * 32 + lane;
+      const int row0 = m_tile * BM + q * 32;   // this warp's first row
+      const int nrows = min(32, g.m - row0);   // its rows below m (may be <= 0)
+      uint8_t* slot = reinterpret_cast<uint8_t*>(full) + 256 + 2048 + q * 4096;
       const uint32_t tbase =
           tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BN);
       if constexpr (EPI == kEpiF32) {
-        float* obase = static_cast<float*>(g.out) + split * g.split_stride +
-                       static_cast<size_t>(row) * g.ldo;
+        float* wbase = static_cast<float*>(g.out) + split * g.split_stride +
+                       static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           float v[32];
           tmem_ld32(tbase + c * 32, v);
           const int col0 = n_tile * BN + c * 32;
-          if (row < g.m && col0 < g.n_out) {
-            float* o = obase + col0;
-            if (col0 + 32 <= g.n_out) {
+          if (nrows <= 0 || col0 >= g.n_out) continue;
+          if (col0 + 32 <= g.n_out) {
+            uint4 pc[8];
 #pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            } else {
+            for (int i = 0; i < 8; ++i) pc[i] = pack_f32x4(v + 4 * i);
+            stage_pieces(slot, lane, 0, pc, 8);
+            flush_rows(slot, lane, reinterpret_cast<uint8_t*>(wbase + col0),
+                       static_cast<size_t>(g.ldo) * 4, nrows);
+          } else if (lane < nrows) {
+            float* o = wbase + static_cast<size_t>(lane) * g.ldo + col0;
 #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < g.n_out) o[j] = v[j];
-            }
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < g.n_out) o[j] = v[j];
           }
         }
       } else if constexpr (EPI == kEpiF16) {
-        __half* obase = static_cast<__half*>(g.out) + static_cast<size_t>(row) * g.ldo;
+        __half* wbase =
+            static_cast<__half*>(g.out) + static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          tmem_ld32(tbase + c * 32, v);
+        for (int c = 0; c < BN / 32; c += 2) {
+          float lo[32], hi[32];
+          tmem_ld32(tbase + c * 32, lo);
+          tmem_ld32(tbase + (c + 1) * 32, hi);
           const int col0 = n_tile * BN + c * 32;
-          if (row < g.m && col0 < g.n_out) store_f16x32(obase + col0, v, col0, g.n_out);
+          if (nrows <= 0 || col0 >= g.n_out) continue;
+          if (col0 + 64 <= g.n_out) {
+            uint4 pc[8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              pc[i] = pack_f16x8(lo + 8 * i);
+              pc[4 + i] = pack_f16x8(hi + 8 * i);
+            }
+            stage_pieces(slot, lane, 0, pc, 8);
+            flush_rows(slot, lane, reinterpret_cast<uint8_t*>(wbase + col0),
+                       static_cast<size_t>(g.ldo) * 2, nrows);
+          } else if (lane < nrows) {
+            __half* o = wbase + static_cast<size_t>(lane) * g.ldo;
+            store_f16x32(o + col0, lo, col0, g.n_out);
+            if (col0 + 32 < g.n_out) store_f16x32(o + col0 + 32, hi, col0 + 32, g.n_out);
+          }
         }
       } else if constexpr (EPI == kEpiRopeF16) {
         // 64-dim heads: columns c and c + 32 of a head form a rotation pair.
-        __half* obase = static_cast<__half*>(g.out) + static_cast<size_t>(row) * g.ldo;
+        __half* wbase =
+            static_cast<__half*>(g.out) + static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
         // Table [pair][position]: the rows of a tile are mostly consecutive
         // positions, so a warp's reads of one pair are contiguous.
         const int p = row < g.m ? g.epi.pos[row] : 0;
@@ -271,74 +352,121 @@ __global__ void __launch_bounds__(192, 1)
           tmem_ld32(tbase + c * 32, lo);
           tmem_ld32(tbase + (c + 1) * 32, hi);
           const int col0 = n_tile * BN + c * 32;
-          if (row < g.m && col0 < g.n_out) {
-            if (col0 < 2 * g.epi.q_cols) {
-              const float sc = col0 < g.epi.q_cols ? g.epi.q_scale : 1.0f;
+          if (nrows <= 0 || col0 >= g.n_out) continue;
+          if (col0 < 2 * g.epi.q_cols) {
+            const float sc = col0 < g.epi.q_cols ? g.epi.q_scale : 1.0f;
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const float2 cs = rt[j * rs];
-                const float a = lo[j], b = hi[j];
-                lo[j] = (a * cs.x - b * cs.y) * sc;
-                hi[j] = (b * cs.x + a * cs.y) * sc;
-              }
+            for (int j = 0; j < 32; ++j) {
+              const float2 cs = rt[j * rs];
+              const float a = lo[j], b = hi[j];
+              lo[j] = (a * cs.x - b * cs.y) * sc;
+              hi[j] = (b * cs.x + a * cs.y) * sc;
             }
-            store_f16x32(obase + col0, lo, col0, g.n_out);
-            store_f16x32(obase + col0 + 32, hi, col0 + 32, g.n_out);
+          }
+          if (col0 + 64 <= g.n_out) {
+            uint4 pc[8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              pc[i] = pack_f16x8(lo + 8 * i);
+              pc[4 + i] = pack_f16x8(hi + 8 * i);
+            }
+            stage_pieces(slot, lane, 0, pc, 8);
+            flush_rows(slot, lane, reinterpret_cast<uint8_t*>(wbase + col0),
+                       static_cast<size_t>(g.ldo) * 2, nrows);
+          } else if (lane < nrows) {
+            __half* o = wbase + static_cast<size_t>(lane) * g.ldo;
+            store_f16x32(o + col0, lo, col0, g.n_out);
+            if (col0 + 32 < g.n_out) store_f16x32(o + col0 + 32, hi, col0 + 32, g.n_out);
           }
         }
       } else if constexpr (EPI == kEpiBiasF16 || EPI == kEpiBiasReluF16) {
-        __half* obase = static_cast<__half*>(g.out) + static_cast<size_t>(row) * g.ldo;
+        __half* wbase =
+            static_cast<__half*>(g.out) + static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          tmem_ld32(tbase + c * 32, v);
+        for (int c = 0; c < BN / 32; c += 2) {
+          float v[2][32];
+          tmem_ld32(tbase + c * 32, v[0]);
+          tmem_ld32(tbase + (c + 1) * 32, v[1]);
           const int col0 = n_tile * BN + c * 32;
-          if (row < g.m && col0 < g.n_out) {
+          if (nrows <= 0 || col0 >= g.n_out) continue;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              const float b = col0 + j < g.n_out ? g.epi.bias[col0 + j] : 0.f;
-              v[j] += b;
-              if constexpr (EPI == kEpiBiasReluF16) v[j] = fmaxf(v[j], 0.f);
+              const int col = col0 + 32 * h + j;
+              const float b = col < g.n_out ? g.epi.bias[col] : 0.f;
+              v[h][j] += b;
+              if constexpr (EPI == kEpiBiasReluF16) v[h][j] = fmaxf(v[h][j], 0.f);
             }
-            store_f16x32(obase + col0, v, col0, g.n_out);
+          }
+          if (col0 + 64 <= g.n_out) {
+            uint4 pc[8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              pc[i] = pack_f16x8(v[0] + 8 * i);
+              pc[4 + i] = pack_f16x8(v[1] + 8 * i);
+            }
+            stage_pieces(slot, lane, 0, pc, 8);
+            flush_rows(slot, lane, reinterpret_cast<uint8_t*>(wbase + col0),
+                       static_cast<size_t>(g.ldo) * 2, nrows);
+          } else if (lane < nrows) {
+            __half* o = wbase + static_cast<size_t>(lane) * g.ldo;
+            store_f16x32(o + col0, v[0], col0, g.n_out);
+            if (col0 + 32 < g.n_out) store_f16x32(o + col0 + 32, v[1], col0 + 32, g.n_out);
           }
         }
       } else if constexpr (EPI == kEpiResidF32) {
         // Each output element belongs to one tile (no split-K), so the
-        // read-modify-write of the residual row is race-free. The bias chunk
-        // is read into registers before the row is touched, so no bias load
-        // waits behind a store to the (possibly aliasing) residual row.
-        float* __restrict__ obase = static_cast<float*>(g.out) + static_cast<size_t>(row) * g.ldo;
+        // read-modify-write of the residual row is race-free. The accumulator
+        // chunk is staged by row; then each lane updates 16 bytes of four
+        // rows per step (a row segment per 8 lanes). Its bias values are read
+        // before any row is touched, so no bias load waits behind a store to
+        // the (possibly aliasing) residual row.
+        float* __restrict__ wbase =
+            static_cast<float*>(g.out) + static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
         const float* __restrict__ bias = g.epi.bias;
         const bool bias_first = g.epi.bias_first != 0;
+        const int pc4 = lane & 7;  // this lane's 4 columns of a chunk: 4 pc4 .. 4 pc4 + 3
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
-          float v[32], b[32];
+          float v[32];
           const int col0 = n_tile * BN + c * 32;
+          float bl[4];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) b[j] = (bias && col0 + j < g.n_out) ? __ldg(bias + col0 + j) : 0.f;
+          for (int e = 0; e < 4; ++e) {
+            const int col = col0 + 4 * pc4 + e;
+            bl[e] = (bias && col < g.n_out) ? __ldg(bias + col) : 0.f;
+          }
           tmem_ld32(tbase + c * 32, v);
-          if (row < g.m && col0 < g.n_out) {
-            float* __restrict__ o = obase + col0;
-            if (col0 + 32 <= g.n_out) {
-              float4 xv[8];
+          if (nrows <= 0 || col0 >= g.n_out) continue;
+          if (col0 + 32 <= g.n_out) {
+            uint4 pc[8];
 #pragma unroll
-              for (int q = 0; q < 8; ++q) xv[q] = *reinterpret_cast<const float4*>(o + 4 * q);
+            for (int i = 0; i < 8; ++i) pc[i] = pack_f32x4(v + 4 * i);
+            stage_pieces(slot, lane, 0, pc, 8);
+            __syncwarp();
 #pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                float* x = reinterpret_cast<float*>(&xv[q]);
+            for (int i = 0; i < 8; ++i) {
+              const int r = 4 * i + (lane >> 3);
+              if (r >= nrows) continue;
+              const float4 a = *reinterpret_cast<const float4*>(slot + r * 128 + ((pc4 ^ (r & 7)) << 4));
+              float* __restrict__ o = wbase + static_cast<size_t>(r) * g.ldo + col0 + 4 * pc4;
+              float4 x = *reinterpret_cast<const float4*>(o);
+              const float av[4] = {a.x, a.y, a.z, a.w};
+              float* xe = reinterpret_cast<float*>(&x);
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const int j = 4 * q + e;
-                  x[e] = bias_first ? (v[j] + b[j]) + x[e] : (x[e] + v[j]) + b[j];
-                }
-                *reinterpret_cast<float4*>(o + 4 * q) = xv[q];
-              }
-            } else {
+              for (int e = 0; e < 4; ++e)
+                xe[e] = bias_first ? (av[e] + bl[e]) + xe[e] : (xe[e] + av[e]) + bl[e];
+              *reinterpret_cast<float4*>(o) = x;
+            }
+            __syncwarp();
+          } else if (lane < nrows) {
+            float* __restrict__ o = wbase + static_cast<size_t>(lane) * g.ldo + col0;
 #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < g.n_out)
-                  o[j] = bias_first ? (v[j] + b[j]) + o[j] : (o[j] + v[j]) + b[j];
+            for (int j = 0; j < 32; ++j) {
+              if (col0 + j >= g.n_out) continue;
+              const float b = bias ? __ldg(bias + col0 + j) : 0.f;
+              o[j] = bias_first ? (v[j] + b) + o[j] : (o[j] + v[j]) + b;
             }
           }
         }
@@ -354,6 +482,19 @@ __global__ void __launch_bounds__(192, 1)
         const bool is_q = h < q.heads;
         const bool is_v = h >= q.heads + q.kv_heads;
         const bool ok_row = row < g.m;
+        const int crow = q.base + (ok_row ? row : 0);
+        // Table [pair][position]: consecutive rows read consecutive entries.
+        // Each chunk's 32 entries are requested a step ahead of their use
+        // (chunk 0's before the sum of squares), so their latency overlaps
+        // other work.
+        const float2* rt = q.rope + (ok_row ? q.meta[crow].pos : 0);
+        const size_t rs = static_cast<size_t>(q.rope_stride);
+        const int half_rot = q.rope_dims / 2;
+        float2 cs[32];
+        if (!is_v && 0 < half_rot) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) cs[j] = rt[static_cast<size_t>(j) * rs];
+        }
         float ssp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
         for (int c = 0; c < 8; ++c) {
@@ -364,30 +505,28 @@ __global__ void __launch_bounds__(192, 1)
         }
         const float ss = ((ssp[0] + ssp[1]) + (ssp[2] + ssp[3])) + ((ssp[4] + ssp[5]) + (ssp[6] + ssp[7]));
         const float inv = (is_v && !q.v_norm) ? 1.0f : rsqrtf(ss / 256.0f + q.eps);
-        const int crow = q.base + (ok_row ? row : 0);
-        __half* orow;
-        if (is_q)
-          orow = q.q16 + static_cast<size_t>(ok_row ? row : 0) * q.heads * 256 + h * 256;
-        else
-          orow = q.kv + static_cast<size_t>(crow) * 2 * q.kv_heads * 256 + (h - q.heads) * 256;
+        // This warp's first output row (rows are contiguous in both targets).
+        const int wrow = row0 > 0 ? row0 : 0;
+        uint8_t* wbase;
+        size_t wstride;
+        if (is_q) {
+          wbase = reinterpret_cast<uint8_t*>(q.q16 + static_cast<size_t>(wrow) * q.heads * 256 + h * 256);
+          wstride = static_cast<size_t>(q.heads) * 256 * 2;
+        } else {
+          wbase = reinterpret_cast<uint8_t*>(
+              q.kv + static_cast<size_t>(q.base + wrow) * 2 * q.kv_heads * 256 + (h - q.heads) * 256);
+          wstride = static_cast<size_t>(2 * q.kv_heads) * 256 * 2;
+        }
         const float* wn = epi_consts + (is_q ? 0 : 256);
-        // Table [pair][position]: consecutive rows read consecutive entries.
-        const float2* rt = q.rope + (ok_row ? q.meta[crow].pos : 0);
-        const size_t rs = static_cast<size_t>(q.rope_stride);
         const float scale = is_q ? q.q_scale : 1.0f;
-        const int half_rot = q.rope_dims / 2;
+        // Dims d and d + 128 rotate together: chunk c of each half per step,
+        // both staged by row and stored as two 64-byte row segments.
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           float a[32], b[32];
-          float2 cs[32];
           const bool rot = !is_v && c * 32 < half_rot;
-          if (rot) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) cs[j] = rt[static_cast<size_t>(c * 32 + j) * rs];
-          }
           tmem_ld32(tbase + c * 32, a);
           tmem_ld32(tbase + (c + 4) * 32, b);
-          if (!ok_row) continue;
           if (is_v) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
@@ -410,25 +549,48 @@ __global__ void __launch_bounds__(192, 1)
               b[j] = y2 * scale;
             }
           }
-          store_f16x32(orow + c * 32, a, 0, 32);
-          store_f16x32(orow + 128 + c * 32, b, 0, 32);
+          uint4 pc[8];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            pc[i] = pack_f16x8(a + 8 * i);
+            pc[4 + i] = pack_f16x8(b + 8 * i);
+          }
+          if (c + 1 < 4 && !is_v && (c + 1) * 32 < half_rot) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) cs[j] = rt[static_cast<size_t>((c + 1) * 32 + j) * rs];
+          }
+          if (nrows > 0) {
+            stage_pieces(slot, lane, 0, pc, 8);
+            flush_rows_split(slot, lane, wbase + c * 64, wbase + 256 + c * 64, wstride, nrows);
+          }
         }
       } else {
         // GeGLU: accumulator columns 0..127 hold the gate products, 128..255
         // the up products of the same 128 output columns.
         static_assert(BN == 256, "GeGLU tiles pair 128 gate rows with 128 up rows");
-        __half* obase = static_cast<__half*>(g.out) + static_cast<size_t>(row) * g.ldo;
+        __half* wbase =
+            static_cast<__half*>(g.out) + static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           float gv[32], uv[32];
           tmem_ld32(tbase + c * 32, gv);
           tmem_ld32(tbase + 128 + c * 32, uv);
-          const int col0 = n_tile * 128 + c * 32;
-          if (row < g.m && col0 < g.n_out) {
+          const int col0 = n_tile * 128 + (c & ~1) * 32;  // first column of this chunk pair
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              gv[j] = ((EPI == kEpiGeGluTanh) ? gelu_tanh(gv[j]) : gelu_erf(gv[j])) * uv[j];
-            store_f16x32(obase + col0, gv, col0, g.n_out);
+          for (int j = 0; j < 32; ++j)
+            gv[j] = ((EPI == kEpiGeGluTanh) ? gelu_tanh(gv[j]) : gelu_erf(gv[j])) * uv[j];
+          if (nrows <= 0 || col0 >= g.n_out) continue;
+          if (col0 + 64 <= g.n_out) {
+            uint4 pc[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) pc[i] = pack_f16x8(gv + 8 * i);
+            stage_pieces(slot, lane, (c & 1) * 4, pc, 4);
+            if (c & 1)
+              flush_rows(slot, lane, reinterpret_cast<uint8_t*>(wbase + col0),
+                         static_cast<size_t>(g.ldo) * 2, nrows);
+          } else if (lane < nrows) {
+            const int cc = col0 + (c & 1) * 32;
+            if (cc < g.n_out) store_f16x32(wbase + static_cast<size_t>(lane) * g.ldo + cc, gv, cc, g.n_out);
           }
         }
       }

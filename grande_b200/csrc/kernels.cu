@@ -360,103 +360,182 @@ __global__ void pl_gate_kernel(const float* __restrict__ g, const float* __restr
 
 // ---- logits at readout rows (logits.wgsl) ----------------------------------
 
-// Element k (k % 4 == 0) and the three after it of vocab row v as f32
-// (QTensor::get): Q4 blocks hold elements 0..15 in the low nibbles of their
-// 16 bytes and 16..31 in the high nibbles.
+// One 32-element block of a table row as stored (model.rs:338-371): its codes
+// and its scale.
 template <int DT>
-__device__ __forceinline__ float4 load4_f32(const uint8_t* __restrict__ codes,
-                                            const uint8_t* __restrict__ scales, size_t v, int nb,
-                                            int k) {
-  const size_t gb = v * nb + (k >> 5);
-  const int e = k & 31;
+struct RawBlock {
+  uint4 c[DT == kF16 ? 4 : (DT == kQ8 ? 2 : 1)];
+  float scale;
+};
+
+template <int DT>
+__device__ __forceinline__ void load_raw_block(const uint8_t* __restrict__ codes,
+                                               const uint8_t* __restrict__ scales, size_t gb,
+                                               bool ok, RawBlock<DT>& r) {
+  constexpr int NC = DT == kF16 ? 4 : (DT == kQ8 ? 2 : 1);
+  if (!ok) {
+#pragma unroll
+    for (int i = 0; i < NC; ++i) r.c[i] = make_uint4(0u, 0u, 0u, 0u);
+    r.scale = 0.f;
+    return;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(codes + gb * (NC * 16));
+#pragma unroll
+  for (int i = 0; i < NC; ++i) r.c[i] = src[i];
   if constexpr (DT == kF16) {
-    const uint2 q = *reinterpret_cast<const uint2*>(codes + (gb * 32 + e) * 2);
-    const __half2 a = *reinterpret_cast<const __half2*>(&q.x);
-    const __half2 b = *reinterpret_cast<const __half2*>(&q.y);
-    const float2 fa = __half22float2(a), fb = __half22float2(b);
-    return make_float4(fa.x, fa.y, fb.x, fb.y);
+    r.scale = 1.f;
   } else {
-    const uint16_t sb =
-        static_cast<uint16_t>(scales[2 * gb]) | (static_cast<uint16_t>(scales[2 * gb + 1]) << 8);
-    const float dq = half_bits_to_float(sb);
-    if constexpr (DT == kQ8) {
-      const uint32_t q = *reinterpret_cast<const uint32_t*>(codes + gb * 32 + e);
-      return make_float4(static_cast<float>(static_cast<int8_t>(q & 0xff)) * dq,
-                         static_cast<float>(static_cast<int8_t>((q >> 8) & 0xff)) * dq,
-                         static_cast<float>(static_cast<int8_t>((q >> 16) & 0xff)) * dq,
-                         static_cast<float>(static_cast<int8_t>(q >> 24)) * dq);
-    } else {
-      const uint32_t q = *reinterpret_cast<const uint32_t*>(codes + gb * 16 + (e & 15));
-      const int sh = e < 16 ? 0 : 4;
-      return make_float4((static_cast<float>((q >> sh) & 0xf) - 8.0f) * dq,
-                         (static_cast<float>((q >> (8 + sh)) & 0xf) - 8.0f) * dq,
-                         (static_cast<float>((q >> (16 + sh)) & 0xf) - 8.0f) * dq,
-                         (static_cast<float>((q >> (24 + sh)) & 0xf) - 8.0f) * dq);
-    }
+    const uint16_t sb = *reinterpret_cast<const uint16_t*>(scales + 2 * gb);
+    r.scale = half_bits_to_float(sb);
   }
 }
 
-constexpr int kLogitsVocab = 4;   // vocab rows per warp at once
+// Elements 4 j .. 4 j + 3 of a block as f32 (QTensor::get, model.rs:508-525):
+// Q4 blocks hold elements 0..15 in the low nibbles of their 16 bytes and
+// 16..31 in the high nibbles.
+template <int DT, int J>
+__device__ __forceinline__ float4 raw_chunk(const RawBlock<DT>& r) {
+  if constexpr (DT == kF16) {
+    const uint4 q = r.c[J / 2];
+    const uint32_t lo = (J & 1) ? q.z : q.x, hi = (J & 1) ? q.w : q.y;
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&lo));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hi));
+    return make_float4(a.x, a.y, b.x, b.y);
+  } else if constexpr (DT == kQ8) {
+    // Code c as (c + 128) in the mantissa of 2^23, less 2^23 + 128: c exactly,
+    // with integer and add instructions instead of the conversion unit.
+    const uint4 q = r.c[J / 4];
+    const uint32_t w = ((J & 3) == 0 ? q.x : (J & 3) == 1 ? q.y : (J & 3) == 2 ? q.z : q.w) ^
+                       0x80808080u;
+    return make_float4((__uint_as_float(0x4B000000u | (w & 0xff)) - 8388736.0f) * r.scale,
+                       (__uint_as_float(0x4B000000u | ((w >> 8) & 0xff)) - 8388736.0f) * r.scale,
+                       (__uint_as_float(0x4B000000u | ((w >> 16) & 0xff)) - 8388736.0f) * r.scale,
+                       (__uint_as_float(0x4B000000u | (w >> 24)) - 8388736.0f) * r.scale);
+  } else {
+    // Nibble q in the mantissa of 2^23, less 2^23 + 8: q - 8 exactly.
+    const uint4 q = r.c[0];
+    const uint32_t w = (J & 3) == 0 ? q.x : (J & 3) == 1 ? q.y : (J & 3) == 2 ? q.z : q.w;
+    constexpr int sh = J < 4 ? 0 : 4;
+    return make_float4(
+        (__uint_as_float(0x4B000000u | ((w >> sh) & 0xf)) - 8388616.0f) * r.scale,
+        (__uint_as_float(0x4B000000u | ((w >> (8 + sh)) & 0xf)) - 8388616.0f) * r.scale,
+        (__uint_as_float(0x4B000000u | ((w >> (16 + sh)) & 0xf)) - 8388616.0f) * r.scale,
+        (__uint_as_float(0x4B000000u | ((w >> (24 + sh)) & 0xf)) - 8388616.0f) * r.scale);
+  }
+}
+
 constexpr int kLogitsRows = 12;   // readout rows per pass over the table
 
-// logits.wgsl in f32: out[r, v] = sum_k rows[r, k] * W[v, k] (+ the host
-// softcap). A warp takes kLogitsVocab vocab rows against up to kLogitsRows
-// readout rows staged in shared memory; lane l owns elements 4 l + 128 i,
-// so each readout float4 it reads from shared memory serves kLogitsVocab
-// rows of the table and a warp's reads are conflict-free. d % 32 == 0.
 template <int DT>
-__global__ void __launch_bounds__(256) logits_kernel(const float* __restrict__ rows, int nrows,
+constexpr int logits_group() {
+  return DT == kF16 ? 2 : 4;  // vocab rows a warp takes at once
+}
+
+// logits.wgsl in f32: out[r, v] = sum_k rows[r, k] * W[v, k] (+ the host
+// softcap). A warp takes logits_group vocab rows at a time against up to
+// kLogitsRows readout rows staged in shared memory. Lane l owns blocks
+// l, l + 32, ... of each vocab row: its codes are one coalesced 16-byte
+// piece per 16 bytes of block, and the next block's codes are requested while
+// the current one is multiplied, so loads stay in flight. The readout rows'
+// 16-byte chunk j of block b sits at chunk j ^ (b & 7) of the block, so the
+// lanes' reads of one chunk are conflict-free. d % 32 == 0.
+template <int DT>
+__global__ void __launch_bounds__(256, 1) logits_kernel(const float* __restrict__ rows, int nrows,
                                                      const uint8_t* __restrict__ codes,
                                                      const uint8_t* __restrict__ scales,
                                                      int vocab, int d, float softcap,
                                                      float* __restrict__ out) {
+  constexpr int G = logits_group<DT>();
   griddep_wait();
-  extern __shared__ float xs[];  // [kLogitsRows][d]
+  extern __shared__ float4 xs4[];  // [kLogitsRows][d / 4], chunks swizzled per block
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nwarps = blockDim.x >> 5;
   const int nb = d / 32;
-  const int steps = (d + 127) / 128;
+  const int nbl = (nb + 31) / 32;  // blocks per lane
+  const int ngroups = (vocab + G - 1) / G;
+  const int gstride = gridDim.x * (blockDim.x >> 5);
+  const int d4 = d / 4;
   for (int r0 = 0; r0 < nrows; r0 += kLogitsRows) {
     const int nr = min(kLogitsRows, nrows - r0);
     __syncthreads();
-    for (int i = threadIdx.x; i < nr * d; i += blockDim.x)
-      xs[i] = rows[static_cast<size_t>(r0) * d + i];
+    {
+      const float4* src = reinterpret_cast<const float4*>(rows + static_cast<size_t>(r0) * d);
+      const int n4 = nr * d4;
+#pragma unroll 8
+      for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        const int r = i / d4, c = i - r * d4;  // chunk c of row r: block c / 8, chunk c % 8
+        xs4[r * d4 + (c & ~7) + ((c ^ (c >> 3)) & 7)] = src[i];
+      }
+    }
     __syncthreads();
-    for (int v0 = (blockIdx.x * nwarps + warp) * kLogitsVocab; v0 < vocab;
-         v0 += gridDim.x * nwarps * kLogitsVocab) {
-      float acc[kLogitsVocab][kLogitsRows];
+    int g = blockIdx.x * (blockDim.x >> 5) + warp;
+    RawBlock<DT> cur[G], nxt[G];
+    auto load = [&](RawBlock<DT>(&dst)[G], int gg, int i) {
+      const int b = lane + 32 * i;
 #pragma unroll
-      for (int u = 0; u < kLogitsVocab; ++u)
+      for (int u = 0; u < G; ++u) {
+        const int v = gg * G + u;
+        load_raw_block<DT>(codes, scales, static_cast<size_t>(v) * nb + b, b < nb && v < vocab,
+                           dst[u]);
+      }
+    };
+    if (g < ngroups) load(cur, g, 0);
+    for (; g < ngroups; g += gstride) {
+      float acc[G][kLogitsRows];
+#pragma unroll
+      for (int u = 0; u < G; ++u)
 #pragma unroll
         for (int r = 0; r < kLogitsRows; ++r) acc[u][r] = 0.f;
-#pragma unroll 2
-      for (int i = 0; i < steps; ++i) {
-        const int k = 4 * lane + 128 * i;
-        if (k >= d) continue;  // d % 32 == 0: the lane's four elements are all in or all out
-        float4 w[kLogitsVocab];
+      for (int i = 0; i < nbl; ++i) {
+        // The next (group, block) of this warp, fetched ahead.
+        const int ng = i + 1 < nbl ? g : g + gstride;
+        const int ni = i + 1 < nbl ? i + 1 : 0;
+        if (ng < ngroups) load(nxt, ng, ni);
+        const int b = lane + 32 * i;
+        const float4* xb = xs4 + (b < nb ? b : 0) * 8;
+        const int sw = b & 7;
+#define OMG_LOGITS_CHUNK(J)                                                          \
+  {                                                                                  \
+    float4 x[kLogitsRows];                                                           \
+    _Pragma("unroll") for (int r = 0; r < kLogitsRows; ++r) x[r] =                   \
+        xb[(r < nr ? r : 0) * d4 + ((J) ^ sw)];                                      \
+    float4 w[G];                                                                     \
+    _Pragma("unroll") for (int u = 0; u < G; ++u) w[u] = raw_chunk<DT, J>(cur[u]);   \
+    /* Component-major: consecutive FMAs update different accumulators. */           \
+    _Pragma("unroll") for (int r = 0; r < kLogitsRows; ++r)                          \
+        _Pragma("unroll") for (int u = 0; u < G; ++u) acc[u][r] =                    \
+            fmaf(w[u].x, x[r].x, acc[u][r]);                                         \
+    _Pragma("unroll") for (int r = 0; r < kLogitsRows; ++r)                          \
+        _Pragma("unroll") for (int u = 0; u < G; ++u) acc[u][r] =                    \
+            fmaf(w[u].y, x[r].y, acc[u][r]);                                         \
+    _Pragma("unroll") for (int r = 0; r < kLogitsRows; ++r)                          \
+        _Pragma("unroll") for (int u = 0; u < G; ++u) acc[u][r] =                    \
+            fmaf(w[u].z, x[r].z, acc[u][r]);                                         \
+    _Pragma("unroll") for (int r = 0; r < kLogitsRows; ++r)                          \
+        _Pragma("unroll") for (int u = 0; u < G; ++u) acc[u][r] =                    \
+            fmaf(w[u].w, x[r].w, acc[u][r]);                                         \
+  }
+        OMG_LOGITS_CHUNK(0)
+        OMG_LOGITS_CHUNK(1)
+        OMG_LOGITS_CHUNK(2)
+        OMG_LOGITS_CHUNK(3)
+        OMG_LOGITS_CHUNK(4)
+        OMG_LOGITS_CHUNK(5)
+        OMG_LOGITS_CHUNK(6)
+        OMG_LOGITS_CHUNK(7)
+#undef OMG_LOGITS_CHUNK
 #pragma unroll
-        for (int u = 0; u < kLogitsVocab; ++u)
-          w[u] = v0 + u < vocab ? load4_f32<DT>(codes, scales, static_cast<size_t>(v0 + u), nb, k)
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int r = 0; r < kLogitsRows; ++r) {
-          if (r < nr) {
-            const float4 x = *reinterpret_cast<const float4*>(xs + r * d + k);
-#pragma unroll
-            for (int u = 0; u < kLogitsVocab; ++u)
-              acc[u][r] += w[u].x * x.x + w[u].y * x.y + w[u].z * x.z + w[u].w * x.w;
-          }
-        }
+        for (int u = 0; u < G; ++u) cur[u] = nxt[u];
       }
 #pragma unroll
-      for (int u = 0; u < kLogitsVocab; ++u)
+      for (int u = 0; u < G; ++u)
 #pragma unroll
         for (int r = 0; r < kLogitsRows; ++r) {
           if (r < nr) {
             float z = warp_sum(acc[u][r]);
-            if (lane == 0 && v0 + u < vocab) {
+            const int v = g * G + u;
+            if (lane == 0 && v < vocab) {
               if (softcap > 0.f) z = softcap * tanhf(z / softcap);
-              out[static_cast<size_t>(r0 + r) * vocab + v0 + u] = z;
+              out[static_cast<size_t>(r0 + r) * vocab + v] = z;
             }
           }
         }
@@ -572,9 +651,10 @@ void launch_logits(int dtype, const float* rows, int nrows, const void* codes, c
   const size_t smem = static_cast<size_t>(kLogitsRows) * d * 4;
   const auto* c = static_cast<const uint8_t*>(codes);
   const auto* sc = static_cast<const uint8_t*>(scales);
-  // One sweep of the table: 4 vocab rows per warp, 8 warps per CTA.
-  (void)num_sms;
-  const int grid = (vocab + 31) / 32;
+  // Persistent sweep of the table: one CTA per SM, staging the readout rows
+  // once; 8 warps per CTA, a group of vocab rows per warp at a time.
+  const int groups = (vocab + 1) / 2;  // an upper bound for every table type
+  const int grid = std::max(1, std::min((groups + 7) / 8, num_sms > 0 ? num_sms : 148));
   if (dtype == kQ4) {
     launch_pdl(logits_kernel<kQ4>, dim3(grid), dim3(256), smem, s, rows, nrows, c, sc, vocab, d, softcap,
                out);

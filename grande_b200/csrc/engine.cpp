@@ -340,7 +340,7 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
   cap_rows_ = (capacity + 63) / 64 * 64;
   const size_t C = capacity;
   const size_t Cpad = cap_rows_;
-  const int S = 2;  // split-K slabs the f32 GEMM outputs may use
+  const int S = 4;  // split-K slabs the f32 GEMM outputs may use
 
   // Workspace. Zero-initialised, so rows a kernel reads but no pass has
   // written (padding, stale tile tails) are finite.
@@ -367,6 +367,7 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
   for (int l = 0; l < L; ++l)
     if (c.has_kv(l)) kv_[l].alloc(Cpad * 2 * c.kv_heads * c.head_dim[l] * 2);
   attn_ctas_.alloc(Cpad * sizeof(int2));
+  mlp_ready_.alloc((Cpad + 127) / 128 * S * sizeof(int));
   {
     char err[256];
     if (!attention_map_q(&attn_tq_, q16_.p, static_cast<int>(Cpad), c.heads, c.kv_heads, err,
@@ -392,9 +393,13 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
   final_norm_ = norm("final_norm");
   char err[512];
   auto plan = [&](GemmPlan* p, const void* a, int lda, const __half* w, int w_rows, int n_out,
-                  int k, int epi, const char* what, int l) {
+                  int k, int epi, const char* what, int l, int force_splits = 0) {
     int bn = 256, splits = 1;
     if (epi == kEpiF32) gemm_pick(n_out, k, num_sms_, &bn, &splits);
+    if (force_splits > 0) {
+      bn = 256;
+      splits = force_splits;
+    }
     if (!gemm_plan(p, a, static_cast<int>(C), lda, w, w_rows, n_out, k, epi, bn,
                    std::min(splits, S), err, sizeof err))
       fail("layer %d %s: %s", l, what, err);
@@ -430,7 +435,17 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
     plan(&ly.o, attn16_.p, attn_w, ly.w_o, d, d, attn_w, kEpiF32, "o", l);
     plan(&ly.gate_up, h16_.p, d, ly.w_gu, (ly.ff + 127) / 128 * 256, ly.ff, d, kEpiGeGluTanh,
          "gate_up", l);
-    plan(&ly.down, act16_.p, ly.ff, ly.w_down, d, d, ly.ff, kEpiF32, "down", l);
+    // The down projection joins gate_up's launch when its split-K units run
+    // as many K blocks as a gate_up tile (a split count that depends on the
+    // layer's shape only).
+    const int kb_up = (d + 63) / 64, kb_dn = (ly.ff + 63) / 64;
+    const int fuse_splits = kb_dn % kb_up == 0 ? kb_dn / kb_up : 0;
+    if (fuse_splits >= 1 && fuse_splits <= S) {
+      plan(&ly.down, act16_.p, ly.ff, ly.w_down, d, d, ly.ff, kEpiF32, "down", l, fuse_splits);
+      ly.fused_mlp = gemm_mlp_ok(ly.gate_up, ly.down);
+    }
+    if (!ly.fused_mlp)
+      plan(&ly.down, act16_.p, ly.ff, ly.w_down, d, d, ly.ff, kEpiF32, "down", l);
     if (P > 0) {
       ly.pl_norm = norm(n("pl_norm"));
       plan(&ly.pl_gate, x16_.p, d, lin(n("pl_gate")), P, P, d, kEpiF32, "pl_gate", l);
@@ -692,6 +707,10 @@ int Engine::launch_forward(const Packing& p, Want want) {
     if (profiling_) prof_mark(name);
   };
   CUDA_TRY(cudaMemsetAsync(status, 0, 4, stream_));
+  // Fused FFN launches count finished up tiles per row tile, cumulatively over
+  // the pass (each launch waits for its own running total).
+  CUDA_TRY(cudaMemsetAsync(mlp_ready_.p, 0, mlp_ready_.bytes, stream_));
+  int mlp_target = 0;
 
   k("embed_norm");
   launch_embed_norm(embed_.dtype, ids_.as<int>(), t, embed_.codes.p, embed_.scales.p, d,
@@ -807,10 +826,17 @@ int Engine::launch_forward(const Packing& p, Want want) {
                          c.eps, c.norm_offset, 1.0f, x_.as<float>(), nullptr, ly.ffn_norm,
                          h16_.as<__half>(), d, nullptr, nullptr, stream_);
     // GeGLU and down projection.
-    k("gemm_gate_up");
-    gemm_run(ly.gate_up, t, act16_.p, ly.ff, 0, status, stream_);
-    k("gemm_down");
-    gemm_run(ly.down, t, a32_.p, d, slab_a, status, stream_);
+    if (ly.fused_mlp) {
+      k("gemm_mlp");
+      mlp_target += 4 * ly.gate_up.s.n_tiles / ly.down.s.splits;
+      gemm_run_mlp(ly.gate_up, ly.down, t, act16_.p, ly.ff, a32_.p, d, slab_a,
+                   mlp_ready_.as<int>(), mlp_target, status, stream_);
+    } else {
+      k("gemm_gate_up");
+      gemm_run(ly.gate_up, t, act16_.p, ly.ff, 0, status, stream_);
+      k("gemm_down");
+      gemm_run(ly.down, t, a32_.p, d, slab_a, status, stream_);
+    }
     const int* rmap = last ? row_map_.as<int>() : nullptr;
     float* rows = last ? rows_.as<float>() : nullptr;
     __half* hnext = last ? nullptr : h16_.as<__half>();

@@ -213,6 +213,7 @@ class Engine {
     const float *pl_norm = nullptr;
     const float* next_norm;  // the norm that reads the stream after this layer
     float out_scale = 1.f;
+    bool fused_mlp = false;  // gate_up and down as one launch (gemm_run_mlp)
     int hd, ff, qkv_w;
     bool sliding, has_kv;
     int kv_src;
@@ -293,7 +294,7 @@ class Engine {
   int max_qkv_ = 0, max_attn_ = 0, max_ff_ = 0;
 
   // Workspace.
-  DevBuffer attn_ctas_, attn_sched_;
+  DevBuffer attn_ctas_, attn_sched_, mlp_ready_;
   PinnedBuffer h_attn_ctas_, h_attn_sched_;
   CUtensorMap attn_tq_;
   std::vector<CUtensorMap> attn_tkv_;  // per layer owning head_dim-256 K/V

@@ -153,6 +153,324 @@ __device__ __forceinline__ void flush_rows_split(uint8_t* slot, int lane, uint8_
   __syncwarp();
 }
 
+// Epilogue of one accumulator tile: epilogue warp q (lanes = TMEM lanes
+// 32 q .. 32 q + 31, one output row each) drains its rows from `tbase` and
+// stores them through its staging slot.
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& g, int m_tile, int n_tile, int split,
+                                              uint32_t tbase, int q, int lane, uint8_t* slot,
+                                              const float* epi_consts) {
+  const int row = m_tile * BM + q * 32 + lane;
+  const int row0 = m_tile * BM + q * 32;   // this warp's first row
+  const int nrows = min(32, g.m - row0);   // its rows below m (may be <= 0)
+  if constexpr (EPI == kEpiF32) {
+    float* wbase = static_cast<float*>(g.out) + split * g.split_stride +
+                   static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      float v[32];
+      tmem_ld32(tbase + c * 32, v);
+      const int col0 = n_tile * BN + c * 32;
+      if (nrows <= 0 || col0 >= g.n_out) continue;
+      if (col0 + 32 <= g.n_out) {
+        uint4 pc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pc[i] = pack_f32x4(v + 4 * i);
+        stage_pieces(slot, lane, 0, pc, 8);
+        flush_rows(slot, lane, reinterpret_cast<uint8_t*>(wbase + col0),
+                   static_cast<size_t>(g.ldo) * 4, nrows);
+      } else if (lane < nrows) {
+        float* o = wbase + static_cast<size_t>(lane) * g.ldo + col0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < g.n_out) o[j] = v[j];
+      }
+    }
+  } else if constexpr (EPI == kEpiF16) {
+    __half* wbase =
+        static_cast<__half*>(g.out) + static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; c += 2) {
+      float lo[32], hi[32];
+      tmem_ld32(tbase + c * 32, lo);
+      tmem_ld32(tbase + (c + 1) * 32, hi);
+      const int col0 = n_tile * BN + c * 32;
+      if (nrows <= 0 || col0 >= g.n_out) continue;
+      if (col0 + 64 <= g.n_out) {
+        uint4 pc[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          pc[i] = pack_f16x8(lo + 8 * i);
+          pc[4 + i] = pack_f16x8(hi + 8 * i);
+        }
+        stage_pieces(slot, lane, 0, pc, 8);
+        flush_rows(slot, lane, reinterpret_cast<uint8_t*>(wbase + col0),
+                   static_cast<size_t>(g.ldo) * 2, nrows);
+      } else if (lane < nrows) {
+        __half* o = wbase + static_cast<size_t>(lane) * g.ldo;
+        store_f16x32(o + col0, lo, col0, g.n_out);
+        if (col0 + 32 < g.n_out) store_f16x32(o + col0 + 32, hi, col0 + 32, g.n_out);
+      }
+    }
+  } else if constexpr (EPI == kEpiRopeF16) {
+    // 64-dim heads: columns c and c + 32 of a head form a rotation pair.
+    __half* wbase =
+        static_cast<__half*>(g.out) + static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
+    // Table [pair][position]: the rows of a tile are mostly consecutive
+    // positions, so a warp's reads of one pair are contiguous.
+    const int p = row < g.m ? g.epi.pos[row] : 0;
+    const float2* rt = g.epi.rope + p;
+    const size_t rs = static_cast<size_t>(g.epi.rope_stride);
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; c += 2) {
+      float lo[32], hi[32];
+      tmem_ld32(tbase + c * 32, lo);
+      tmem_ld32(tbase + (c + 1) * 32, hi);
+      const int col0 = n_tile * BN + c * 32;
+      if (nrows <= 0 || col0 >= g.n_out) continue;
+      if (col0 < 2 * g.epi.q_cols) {
+        const float sc = col0 < g.epi.q_cols ? g.epi.q_scale : 1.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float2 cs = rt[j * rs];
+          const float a = lo[j], b = hi[j];
+          lo[j] = (a * cs.x - b * cs.y) * sc;
+          hi[j] = (b * cs.x + a * cs.y) * sc;
+        }
+      }
+      if (col0 + 64 <= g.n_out) {
+        uint4 pc[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          pc[i] = pack_f16x8(lo + 8 * i);
+          pc[4 + i] = pack_f16x8(hi + 8 * i);
+        }
+        stage_pieces(slot, lane, 0, pc, 8);
+        flush_rows(slot, lane, reinterpret_cast<uint8_t*>(wbase + col0),
+                   static_cast<size_t>(g.ldo) * 2, nrows);
+      } else if (lane < nrows) {
+        __half* o = wbase + static_cast<size_t>(lane) * g.ldo;
+        store_f16x32(o + col0, lo, col0, g.n_out);
+        if (col0 + 32 < g.n_out) store_f16x32(o + col0 + 32, hi, col0 + 32, g.n_out);
+      }
+    }
+  } else if constexpr (EPI == kEpiBiasF16 || EPI == kEpiBiasReluF16) {
+    __half* wbase =
+        static_cast<__half*>(g.out) + static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; c += 2) {
+      float v[2][32];
+      tmem_ld32(tbase + c * 32, v[0]);
+      tmem_ld32(tbase + (c + 1) * 32, v[1]);
+      const int col0 = n_tile * BN + c * 32;
+      if (nrows <= 0 || col0 >= g.n_out) continue;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int col = col0 + 32 * h + j;
+          const float b = col < g.n_out ? g.epi.bias[col] : 0.f;
+          v[h][j] += b;
+          if constexpr (EPI == kEpiBiasReluF16) v[h][j] = fmaxf(v[h][j], 0.f);
+        }
+      }
+      if (col0 + 64 <= g.n_out) {
+        uint4 pc[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          pc[i] = pack_f16x8(v[0] + 8 * i);
+          pc[4 + i] = pack_f16x8(v[1] + 8 * i);
+        }
+        stage_pieces(slot, lane, 0, pc, 8);
+        flush_rows(slot, lane, reinterpret_cast<uint8_t*>(wbase + col0),
+                   static_cast<size_t>(g.ldo) * 2, nrows);
+      } else if (lane < nrows) {
+        __half* o = wbase + static_cast<size_t>(lane) * g.ldo;
+        store_f16x32(o + col0, v[0], col0, g.n_out);
+        if (col0 + 32 < g.n_out) store_f16x32(o + col0 + 32, v[1], col0 + 32, g.n_out);
+      }
+    }
+  } else if constexpr (EPI == kEpiResidF32) {
+    // Each output element belongs to one tile (no split-K), so the
+    // read-modify-write of the residual row is race-free. The accumulator
+    // chunk is staged by row; then each lane updates 16 bytes of four
+    // rows per step (a row segment per 8 lanes). Its bias values are read
+    // before any row is touched, so no bias load waits behind a store to
+    // the (possibly aliasing) residual row.
+    float* __restrict__ wbase =
+        static_cast<float*>(g.out) + static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
+    const float* __restrict__ bias = g.epi.bias;
+    const bool bias_first = g.epi.bias_first != 0;
+    const int pc4 = lane & 7;  // this lane's 4 columns of a chunk: 4 pc4 .. 4 pc4 + 3
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      float v[32];
+      const int col0 = n_tile * BN + c * 32;
+      float bl[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = col0 + 4 * pc4 + e;
+        bl[e] = (bias && col < g.n_out) ? __ldg(bias + col) : 0.f;
+      }
+      tmem_ld32(tbase + c * 32, v);
+      if (nrows <= 0 || col0 >= g.n_out) continue;
+      if (col0 + 32 <= g.n_out) {
+        uint4 pc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pc[i] = pack_f32x4(v + 4 * i);
+        stage_pieces(slot, lane, 0, pc, 8);
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = 4 * i + (lane >> 3);
+          if (r >= nrows) continue;
+          const float4 a = *reinterpret_cast<const float4*>(slot + r * 128 + ((pc4 ^ (r & 7)) << 4));
+          float* __restrict__ o = wbase + static_cast<size_t>(r) * g.ldo + col0 + 4 * pc4;
+          float4 x = *reinterpret_cast<const float4*>(o);
+          const float av[4] = {a.x, a.y, a.z, a.w};
+          float* xe = reinterpret_cast<float*>(&x);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            xe[e] = bias_first ? (av[e] + bl[e]) + xe[e] : (xe[e] + av[e]) + bl[e];
+          *reinterpret_cast<float4*>(o) = x;
+        }
+        __syncwarp();
+      } else if (lane < nrows) {
+        float* __restrict__ o = wbase + static_cast<size_t>(lane) * g.ldo + col0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (col0 + j >= g.n_out) continue;
+          const float b = bias ? __ldg(bias + col0 + j) : 0.f;
+          o[j] = bias_first ? (v[j] + b) + o[j] : (o[j] + v[j]) + b;
+        }
+      }
+    }
+  } else if constexpr (EPI == kEpiQkPrep) {
+    // qk_prep.wgsl on the accumulator: this tile is head n_tile of the
+    // row, all 256 of its dims in this thread's TMEM lane. Loads are
+    // batched ahead of the math (one thread per row has little else to
+    // hide their latency with): the norm weights come from shared memory,
+    // each 32-pair chunk's RoPE entries are read before they are used.
+    static_assert(BN == 256, "one 256-column tile per head");
+    const QkEpi& q = g.epi.qk;
+    const int h = n_tile;
+    const bool is_q = h < q.heads;
+    const bool is_v = h >= q.heads + q.kv_heads;
+    const bool ok_row = row < g.m;
+    const int crow = q.base + (ok_row ? row : 0);
+    // Table [pair][position]: consecutive rows read consecutive entries.
+    // Each chunk's 32 entries are requested a step ahead of their use
+    // (chunk 0's before the sum of squares), so their latency overlaps
+    // other work.
+    const float2* rt = q.rope + (ok_row ? q.meta[crow].pos : 0);
+    const size_t rs = static_cast<size_t>(q.rope_stride);
+    const int half_rot = q.rope_dims / 2;
+    float2 cs[32];
+    if (!is_v && 0 < half_rot) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) cs[j] = rt[static_cast<size_t>(j) * rs];
+    }
+    float ssp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+    for (int c = 0; c < 8; ++c) {
+      float v[32];
+      tmem_ld32(tbase + c * 32, v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ssp[j & 7] = fmaf(v[j], v[j], ssp[j & 7]);
+    }
+    const float ss = ((ssp[0] + ssp[1]) + (ssp[2] + ssp[3])) + ((ssp[4] + ssp[5]) + (ssp[6] + ssp[7]));
+    const float inv = (is_v && !q.v_norm) ? 1.0f : rsqrtf(ss / 256.0f + q.eps);
+    // This warp's first output row (rows are contiguous in both targets).
+    const int wrow = row0 > 0 ? row0 : 0;
+    uint8_t* wbase;
+    size_t wstride;
+    if (is_q) {
+      wbase = reinterpret_cast<uint8_t*>(q.q16 + static_cast<size_t>(wrow) * q.heads * 256 + h * 256);
+      wstride = static_cast<size_t>(q.heads) * 256 * 2;
+    } else {
+      wbase = reinterpret_cast<uint8_t*>(
+          q.kv + static_cast<size_t>(q.base + wrow) * 2 * q.kv_heads * 256 + (h - q.heads) * 256);
+      wstride = static_cast<size_t>(2 * q.kv_heads) * 256 * 2;
+    }
+    const float* wn = epi_consts + (is_q ? 0 : 256);
+    const float scale = is_q ? q.q_scale : 1.0f;
+    // Dims d and d + 128 rotate together: chunk c of each half per step,
+    // both staged by row and stored as two 64-byte row segments.
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float a[32], b[32];
+      const bool rot = !is_v && c * 32 < half_rot;
+      tmem_ld32(tbase + c * 32, a);
+      tmem_ld32(tbase + (c + 4) * 32, b);
+      if (is_v) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          a[j] *= inv;
+          b[j] *= inv;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int dd = c * 32 + j;
+          float y1 = a[j] * inv * (q.offset + wn[dd]);
+          float y2 = b[j] * inv * (q.offset + wn[dd + 128]);
+          if (rot && dd < half_rot) {
+            const float r1 = y1 * cs[j].x - y2 * cs[j].y;
+            const float r2 = y2 * cs[j].x + y1 * cs[j].y;
+            y1 = r1;
+            y2 = r2;
+          }
+          a[j] = y1 * scale;
+          b[j] = y2 * scale;
+        }
+      }
+      uint4 pc[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        pc[i] = pack_f16x8(a + 8 * i);
+        pc[4 + i] = pack_f16x8(b + 8 * i);
+      }
+      if (c + 1 < 4 && !is_v && (c + 1) * 32 < half_rot) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) cs[j] = rt[static_cast<size_t>((c + 1) * 32 + j) * rs];
+      }
+      if (nrows > 0) {
+        stage_pieces(slot, lane, 0, pc, 8);
+        flush_rows_split(slot, lane, wbase + c * 64, wbase + 256 + c * 64, wstride, nrows);
+      }
+    }
+  } else {
+    // GeGLU: accumulator columns 0..127 hold the gate products, 128..255
+    // the up products of the same 128 output columns.
+    static_assert(BN == 256, "GeGLU tiles pair 128 gate rows with 128 up rows");
+    __half* wbase =
+        static_cast<__half*>(g.out) + static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float gv[32], uv[32];
+      tmem_ld32(tbase + c * 32, gv);
+      tmem_ld32(tbase + 128 + c * 32, uv);
+      const int col0 = n_tile * 128 + (c & ~1) * 32;  // first column of this chunk pair
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        gv[j] = ((EPI == kEpiGeGluTanh) ? gelu_tanh(gv[j]) : gelu_erf(gv[j])) * uv[j];
+      if (nrows <= 0 || col0 >= g.n_out) continue;
+      if (col0 + 64 <= g.n_out) {
+        uint4 pc[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pc[i] = pack_f16x8(gv + 8 * i);
+        stage_pieces(slot, lane, (c & 1) * 4, pc, 4);
+        if (c & 1)
+          flush_rows(slot, lane, reinterpret_cast<uint8_t*>(wbase + col0),
+                     static_cast<size_t>(g.ldo) * 2, nrows);
+      } else if (lane < nrows) {
+        const int cc = col0 + (c & 1) * 32;
+        if (cc < g.n_out) store_f16x32(wbase + static_cast<size_t>(lane) * g.ldo + cc, gv, cc, g.n_out);
+      }
+    }
+  }
+}
+
 // Persistent: CTA b handles tiles b, b + gridDim.x, ... Tile t is
 // (m = t % m_tiles, n = (t / m_tiles) % n_tiles, split = t / (m_tiles * n_tiles)):
 // the CTAs running at once share few weight tiles, which stay in L2 while
@@ -282,319 +600,233 @@ __global__ void __launch_bounds__(192, 1)
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-      const int row = m_tile * BM + q * 32 + lane;
-      const int row0 = m_tile * BM + q * 32;   // this warp's first row
-      const int nrows = min(32, g.m - row0);   // its rows below m (may be <= 0)
       uint8_t* slot = reinterpret_cast<uint8_t*>(full) + 256 + 2048 + q * 4096;
       const uint32_t tbase =
           tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BN);
-      if constexpr (EPI == kEpiF32) {
-        float* wbase = static_cast<float*>(g.out) + split * g.split_stride +
-                       static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          tmem_ld32(tbase + c * 32, v);
-          const int col0 = n_tile * BN + c * 32;
-          if (nrows <= 0 || col0 >= g.n_out) continue;
-          if (col0 + 32 <= g.n_out) {
-            uint4 pc[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) pc[i] = pack_f32x4(v + 4 * i);
-            stage_pieces(slot, lane, 0, pc, 8);
-            flush_rows(slot, lane, reinterpret_cast<uint8_t*>(wbase + col0),
-                       static_cast<size_t>(g.ldo) * 4, nrows);
-          } else if (lane < nrows) {
-            float* o = wbase + static_cast<size_t>(lane) * g.ldo + col0;
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < g.n_out) o[j] = v[j];
-          }
-        }
-      } else if constexpr (EPI == kEpiF16) {
-        __half* wbase =
-            static_cast<__half*>(g.out) + static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; c += 2) {
-          float lo[32], hi[32];
-          tmem_ld32(tbase + c * 32, lo);
-          tmem_ld32(tbase + (c + 1) * 32, hi);
-          const int col0 = n_tile * BN + c * 32;
-          if (nrows <= 0 || col0 >= g.n_out) continue;
-          if (col0 + 64 <= g.n_out) {
-            uint4 pc[8];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              pc[i] = pack_f16x8(lo + 8 * i);
-              pc[4 + i] = pack_f16x8(hi + 8 * i);
-            }
-            stage_pieces(slot, lane, 0, pc, 8);
-            flush_rows(slot, lane, reinterpret_cast<uint8_t*>(wbase + col0),
-                       static_cast<size_t>(g.ldo) * 2, nrows);
-          } else if (lane < nrows) {
-            __half* o = wbase + static_cast<size_t>(lane) * g.ldo;
-            store_f16x32(o + col0, lo, col0, g.n_out);
-            if (col0 + 32 < g.n_out) store_f16x32(o + col0 + 32, hi, col0 + 32, g.n_out);
-          }
-        }
-      } else if constexpr (EPI == kEpiRopeF16) {
-        // 64-dim heads: columns c and c + 32 of a head form a rotation pair.
-        __half* wbase =
-            static_cast<__half*>(g.out) + static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
-        // Table [pair][position]: the rows of a tile are mostly consecutive
-        // positions, so a warp's reads of one pair are contiguous.
-        const int p = row < g.m ? g.epi.pos[row] : 0;
-        const float2* rt = g.epi.rope + p;
-        const size_t rs = static_cast<size_t>(g.epi.rope_stride);
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; c += 2) {
-          float lo[32], hi[32];
-          tmem_ld32(tbase + c * 32, lo);
-          tmem_ld32(tbase + (c + 1) * 32, hi);
-          const int col0 = n_tile * BN + c * 32;
-          if (nrows <= 0 || col0 >= g.n_out) continue;
-          if (col0 < 2 * g.epi.q_cols) {
-            const float sc = col0 < g.epi.q_cols ? g.epi.q_scale : 1.0f;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float2 cs = rt[j * rs];
-              const float a = lo[j], b = hi[j];
-              lo[j] = (a * cs.x - b * cs.y) * sc;
-              hi[j] = (b * cs.x + a * cs.y) * sc;
-            }
-          }
-          if (col0 + 64 <= g.n_out) {
-            uint4 pc[8];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              pc[i] = pack_f16x8(lo + 8 * i);
-              pc[4 + i] = pack_f16x8(hi + 8 * i);
-            }
-            stage_pieces(slot, lane, 0, pc, 8);
-            flush_rows(slot, lane, reinterpret_cast<uint8_t*>(wbase + col0),
-                       static_cast<size_t>(g.ldo) * 2, nrows);
-          } else if (lane < nrows) {
-            __half* o = wbase + static_cast<size_t>(lane) * g.ldo;
-            store_f16x32(o + col0, lo, col0, g.n_out);
-            if (col0 + 32 < g.n_out) store_f16x32(o + col0 + 32, hi, col0 + 32, g.n_out);
-          }
-        }
-      } else if constexpr (EPI == kEpiBiasF16 || EPI == kEpiBiasReluF16) {
-        __half* wbase =
-            static_cast<__half*>(g.out) + static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; c += 2) {
-          float v[2][32];
-          tmem_ld32(tbase + c * 32, v[0]);
-          tmem_ld32(tbase + (c + 1) * 32, v[1]);
-          const int col0 = n_tile * BN + c * 32;
-          if (nrows <= 0 || col0 >= g.n_out) continue;
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int col = col0 + 32 * h + j;
-              const float b = col < g.n_out ? g.epi.bias[col] : 0.f;
-              v[h][j] += b;
-              if constexpr (EPI == kEpiBiasReluF16) v[h][j] = fmaxf(v[h][j], 0.f);
-            }
-          }
-          if (col0 + 64 <= g.n_out) {
-            uint4 pc[8];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              pc[i] = pack_f16x8(v[0] + 8 * i);
-              pc[4 + i] = pack_f16x8(v[1] + 8 * i);
-            }
-            stage_pieces(slot, lane, 0, pc, 8);
-            flush_rows(slot, lane, reinterpret_cast<uint8_t*>(wbase + col0),
-                       static_cast<size_t>(g.ldo) * 2, nrows);
-          } else if (lane < nrows) {
-            __half* o = wbase + static_cast<size_t>(lane) * g.ldo;
-            store_f16x32(o + col0, v[0], col0, g.n_out);
-            if (col0 + 32 < g.n_out) store_f16x32(o + col0 + 32, v[1], col0 + 32, g.n_out);
-          }
-        }
-      } else if constexpr (EPI == kEpiResidF32) {
-        // Each output element belongs to one tile (no split-K), so the
-        // read-modify-write of the residual row is race-free. The accumulator
-        // chunk is staged by row; then each lane updates 16 bytes of four
-        // rows per step (a row segment per 8 lanes). Its bias values are read
-        // before any row is touched, so no bias load waits behind a store to
-        // the (possibly aliasing) residual row.
-        float* __restrict__ wbase =
-            static_cast<float*>(g.out) + static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
-        const float* __restrict__ bias = g.epi.bias;
-        const bool bias_first = g.epi.bias_first != 0;
-        const int pc4 = lane & 7;  // this lane's 4 columns of a chunk: 4 pc4 .. 4 pc4 + 3
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          const int col0 = n_tile * BN + c * 32;
-          float bl[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int col = col0 + 4 * pc4 + e;
-            bl[e] = (bias && col < g.n_out) ? __ldg(bias + col) : 0.f;
-          }
-          tmem_ld32(tbase + c * 32, v);
-          if (nrows <= 0 || col0 >= g.n_out) continue;
-          if (col0 + 32 <= g.n_out) {
-            uint4 pc[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) pc[i] = pack_f32x4(v + 4 * i);
-            stage_pieces(slot, lane, 0, pc, 8);
-            __syncwarp();
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int r = 4 * i + (lane >> 3);
-              if (r >= nrows) continue;
-              const float4 a = *reinterpret_cast<const float4*>(slot + r * 128 + ((pc4 ^ (r & 7)) << 4));
-              float* __restrict__ o = wbase + static_cast<size_t>(r) * g.ldo + col0 + 4 * pc4;
-              float4 x = *reinterpret_cast<const float4*>(o);
-              const float av[4] = {a.x, a.y, a.z, a.w};
-              float* xe = reinterpret_cast<float*>(&x);
-#pragma unroll
-              for (int e = 0; e < 4; ++e)
-                xe[e] = bias_first ? (av[e] + bl[e]) + xe[e] : (xe[e] + av[e]) + bl[e];
-              *reinterpret_cast<float4*>(o) = x;
-            }
-            __syncwarp();
-          } else if (lane < nrows) {
-            float* __restrict__ o = wbase + static_cast<size_t>(lane) * g.ldo + col0;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (col0 + j >= g.n_out) continue;
-              const float b = bias ? __ldg(bias + col0 + j) : 0.f;
-              o[j] = bias_first ? (v[j] + b) + o[j] : (o[j] + v[j]) + b;
-            }
-          }
-        }
-      } else if constexpr (EPI == kEpiQkPrep) {
-        // qk_prep.wgsl on the accumulator: this tile is head n_tile of the
-        // row, all 256 of its dims in this thread's TMEM lane. Loads are
-        // batched ahead of the math (one thread per row has little else to
-        // hide their latency with): the norm weights come from shared memory,
-        // each 32-pair chunk's RoPE entries are read before they are used.
-        static_assert(BN == 256, "one 256-column tile per head");
-        const QkEpi& q = g.epi.qk;
-        const int h = n_tile;
-        const bool is_q = h < q.heads;
-        const bool is_v = h >= q.heads + q.kv_heads;
-        const bool ok_row = row < g.m;
-        const int crow = q.base + (ok_row ? row : 0);
-        // Table [pair][position]: consecutive rows read consecutive entries.
-        // Each chunk's 32 entries are requested a step ahead of their use
-        // (chunk 0's before the sum of squares), so their latency overlaps
-        // other work.
-        const float2* rt = q.rope + (ok_row ? q.meta[crow].pos : 0);
-        const size_t rs = static_cast<size_t>(q.rope_stride);
-        const int half_rot = q.rope_dims / 2;
-        float2 cs[32];
-        if (!is_v && 0 < half_rot) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) cs[j] = rt[static_cast<size_t>(j) * rs];
-        }
-        float ssp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-        for (int c = 0; c < 8; ++c) {
-          float v[32];
-          tmem_ld32(tbase + c * 32, v);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) ssp[j & 7] = fmaf(v[j], v[j], ssp[j & 7]);
-        }
-        const float ss = ((ssp[0] + ssp[1]) + (ssp[2] + ssp[3])) + ((ssp[4] + ssp[5]) + (ssp[6] + ssp[7]));
-        const float inv = (is_v && !q.v_norm) ? 1.0f : rsqrtf(ss / 256.0f + q.eps);
-        // This warp's first output row (rows are contiguous in both targets).
-        const int wrow = row0 > 0 ? row0 : 0;
-        uint8_t* wbase;
-        size_t wstride;
-        if (is_q) {
-          wbase = reinterpret_cast<uint8_t*>(q.q16 + static_cast<size_t>(wrow) * q.heads * 256 + h * 256);
-          wstride = static_cast<size_t>(q.heads) * 256 * 2;
-        } else {
-          wbase = reinterpret_cast<uint8_t*>(
-              q.kv + static_cast<size_t>(q.base + wrow) * 2 * q.kv_heads * 256 + (h - q.heads) * 256);
-          wstride = static_cast<size_t>(2 * q.kv_heads) * 256 * 2;
-        }
-        const float* wn = epi_consts + (is_q ? 0 : 256);
-        const float scale = is_q ? q.q_scale : 1.0f;
-        // Dims d and d + 128 rotate together: chunk c of each half per step,
-        // both staged by row and stored as two 64-byte row segments.
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float a[32], b[32];
-          const bool rot = !is_v && c * 32 < half_rot;
-          tmem_ld32(tbase + c * 32, a);
-          tmem_ld32(tbase + (c + 4) * 32, b);
-          if (is_v) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              a[j] *= inv;
-              b[j] *= inv;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int dd = c * 32 + j;
-              float y1 = a[j] * inv * (q.offset + wn[dd]);
-              float y2 = b[j] * inv * (q.offset + wn[dd + 128]);
-              if (rot && dd < half_rot) {
-                const float r1 = y1 * cs[j].x - y2 * cs[j].y;
-                const float r2 = y2 * cs[j].x + y1 * cs[j].y;
-                y1 = r1;
-                y2 = r2;
-              }
-              a[j] = y1 * scale;
-              b[j] = y2 * scale;
-            }
-          }
-          uint4 pc[8];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            pc[i] = pack_f16x8(a + 8 * i);
-            pc[4 + i] = pack_f16x8(b + 8 * i);
-          }
-          if (c + 1 < 4 && !is_v && (c + 1) * 32 < half_rot) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) cs[j] = rt[static_cast<size_t>((c + 1) * 32 + j) * rs];
-          }
-          if (nrows > 0) {
-            stage_pieces(slot, lane, 0, pc, 8);
-            flush_rows_split(slot, lane, wbase + c * 64, wbase + 256 + c * 64, wstride, nrows);
-          }
-        }
-      } else {
-        // GeGLU: accumulator columns 0..127 hold the gate products, 128..255
-        // the up products of the same 128 output columns.
-        static_assert(BN == 256, "GeGLU tiles pair 128 gate rows with 128 up rows");
-        __half* wbase =
-            static_cast<__half*>(g.out) + static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float gv[32], uv[32];
-          tmem_ld32(tbase + c * 32, gv);
-          tmem_ld32(tbase + 128 + c * 32, uv);
-          const int col0 = n_tile * 128 + (c & ~1) * 32;  // first column of this chunk pair
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            gv[j] = ((EPI == kEpiGeGluTanh) ? gelu_tanh(gv[j]) : gelu_erf(gv[j])) * uv[j];
-          if (nrows <= 0 || col0 >= g.n_out) continue;
-          if (col0 + 64 <= g.n_out) {
-            uint4 pc[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) pc[i] = pack_f16x8(gv + 8 * i);
-            stage_pieces(slot, lane, (c & 1) * 4, pc, 4);
-            if (c & 1)
-              flush_rows(slot, lane, reinterpret_cast<uint8_t*>(wbase + col0),
-                         static_cast<size_t>(g.ldo) * 2, nrows);
-          } else if (lane < nrows) {
-            const int cc = col0 + (c & 1) * 32;
-            if (cc < g.n_out) store_f16x32(wbase + static_cast<size_t>(lane) * g.ldo + cc, gv, cc, g.n_out);
-          }
-        }
-      }
+      epilogue_tile<BN, EPI>(g, m_tile, n_tile, split, tbase, q, lane, slot, epi_consts);
       // This warp is done with accumulator b.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Orders this thread's generic-proxy global accesses with async-proxy (TMA)
+// accesses to global memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Gate+up and down projections of one FFN in one persistent launch. Units:
+// the up tiles in the standalone order (m = t % m_tiles, n = t / m_tiles, so
+// the CTAs running at once share weight tiles in L2), then the down units
+// split-major (split, then m fastest, then n). CTA b takes units b,
+// b + gridDim.x, ... Both problems' units run the same number of K blocks
+// (down's split count is chosen so), so the rounds stay even and the down
+// units fill what would be the up projection's last, partial round. Down
+// split s of M tile m reads the activation columns that up column tiles
+// [s * band, (s + 1) * band) of m store: every epilogue warp of such an up
+// tile counts itself in ready[m * splits + s] once its rows are stored
+// (cumulative over a pass: this launch's count is reached at ready_target),
+// and the down unit's producer waits for that count before its first load.
+// Up tiles finish band by band in unit order, so a down unit rarely waits.
+// Each unit's result is the one the two separate launches compute.
+struct MlpArgs {
+  GemmArgs up, down;
+  int* ready;
+  int ready_target;
+  int band;  // up column tiles per down split
+};
+
+template <int EPI_UP>
+__global__ void __launch_bounds__(192, 1)
+    gemm_mlp_kernel(const __grid_constant__ CUtensorMap ta_up,
+                    const __grid_constant__ CUtensorMap tb_up,
+                    const __grid_constant__ CUtensorMap ta_dn,
+                    const __grid_constant__ CUtensorMap tb_dn, MlpArgs g) {
+  constexpr int BN = 256;
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + C::STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + C::STAGES * C::B_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* epi_consts = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);
+  uint32_t* status = g.up.status;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int up_units = g.up.m_tiles * g.up.n_tiles;
+  const int dn_per_split = g.down.m_tiles * g.down.n_tiles;
+  const int total = up_units + dn_per_split * g.down.splits;
+  struct Unit {
+    bool up;
+    int m, n, split, kb0, kb1;
+  };
+  auto decode = [&](int u) {
+    Unit x;
+    if (u < up_units) {
+      x.up = true;
+      x.m = u % g.up.m_tiles;
+      x.n = u / g.up.m_tiles;
+      x.split = 0;
+      x.kb0 = 0;
+      x.kb1 = g.up.kb_total;
+    } else {
+      const int v = u - up_units;
+      const int r = v % dn_per_split;
+      x.up = false;
+      x.split = v / dn_per_split;
+      x.m = r % g.down.m_tiles;
+      x.n = r / g.down.m_tiles;
+      x.kb0 = x.split * g.down.kb_per_split;
+      x.kb1 = min(g.down.kb_total, x.kb0 + g.down.kb_per_split);
+    }
+    return x;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&ta_up);
+    prefetch_tmap(&tb_up);
+    prefetch_tmap(&ta_dn);
+    prefetch_tmap(&tb_dn);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  griddep_wait();
+  griddep_launch();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      for (int u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
+        const Unit x = decode(u);
+        if (!x.up) {
+          // This unit's activation columns of its rows: every up tile of the
+          // band stored.
+          const int* rp = g.ready + x.m * g.down.splits + x.split;
+          const long long t0 = clock64();
+          bool ok = true;
+          while (ld_acquire_gpu(rp) < g.ready_target) {
+            if (*abort_flag) {
+              ok = false;
+              break;
+            }
+            if (clock64() - t0 > kWaitLimitClocks) {
+              *abort_flag = 1;
+              atomicCAS(status, 0u, static_cast<uint32_t>(kDevWaitTimeout));
+              ok = false;
+              break;
+            }
+            __nanosleep(64);
+          }
+          if (!ok) break;
+          fence_proxy_async_global();
+        }
+        const CUtensorMap* ta = x.up ? &ta_up : &ta_dn;
+        const CUtensorMap* tb = x.up ? &tb_up : &tb_dn;
+        bool ok = true;
+        for (int kb = x.kb0; kb < x.kb1; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, status)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+          tma_load_2d(sa + s * C::A_BYTES, ta, &full[s], kb * BK, x.m * BM);
+          tma_load_2d(sb + s * C::B_BYTES, tb, &full[s], kb * BK, x.n * BN);
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(BM, BN);
+      int it = 0, local = 0;
+      for (int u = blockIdx.x; u < total; u += gridDim.x, ++local) {
+        const Unit x = decode(u);
+        const int b = local & 1;
+        if (!mbar_wait(&tempty[b], ((local >> 1) & 1) ^ 1, abort_flag, status)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(b * BN);
+        bool ok = true;
+        for (int kb = x.kb0; kb < x.kb1; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort_flag, status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = sw128_desc(sa + s * C::A_BYTES);
+          const uint64_t db = sw128_desc(sb + s * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16(d, da + 2 * k, db + 2 * k, idesc, (kb > x.kb0 || k > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&tfull[b]);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    int local = 0;
+    for (int u = blockIdx.x; u < total; u += gridDim.x, ++local) {
+      const Unit x = decode(u);
+      const int b = local & 1;
+      int ok = 0;
+      if (lane == 0) ok = mbar_wait(&tfull[b], (local >> 1) & 1, abort_flag, status) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      uint8_t* slot = reinterpret_cast<uint8_t*>(full) + 256 + 2048 + q * 4096;
+      const uint32_t tbase =
+          tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BN);
+      if (x.up) {
+        epilogue_tile<BN, EPI_UP>(g.up, x.m, x.n, 0, tbase, q, lane, slot, epi_consts);
+        // Publish this warp's rows to the down units' loads (another proxy,
+        // other SMs), then count the warp in.
+        fence_proxy_async_global();
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(g.ready + x.m * g.down.splits + x.n / g.band, 1);
+      } else {
+        epilogue_tile<BN, kEpiF32>(g.down, x.m, x.n, x.split, tbase, q, lane, slot, epi_consts);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
@@ -674,6 +906,10 @@ bool make_tmap_f16(CUtensorMap* m, const void* base, int rank, const uint64_t* d
 }
 
 void gemm_setup_device() {
+  cudaFuncSetAttribute(gemm_mlp_kernel<kEpiGeGluTanh>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       Cfg<256>::SMEM);
+  cudaFuncSetAttribute(gemm_mlp_kernel<kEpiGeGluErf>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       Cfg<256>::SMEM);
   set_smem_attr<128, kEpiF32>();
   set_smem_attr<256, kEpiF32>();
   set_smem_attr<128, kEpiF16>();
@@ -834,6 +1070,53 @@ void gemm_run_epi(const GemmPlan& p, int m, void* out, int ldo, const GemmEpi& e
       gemm_run(p, m, out, ldo, 0, status, stream);
       break;
   }
+}
+
+
+bool gemm_mlp_ok(const GemmPlan& up, const GemmPlan& down) {
+  const int kb_up = (up.s.k + BK - 1) / BK;
+  const int kb_dn = (down.s.k + BK - 1) / BK;
+  // Down split s must read exactly the columns of up column tiles
+  // [s * band, (s + 1) * band) (an up tile stores 128 activation columns).
+  const int kb_split = (kb_dn + down.s.splits - 1) / down.s.splits;
+  return (up.s.epi == kEpiGeGluTanh || up.s.epi == kEpiGeGluErf) && up.s.bn == 256 &&
+         down.s.epi == kEpiF32 && down.s.bn == 256 && kb_split == kb_up &&
+         kb_dn == kb_split * down.s.splits && kb_split % 2 == 0 &&
+         up.s.n_tiles == down.s.splits * (kb_split / 2) && up.s.n_out == down.s.k;
+}
+
+void gemm_run_mlp(const GemmPlan& up, const GemmPlan& down, int m, void* act, int ld_act,
+                  void* slabs, int ld_slab, size_t split_stride, int* ready, int ready_target,
+                  uint32_t* status, cudaStream_t stream) {
+  if (m <= 0) return;
+  MlpArgs a{};
+  auto fill = [&](GemmArgs& x, const GemmPlan& p, void* out, int ldo, size_t stride) {
+    x.m = m;
+    x.n_out = p.s.n_out;
+    x.kb_total = (p.s.k + BK - 1) / BK;
+    x.kb_per_split = (x.kb_total + p.s.splits - 1) / p.s.splits;
+    x.out = out;
+    x.ldo = ldo;
+    x.split_stride = stride;
+    x.status = status;
+    x.m_tiles = (m + BM - 1) / BM;
+    x.n_tiles = p.s.n_tiles;
+    x.splits = p.s.splits;
+  };
+  fill(a.up, up, act, ld_act, 0);
+  fill(a.down, down, slabs, ld_slab, split_stride);
+  a.up.splits = 1;
+  a.ready = ready;
+  a.ready_target = ready_target;
+  a.band = a.down.kb_per_split / 2;
+  const int total = a.up.m_tiles * a.up.n_tiles + a.down.m_tiles * a.down.n_tiles * a.down.splits;
+  const int grid = total < up.num_sms ? total : up.num_sms;
+  if (up.s.epi == kEpiGeGluTanh)
+    launch_pdl(gemm_mlp_kernel<kEpiGeGluTanh>, dim3(grid), dim3(192), Cfg<256>::SMEM, stream, up.a,
+               up.b, down.a, down.b, a);
+  else
+    launch_pdl(gemm_mlp_kernel<kEpiGeGluErf>, dim3(grid), dim3(192), Cfg<256>::SMEM, stream, up.a,
+               up.b, down.a, down.b, a);
 }
 
 }  // namespace omg

@@ -96,6 +96,18 @@ void gemm_run(const GemmPlan& p, int m, void* out, int ldo, size_t split_stride,
 void gemm_run_epi(const GemmPlan& p, int m, void* out, int ldo, const GemmEpi& epi,
                   uint32_t* status, cudaStream_t stream);
 
+// Gate+up (GeGLU epilogue into `act`) and down (f32 split slabs) of one FFN
+// as one persistent launch whose down units start as soon as the up tiles
+// of their columns are stored. Needs both plans at BN 256 and the down
+// split's K blocks equal to the up projection's (gemm_mlp_ok). `ready` holds
+// one counter per (128-row tile, down split), zeroed at the start of a pass;
+// `ready_target` is the running sum over the pass's fused launches of
+// 4 x (up column tiles / down splits).
+bool gemm_mlp_ok(const GemmPlan& up, const GemmPlan& down);
+void gemm_run_mlp(const GemmPlan& up, const GemmPlan& down, int m, void* act, int ld_act,
+                  void* slabs, int ld_slab, size_t split_stride, int* ready, int ready_target,
+                  uint32_t* status, cudaStream_t stream);
+
 // Encode a TMA tensor map over f16 data with the 128-byte swizzle: `rank`
 // dimensions innermost first, byte strides of dimensions 1..rank-1, box
 // extents per dimension (the innermost box must be 64 elements = 128 bytes).

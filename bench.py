@@ -300,6 +300,8 @@ def run_b200(a, dist: Dist):
                     "restore_ms": round(rm, 3), "save_gbs": round(nbytes / sm / 1e6, 2),
                     "restore_gbs": round(nbytes / rm / 1e6, 2)}
     prof = eng.profile_forward([req], Want.LOGITS, a.profile_iters, resident=resident)
+    kv_bcast = bench_kv_broadcast(eng, synth.request(shape, seed=1000).prefix, dist) \
+        if resident and dist.world > 1 else None
     t_pass = len(req.prefix) * (0 if resident else 1) + sum(len(b.tokens) for b in req.branches)
     # The dominant kernel: the FFN (gate+up with the fused GeGLU, and down) as
     # one launch where the engine fuses them, else the gate+up GEMM alone.
@@ -354,6 +356,8 @@ def run_b200(a, dist: Dist):
     }
     if kv_state:
         out["kv_state"] = kv_state
+    if kv_bcast:
+        out["kv_broadcast"] = kv_bcast
     if dist.world == 1 and not a.no_cpu_baseline:
         cb = cpu_sample(shape, a.cpu_sample_layers)
         out["cpu_baseline"] = {
@@ -487,6 +491,45 @@ def run_laya(a, dist: Dist):
     if dist.rank == 0:
         print(json.dumps(out), flush=True)
     eng.close()
+
+
+def bench_kv_broadcast(eng, prefix, dist: Dist, iters: int = 10):
+    """One state's K/V handed from rank 0 to every rank (grande_b200/split.py:
+    export on rank 0, one NCCL broadcast, import on the others), the step that
+    lets one state's branches run on several GPUs. CUDA events on torch's
+    stream (where the broadcast runs; export and import complete before they
+    return), max over ranks, median of `iters`."""
+    import torch
+    import torch.distributed as tdist
+    from grande_b200.engine import Want
+    from grande_b200.split import share_prefix
+    if dist.rank == 0 and not eng.is_resident(prefix):
+        eng.evaluate(prefix, [], Want.LOGITS)
+    nbytes = eng.state_image_bytes(len(prefix))
+    dev = torch.device("cuda", dist.local)
+    buf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    shares, bcasts = [], []
+    for i in range(iters + 2):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        ev[0].record(stream)
+        share_prefix(eng, prefix, src=0)
+        ev[1].record(stream)
+        ev[2].record(stream)
+        tdist.broadcast(buf, src=0)
+        ev[3].record(stream)
+        torch.cuda.synchronize(dev)
+        if i >= 2:
+            shares.append(dist.max(ev[0].elapsed_time(ev[1])))
+            bcasts.append(dist.max(ev[2].elapsed_time(ev[3])))
+    share_ms, bcast_ms = statistics.median(shares), statistics.median(bcasts)
+    return {"tokens": len(prefix), "bytes": nbytes, "ranks": dist.world,
+            "share_ms": round(share_ms, 4), "broadcast_ms": round(bcast_ms, 4),
+            "broadcast_gbs": round(nbytes / bcast_ms / 1e6, 1),
+            "what": "export on rank 0 + NCCL broadcast + import on the others (share_ms); "
+                    "the broadcast alone (broadcast_ms); CUDA events, max over ranks"}
 
 
 def read_traffic(kernel: str, config: str):

@@ -92,6 +92,9 @@ PROTOTYPES: dict[str, tuple] = {
     "omg_engine_set_state_cache": (C.c_int, [vp, sz, cs, cs]),
     "omg_engine_save_state": (C.c_int, [vp, u32p, sz, pp]),
     "omg_engine_restore_state": (C.c_int, [vp, vp]),
+    "omg_engine_state_image_bytes": (sz, [vp, sz]),
+    "omg_engine_export_state_device": (C.c_int, [vp, u32p, sz, vp, sz]),
+    "omg_engine_import_state_device": (C.c_int, [vp, u32p, sz, vp, sz]),
     "omg_engine_gather_per_layer": (C.c_int, [vp, u32p, sz, u8p, sz]),
     "omg_engine_get_info": (C.c_int, [vp, C.POINTER(EngineInfo)]),
     "omg_engine_time_forward": (C.c_int, [vp, GroupP, sz, C.c_int, C.c_int, C.c_int, f32p,

@@ -216,6 +216,28 @@ int omg_engine_restore_state(omg_engine* e, const omg_state* s) {
   });
 }
 
+size_t omg_engine_state_image_bytes(omg_engine* e, size_t n) {
+  if (!e || !e->e) return 0;
+  return e->e->state_image_bytes(n);
+}
+
+int omg_engine_export_state_device(omg_engine* e, const uint32_t* prefix, size_t n, void* dst,
+                                   size_t cap) {
+  return guarded([&] {
+    eng(e).export_state_device(prefix, n, dst, cap);
+    return 0;
+  });
+}
+
+int omg_engine_import_state_device(omg_engine* e, const uint32_t* prefix, size_t n,
+                                   const void* src, size_t nbytes) {
+  return guarded([&] {
+    if (n && !prefix) fail("prefix is null");
+    eng(e).import_state_device(prefix, n, src, nbytes);
+    return 0;
+  });
+}
+
 int omg_engine_gather_per_layer(omg_engine* e, const uint32_t* ids, size_t n, uint8_t* out,
                                 size_t cap) {
   return guarded([&] {

@@ -3,6 +3,8 @@
 
 #include <sys/stat.h>
 
+#include <cuda_profiler_api.h>
+
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
@@ -960,7 +962,11 @@ std::string Engine::profile_forward(const GroupIn* groups, size_t n, Want want, 
   upload(p, rows.empty() ? nullptr : rows.data(), rows.size());
   profiling_ = true;
   prof_used_ = 0;
+  // The profiled passes are the range an external profiler run with
+  // --profile-from-start off captures.
+  CUDA_TRY(cudaProfilerStart());
   for (int i = 0; i < iters; ++i) launch_forward(p, want);
+  CUDA_TRY(cudaProfilerStop());
   profiling_ = false;
   CUDA_TRY(cudaMemcpyAsync(h_status_.p, status_.p, 4, cudaMemcpyDeviceToHost, stream_));
   CUDA_TRY(cudaStreamSynchronize(stream_));
@@ -1146,6 +1152,78 @@ void Engine::restore_state(const SavedState& s) {
   CUDA_TRY(cudaStreamSynchronize(stream_));
   std::lock_guard<std::mutex> g(mu_);
   resident_ = s.prefix;
+}
+
+size_t Engine::state_image_bytes(size_t n) const {
+  size_t total = 0;
+  for (int l = 0; l < config.layers; ++l) {
+    if (!config.has_kv(l)) continue;
+    auto [r0, r1] = state_rows(l, n);
+    total += (r1 - r0) * static_cast<size_t>(2) * config.kv_heads * config.head_dim[l] * 2;
+  }
+  return total;
+}
+
+namespace {
+// `p` must be device memory of GPU `device` (a collective writes or reads it there).
+void check_device_ptr(const void* p, int device, const char* what) {
+  cudaPointerAttributes a{};
+  if (!p || cudaPointerGetAttributes(&a, p) != cudaSuccess ||
+      (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged) || a.device != device) {
+    cudaGetLastError();
+    fail("%s is not device memory of GPU %d", what, device);
+  }
+}
+}  // namespace
+
+void Engine::export_state_device(const uint32_t* prefix, size_t n, void* dst, size_t cap) {
+  CUDA_TRY(cudaSetDevice(device_));
+  if (!is_resident(prefix, n)) fail("export_state_device: the prefix is not resident");
+  const size_t need = state_image_bytes(n);
+  if (cap < need) fail("export_state_device: buffer holds %zu bytes, need %zu", cap, need);
+  check_device_ptr(dst, device_, "export_state_device: dst");
+  size_t off = 0;
+  for (int l = 0; l < config.layers; ++l) {
+    if (!config.has_kv(l)) continue;
+    auto [r0, r1] = state_rows(l, n);
+    const size_t row_bytes = static_cast<size_t>(2) * config.kv_heads * config.head_dim[l] * 2;
+    const size_t bytes = (r1 - r0) * row_bytes;
+    if (bytes)
+      CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(dst) + off, kv_[l].as<uint8_t>() + r0 * row_bytes,
+                               bytes, cudaMemcpyDeviceToDevice, stream_));
+    off += bytes;
+  }
+  CUDA_TRY(cudaStreamSynchronize(stream_));
+}
+
+void Engine::import_state_device(const uint32_t* prefix, size_t n, const void* src,
+                                 size_t nbytes) {
+  CUDA_TRY(cudaSetDevice(device_));
+  if (n > capacity) fail("state of %zu tokens exceeds the engine capacity %zu", n, capacity);
+  const size_t need = state_image_bytes(n);
+  if (nbytes != need)
+    fail("import_state_device: %zu bytes for a %zu-token state, expected %zu", nbytes, n, need);
+  check_device_ptr(src, device_, "import_state_device: src");
+  size_t off = 0;
+  for (int l = 0; l < config.layers; ++l) {
+    if (!config.has_kv(l)) continue;
+    auto [r0, r1] = state_rows(l, n);
+    const size_t row_bytes = static_cast<size_t>(2) * config.kv_heads * config.head_dim[l] * 2;
+    const size_t bytes = (r1 - r0) * row_bytes;
+    if (bytes)
+      CUDA_TRY(cudaMemcpyAsync(kv_[l].as<uint8_t>() + r0 * row_bytes,
+                               static_cast<const uint8_t*>(src) + off, bytes,
+                               cudaMemcpyDeviceToDevice, stream_));
+    off += bytes;
+  }
+  std::vector<TokMeta> meta(n);
+  for (size_t i = 0; i < n; ++i) meta[i] = {static_cast<int>(i), 0, 0, static_cast<int>(i + 1)};
+  if (n)
+    CUDA_TRY(cudaMemcpyAsync(meta_.p, meta.data(), n * sizeof(TokMeta), cudaMemcpyHostToDevice,
+                             stream_));
+  CUDA_TRY(cudaStreamSynchronize(stream_));
+  std::lock_guard<std::mutex> g(mu_);
+  resident_ = std::vector<uint32_t>(prefix, prefix + n);
 }
 
 std::string Engine::state_path(const uint32_t* prefix, size_t n) const {

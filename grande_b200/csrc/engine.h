@@ -180,6 +180,12 @@ class Engine {
   void set_state_cache(size_t bytes, const std::string& dir, const std::string& model_id);
   SavedState save_state(const uint32_t* prefix, size_t n);
   void restore_state(const SavedState& s);
+  // A state's K/V rows as one device buffer on this engine's GPU (the layer
+  // payloads of save_state, f16, concatenated in layer order), so that a
+  // collective can move a prefill from one GPU to others without a host copy.
+  size_t state_image_bytes(size_t n) const;
+  void export_state_device(const uint32_t* prefix, size_t n, void* dst, size_t cap);
+  void import_state_device(const uint32_t* prefix, size_t n, const void* src, size_t nbytes);
   int embed_dtype() const { return embed_.dtype; }
   cudaStream_t stream() const { return stream_; }
   int device() const { return device_; }

@@ -4,6 +4,8 @@
 // scorer / act head (:1442-1543).
 #include "laya.h"
 
+#include <cuda_profiler_api.h>
+
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -843,7 +845,11 @@ std::string LayaEngine::profile_forward(const LayaSequence* seqs, size_t n, int 
   upload(p);
   profiling_ = true;
   prof_used_ = 0;
+  // The profiled passes are the range an external profiler run with
+  // --profile-from-start off captures.
+  CUDA_TRY(cudaProfilerStart());
   for (int i = 0; i < iters; ++i) launch_forward(p);
+  CUDA_TRY(cudaProfilerStop());
   profiling_ = false;
   CUDA_TRY(cudaMemcpyAsync(h_status_.p, status_.p, 4, cudaMemcpyDeviceToHost, stream_));
   CUDA_TRY(cudaStreamSynchronize(stream_));

@@ -328,6 +328,27 @@ class Engine:
     def restore_state(self, state: SavedState):
         check(lib().omg_engine_restore_state(self._h, state._h))
 
+    # ---- a state moved between GPUs (no host copy) ----------------------------
+
+    def state_image_bytes(self, n_prefix: int) -> int:
+        """Bytes of the device image of an `n_prefix`-token state (the f16 K/V
+        rows save_state returns, layer payloads concatenated)."""
+        return int(lib().omg_engine_state_image_bytes(self._h, n_prefix))
+
+    def export_state_device(self, prefix, dst_ptr: int, cap: int):
+        """Copy the resident `prefix`'s K/V rows into device memory at
+        `dst_ptr` (this engine's GPU); complete on return."""
+        p = np.ascontiguousarray(np.asarray(prefix, dtype=np.int64).astype(np.uint32))
+        check(lib().omg_engine_export_state_device(self._h, _lib.ptr(p, C.c_uint32), p.size,
+                                                   C.c_void_p(dst_ptr), cap))
+
+    def import_state_device(self, prefix, src_ptr: int, nbytes: int):
+        """Make `prefix` resident from a device image at `src_ptr` (this
+        engine's GPU), as restore_state does from a SavedState."""
+        p = np.ascontiguousarray(np.asarray(prefix, dtype=np.int64).astype(np.uint32))
+        check(lib().omg_engine_import_state_device(self._h, _lib.ptr(p, C.c_uint32), p.size,
+                                                   C.c_void_p(src_ptr), nbytes))
+
     def gather_per_layer(self, ids) -> bytes:
         i = np.ascontiguousarray(np.asarray(ids, dtype=np.int64).astype(np.uint32))
         n = i.size * self.per_layer_dim * self.layers * 2

@@ -172,6 +172,21 @@ int omg_engine_save_state(omg_engine* e, const uint32_t* prefix, size_t n, omg_s
 /* Engine::restore_state (engine.rs:2051-2092): the prefix becomes resident. */
 int omg_engine_restore_state(omg_engine* e, const omg_state* s);
 
+/* A state moved between GPUs without a host copy (extends Engine::save_state /
+ * restore_state, engine.rs:1977-2092, which the reference runs on one device):
+ * the image is save_state's layer payloads (f16 K/V rows, sliding layers
+ * window-only) concatenated in layer order, in device memory of the engine's
+ * GPU, so one NCCL broadcast can hand a prefill to the GPUs that run the rest
+ * of its branches. state_image_bytes: the image size of an n-token state.
+ * export: the prefix must be resident; the copy is complete on return.
+ * import: the prefix becomes resident, as after restore_state; the caller
+ * makes sure whatever wrote `src` (a collective on another stream) is done. */
+size_t omg_engine_state_image_bytes(omg_engine* e, size_t n);
+int omg_engine_export_state_device(omg_engine* e, const uint32_t* prefix, size_t n, void* dst,
+                                   size_t cap);
+int omg_engine_import_state_device(omg_engine* e, const uint32_t* prefix, size_t n,
+                                   const void* src, size_t nbytes);
+
 /* Engine::gather_per_layer (engine.rs:1370-1381) with the engine's table:
  * f16 LE rows for `ids`, n * layers * P * 2 bytes. */
 int omg_engine_gather_per_layer(omg_engine* e, const uint32_t* ids, size_t n, uint8_t* out,

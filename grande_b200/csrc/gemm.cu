@@ -28,12 +28,31 @@ struct GemmArgs {
   int kb_total;      // 64-wide K blocks
   int kb_per_split;  // K blocks per split-K slab
   int m_tiles, n_tiles, splits;
+  int n_fast;        // tile order: 0 = M tile fastest, 1 = N tile fastest
   void* out;
   int ldo;           // output row stride in elements
   size_t split_stride;
   uint32_t* status;
   GemmEpi epi;
 };
+
+// Tile t of a launch: split-major, then (m fastest) or (n fastest).
+// M-fastest suits the decoder's projections (a few M tiles against a large
+// weight: the CTAs running at once share weight tiles in L2); N-fastest the
+// encoder's (32k rows against a weight of a few MB: each block of A rows is
+// read from HBM once, by CTAs running side by side).
+struct TileId {
+  int m, n, split;
+};
+__device__ __forceinline__ TileId decode_tile(const GemmArgs& g, int t) {
+  const int mn = g.m_tiles * g.n_tiles;
+  const int r = t % mn;
+  TileId x;
+  x.split = t / mn;
+  x.m = g.n_fast ? r / g.n_tiles : r % g.m_tiles;
+  x.n = g.n_fast ? r % g.n_tiles : r / g.m_tiles;
+  return x;
+}
 
 template <int BN>
 struct Cfg {
@@ -58,15 +77,18 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 
 __device__ __forceinline__ float erf_as(float x) {
   // Abramowitz & Stegun 7.1.26, the erf the reference's ModernBERT GeGLU
-  // uses (matmul_gated.wgsl:114-124).
+  // uses (matmul_gated.wgsl:114-124). The formula's own error is 1.5e-7 and
+  // WGSL's `/` and `exp` are not correctly rounded either, so the reciprocal
+  // and the exponential use the fast hardware forms (a few ulp): this
+  // epilogue runs once per output element of the encoder's largest GEMM and
+  // its instruction count, not the tensor pipe, set that GEMM's pace.
   const float s = x < 0.f ? -1.f : (x > 0.f ? 1.f : 0.f);
   const float a = fabsf(x);
-  const float t = 1.0f / (1.0f + 0.3275911f * a);
-  const float y =
-      1.0f -
-      (((((1.061405429f * t - 1.453152027f) * t) + 1.421413741f) * t - 0.284496736f) * t +
-       0.254829592f) *
-          t * expf(-a * a);
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, a, 1.0f));
+  const float p =
+      fmaf(fmaf(fmaf(fmaf(1.061405429f, t, -1.453152027f), t, 1.421413741f), t, -0.284496736f),
+           t, 0.254829592f);
+  const float y = 1.0f - p * t * __expf(-a * a);
   return s * y;
 }
 
@@ -221,6 +243,13 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, int m_tile, int
     const int p = row < g.m ? g.epi.pos[row] : 0;
     const float2* rt = g.epi.rope + p;
     const size_t rs = static_cast<size_t>(g.epi.rope_stride);
+    // Every head of the row rotates by the same 32 (cos, sin) pairs: read
+    // them once per tile, all in flight together, before the first chunk.
+    float2 cs[32];
+    if (n_tile * BN < 2 * g.epi.q_cols) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) cs[j] = rt[j * rs];
+    }
 #pragma unroll 1
     for (int c = 0; c < BN / 32; c += 2) {
       float lo[32], hi[32];
@@ -232,10 +261,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, int m_tile, int
         const float sc = col0 < g.epi.q_cols ? g.epi.q_scale : 1.0f;
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const float2 cs = rt[j * rs];
           const float a = lo[j], b = hi[j];
-          lo[j] = (a * cs.x - b * cs.y) * sc;
-          hi[j] = (b * cs.x + a * cs.y) * sc;
+          lo[j] = (a * cs[j].x - b * cs[j].y) * sc;
+          hi[j] = (b * cs[j].x + a * cs[j].y) * sc;
         }
       }
       if (col0 + 64 <= g.n_out) {
@@ -302,6 +330,53 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, int m_tile, int
     const float* __restrict__ bias = g.epi.bias;
     const bool bias_first = g.epi.bias_first != 0;
     const int pc4 = lane & 7;  // this lane's 4 columns of a chunk: 4 pc4 .. 4 pc4 + 3
+    if (nrows == 32 && (n_tile + 1) * BN <= g.n_out) {
+      // Whole 32-row x BN block: the residual values of chunk c + 1 are
+      // loaded before chunk c is stored, so each chunk's loads are in flight
+      // together and overlap the previous chunk's math and stores (the
+      // caller has asked L2 for these rows a tile ahead).
+      float* __restrict__ xrow = wbase + static_cast<size_t>(lane >> 3) * g.ldo + n_tile * BN + 4 * pc4;
+      const size_t step = static_cast<size_t>(4) * g.ldo;  // rows r and r + 4
+      auto load = [&](float4 (&x)[8], int c) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = *reinterpret_cast<const float4*>(xrow + i * step + c * 32);
+      };
+      auto update = [&](float4 (&x)[8], int c) {
+        const int col = n_tile * BN + c * 32 + 4 * pc4;
+        float bl[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) bl[e] = bias ? __ldg(bias + col + e) : 0.f;
+        float v[32];
+        tmem_ld32(tbase + c * 32, v);
+        uint4 pc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pc[i] = pack_f32x4(v + 4 * i);
+        stage_pieces(slot, lane, 0, pc, 8);
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = 4 * i + (lane >> 3);
+          const float4 a = *reinterpret_cast<const float4*>(slot + r * 128 + ((pc4 ^ (r & 7)) << 4));
+          const float av[4] = {a.x, a.y, a.z, a.w};
+          float* xe = reinterpret_cast<float*>(&x[i]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            xe[e] = bias_first ? (av[e] + bl[e]) + xe[e] : (xe[e] + av[e]) + bl[e];
+          *reinterpret_cast<float4*>(xrow + i * step + c * 32) = x[i];
+        }
+        __syncwarp();
+      };
+      float4 xa[8], xb[8];
+      load(xa, 0);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; c += 2) {
+        load(xb, c + 1);
+        update(xa, c);
+        if (c + 2 < BN / 32) load(xa, c + 2);
+        update(xb, c + 1);
+      }
+      return;
+    }
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       float v[32];
@@ -471,10 +546,23 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, int m_tile, int
   }
 }
 
-// Persistent: CTA b handles tiles b, b + gridDim.x, ... Tile t is
-// (m = t % m_tiles, n = (t / m_tiles) % n_tiles, split = t / (m_tiles * n_tiles)):
-// the CTAs running at once share few weight tiles, which stay in L2 while
-// every M tile of them is computed.
+// L2 prefetch of the residual rows tile `tile` of a kEpiResidF32 GEMM
+// updates: lane i of epilogue warp q asks for its own row's BN columns.
+template <int BN>
+__device__ __forceinline__ void residual_prefetch(const GemmArgs& g, int tile, int q, int lane) {
+  if (tile >= g.m_tiles * g.n_tiles * g.splits) return;
+  const TileId id = decode_tile(g, tile);
+  const int row = id.m * BM + q * 32 + lane;
+  const int col0 = id.n * BN;
+  if (row >= g.m) return;
+  const float* p = static_cast<const float*>(g.out) + static_cast<size_t>(row) * g.ldo + col0;
+  const int n = min(BN, g.n_out - col0);
+#pragma unroll 1
+  for (int c = 0; c < n; c += 32) prefetch_l2(p + c);
+}
+
+// Persistent: CTA b handles tiles b, b + gridDim.x, ... in decode_tile's
+// order.
 template <int BN, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
@@ -526,9 +614,8 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       int it = 0;
       for (int tile = blockIdx.x; tile < total && !*abort_flag; tile += gridDim.x) {
-        const int m_tile = tile % g.m_tiles;
-        const int n_tile = (tile / g.m_tiles) % g.n_tiles;
-        const int split = tile / (g.m_tiles * g.n_tiles);
+        const TileId id = decode_tile(g, tile);
+        const int m_tile = id.m, n_tile = id.n, split = id.split;
         const int kb0 = split * g.kb_per_split;
         const int kb1 = min(g.kb_total, kb0 + g.kb_per_split);
         bool ok = true;
@@ -590,11 +677,13 @@ __global__ void __launch_bounds__(192, 1)
       asm volatile("bar.sync 1, 128;" ::: "memory");
     }
     int local = 0;
+    if constexpr (EPI == kEpiResidF32) residual_prefetch<BN>(g, blockIdx.x, q, lane);
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++local) {
-      const int m_tile = tile % g.m_tiles;
-      const int n_tile = (tile / g.m_tiles) % g.n_tiles;
-      const int split = tile / (g.m_tiles * g.n_tiles);
+      const TileId id = decode_tile(g, tile);
+      const int m_tile = id.m, n_tile = id.n, split = id.split;
       const int b = local & 1;
+      // The residual rows the next tile updates, requested a tile ahead.
+      if constexpr (EPI == kEpiResidF32) residual_prefetch<BN>(g, tile + gridDim.x, q, lane);
       int ok = 0;
       if (lane == 0) ok = mbar_wait(&tfull[b], (local >> 1) & 1, abort_flag, g.status) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -862,6 +951,9 @@ bool make_tmap_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t out
   return make_tmap_f16(m, base, 2, dims, strides, box, err, errlen);
 }
 
+// N-fastest tile order when the A rows outweigh the weight rows four to one.
+int n_fast_order(int m, int n) { return static_cast<int64_t>(m) > 4 * static_cast<int64_t>(n) ? 1 : 0; }
+
 template <int BN, int EPI>
 void set_smem_attr() {
   cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1008,6 +1100,7 @@ void gemm_run(const GemmPlan& p, int m, void* out, int ldo, size_t split_stride,
   a.m_tiles = (m + BM - 1) / BM;
   a.n_tiles = p.s.n_tiles;
   a.splits = p.s.splits;
+  a.n_fast = n_fast_order(m, p.s.n_tiles * p.s.bn);
   switch (p.s.epi) {
     case kEpiF32:
       if (p.s.bn == 256)
@@ -1047,6 +1140,7 @@ void gemm_run_epi(const GemmPlan& p, int m, void* out, int ldo, const GemmEpi& e
   a.m_tiles = (m + BM - 1) / BM;
   a.n_tiles = p.s.n_tiles;
   a.splits = 1;
+  a.n_fast = n_fast_order(m, p.s.n_tiles * p.s.bn);
   a.epi = epi;
   const bool wide = p.s.bn == 256;
   switch (p.s.epi) {

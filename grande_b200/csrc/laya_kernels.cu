@@ -34,16 +34,17 @@ constexpr int kLnMaxVec = 16;  // float4 per lane: d <= 2048
 
 // Mean, then the variance around it (layernorm.wgsl:51-61), of a row held as
 // float4s by one warp (lane l owns float4 l + 32 k, k < nv).
-__device__ __forceinline__ void ln_stats(const float4 (&v)[kLnMaxVec], int nv, int d, float eps,
+template <int N>
+__device__ __forceinline__ void ln_stats(const float4 (&v)[N], int nv, int d, float eps,
                                          float* mean, float* inv) {
   float s = 0.f;
 #pragma unroll
-  for (int k = 0; k < kLnMaxVec; ++k)
+  for (int k = 0; k < N; ++k)
     if (k < nv) s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
   const float m = warp_sum(s) / static_cast<float>(d);
   float q = 0.f;
 #pragma unroll
-  for (int k = 0; k < kLnMaxVec; ++k)
+  for (int k = 0; k < N; ++k)
     if (k < nv) {
       const float a = v[k].x - m, b = v[k].y - m, c = v[k].z - m, e = v[k].w - m;
       q += (a * a + b * b) + (c * c + e * e);
@@ -67,25 +68,27 @@ __device__ __forceinline__ void store_h4(__half* p, float4 v) {
 
 __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 
-// One warp per row, 8 rows per CTA.
+// One warp per row, 8 rows per CTA; NV = d / 128 float4s per lane, so the
+// registers a row takes (and with them how many rows an SM keeps in
+// flight) follow the row width.
+template <int NV>
 __global__ void __launch_bounds__(256) laya_ln_kernel(LayaLnArgs a) {
   griddep_wait();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= a.t) return;
-  const int nv = a.d / 128;
+  constexpr int nv = NV;
   float* xr = a.x + static_cast<size_t>(row) * a.d;
-  float4 v[kLnMaxVec];
+  float4 v[NV];
 #pragma unroll
-  for (int k = 0; k < kLnMaxVec; ++k)
-    if (k < nv) v[k] = ld4(xr + (lane + 32 * k) * 4);
+  for (int k = 0; k < NV; ++k) v[k] = ld4(xr + (lane + 32 * k) * 4);
   float mean, inv;
   ln_stats(v, nv, a.d, a.eps, &mean, &inv);
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
   __half* hr = a.h16 ? a.h16 + static_cast<size_t>(row) * a.d : nullptr;
   if (!a.in_place) {
 #pragma unroll
-    for (int k = 0; k < kLnMaxVec; ++k)
+    for (int k = 0; k < NV; ++k)
       if (k < nv) {
         const int c = (lane + 32 * k) * 4;
         store_h4(hr + c, ln_apply(v[k], mean, inv, ld4(a.w1 + c), a.b1 ? ld4(a.b1 + c) : zero));
@@ -94,7 +97,7 @@ __global__ void __launch_bounds__(256) laya_ln_kernel(LayaLnArgs a) {
   }
   const float* te = a.type_emb ? a.type_emb + static_cast<size_t>(a.qtype[row]) * a.d : nullptr;
 #pragma unroll
-  for (int k = 0; k < kLnMaxVec; ++k)
+  for (int k = 0; k < NV; ++k)
     if (k < nv) {
       const int c = (lane + 32 * k) * 4;
       float4 y = ln_apply(v[k], mean, inv, ld4(a.w1 + c), a.b1 ? ld4(a.b1 + c) : zero);
@@ -112,7 +115,7 @@ __global__ void __launch_bounds__(256) laya_ln_kernel(LayaLnArgs a) {
   if (!a.w2) return;
   ln_stats(v, nv, a.d, a.eps, &mean, &inv);
 #pragma unroll
-  for (int k = 0; k < kLnMaxVec; ++k)
+  for (int k = 0; k < NV; ++k)
     if (k < nv) {
       const int c = (lane + 32 * k) * 4;
       store_h4(hr + c, ln_apply(v[k], mean, inv, ld4(a.w2 + c), a.b2 ? ld4(a.b2 + c) : zero));
@@ -446,7 +449,19 @@ void launch_laya_embed_ln(int dtype, const int* ids, int t, const void* codes, c
 
 void launch_laya_ln(const LayaLnArgs& a, cudaStream_t s) {
   if (a.t <= 0) return;
-  launch_pdl(laya_ln_kernel, dim3(static_cast<unsigned>((a.t + 7) / 8)), dim3(256), 0, s, a);
+  const dim3 grid(static_cast<unsigned>((a.t + 7) / 8));
+  switch (a.d / 128) {
+#define OMG_LN_CASE(n) \
+  case n:              \
+    launch_pdl(laya_ln_kernel<n>, grid, dim3(256), 0, s, a); \
+    break;
+    OMG_LN_CASE(1) OMG_LN_CASE(2) OMG_LN_CASE(3) OMG_LN_CASE(4) OMG_LN_CASE(5) OMG_LN_CASE(6)
+    OMG_LN_CASE(7) OMG_LN_CASE(8) OMG_LN_CASE(9) OMG_LN_CASE(10) OMG_LN_CASE(11)
+    OMG_LN_CASE(12) OMG_LN_CASE(13) OMG_LN_CASE(14) OMG_LN_CASE(15) OMG_LN_CASE(16)
+#undef OMG_LN_CASE
+    default:
+      break;
+  }
 }
 
 void launch_laya_gather(const float* x, int d, const int* row_map, int n, float* rows,

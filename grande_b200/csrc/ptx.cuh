@@ -124,6 +124,11 @@ __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 
+// Bring the 128-byte line holding `p` into L2 (no register result, no wait).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
+}
+
 // ---- tcgen05: tensor memory ------------------------------------------------
 
 // Allocate `ncols` TMEM columns (power of two, >= 32); one full warp calls it.

@@ -103,3 +103,36 @@ def test_gated_config_shape(device):
     exp = gelu_tanh(xf @ wg.astype(np.float32).T) * (xf @ wu.astype(np.float32).T)
     got = run_gemm(device, x16, w, n, 1)
     assert rel_err(got, exp) < TOL + 1e-3
+
+
+def gelu_erf(x):
+    from scipy.special import erf
+    return 0.5 * x * (1.0 + erf(x / np.sqrt(2.0)))
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+def test_matmul_n_fastest_order(device, bn):
+    """Rows outnumber weight rows more than four to one: the tiles are
+    walked N-fastest (the encoder's shapes); same result."""
+    m, n, k = 4100, 300, 192
+    rng = np.random.default_rng(bn)
+    x16 = rng.uniform(-1, 1, (m, k)).astype(np.float16)
+    w16 = rng.uniform(-1, 1, (n, k)).astype(np.float16)
+    exp = x16.astype(np.float64) @ w16.astype(np.float64).T
+    got = run_gemm(device, x16, w16, n, 0, bn=bn, splits=1)
+    assert rel_err(got, exp) < TOL
+
+
+def test_gated_erf_encoder_rows(device):
+    """The erf GeGLU epilogue (matmul_gated.wgsl:114-134, GELU_ERF = 1) on
+    an encoder-like shape, against the exact erf GELU."""
+    m, n, k = 2100, 200, 128
+    rng = np.random.default_rng(5)
+    x16 = rng.uniform(-1, 1, (m, k)).astype(np.float16)
+    wg = (rng.uniform(-1, 1, (n, k)) * 0.3).astype(np.float16)
+    wu = (rng.uniform(-1, 1, (n, k)) * 0.3).astype(np.float16)
+    w = interleave_gate_up(wg, wu)
+    xd = x16.astype(np.float64)
+    exp = gelu_erf(xd @ wg.astype(np.float64).T) * (xd @ wu.astype(np.float64).T)
+    got = run_gemm(device, x16, w, n, 2)
+    assert rel_err(got, exp) < TOL + 1e-3

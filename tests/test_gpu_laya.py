@@ -84,6 +84,18 @@ def test_mmbert_shape_two_layers():
     check_rows(m, seqs, capacity=1024, max_rows=64)
 
 
+def test_large_batch_n_fastest_tiles():
+    """48 sequences of 128 tokens (6,144 rows): every projection has more
+    than four times as many rows as weight rows, so the GEMMs walk their
+    tiles N-fastest and the in-place residual epilogue takes its whole-block
+    path, as at the mmBERT bench size."""
+    m = LayaModel(small(layers=2, window=64), 31, O.Q8, O.Q8)
+    rng = np.random.default_rng(11)
+    seqs = [Sequence([1] + list(rng.integers(5, 96, 127)), [int(rng.integers(1, 128))], i % 3)
+            for i in range(48)]
+    check_rows(m, seqs, capacity=48 * 128, max_rows=128)
+
+
 @pytest.mark.parametrize("long", [False, True])
 def test_sequences_are_isolated(long):
     """A sequence's rows do not depend on what is packed beside it: the same

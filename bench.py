@@ -17,8 +17,12 @@ collective on the data path). Rank 0 prints one JSON line.
   with host buffers: ids/metadata uploaded and logits read back every step,
   a fresh state each step (the resident prefix is evicted), CUDA events on
   the engine's stream around the K calls.
-* ``roofline``: the GeGLU GEMM (the largest kernel) from per-launch CUDA
-  events, against MEASURED_PEAKS.json.
+* ``roofline``: the largest kernel -- the fused FFN launch (gate+up with the
+  GeGLU epilogue, then down) on the decoder, the erf-GeGLU Wi GEMM on the
+  encoder -- from per-launch CUDA events, against MEASURED_PEAKS.json, with
+  ``traffic`` from the committed ncu summary under profiles/.
+* ``kv_broadcast`` (resident config, N > 1): one state's K/V handed from
+  rank 0 to every rank with one NCCL broadcast (grande_b200/split.py).
 * ``cpu_baseline`` / ``--impl reference``: the reference's CPU forward
   (tests/reference.rs), restated in oracle/, on the host cores.
 
@@ -472,7 +476,7 @@ def run_laya(a, dist: Dist):
         "roofline": {"kernel": "gemm_wi (tcgen05, fused erf GeGLU)", "bound": "tensor",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "peak_kind": f"{pk_kind} sustained",
-                     "traffic": None, "avg_launch_ms": round(wi_avg, 5),
+                     "traffic": read_traffic("gemm_wi", a.config), "avg_launch_ms": round(wi_avg, 5),
                      "flop_per_launch": flops_wi},
         "kernels_ms_per_pass": {k: round(v[1] / a.profile_iters, 4) for k, v in prof.items()},
         "clocks": clk,

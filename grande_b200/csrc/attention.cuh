@@ -59,12 +59,44 @@ struct AttnFlashRun {
   int tile0, ntiles;    // its key tiles: tiles[tile0 .. tile0 + ntiles)
 };
 
+// A run's key tiles are split into chunks of kAttnChunkTiles grid tiles,
+// counted from the group's first cache row (so a token's chunks do not
+// depend on what shares its run). One CTA per (item, KV head): a run whose
+// tiles fall in one chunk writes its output directly (slot -1); a run that
+// spans several writes, per chunk, the unnormalised O (f32) and the row's
+// (reference max, sum) to a partial slot, and a merge combines the chunks in
+// order. The chain of dependent key tiles per CTA is at most a chunk.
+constexpr int kAttnChunkTiles = 3;
+
+// Parts of a pass's staged attention schedule: the visibility intervals,
+// then per window (sliding, global) runs, tiles, items and merges.
+constexpr int kAttnSchedParts = 9;
+constexpr int attn_sched_part(int window_kind, int what) { return 1 + 4 * window_kind + what; }
+
+struct AttnFlashItem {
+  int run;      // index into the runs
+  int t0, nt;   // tiles[run.tile0 + t0 .. + nt)
+  int slot;     // partial slot (x kv_heads + KV head), or -1: final output
+};
+
+struct AttnFlashMerge {
+  int run;
+  int slot0;    // its chunk c sits in slot slot0 + c
+  int nchunks;
+};
+
 struct AttnFlashArgs {
   const int4* vis;       // per workspace token: visible cache rows [x, y) U [z, w), no window
   const TokMeta* meta;   // cache-row order
   const AttnFlashRun* runs;
   const int* tiles;      // first cache row of each key tile
   int n_runs;
+  const AttnFlashItem* items;
+  int n_items;
+  const AttnFlashMerge* merges;
+  int n_merges;
+  float* part_o;         // [slot x kv_heads][128 rows][256] unnormalised O
+  float2* part_ml;       // [slot x kv_heads][128 rows] (reference max, row sum)
   __half* out;           // [t, heads * 256] f16
   uint32_t* status;      // device status word (bounded waits)
   int t, base, heads, kv_heads, hpg, window;
@@ -82,9 +114,11 @@ void attention_intervals(const TokMeta* meta_ws, int t, int base, std::vector<in
 bool attention_check_intervals(const TokMeta* meta_all, int t, int base, const int4* vis,
                                int window);
 
-// Runs of a pass and their key tiles for one window (0 = global).
-void attention_flash_runs(const TokMeta* meta_ws, const int4* vis, int t, int hpg, int window,
-                          std::vector<AttnFlashRun>* runs, std::vector<int>* tiles);
+// Runs of a pass, their key tiles, and the CTA items / merges of the chunk
+// split for one window (0 = global). Returns the partial slots used.
+int attention_flash_runs(const TokMeta* meta_ws, const int4* vis, int t, int hpg, int window,
+                         std::vector<AttnFlashRun>* runs, std::vector<int>* tiles,
+                         std::vector<AttnFlashItem>* items, std::vector<AttnFlashMerge>* merges);
 
 // Tensor maps of the tensor-core kernel: q16 [t_cap][heads * 256] f16 and one
 // layer's K/V cache [rows_cap][2 * kv_heads * 256] f16 (64-key boxes).
@@ -97,6 +131,11 @@ bool attention_map_kv(CUtensorMap* m, const void* kv, int rows_cap, int kv_heads
 // so P carries ~22 bits instead of f16's 11.
 void launch_attention_flash(const CUtensorMap& tq, const CUtensorMap& tkv,
                             const AttnFlashArgs& a, bool p_lo, cudaStream_t s);
+
+// Combine the chunk partials of the split runs (after launch_attention_flash,
+// when a.n_merges > 0): per row, out = sum_c w_c O_c / sum_c w_c l_c with
+// w_c = exp(m_c - max_c m_c), chunks in order.
+void launch_attention_merge(const AttnFlashArgs& a, cudaStream_t s);
 
 // Dynamic shared memory the attention kernels need (set once per device).
 void attention_setup_device();

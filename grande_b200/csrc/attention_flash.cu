@@ -111,11 +111,12 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const AttnFlashRun run = g.runs[blockIdx.x];
+  const AttnFlashItem item = g.items[blockIdx.x];
+  const AttnFlashRun run = g.runs[item.run];
   const int kvh = blockIdx.y;
   const int tok_per_tile = kAttnTileRows / g.hpg;
-  const int* tiles = g.tiles + run.tile0;
-  const int nt = run.ntiles;
+  const int* tiles = g.tiles + run.tile0 + item.t0;
+  const int nt = item.nt;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < B_N; ++i) mbar_init(&bars[i], (i == B_P0 || i == B_P1) ? 4 : 1);
@@ -130,7 +131,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   griddep_wait();
-  griddep_launch();  // one CTA per (run, KV head): a single wave
+  griddep_launch();  // one CTA per (item, KV head)
 
   if (warp == 0) {
     if (lane == 0) {
@@ -364,8 +365,42 @@ __global__ void __launch_bounds__(192, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[B_P0 + slot]);
     }
-    if (ok && warp_wait(&bars[B_O0 + ((nt - 1) & 1)], ((nt - 1) >> 1) & 1, abort_flag, g.status,
-                        lane)) {
+    const bool done =
+        ok && warp_wait(&bars[B_O0 + ((nt - 1) & 1)], ((nt - 1) >> 1) & 1, abort_flag, g.status, lane);
+    if (done && item.slot >= 0) {
+      tc_fence_after();
+      // One chunk of a split run: this row's reference max and sum, and its
+      // unnormalised O (f32) in two 128-column halves, each staged in the Q
+      // buffer like the f16 output below (512 bytes per row) and stored a
+      // row per warp instruction.
+      const size_t ps = static_cast<size_t>(item.slot) * g.kv_heads + kvh;
+      g.part_ml[ps * kAttnTileRows + r] = make_float2(m_ref, l);
+      float* po = g.part_o + ps * kAttnTileRows * FA_HD;
+      uint8_t* stage = qs;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float o[32];
+          tmem_ld32(trow + FA_TMEM_O + (4 * half + c) * 32, o);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int piece = 8 * c + e;
+            *reinterpret_cast<uint4*>(stage + r * 512 + ((piece ^ (r & 7)) << 4)) =
+                make_uint4(__float_as_uint(o[4 * e]), __float_as_uint(o[4 * e + 1]),
+                           __float_as_uint(o[4 * e + 2]), __float_as_uint(o[4 * e + 3]));
+          }
+        }
+        __syncwarp();
+        for (int i = 0; i < 32; ++i) {
+          const int row = 32 * q4 + i;
+          const uint4 v =
+              *reinterpret_cast<const uint4*>(stage + row * 512 + ((lane ^ (row & 7)) << 4));
+          *reinterpret_cast<uint4*>(po + static_cast<size_t>(row) * FA_HD + 128 * half + 4 * lane) = v;
+        }
+        __syncwarp();
+      }
+    } else if (done) {
       tc_fence_after();
       // out = O / l as f16, staged in the Q buffer (every S MMA is done):
       // row r at r * 512 bytes, its 16-byte piece p at slot p ^ (r & 7), so
@@ -418,6 +453,80 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// A warp per query row of a split run (8 rows per CTA; grid.x = merges x 16
+// row groups, grid.y = KV heads), lane l holding dims 8 l .. 8 l + 7. Lane c
+// reads chunk c's (max, sum); the chunk with the largest reference max
+// weighs exactly 1 and a chunk the row sees nothing of contributes exact
+// zeros, so a row whose keys all sit in one chunk gets the bits the unsplit
+// path writes, whatever else shares its run. Chunks are added in order, four
+// at a time with all their loads issued first.
+constexpr int kMergeRows = 8;
+
+__global__ void __launch_bounds__(32 * kMergeRows) attention_merge_kernel(AttnFlashArgs g) {
+  griddep_wait();
+  constexpr int groups = kAttnTileRows / kMergeRows;
+  const AttnFlashMerge mg = g.merges[blockIdx.x / groups];
+  const AttnFlashRun run = g.runs[mg.run];
+  const int kvh = blockIdx.y;
+  const int lane = threadIdx.x & 31;
+  const int r = (blockIdx.x % groups) * kMergeRows + (threadIdx.x >> 5);
+  const int tok_per_tile = kAttnTileRows / g.hpg;
+  if (r < min(run.ntok, tok_per_tile) * g.hpg) {
+    const size_t kvs = static_cast<size_t>(g.kv_heads);
+    auto slot_row = [&](int c) {
+      return ((static_cast<size_t>(mg.slot0 + c)) * kvs + kvh) * kAttnTileRows + r;
+    };
+    // The row's overall reference max (chunks beyond 32 folded per lane).
+    float mmax = -INFINITY;
+    for (int c = lane; c < mg.nchunks; c += 32) mmax = fmaxf(mmax, g.part_ml[slot_row(c)].x);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, o));
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float lsum = 0.f;
+    for (int c0 = 0; c0 < mg.nchunks; c0 += 4) {
+      float4 a[4], b[4];
+      float2 ml[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (c0 + k < mg.nchunks) {
+          const size_t sr = slot_row(c0 + k);
+          ml[k] = g.part_ml[sr];
+          const float4* src = reinterpret_cast<const float4*>(g.part_o + sr * FA_HD + 8 * lane);
+          a[k] = src[0];
+          b[k] = src[1];
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (c0 + k >= mg.nchunks) break;
+        // exp2(-inf) = +0 for a chunk the row sees nothing of.
+        const float w = ml[k].x == mmax ? 1.0f : fa_exp2((ml[k].x - mmax) * kLog2e);
+        acc[0] = fmaf(w, a[k].x, acc[0]);
+        acc[1] = fmaf(w, a[k].y, acc[1]);
+        acc[2] = fmaf(w, a[k].z, acc[2]);
+        acc[3] = fmaf(w, a[k].w, acc[3]);
+        acc[4] = fmaf(w, b[k].x, acc[4]);
+        acc[5] = fmaf(w, b[k].y, acc[5]);
+        acc[6] = fmaf(w, b[k].z, acc[6]);
+        acc[7] = fmaf(w, b[k].w, acc[7]);
+        lsum = fmaf(w, ml[k].y, lsum);
+      }
+    }
+    const float inv = lsum > 0.f ? 1.0f / lsum : 0.f;
+    const int tl = r / g.hpg, hh = r - tl * g.hpg;
+    __half* orow = g.out +
+                   (static_cast<size_t>(run.tok0 + tl) * g.heads + kvh * g.hpg + hh) * FA_HD + 8 * lane;
+    uint32_t w4[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const __half2 h = __floats2half2_rn(acc[2 * q] * inv, acc[2 * q + 1] * inv);
+      w4[q] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(orow) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+  }
+  griddep_launch();
+}
+
 }  // namespace
 
 void attention_intervals(const TokMeta* m, int t, int base, std::vector<int4>* vis) {
@@ -458,10 +567,14 @@ bool attention_check_intervals(const TokMeta* meta_all, int t, int base, const i
   return true;
 }
 
-void attention_flash_runs(const TokMeta* m, const int4* vis, int t, int hpg, int window,
-                          std::vector<AttnFlashRun>* runs, std::vector<int>* tiles) {
+int attention_flash_runs(const TokMeta* m, const int4* vis, int t, int hpg, int window,
+                         std::vector<AttnFlashRun>* runs, std::vector<int>* tiles,
+                         std::vector<AttnFlashItem>* items, std::vector<AttnFlashMerge>* merges) {
   runs->clear();
   tiles->clear();
+  items->clear();
+  merges->clear();
+  int slots = 0;
   const int tok_per_tile = kAttnTileRows / hpg;
   std::vector<int2> ivs;
   for (int i = 0; i < t;) {
@@ -495,9 +608,31 @@ void attention_flash_runs(const TokMeta* m, const int4* vis, int t, int hpg, int
         if (any) tiles->push_back(k0);
       }
     }
-    runs->push_back(AttnFlashRun{i, n, first, static_cast<int>(tiles->size()) - first});
+    const int nt = static_cast<int>(tiles->size()) - first;
+    const int ri = static_cast<int>(runs->size());
+    runs->push_back(AttnFlashRun{i, n, first, nt});
+    // Chunks: grid tile index (from row_lo) / kAttnChunkTiles.
+    auto chunk_of = [&](int j) { return ((*tiles)[first + j] - row_lo) / kAttnTileKeys / kAttnChunkTiles; };
+    int nchunks = 0;
+    for (int j = 0; j < nt; ++j)
+      if (j == 0 || chunk_of(j) != chunk_of(j - 1)) ++nchunks;
+    if (nchunks <= 1) {
+      items->push_back(AttnFlashItem{ri, 0, nt, -1});
+    } else {
+      merges->push_back(AttnFlashMerge{ri, slots, nchunks});
+      int c = 0;
+      for (int j = 0; j < nt;) {
+        int e = j + 1;
+        while (e < nt && chunk_of(e) == chunk_of(j)) ++e;
+        items->push_back(AttnFlashItem{ri, j, e - j, slots + c});
+        ++c;
+        j = e;
+      }
+      slots += nchunks;
+    }
     i += n;
   }
+  return slots;
 }
 
 bool attention_map_q(CUtensorMap* mp, const void* q16, int t_cap, int heads, int kv_heads,
@@ -534,12 +669,18 @@ void attention_flash_setup_device() {
 
 void launch_attention_flash(const CUtensorMap& tq, const CUtensorMap& tkv,
                             const AttnFlashArgs& a, bool p_lo, cudaStream_t s) {
-  if (a.n_runs <= 0) return;
-  dim3 grid(a.n_runs, a.kv_heads);
+  if (a.n_items <= 0) return;
+  dim3 grid(a.n_items, a.kv_heads);
   if (p_lo)
     launch_pdl(attention_flash_kernel<true>, grid, dim3(192), fa_smem<true>(), s, tq, tkv, a);
   else
     launch_pdl(attention_flash_kernel<false>, grid, dim3(192), fa_smem<false>(), s, tq, tkv, a);
+}
+
+void launch_attention_merge(const AttnFlashArgs& a, cudaStream_t s) {
+  if (a.n_merges <= 0) return;
+  launch_pdl(attention_merge_kernel, dim3(a.n_merges * (kAttnTileRows / kMergeRows), a.kv_heads),
+             dim3(32 * kMergeRows), 0, s, a);
 }
 
 }  // namespace omg

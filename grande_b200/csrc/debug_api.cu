@@ -109,12 +109,24 @@ extern "C" int omg_debug_attention(int device, const uint16_t* q, const uint16_t
         return set_error("attention: the packing's visibility is not two intervals per token");
       std::vector<omg::AttnFlashRun> runs;
       std::vector<int> tiles;
-      omg::attention_flash_runs(hm + base, vis.data(), t, heads / kv_heads, window, &runs, &tiles);
-      DevBuf dv, dr, dti, dst;
+      std::vector<omg::AttnFlashItem> items;
+      std::vector<omg::AttnFlashMerge> merges;
+      const int slots = omg::attention_flash_runs(hm + base, vis.data(), t, heads / kv_heads, window,
+                                                  &runs, &tiles, &items, &merges);
+      DevBuf dv, dr, dti, dst, dit, dmg, dpo, dpml;
+      const size_t prow = static_cast<size_t>(std::max(slots, 1)) * kv_heads * omg::kAttnTileRows;
       if (!dv.alloc(vis.size() * sizeof(int4)) ||
           !dr.alloc(runs.size() * sizeof(omg::AttnFlashRun)) ||
-          !dti.alloc(std::max<size_t>(tiles.size(), 1) * sizeof(int)) || !dst.alloc(4))
+          !dti.alloc(std::max<size_t>(tiles.size(), 1) * sizeof(int)) || !dst.alloc(4) ||
+          !dit.alloc(items.size() * sizeof(omg::AttnFlashItem)) ||
+          !dmg.alloc(std::max<size_t>(merges.size(), 1) * sizeof(omg::AttnFlashMerge)) ||
+          !dpo.alloc(prow * 256 * sizeof(float)) || !dpml.alloc(prow * sizeof(float2)))
         return set_error("cudaMalloc failed");
+      CUDA_TRY(cudaMemcpy(dit.p, items.data(), items.size() * sizeof(omg::AttnFlashItem),
+                          cudaMemcpyHostToDevice));
+      if (!merges.empty())
+        CUDA_TRY(cudaMemcpy(dmg.p, merges.data(), merges.size() * sizeof(omg::AttnFlashMerge),
+                            cudaMemcpyHostToDevice));
       CUDA_TRY(cudaMemcpy(dv.p, vis.data(), vis.size() * sizeof(int4), cudaMemcpyHostToDevice));
       CUDA_TRY(cudaMemcpy(dr.p, runs.data(), runs.size() * sizeof(omg::AttnFlashRun),
                           cudaMemcpyHostToDevice));
@@ -131,6 +143,12 @@ extern "C" int omg_debug_attention(int device, const uint16_t* q, const uint16_t
       a.runs = static_cast<const omg::AttnFlashRun*>(dr.p);
       a.tiles = static_cast<const int*>(dti.p);
       a.n_runs = static_cast<int>(runs.size());
+      a.items = static_cast<const omg::AttnFlashItem*>(dit.p);
+      a.n_items = static_cast<int>(items.size());
+      a.merges = static_cast<const omg::AttnFlashMerge*>(dmg.p);
+      a.n_merges = static_cast<int>(merges.size());
+      a.part_o = static_cast<float*>(dpo.p);
+      a.part_ml = static_cast<float2*>(dpml.p);
       a.out = static_cast<__half*>(dout.p);
       a.status = static_cast<uint32_t*>(dst.p);
       a.t = t;
@@ -140,6 +158,7 @@ extern "C" int omg_debug_attention(int device, const uint16_t* q, const uint16_t
       a.hpg = heads / kv_heads;
       a.window = window;
       omg::launch_attention_flash(tq, tkv, a, p_lo != 0, 0);
+      if (a.n_merges > 0) omg::launch_attention_merge(a, 0);
       CUDA_TRY(cudaGetLastError());
       CUDA_TRY(cudaDeviceSynchronize());
       uint32_t st = 0;

@@ -623,19 +623,24 @@ Engine::Packing Engine::pack(const GroupIn* groups, size_t n, size_t first,
     const int t = static_cast<int>(p.t), base = static_cast<int>(p.base);
     const int hpg = config.heads / config.kv_heads;
     attention_intervals(p.meta.data(), t, base, &p.attn_vis);
+    p.attn_slots = 0;
     for (int w = 0; w < 2; ++w)
-      attention_flash_runs(p.meta.data(), p.attn_vis.data(), t, hpg, w == 0 ? config.window : 0,
-                           &p.attn_runs[w], &p.attn_tiles[w]);
+      p.attn_slots = std::max(
+          p.attn_slots, attention_flash_runs(p.meta.data(), p.attn_vis.data(), t, hpg,
+                                             w == 0 ? config.window : 0, &p.attn_runs[w],
+                                             &p.attn_tiles[w], &p.attn_items[w], &p.attn_merges[w]));
     size_t off = 0;
     auto put = [&](int i, size_t bytes) {
       p.attn_off[i] = off;
       off += (bytes + 255) / 256 * 256;
     };
     put(0, p.attn_vis.size() * sizeof(int4));
-    put(1, p.attn_runs[0].size() * sizeof(AttnFlashRun));
-    put(2, p.attn_tiles[0].size() * sizeof(int));
-    put(3, p.attn_runs[1].size() * sizeof(AttnFlashRun));
-    put(4, p.attn_tiles[1].size() * sizeof(int));
+    for (int w = 0; w < 2; ++w) {
+      put(attn_sched_part(w, 0), p.attn_runs[w].size() * sizeof(AttnFlashRun));
+      put(attn_sched_part(w, 1), p.attn_tiles[w].size() * sizeof(int));
+      put(attn_sched_part(w, 2), p.attn_items[w].size() * sizeof(AttnFlashItem));
+      put(attn_sched_part(w, 3), p.attn_merges[w].size() * sizeof(AttnFlashMerge));
+    }
     p.attn_bytes = off;
   }
   // out_index[w] = device row of wanted slot w, paired with its flat out row.
@@ -667,12 +672,27 @@ void Engine::upload(const Packing& p, const uint8_t* per_layer_rows, size_t rows
     uint8_t* h = h_attn_sched_.as<uint8_t>();
     std::memcpy(h + p.attn_off[0], p.attn_vis.data(), p.attn_vis.size() * sizeof(int4));
     for (int w = 0; w < 2; ++w) {
-      std::memcpy(h + p.attn_off[1 + 2 * w], p.attn_runs[w].data(),
+      std::memcpy(h + p.attn_off[attn_sched_part(w, 0)], p.attn_runs[w].data(),
                   p.attn_runs[w].size() * sizeof(AttnFlashRun));
-      std::memcpy(h + p.attn_off[2 + 2 * w], p.attn_tiles[w].data(),
+      std::memcpy(h + p.attn_off[attn_sched_part(w, 1)], p.attn_tiles[w].data(),
                   p.attn_tiles[w].size() * sizeof(int));
+      std::memcpy(h + p.attn_off[attn_sched_part(w, 2)], p.attn_items[w].data(),
+                  p.attn_items[w].size() * sizeof(AttnFlashItem));
+      std::memcpy(h + p.attn_off[attn_sched_part(w, 3)], p.attn_merges[w].data(),
+                  p.attn_merges[w].size() * sizeof(AttnFlashMerge));
     }
     CUDA_TRY(cudaMemcpyAsync(attn_sched_.p, h, p.attn_bytes, cudaMemcpyHostToDevice, stream_));
+  }
+  // Partials of the chunk-split attention, grown to the largest pass seen
+  // (a new buffer is a new graph key, so no cached graph keeps the old one).
+  {
+    const size_t rows = static_cast<size_t>(p.attn_slots) * config.kv_heads * kAttnTileRows;
+    if (attn_part_ml_.bytes < rows * sizeof(float2)) {
+      CUDA_TRY(cudaStreamSynchronize(stream_));
+      const size_t cap = std::max<size_t>(rows * 2, 8 * kAttnTileRows);
+      attn_part_o_.alloc(cap * 256 * sizeof(float), false);
+      attn_part_ml_.alloc(cap * sizeof(float2), false);
+    }
   }
   std::memcpy(h_attn_ctas_.p, p.attn_ctas.data(), p.attn_ctas.size() * sizeof(int2));
   CUDA_TRY(cudaMemcpyAsync(attn_ctas_.p, h_attn_ctas_.p, p.attn_ctas.size() * sizeof(int2),
@@ -790,9 +810,15 @@ int Engine::launch_forward(const Packing& p, Want want) {
       AttnFlashArgs ta{};
       ta.vis = reinterpret_cast<const int4*>(sched + p.attn_off[0]);
       ta.meta = meta_.as<TokMeta>();
-      ta.runs = reinterpret_cast<const AttnFlashRun*>(sched + p.attn_off[1 + 2 * w]);
-      ta.tiles = reinterpret_cast<const int*>(sched + p.attn_off[2 + 2 * w]);
+      ta.runs = reinterpret_cast<const AttnFlashRun*>(sched + p.attn_off[attn_sched_part(w, 0)]);
+      ta.tiles = reinterpret_cast<const int*>(sched + p.attn_off[attn_sched_part(w, 1)]);
       ta.n_runs = static_cast<int>(p.attn_runs[w].size());
+      ta.items = reinterpret_cast<const AttnFlashItem*>(sched + p.attn_off[attn_sched_part(w, 2)]);
+      ta.n_items = static_cast<int>(p.attn_items[w].size());
+      ta.merges = reinterpret_cast<const AttnFlashMerge*>(sched + p.attn_off[attn_sched_part(w, 3)]);
+      ta.n_merges = static_cast<int>(p.attn_merges[w].size());
+      ta.part_o = attn_part_o_.as<float>();
+      ta.part_ml = attn_part_ml_.as<float2>();
       ta.out = attn16_.as<__half>();
       ta.status = status;
       ta.t = t;
@@ -803,6 +829,10 @@ int Engine::launch_forward(const Packing& p, Want want) {
       ta.window = ly.sliding ? c.window : 0;
       k("attention");
       launch_attention_flash(attn_tq_, attn_tkv_[ly.kv_src], ta, kAttnPLo, stream_);
+      if (ta.n_merges > 0) {
+        k("attention_merge");
+        launch_attention_merge(ta, stream_);
+      }
     } else {
       AttnArgs aa{};
       aa.q = q16_.as<__half>();
@@ -879,8 +909,10 @@ int Engine::launch_forward(const Packing& p, Want want) {
 bool Engine::GraphKey::operator==(const GraphKey& o) const {
   return t == o.t && base == o.base && nwanted == o.nwanted && ctas == o.ctas &&
          sched_bytes == o.sched_bytes && want == o.want && sched == o.sched &&
-         std::equal(attn_off, attn_off + 5, o.attn_off) && runs[0] == o.runs[0] &&
-         runs[1] == o.runs[1] && tiles[0] == o.tiles[0] && tiles[1] == o.tiles[1];
+         std::equal(attn_off, attn_off + kAttnSchedParts, o.attn_off) && runs[0] == o.runs[0] &&
+         runs[1] == o.runs[1] && tiles[0] == o.tiles[0] && tiles[1] == o.tiles[1] &&
+         items[0] == o.items[0] && items[1] == o.items[1] && merges[0] == o.merges[0] &&
+         merges[1] == o.merges[1] && part == o.part;
 }
 
 Engine::GraphKey Engine::graph_key(const Packing& p, Want want) const {
@@ -890,11 +922,14 @@ Engine::GraphKey Engine::graph_key(const Packing& p, Want want) const {
   k.nwanted = p.nwanted;
   k.ctas = p.attn_ctas.size();
   k.sched_bytes = p.attn_bytes;
-  std::copy(p.attn_off, p.attn_off + 5, k.attn_off);
+  std::copy(p.attn_off, p.attn_off + kAttnSchedParts, k.attn_off);
   for (int w = 0; w < 2; ++w) {
     k.runs[w] = p.attn_runs[w].size();
     k.tiles[w] = p.attn_tiles[w].size();
+    k.items[w] = p.attn_items[w].size();
+    k.merges[w] = p.attn_merges[w].size();
   }
+  k.part = attn_part_o_.p;
   k.want = static_cast<int>(want);
   k.sched = attn_sched_.p;
   return k;

@@ -239,7 +239,12 @@ class Engine {
     std::vector<int4> attn_vis;
     std::vector<AttnFlashRun> attn_runs[2];
     std::vector<int> attn_tiles[2];
-    size_t attn_off[5] = {}, attn_bytes = 0;
+    std::vector<AttnFlashItem> attn_items[2];
+    std::vector<AttnFlashMerge> attn_merges[2];
+    int attn_slots = 0;  // partial slots of the chunk split (the larger window's)
+    // Offsets in the staged schedule block: vis, then per window
+    // runs, tiles, items, merges.
+    size_t attn_off[kAttnSchedParts] = {}, attn_bytes = 0;
     size_t t = 0, base = 0, nwanted = 0;
   };
 
@@ -248,7 +253,9 @@ class Engine {
   // addresses and is uploaded before each pass.
   struct GraphKey {
     size_t t = 0, base = 0, nwanted = 0, ctas = 0, sched_bytes = 0;
-    size_t attn_off[5] = {};
+    size_t attn_off[kAttnSchedParts] = {};
+    size_t items[2] = {}, merges[2] = {};
+    const void* part = nullptr;
     size_t runs[2] = {}, tiles[2] = {};
     int want = 0;
     const void* sched = nullptr;
@@ -301,6 +308,9 @@ class Engine {
 
   // Workspace.
   DevBuffer attn_ctas_, attn_sched_, mlp_ready_;
+  // Chunk-split attention partials: O [slots x kv_heads][128][256] f32 and
+  // (max, sum) [slots x kv_heads][128], grown to the largest pass seen.
+  DevBuffer attn_part_o_, attn_part_ml_;
   PinnedBuffer h_attn_ctas_, h_attn_sched_;
   CUtensorMap attn_tq_;
   std::vector<CUtensorMap> attn_tkv_;  // per layer owning head_dim-256 K/V

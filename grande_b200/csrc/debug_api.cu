@@ -48,8 +48,12 @@ extern "C" int omg_debug_gemm(int device, const uint16_t* x_f16, int m, int k, i
     CUDA_TRY(cudaMemset(dstat.p, 0, 4));
     GemmPlan plan;
     char err[256];
-    if (!gemm_plan(&plan, dx.p, m, lda, dw.p, w_rows, n_out, k, epi, bn, splits, err, sizeof err))
+    // bn 512 asks for the CTA-pair kernel (256 x 256 tiles over two SMs).
+    const bool pair = bn == 512;
+    if (!gemm_plan(&plan, dx.p, m, lda, dw.p, w_rows, n_out, k, epi, pair ? 256 : bn, splits, err,
+                   sizeof err))
       return set_error(err);
+    if (pair && !gemm_plan_pair(&plan, dw.p, w_rows, true, err, sizeof err)) return set_error(err);
     const int sp = f32 ? plan.s.splits : 1;
     const size_t slab = static_cast<size_t>(m) * ldo;
     const size_t ob = slab * sp * (f32 ? 4 : 2);
@@ -195,7 +199,8 @@ extern "C" int omg_debug_attention(int device, const uint16_t* q, const uint16_t
 
 // Time `iters` launches of the GEMM on device-resident random operands
 // (m x k activations, n x k weights, f16) with CUDA events; *ms gets the
-// average per launch. For the kernel sweeps behind profiles/.
+// average per launch (bn 512: the CTA-pair kernel). For the kernel sweeps
+// behind profiles/.
 extern "C" int omg_debug_gemm_time(int device, int m, int n, int k, int epi, int bn, int splits,
                                    int iters, float* ms) {
   return guarded([&]() -> int {
@@ -217,8 +222,11 @@ extern "C" int omg_debug_gemm_time(int device, int m, int n, int k, int epi, int
     CUDA_TRY(cudaMemset(dstat.p, 0, 4));
     GemmPlan plan;
     char err[256];
-    if (!gemm_plan(&plan, dx.p, m, k, dw.p, w_rows, n, k, epi, bn, splits, err, sizeof err))
+    const bool pair = bn == 512;  // the CTA-pair kernel
+    if (!gemm_plan(&plan, dx.p, m, k, dw.p, w_rows, n, k, epi, pair ? 256 : bn, splits, err,
+                   sizeof err))
       return set_error(err);
+    if (pair && !gemm_plan_pair(&plan, dw.p, w_rows, true, err, sizeof err)) return set_error(err);
     cudaEvent_t a, b;
     CUDA_TRY(cudaEventCreate(&a));
     CUDA_TRY(cudaEventCreate(&b));

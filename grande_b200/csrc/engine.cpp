@@ -405,6 +405,10 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
     if (!gemm_plan(p, a, static_cast<int>(C), lda, w, w_rows, n_out, k, epi, bn,
                    std::min(splits, S), err, sizeof err))
       fail("layer %d %s: %s", l, what, err);
+    // Passes of many rows (a long state's prefill) take the CTA-pair kernel.
+    if (p->s.bn == 256 && epi != kEpiBiasF16 && epi != kEpiBiasReluF16 &&
+        !gemm_plan_pair(p, w, w_rows, false, err, sizeof err))
+      fail("layer %d %s: %s", l, what, err);
   };
   layers_.resize(L);
   for (int l = 0; l < L; ++l) {
@@ -858,7 +862,9 @@ int Engine::launch_forward(const Packing& p, Want want) {
                          c.eps, c.norm_offset, 1.0f, x_.as<float>(), nullptr, ly.ffn_norm,
                          h16_.as<__half>(), d, nullptr, nullptr, stream_);
     // GeGLU and down projection.
-    if (ly.fused_mlp) {
+    // The fused FFN launch on one-CTA tiles, or, for passes long enough for
+    // the CTA-pair kernel, its two projections as pair launches.
+    if (ly.fused_mlp && !use_pair(ly.gate_up, t)) {
       k("gemm_mlp");
       mlp_target += 4 * ly.gate_up.s.n_tiles / ly.down.s.splits;
       gemm_run_mlp(ly.gate_up, ly.down, t, act16_.p, ly.ff, a32_.p, d, slab_a,

@@ -707,6 +707,205 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ---- CTA-pair GEMM (tcgen05 cta_group::2) ---------------------------------
+//
+// A cluster of two CTAs on one TPC computes 256-row x 256-column tiles: CTA
+// rank r stages its own 128 rows of A (M tile 2 p + r of pair tile p) and
+// its half of the 256 weight rows (rows 128 r .. 128 r + 127 of the tile),
+// 32 KB per 64-wide K step instead of 48, so six steps are in flight per SM
+// instead of four. The leader's MMA thread issues M = 256, N = 256 MMAs that
+// read both CTAs' halves; each CTA's TMEM receives its own 128 rows, which
+// its epilogue warps drain with the same epilogue as the one-CTA kernel.
+//
+// Barriers (same offsets in both CTAs): full[s] on the leader counts both
+// CTAs' TMA bytes (the leader posts the expectation; each CTA's loads
+// complete on the leader's barrier); empty[s] and tfull[b] are signalled in
+// both CTAs by the leader's commits; tempty[b] on the leader counts the
+// epilogue warps of both CTAs (the peer's arrive remotely).
+struct Cfg2 {
+  static constexpr int STAGES = 6;
+  static constexpr int A_BYTES = BM * BK * 2;       // 128 rows of A
+  static constexpr int B_BYTES = 128 * BK * 2;      // this CTA's 128 weight rows
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + 2048 + 4 * 4096;
+  static constexpr uint32_t TMEM_COLS = 512;        // two 256-column accumulators
+};
+
+// Pair tile t: split-major, then (M pair fastest) or (N fastest).
+__device__ __forceinline__ TileId decode_pair_tile(const GemmArgs& g, int m_pairs, int t) {
+  const int mn = m_pairs * g.n_tiles;
+  const int r = t % mn;
+  TileId x;
+  x.split = t / mn;
+  x.m = g.n_fast ? r / g.n_tiles : r % m_pairs;
+  x.n = g.n_fast ? r % g.n_tiles : r / m_pairs;
+  return x;
+}
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    gemm2_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
+                 GemmArgs g) {
+  constexpr int BN = 256;
+  using C = Cfg2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + C::STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + C::STAGES * C::B_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;   // [2] accumulator ready (both CTAs)
+  uint64_t* tempty = tfull + 2;          // [2] accumulator drained (leader: 8 warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* epi_consts = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = static_cast<int>(cluster_index());
+  const int npairs = static_cast<int>(cluster_count());
+  const int m_pairs = (g.m_tiles + 1) / 2;
+  const int total = m_pairs * g.n_tiles * g.splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tma);
+    prefetch_tmap(&tmb);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  griddep_wait();
+  griddep_launch();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      for (int tile = pair; tile < total && !*abort_flag; tile += npairs) {
+        const TileId id = decode_pair_tile(g, m_pairs, tile);
+        const int m_tile = 2 * id.m + static_cast<int>(rank);
+        const int kb0 = id.split * g.kb_per_split;
+        const int kb1 = min(g.kb_total, kb0 + g.kb_per_split);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, g.status)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * C::STAGE_BYTES);
+          const uint32_t bar = cluster_addr(&full[s], 0);
+          tma_load_2d_pair(sa + s * C::A_BYTES, &tma, bar, kb * BK, m_tile * BM);
+          tma_load_2d_pair(sb + s * C::B_BYTES, &tmb, bar, kb * BK,
+                           id.n * BN + 128 * static_cast<int>(rank));
+        }
+        if (!ok) break;
+      }
+      // The leader's last commits to this CTA's empty barriers are
+      // asynchronous: see them land before the CTA can exit.
+      for (int j = max(0, it - C::STAGES); j < it && !*abort_flag; ++j)
+        if (!mbar_wait(&empty[j % C::STAGES], (j / C::STAGES) & 1, abort_flag, g.status)) break;
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(2 * BM, BN);
+      int it = 0, local = 0;
+      for (int tile = pair; tile < total; tile += npairs, ++local) {
+        const TileId id = decode_pair_tile(g, m_pairs, tile);
+        const int kb0 = id.split * g.kb_per_split;
+        const int kb1 = min(g.kb_total, kb0 + g.kb_per_split);
+        const int b = local & 1;
+        if (!mbar_wait(&tempty[b], ((local >> 1) & 1) ^ 1, abort_flag, g.status)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(b * BN);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort_flag, g.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = sw128_desc(sa + s * C::A_BYTES);
+          const uint64_t db = sw128_desc(sb + s * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16_pair(d, da + 2 * k, db + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          umma_commit_pair(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[b]);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    if constexpr (EPI == kEpiQkPrep) {
+      for (int i = threadIdx.x - 64; i < 512; i += 128) {
+        const float* src = i < 256 ? g.epi.qk.qn : g.epi.qk.kn;
+        epi_consts[i] = src ? src[i & 255] : 0.f;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+    }
+    auto prefetch = [&](int tile) {
+      // The residual rows of this CTA's half of pair tile `tile`, into L2.
+      if constexpr (EPI == kEpiResidF32) {
+        if (tile >= total) return;
+        const TileId id = decode_pair_tile(g, m_pairs, tile);
+        const int row = (2 * id.m + static_cast<int>(rank)) * BM + q * 32 + lane;
+        if (row >= g.m) return;
+        const float* p = static_cast<const float*>(g.out) + static_cast<size_t>(row) * g.ldo + id.n * BN;
+        const int n = min(BN, g.n_out - id.n * BN);
+#pragma unroll 1
+        for (int c = 0; c < n; c += 32) prefetch_l2(p + c);
+      }
+    };
+    prefetch(pair);
+    int local = 0;
+    for (int tile = pair; tile < total; tile += npairs, ++local) {
+      const TileId id = decode_pair_tile(g, m_pairs, tile);
+      const int b = local & 1;
+      prefetch(tile + npairs);
+      int ok = 0;
+      if (lane == 0) ok = mbar_wait(&tfull[b], (local >> 1) & 1, abort_flag, g.status) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      uint8_t* slot = reinterpret_cast<uint8_t*>(full) + 256 + 2048 + q * 4096;
+      const uint32_t tbase =
+          tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BN);
+      epilogue_tile<BN, EPI>(g, 2 * id.m + static_cast<int>(rank), id.n, id.split, tbase, q, lane,
+                             slot, epi_consts);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[b], 0));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  // Neither CTA leaves (or frees TMEM) while the other may still read its
+  // shared memory or signal its barriers.
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, C::TMEM_COLS);
+  }
+}
+
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -960,6 +1159,19 @@ void set_smem_attr() {
                        Cfg<BN>::SMEM);
 }
 
+template <int EPI>
+void set_smem_attr_pair() {
+  cudaFuncSetAttribute(gemm2_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg2::SMEM);
+}
+
+template <int EPI>
+void launch_pair(const GemmPlan& p, const GemmArgs& a, cudaStream_t stream) {
+  const int pairs = ((a.m_tiles + 1) / 2) * a.n_tiles * a.splits;
+  const int max_pairs = p.num_sms / 2;
+  const int grid = 2 * (pairs < max_pairs ? pairs : max_pairs);
+  launch_pdl(gemm2_kernel<EPI>, dim3(grid), dim3(192), Cfg2::SMEM, stream, p.a, p.b_half, a);
+}
+
 template <int BN, int EPI>
 void launch(const GemmPlan& p, const GemmArgs& a, cudaStream_t stream) {
   const int total = a.m_tiles * a.n_tiles * a.splits;
@@ -1017,6 +1229,39 @@ void gemm_setup_device() {
   set_smem_attr<128, kEpiResidF32>();
   set_smem_attr<256, kEpiResidF32>();
   set_smem_attr<256, kEpiQkPrep>();
+  set_smem_attr_pair<kEpiF32>();
+  set_smem_attr_pair<kEpiF16>();
+  set_smem_attr_pair<kEpiGeGluTanh>();
+  set_smem_attr_pair<kEpiGeGluErf>();
+  set_smem_attr_pair<kEpiRopeF16>();
+  set_smem_attr_pair<kEpiResidF32>();
+  set_smem_attr_pair<kEpiQkPrep>();
+}
+
+bool gemm_plan_pair(GemmPlan* p, const void* w, int w_rows, bool always, char* err,
+                    size_t errlen) {
+  if (p->s.bn != 256) {
+    snprintf(err, errlen, "gemm: the CTA-pair kernel needs BN 256 (got %d)", p->s.bn);
+    return false;
+  }
+  switch (p->s.epi) {
+    case kEpiF32: case kEpiF16: case kEpiGeGluTanh: case kEpiGeGluErf: case kEpiRopeF16:
+    case kEpiResidF32: case kEpiQkPrep:
+      break;
+    default:
+      snprintf(err, errlen, "gemm: no CTA-pair kernel for epilogue %d", p->s.epi);
+      return false;
+  }
+  if (!make_tmap_2d(&p->b_half, w, p->s.k, w_rows, static_cast<uint64_t>(p->s.k) * 2, BK, 128, err,
+                    errlen))
+    return false;
+  p->s.pair = always ? 2 : 1;
+  return true;
+}
+
+// Whether a launch over `m` rows takes the CTA-pair kernel.
+bool use_pair(const GemmPlan& p, int m) {
+  return p.s.pair == 2 || (p.s.pair == 1 && (m + BM - 1) / BM >= kPairMinTiles);
 }
 
 void gemm_pick(int n, int k, int num_sms, int* bn, int* splits) {
@@ -1101,6 +1346,16 @@ void gemm_run(const GemmPlan& p, int m, void* out, int ldo, size_t split_stride,
   a.n_tiles = p.s.n_tiles;
   a.splits = p.s.splits;
   a.n_fast = n_fast_order(m, p.s.n_tiles * p.s.bn);
+  if (use_pair(p, m)) {
+    switch (p.s.epi) {
+      case kEpiF32: launch_pair<kEpiF32>(p, a, stream); break;
+      case kEpiF16: launch_pair<kEpiF16>(p, a, stream); break;
+      case kEpiGeGluTanh: launch_pair<kEpiGeGluTanh>(p, a, stream); break;
+      case kEpiGeGluErf: launch_pair<kEpiGeGluErf>(p, a, stream); break;
+      default: break;
+    }
+    return;
+  }
   switch (p.s.epi) {
     case kEpiF32:
       if (p.s.bn == 256)
@@ -1143,6 +1398,15 @@ void gemm_run_epi(const GemmPlan& p, int m, void* out, int ldo, const GemmEpi& e
   a.n_fast = n_fast_order(m, p.s.n_tiles * p.s.bn);
   a.epi = epi;
   const bool wide = p.s.bn == 256;
+  if (use_pair(p, m)) {
+    switch (p.s.epi) {
+      case kEpiRopeF16: launch_pair<kEpiRopeF16>(p, a, stream); break;
+      case kEpiResidF32: launch_pair<kEpiResidF32>(p, a, stream); break;
+      case kEpiQkPrep: launch_pair<kEpiQkPrep>(p, a, stream); break;
+      default: break;
+    }
+    return;
+  }
   switch (p.s.epi) {
     case kEpiRopeF16:
       wide ? launch<256, kEpiRopeF16>(p, a, stream) : launch<128, kEpiRopeF16>(p, a, stream);

@@ -67,6 +67,8 @@ struct GemmShape {
   int splits;    // split-K factor (f32 epilogue only)
   int epi;       // GemmEpilogue
   int n_tiles;   // grid.x
+  int pair;      // CTA-pair kernel (tcgen05 cta_group::2): 0 never, 1 for passes of
+                 // >= kPairMinTiles row tiles, 2 always
 };
 
 // Tensor maps and launch shape of one (activation buffer, weight) pair,
@@ -74,6 +76,7 @@ struct GemmShape {
 struct GemmPlan {
   CUtensorMap a;  // activations [rows_cap, K] f16, box 64 x 128
   CUtensorMap b;  // weights [N_rows, K] f16, box 64 x bn
+  CUtensorMap b_half;  // the same, box 64 x 128 (each CTA of a pair loads half a tile)
   GemmShape s;
   int rows_cap;
   int num_sms;  // persistent grid size (CTAs = min(tiles, SMs))
@@ -84,6 +87,21 @@ struct GemmPlan {
 // stored (for GeGLU: 2 x padded width).
 bool gemm_plan(GemmPlan* p, const void* a, int a_rows_cap, int lda, const void* w, int w_rows,
                int n_out, int k, int epi, int bn, int splits, char* err, size_t errlen);
+
+// Switch a BN-256 plan to the CTA-pair kernel: two CTAs on one TPC share a
+// 256 x 256 tile, each staging its own 128 rows of A and 128 of the 256
+// weight rows, so each SM moves 2/3 of the operand bytes per FLOP and keeps
+// six K steps in flight. Same results as the one-CTA kernel, bit for bit
+// (same K order per output element).
+bool gemm_plan_pair(GemmPlan* p, const void* w, int w_rows, bool always, char* err,
+                    size_t errlen);
+
+// Row tiles from which a pass takes the CTA-pair kernel: with fewer, pairing
+// 128-row tiles wastes too much of the last pair (7 tiles run as 8).
+constexpr int kPairMinTiles = 16;
+
+// Whether a launch of this plan over `m` rows takes the CTA-pair kernel.
+bool use_pair(const GemmPlan& p, int m);
 
 // Launch over `m` rows. f32 epilogue: `out` is [splits][m_stride][ldo] f32
 // (slab z at out + z * split_stride). f16 epilogues: [m][ldo] f16.

@@ -69,6 +69,18 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return s;
 }
 
+// The same for a block of blockDim.x threads (a multiple of 32, <= 1024).
+__device__ __forceinline__ float block_sum_dyn(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float s = 0.f;
+  for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) s += red[i];
+  return s;
+}
+
 // ---- embedding + first norm ------------------------------------------------
 
 template <int DT>
@@ -124,10 +136,13 @@ __global__ void __launch_bounds__(128) embed_norm_kernel(const int* __restrict__
 
 // ---- residual-stream norms -------------------------------------------------
 
-constexpr int kNormThreads = 256;  // NV float4 per thread: d <= 1024 NV
+// One CTA per row, NV float4 per thread and as many threads as the row needs
+// (d / (4 NV), rounded up to whole warps): no idle lanes holding registers
+// (a 2560-wide row took 256 threads x 4 float4 before, 40% of them idle).
+constexpr int kNormMaxThreads = 512;
 
 template <int NV>
-__global__ void __launch_bounds__(kNormThreads) residual_norm_kernel(
+__global__ void __launch_bounds__(kNormMaxThreads) residual_norm_kernel(
     const float* __restrict__ a, int splits, size_t split_stride, int lda, int t, int d,
     const float* __restrict__ w1, float eps, float offset, float out_scale, float* __restrict__ x,
     __half* __restrict__ x16, const float* __restrict__ w2, __half* __restrict__ h16, int ldh,
@@ -135,9 +150,10 @@ __global__ void __launch_bounds__(kNormThreads) residual_norm_kernel(
   griddep_wait();
   // Let the next kernel start its prologue; its CTAs wait for this grid.
   griddep_launch();
-  __shared__ float red[kNormThreads / 32];
+  __shared__ float red[32];
   const int row = blockIdx.x;
   if (row >= t) return;
+  const int nthr = static_cast<int>(blockDim.x);
   const float* ar = a + static_cast<size_t>(row) * lda;
   float* xr = x + static_cast<size_t>(row) * d;
   // Every load of the row up front (the slabs, the residual row and both
@@ -146,7 +162,7 @@ __global__ void __launch_bounds__(kNormThreads) residual_norm_kernel(
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
-    const int i = (threadIdx.x + j * kNormThreads) * 4;
+    const int i = (threadIdx.x + j * nthr) * 4;
     y[j] = xo[j] = wa[j] = wb[j] = zero;
     if (i < d) {
       y[j] = *reinterpret_cast<const float4*>(ar + i);
@@ -158,7 +174,7 @@ __global__ void __launch_bounds__(kNormThreads) residual_norm_kernel(
   for (int z = 1; z < splits; ++z) {
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-      const int i = (threadIdx.x + j * kNormThreads) * 4;
+      const int i = (threadIdx.x + j * nthr) * 4;
       if (i < d) {
         const float4 u = *reinterpret_cast<const float4*>(ar + z * split_stride + i);
         y[j].x += u.x;
@@ -172,11 +188,11 @@ __global__ void __launch_bounds__(kNormThreads) residual_norm_kernel(
 #pragma unroll
   for (int j = 0; j < NV; ++j)
     ss += y[j].x * y[j].x + y[j].y * y[j].y + y[j].z * y[j].z + y[j].w * y[j].w;
-  const float inv1 = rsqrtf(block_sum<kNormThreads>(ss, red) / static_cast<float>(d) + eps);
+  const float inv1 = rsqrtf(block_sum_dyn(ss, red) / static_cast<float>(d) + eps);
   float ss2 = 0.f;
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
-    const int i = (threadIdx.x + j * kNormThreads) * 4;
+    const int i = (threadIdx.x + j * nthr) * 4;
     if (i < d) {
       const float4 ww = wa[j];
       float4 v = y[j];
@@ -198,13 +214,13 @@ __global__ void __launch_bounds__(kNormThreads) residual_norm_kernel(
     }
   }
   if (w2 == nullptr) return;
-  const float inv2 = rsqrtf(block_sum<kNormThreads>(ss2, red) / static_cast<float>(d) + eps);
+  const float inv2 = rsqrtf(block_sum_dyn(ss2, red) / static_cast<float>(d) + eps);
   const int out_row = row_map ? row_map[row] : -1;
   __half* hr = h16 ? h16 + static_cast<size_t>(row) * ldh : nullptr;
   float* orow = out_row >= 0 ? rows_out + static_cast<size_t>(out_row) * d : nullptr;
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
-    const int i = (threadIdx.x + j * kNormThreads) * 4;
+    const int i = (threadIdx.x + j * nthr) * 4;
     if (i < d) {
       const float4 ww = wb[j];
       float4 v = y[j];
@@ -576,18 +592,19 @@ void launch_residual_norm(const float* a, int splits, size_t split_stride, int l
                           __half* x16, const float* w2, __half* h16, int ldh,
                           const int* row_map, float* rows_out, cudaStream_t s) {
   if (t <= 0) return;
+  // Config::validate caps d at 8192.
+  const int nv = d <= 1024 ? 1 : d <= 4096 ? 2 : 4;
+  const int threads = ((d + 4 * nv - 1) / (4 * nv) + 31) / 32 * 32;
 #define OMG_NORM(NV)                                                                        \
-  launch_pdl(residual_norm_kernel<NV>, dim3(t), dim3(kNormThreads), 0, s, a, splits,         \
+  launch_pdl(residual_norm_kernel<NV>, dim3(t), dim3(threads), 0, s, a, splits,              \
              split_stride, lda, t, d, w1, eps, offset, out_scale, x, x16, w2, h16, ldh, row_map, \
              rows_out)
-  if (d <= 1024)
+  if (nv == 1)
     OMG_NORM(1);
-  else if (d <= 2048)
+  else if (nv == 2)
     OMG_NORM(2);
-  else if (d <= 4096)
-    OMG_NORM(4);
   else
-    OMG_NORM(8);
+    OMG_NORM(4);
 #undef OMG_NORM
 }
 

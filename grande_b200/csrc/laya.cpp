@@ -407,6 +407,10 @@ LayaEngine::LayaEngine(LayaBuilder&& b, size_t capacity_, size_t max_rows_)
     if (!gemm_plan(p, a, static_cast<int>(R), lda, W(w), w_rows, n_out, k, epi,
                    n_out % 256 == 0 || epi == kEpiGeGluErf ? 256 : 128, 1, err, sizeof err))
       fail("%s: %s", w.c_str(), err);
+    // Batches of many rows take the CTA-pair kernel (same results).
+    if (p->s.bn == 256 && epi != kEpiBiasF16 && epi != kEpiBiasReluF16 &&
+        !gemm_plan_pair(p, W(w), w_rows, false, err, sizeof err))
+      fail("%s: %s", w.c_str(), err);
   };
   embed_norm_ = V("embed_norm");
   final_norm_ = V("final_norm");

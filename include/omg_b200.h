@@ -266,7 +266,8 @@ int omg_synth_normal(uint64_t seed, const char* name, float mean, float stddev, 
  * f16. epi OMG_EPI_F32 writes f32 [m, ldo] (split-K slabs summed on the host),
  * OMG_EPI_F16 writes f16 [m, ldo], the GeGLU epilogues expect W rows
  * interleaved in 256-row blocks [128 gate | 128 up] and write f16
- * act = gelu(g) * u for n_out columns. bn = 0 picks the engine's tiling.
+ * act = gelu(g) * u for n_out columns. bn = 0 picks the engine's tiling;
+ * bn = 512 runs the CTA-pair kernel (256 x 256 tiles over two SMs).
  * Replaces crates/omg-wgpu/src/shaders/matmul.wgsl:1-9 and
  * matmul_gated.wgsl:1-7 (the tests of crates/omg-wgpu/tests/matmul.rs:201-290). */
 int omg_debug_gemm(int device, const uint16_t* x_f16, int m, int k, int lda, const uint16_t* w_f16,

@@ -136,3 +136,44 @@ def test_gated_erf_encoder_rows(device):
     exp = gelu_erf(xd @ wg.astype(np.float64).T) * (xd @ wu.astype(np.float64).T)
     got = run_gemm(device, x16, w, n, 2)
     assert rel_err(got, exp) < TOL + 1e-3
+
+
+PAIR_SHAPES = [
+    (788, 3072, 2048, 0, 1),    # E2B qkv, 7 row tiles: the last pair has one empty half
+    (788, 2048, 8192, 0, 2),    # E2B down, split-K
+    (300, 520, 256, 0, 1),      # partial row and column tiles
+    (23, 96, 64, 0, 1),         # one partial tile
+    (1000, 700, 192, 3, 1),     # f16 out
+    (4100, 300, 192, 0, 1),     # N-fastest order
+]
+
+
+@pytest.mark.parametrize("m,n,k,epi,splits", PAIR_SHAPES)
+def test_pair_kernel_matches_one_cta_kernel(device, m, n, k, epi, splits):
+    """The CTA-pair (cta_group::2) kernel against the one-CTA kernel on the
+    same operands: same products in the same K order, so the same bits."""
+    rng = np.random.default_rng(m + 3 * n + k)
+    x16 = rng.uniform(-1, 1, (m, k)).astype(np.float16)
+    w16 = rng.uniform(-1, 1, (n, k)).astype(np.float16)
+    one = run_gemm(device, x16, w16, n, epi, bn=256, splits=splits)
+    pair = run_gemm(device, x16, w16, n, epi, bn=512, splits=splits)
+    assert np.array_equal(one, pair)
+    exp = x16.astype(np.float64) @ w16.astype(np.float64).T
+    assert rel_err(pair, exp) < TOL + (1e-3 if epi == 3 else 0.0)
+
+
+@pytest.mark.parametrize("epi", [1, 2])
+def test_pair_kernel_gated(device, epi):
+    m, n, k = 788, 600, 256
+    rng = np.random.default_rng(epi)
+    x16 = rng.uniform(-1, 1, (m, k)).astype(np.float16)
+    wg = (rng.uniform(-1, 1, (n, k)) * 0.3).astype(np.float16)
+    wu = (rng.uniform(-1, 1, (n, k)) * 0.3).astype(np.float16)
+    w = interleave_gate_up(wg, wu)
+    one = run_gemm(device, x16, w, n, epi, bn=256)
+    pair = run_gemm(device, x16, w, n, epi, bn=512)
+    assert np.array_equal(one, pair)
+    xd = x16.astype(np.float64)
+    act = gelu_tanh if epi == 1 else gelu_erf
+    exp = act(xd @ wg.astype(np.float64).T) * (xd @ wu.astype(np.float64).T)
+    assert rel_err(pair, exp) < TOL + 1e-3

@@ -63,6 +63,35 @@ def rows_equal(a, b):
     return len(a) == len(b) and all(np.array_equal(x.rows, y.rows) for x, y in zip(a, b))
 
 
+def test_long_prefix_matches_cpu_reference():
+    """A 2,100-token prefix: the pass has more than 16 row tiles, so its
+    projections run on the CTA-pair (cta_group::2) GEMM and its FFN as two
+    pair launches; rows vs the CPU reference at the reference's 2e-2
+    (reference.rs:380-407), and a branch alone equals the branch beside a
+    resident prefix bit for bit."""
+    for kind, lin, emb in (("g3", F16, F16), ("gqa", Q4, Q8)):
+        m = model(kind, 37, lin, emb)
+        eng = m.engine(capacity=2304, max_rows=16)
+        rng = np.random.default_rng(5)
+        prefix = [int(x) for x in rng.integers(1, m.cfg.vocab, 2100)]
+        branches = [BranchTokens([int(x) for x in rng.integers(1, m.cfg.vocab, 9)], [0, 8]),
+                    BranchTokens([int(x) for x in rng.integers(1, m.cfg.vocab, 5)], [4])]
+        out = eng.evaluate(prefix, branches, Want.HIDDEN)
+        ids, pos, seq = O.pack(prefix, [(b.tokens, b.want) for b in branches])
+        hidden = m.hidden(ids, pos, seq)
+        idx = len(prefix)
+        for b, o in zip(branches, out):
+            for slot, w in enumerate(b.want):
+                exp = hidden[idx + w]
+                d = np.abs(o.rows[slot] - exp).max() / max(np.abs(exp).max(), 1.0)
+                assert d < 2e-2, f"{kind}: relative diff {d}"
+            idx += len(b.tokens)
+        again = eng.evaluate(prefix, branches, Want.HIDDEN)
+        assert eng.prefix_source() == PrefixSource.RESIDENT
+        assert rows_equal(out, again)
+        eng.close()
+
+
 def test_resident_prefix_matches_full_pass():
     """reference.rs:432-480."""
     for m in (model("g3", 13, F16, F16), model("g4", 13, Q4, Q8), model("gqa", 13, Q4, Q8)):

@@ -123,6 +123,8 @@ PROTOTYPES: dict[str, tuple] = {
          C.c_int, C.c_void_p, C.c_int],
     ),
     "omg_debug_gemm_time": (C.c_int, [C.c_int] * 8 + [f32p]),
+    "omg_debug_mlp": (C.c_int, [C.c_int, u16p, C.c_int, C.c_int, u16p, C.c_int, u16p, C.c_int,
+                                u16p, f32p]),
     "omg_laya_config_check": (C.c_int, [cs, C.c_char_p, sz]),
     "omg_laya_config_tensors": (C.c_int, [cs, C.c_char_p, sz, szp]),
     "omg_laya_builder_new": (C.c_int, [cs, C.c_int, pp]),

@@ -81,6 +81,62 @@ extern "C" int omg_debug_gemm(int device, const uint16_t* x_f16, int m, int k, i
   });
 }
 
+// The fused FFN launch on host buffers: act = gelu_tanh(X Wg^T) * (X Wu^T)
+// (f16 [m, ff]) and Y = act Wd^T (f32 [m, d], the split-K slabs summed in
+// order on the host). X [m, d] f16; W_up [2 ff, d] f16 with gate and up rows
+// interleaved in 256-row blocks [128 gate | 128 up]; W_down [d, ff] f16.
+// pair: 0 one-CTA tiles, 1 CTA pairs. Needs d % 128 == 0 and ff % d == 0
+// (the down split's K blocks equal the up projection's).
+extern "C" int omg_debug_mlp(int device, const uint16_t* x, int m, int d, const uint16_t* w_up,
+                             int ff, const uint16_t* w_down, int pair, uint16_t* act_out,
+                             float* y_out) {
+  return guarded([&]() -> int {
+    CUDA_TRY(cudaSetDevice(device));
+    gemm_setup_device();
+    if (m <= 0 || d <= 0 || ff <= 0 || d % 128 != 0 || ff % d != 0)
+      return set_error("debug_mlp: needs d %% 128 == 0 and ff %% d == 0 (d %d, ff %d)", d, ff);
+    const int splits = ff / d;
+    DevBuf dx, dwu, dwd, dact, dslab, dready, dstat;
+    const size_t xb = static_cast<size_t>(m) * d * 2, wub = static_cast<size_t>(2) * ff * d * 2;
+    const size_t wdb = static_cast<size_t>(d) * ff * 2, actb = static_cast<size_t>(m) * ff * 2;
+    const size_t slab = static_cast<size_t>(m) * d;
+    const int m_tiles = (m + 127) / 128;
+    if (!dx.alloc(xb) || !dwu.alloc(wub) || !dwd.alloc(wdb) || !dact.alloc(actb) ||
+        !dslab.alloc(slab * splits * 4) || !dready.alloc(static_cast<size_t>(m_tiles) * splits * 4) ||
+        !dstat.alloc(4))
+      return set_error("cudaMalloc failed");
+    CUDA_TRY(cudaMemcpy(dx.p, x, xb, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(dwu.p, w_up, wub, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(dwd.p, w_down, wdb, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemset(dready.p, 0, static_cast<size_t>(m_tiles) * splits * 4));
+    CUDA_TRY(cudaMemset(dstat.p, 0, 4));
+    GemmPlan up, down;
+    char err[256];
+    if (!gemm_plan(&up, dx.p, m, d, dwu.p, 2 * ff, ff, d, kEpiGeGluTanh, 256, 1, err, sizeof err) ||
+        !gemm_plan(&down, dact.p, m, ff, dwd.p, d, d, ff, kEpiF32, 256, splits, err, sizeof err) ||
+        !gemm_plan_pair(&up, dwu.p, 2 * ff, false, err, sizeof err) ||
+        !gemm_plan_pair(&down, dwd.p, d, false, err, sizeof err))
+      return set_error(err);
+    if (!gemm_mlp_ok(up, down)) return set_error("debug_mlp: shapes not fusable");
+    gemm_run_mlp(up, down, m, dact.p, ff, dslab.p, d, slab, static_cast<int*>(dready.p),
+                 4 * up.s.n_tiles / down.s.splits, static_cast<uint32_t*>(dstat.p), 0, pair ? 1 : 0);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaDeviceSynchronize());
+    uint32_t st = 0;
+    CUDA_TRY(cudaMemcpy(&st, dstat.p, 4, cudaMemcpyDeviceToHost));
+    if (st) return set_error("mlp kernel reported device status %u", st);
+    CUDA_TRY(cudaMemcpy(act_out, dact.p, actb, cudaMemcpyDeviceToHost));
+    std::vector<float> h(slab * splits);
+    CUDA_TRY(cudaMemcpy(h.data(), dslab.p, h.size() * 4, cudaMemcpyDeviceToHost));
+    for (size_t i = 0; i < slab; ++i) {
+      float v = h[i];
+      for (int z = 1; z < splits; ++z) v += h[z * slab + i];
+      y_out[i] = v;
+    }
+    return 0;
+  });
+}
+
 // Block-causal attention on host buffers: q [t, heads * hd] f16 (cache rows
 // base..base+t), kv [rows, 2 * kv_heads * hd] f16, meta 4 ints per cache row
 // (pos, seq, row_lo, row_hi), out [t, heads * hd] f16.

@@ -862,9 +862,9 @@ int Engine::launch_forward(const Packing& p, Want want) {
                          c.eps, c.norm_offset, 1.0f, x_.as<float>(), nullptr, ly.ffn_norm,
                          h16_.as<__half>(), d, nullptr, nullptr, stream_);
     // GeGLU and down projection.
-    // The fused FFN launch on one-CTA tiles, or, for passes long enough for
-    // the CTA-pair kernel, its two projections as pair launches.
-    if (ly.fused_mlp && !use_pair(ly.gate_up, t)) {
+    // The fused FFN launch (on CTA pairs for passes of kPairMlpMinTiles row
+    // tiles or more).
+    if (ly.fused_mlp) {
       k("gemm_mlp");
       mlp_target += 4 * ly.gate_up.s.n_tiles / ly.down.s.splits;
       gemm_run_mlp(ly.gate_up, ly.down, t, act16_.p, ly.ff, a32_.p, d, slab_a,

@@ -1128,6 +1128,209 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// The fused FFN launch on CTA pairs: the units of gemm_mlp_kernel with
+// 256-row pair tiles (CTA rank r of pair tile p holds M tile 2 p + r), the
+// pipeline and barriers of gemm2_kernel. A down unit's producer waits for
+// its own M tile's activation band (a CTA whose half lies past the last M
+// tile has no rows and waits for nothing); the leader's full barrier then
+// holds the MMA until both halves are loaded.
+template <int EPI_UP>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    gemm_mlp2_kernel(const __grid_constant__ CUtensorMap ta_up,
+                     const __grid_constant__ CUtensorMap tb_up,
+                     const __grid_constant__ CUtensorMap ta_dn,
+                     const __grid_constant__ CUtensorMap tb_dn, MlpArgs g) {
+  constexpr int BN = 256;
+  using C = Cfg2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + C::STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + C::STAGES * C::B_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* epi_consts = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);
+  uint32_t* status = g.up.status;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = static_cast<int>(cluster_index());
+  const int npairs = static_cast<int>(cluster_count());
+  const int m_tiles = g.up.m_tiles;
+  const int m_pairs = (m_tiles + 1) / 2;
+  const int up_units = m_pairs * g.up.n_tiles;
+  const int dn_per_split = m_pairs * g.down.n_tiles;
+  const int total = up_units + dn_per_split * g.down.splits;
+  struct Unit {
+    bool up;
+    int m, n, split, kb0, kb1;  // m: this CTA's M tile
+  };
+  auto decode = [&](int u) {
+    Unit x;
+    if (u < up_units) {
+      x.up = true;
+      x.m = 2 * (u % m_pairs) + static_cast<int>(rank);
+      x.n = u / m_pairs;
+      x.split = 0;
+      x.kb0 = 0;
+      x.kb1 = g.up.kb_total;
+    } else {
+      const int v = u - up_units;
+      const int r = v % dn_per_split;
+      x.up = false;
+      x.split = v / dn_per_split;
+      x.m = 2 * (r % m_pairs) + static_cast<int>(rank);
+      x.n = r / m_pairs;
+      x.kb0 = x.split * g.down.kb_per_split;
+      x.kb1 = min(g.down.kb_total, x.kb0 + g.down.kb_per_split);
+    }
+    return x;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&ta_up);
+    prefetch_tmap(&tb_up);
+    prefetch_tmap(&ta_dn);
+    prefetch_tmap(&tb_dn);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  griddep_wait();
+  griddep_launch();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      for (int u = pair; u < total && !*abort_flag; u += npairs) {
+        const Unit x = decode(u);
+        if (!x.up && x.m < m_tiles) {
+          const int* rp = g.ready + x.m * g.down.splits + x.split;
+          const long long t0 = clock64();
+          bool ok = true;
+          while (ld_acquire_gpu(rp) < g.ready_target) {
+            if (*abort_flag) {
+              ok = false;
+              break;
+            }
+            if (clock64() - t0 > kWaitLimitClocks) {
+              *abort_flag = 1;
+              atomicCAS(status, 0u, static_cast<uint32_t>(kDevWaitTimeout));
+              ok = false;
+              break;
+            }
+            __nanosleep(64);
+          }
+          if (!ok) break;
+          fence_proxy_async_global();
+        }
+        const CUtensorMap* ta = x.up ? &ta_up : &ta_dn;
+        const CUtensorMap* tb = x.up ? &tb_up : &tb_dn;
+        bool ok = true;
+        for (int kb = x.kb0; kb < x.kb1; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, status)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * C::STAGE_BYTES);
+          const uint32_t bar = cluster_addr(&full[s], 0);
+          tma_load_2d_pair(sa + s * C::A_BYTES, ta, bar, kb * BK, x.m * BM);
+          tma_load_2d_pair(sb + s * C::B_BYTES, tb, bar, kb * BK,
+                           x.n * BN + 128 * static_cast<int>(rank));
+        }
+        if (!ok) break;
+      }
+      for (int j = max(0, it - C::STAGES); j < it && !*abort_flag; ++j)
+        if (!mbar_wait(&empty[j % C::STAGES], (j / C::STAGES) & 1, abort_flag, status)) break;
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(2 * BM, BN);
+      int it = 0, local = 0;
+      for (int u = pair; u < total; u += npairs, ++local) {
+        const Unit x = decode(u);
+        const int b = local & 1;
+        if (!mbar_wait(&tempty[b], ((local >> 1) & 1) ^ 1, abort_flag, status)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(b * BN);
+        bool ok = true;
+        for (int kb = x.kb0; kb < x.kb1; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort_flag, status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = sw128_desc(sa + s * C::A_BYTES);
+          const uint64_t db = sw128_desc(sb + s * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16_pair(d, da + 2 * k, db + 2 * k, idesc, (kb > x.kb0 || k > 0) ? 1u : 0u);
+          umma_commit_pair(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[b]);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    int local = 0;
+    for (int u = pair; u < total; u += npairs, ++local) {
+      const Unit x = decode(u);
+      const int b = local & 1;
+      int ok = 0;
+      if (lane == 0) ok = mbar_wait(&tfull[b], (local >> 1) & 1, abort_flag, status) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      uint8_t* slot = reinterpret_cast<uint8_t*>(full) + 256 + 2048 + q * 4096;
+      const uint32_t tbase =
+          tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BN);
+      if (x.up) {
+        epilogue_tile<BN, EPI_UP>(g.up, x.m, x.n, 0, tbase, q, lane, slot, epi_consts);
+        if (x.m < m_tiles) {
+          fence_proxy_async_global();
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) atomicAdd(g.ready + x.m * g.down.splits + x.n / g.band, 1);
+        }
+      } else {
+        epilogue_tile<BN, kEpiF32>(g.down, x.m, x.n, x.split, tbase, q, lane, slot, epi_consts);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[b], 0));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, C::TMEM_COLS);
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -1229,6 +1432,10 @@ void gemm_setup_device() {
   set_smem_attr<128, kEpiResidF32>();
   set_smem_attr<256, kEpiResidF32>();
   set_smem_attr<256, kEpiQkPrep>();
+  cudaFuncSetAttribute(gemm_mlp2_kernel<kEpiGeGluTanh>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       Cfg2::SMEM);
+  cudaFuncSetAttribute(gemm_mlp2_kernel<kEpiGeGluErf>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       Cfg2::SMEM);
   set_smem_attr_pair<kEpiF32>();
   set_smem_attr_pair<kEpiF16>();
   set_smem_attr_pair<kEpiGeGluTanh>();
@@ -1445,8 +1652,11 @@ bool gemm_mlp_ok(const GemmPlan& up, const GemmPlan& down) {
 
 void gemm_run_mlp(const GemmPlan& up, const GemmPlan& down, int m, void* act, int ld_act,
                   void* slabs, int ld_slab, size_t split_stride, int* ready, int ready_target,
-                  uint32_t* status, cudaStream_t stream) {
+                  uint32_t* status, cudaStream_t stream, int force_pair) {
   if (m <= 0) return;
+  // force_pair: -1 by row tiles, 0 one-CTA tiles, 1 CTA pairs (kernel tests).
+  const bool pair = up.s.pair && down.s.pair &&
+                    (force_pair >= 0 ? force_pair == 1 : (m + BM - 1) / BM >= kPairMlpMinTiles);
   MlpArgs a{};
   auto fill = [&](GemmArgs& x, const GemmPlan& p, void* out, int ldo, size_t stride) {
     x.m = m;
@@ -1467,6 +1677,19 @@ void gemm_run_mlp(const GemmPlan& up, const GemmPlan& down, int m, void* act, in
   a.ready = ready;
   a.ready_target = ready_target;
   a.band = a.down.kb_per_split / 2;
+  if (pair) {
+    const int m_pairs = (a.up.m_tiles + 1) / 2;
+    const int units = m_pairs * (a.up.n_tiles + a.down.n_tiles * a.down.splits);
+    const int max_pairs = up.num_sms / 2;
+    const int grid = 2 * (units < max_pairs ? units : max_pairs);
+    if (up.s.epi == kEpiGeGluTanh)
+      launch_pdl(gemm_mlp2_kernel<kEpiGeGluTanh>, dim3(grid), dim3(192), Cfg2::SMEM, stream, up.a,
+                 up.b_half, down.a, down.b_half, a);
+    else
+      launch_pdl(gemm_mlp2_kernel<kEpiGeGluErf>, dim3(grid), dim3(192), Cfg2::SMEM, stream, up.a,
+                 up.b_half, down.a, down.b_half, a);
+    return;
+  }
   const int total = a.up.m_tiles * a.up.n_tiles + a.down.m_tiles * a.down.n_tiles * a.down.splits;
   const int grid = total < up.num_sms ? total : up.num_sms;
   if (up.s.epi == kEpiGeGluTanh)

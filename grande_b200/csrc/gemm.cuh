@@ -99,6 +99,10 @@ bool gemm_plan_pair(GemmPlan* p, const void* w, int w_rows, bool always, char* e
 // Row tiles from which a pass takes the CTA-pair kernel: with fewer, pairing
 // 128-row tiles wastes too much of the last pair (7 tiles run as 8).
 constexpr int kPairMinTiles = 16;
+// The fused FFN launch takes CTA pairs from 16 row tiles too. (At an E2B
+// pass's 7 tiles, run as 4 pairs, the deeper pipeline only pays for the
+// empty half: 2.48 vs 2.40-2.44 ms per pass on one-CTA tiles.)
+constexpr int kPairMlpMinTiles = 16;
 
 // Whether a launch of this plan over `m` rows takes the CTA-pair kernel.
 bool use_pair(const GemmPlan& p, int m);
@@ -124,7 +128,7 @@ void gemm_run_epi(const GemmPlan& p, int m, void* out, int ldo, const GemmEpi& e
 bool gemm_mlp_ok(const GemmPlan& up, const GemmPlan& down);
 void gemm_run_mlp(const GemmPlan& up, const GemmPlan& down, int m, void* act, int ld_act,
                   void* slabs, int ld_slab, size_t split_stride, int* ready, int ready_target,
-                  uint32_t* status, cudaStream_t stream);
+                  uint32_t* status, cudaStream_t stream, int force_pair = -1);
 
 // Encode a TMA tensor map over f16 data with the 128-byte swizzle: `rank`
 // dimensions innermost first, byte strides of dimensions 1..rank-1, box

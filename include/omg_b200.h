@@ -273,6 +273,15 @@ int omg_synth_normal(uint64_t seed, const char* name, float mean, float stddev, 
 int omg_debug_gemm(int device, const uint16_t* x_f16, int m, int k, int lda, const uint16_t* w_f16,
                    int w_rows, int n_out, int epi, int bn, int splits, void* out, int ldo);
 
+/* The fused FFN launch (matmul_gated.wgsl then matmul.wgsl for mm_gate_up /
+ * mm_down, engine.rs:1253-1273): act = gelu_tanh(X Wg^T) * (X Wu^T) f16
+ * [m, ff], Y = act Wd^T f32 [m, d]. X [m, d] f16; W_up [2 ff, d] f16 with gate
+ * and up rows interleaved in 256-row blocks [128 gate | 128 up]; W_down
+ * [d, ff] f16. pair = 1 runs it on CTA pairs (tcgen05 cta_group::2), 0 on
+ * one-CTA tiles. Needs d % 128 == 0 and ff % d == 0. */
+int omg_debug_mlp(int device, const uint16_t* x, int m, int d, const uint16_t* w_up, int ff,
+                  const uint16_t* w_down, int pair, uint16_t* act_out, float* y_out);
+
 /* Block-causal GQA attention (replaces crates/omg-wgpu/src/shaders/attention.wgsl:1-35):
  * q [t, heads * hd] f16 for cache rows base..base+t, kv [base + t, 2 * kv_heads * hd]
  * f16 (K heads then V heads per row), meta 4 ints per cache row (position,

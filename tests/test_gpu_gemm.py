@@ -177,3 +177,39 @@ def test_pair_kernel_gated(device, epi):
     act = gelu_tanh if epi == 1 else gelu_erf
     exp = act(xd @ wg.astype(np.float64).T) * (xd @ wu.astype(np.float64).T)
     assert rel_err(pair, exp) < TOL + 1e-3
+
+
+def run_mlp(device, x16, w_up, w_dn, ff, pair):
+    m, d = x16.shape
+    act = np.zeros((m, ff), np.float16)
+    y = np.zeros((m, d), np.float32)
+    L.check(L.lib().omg_debug_mlp(
+        device, L.ptr(x16.view(np.uint16), L.C.c_uint16), m, d,
+        L.ptr(np.ascontiguousarray(w_up).view(np.uint16), L.C.c_uint16), ff,
+        L.ptr(np.ascontiguousarray(w_dn).view(np.uint16), L.C.c_uint16), pair,
+        L.ptr(act.view(np.uint16), L.C.c_uint16), L.ptr(y, L.C.c_float)))
+    return act, y
+
+
+@pytest.mark.parametrize("m", [2100, 700])
+def test_fused_mlp_pair_matches_one_cta(device, m):
+    """The fused FFN launch (gate+up with the GeGLU epilogue, then the split-K
+    down units gated on the activation bands) on CTA pairs and on one-CTA
+    tiles: the same bits; and both against an f64 reference of the two
+    projections (the activation rounded to f16 as the kernel stores it)."""
+    d, ff = 256, 1024
+    rng = np.random.default_rng(m)
+    x16 = rng.uniform(-1, 1, (m, d)).astype(np.float16)
+    wg = (rng.uniform(-1, 1, (ff, d)) * 0.2).astype(np.float16)
+    wu = (rng.uniform(-1, 1, (ff, d)) * 0.2).astype(np.float16)
+    wd = (rng.uniform(-1, 1, (d, ff)) * 0.2).astype(np.float16)
+    w_up = interleave_gate_up(wg, wu)
+    a1, y1 = run_mlp(device, x16, w_up, wd, ff, 0)
+    a2, y2 = run_mlp(device, x16, w_up, wd, ff, 1)
+    assert np.array_equal(a1, a2)
+    assert np.array_equal(y1, y2)
+    xd = x16.astype(np.float64)
+    act = gelu_tanh(xd @ wg.astype(np.float64).T) * (xd @ wu.astype(np.float64).T)
+    assert rel_err(a2.astype(np.float32), act) < TOL + 1e-3
+    exp = a2.astype(np.float64) @ wd.astype(np.float64).T
+    assert rel_err(y2, exp) < TOL

@@ -571,6 +571,10 @@ int LayaEngine::launch_forward(const Packing& p) {
     a.heads = c.heads;
     a.d = d;
     a.window = w == 0 ? c.window : 0;
+    a.single_tile = 1;
+    for (const LayaAttnItem& it : p.items[w])
+      if (it.nk > kLayaTile) a.single_tile = 0;
+    a.num_sms = num_sms_;
     k("attention");
     launch_laya_attention(tqkv_, a, stream_);
   };

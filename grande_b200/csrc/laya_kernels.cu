@@ -424,6 +424,250 @@ __global__ void __launch_bounds__(192, 2)
   }
 }
 
+// The same attention for passes whose items each see one 128-key tile (every
+// sequence <= 128 tokens, as in a batch of questions): a persistent CTA per
+// SM walks (item, head) units; two groups of four softmax warps take
+// alternate units, each group with its own MMA thread and two buffer slots
+// (Q, K, V in shared memory; 128 TMEM columns), so one group's softmax runs
+// while the other's loads, MMAs and output proceed.
+//
+//   warp 0        TMA: Q, K, V of unit i into slot (i & 1, (i >> 1) & 1)
+//   warps 1, 2    MMA for group 0 / 1: S = Q K^T into the slot's TMEM
+//                 columns; after the softmax, O = P V into the first 64 of
+//                 them (S is dead by then)
+//   warps 3-6,    softmax group 0 / 1, one query row per thread: masked max,
+//   7-10          exp, row sum, P (f16) over the slot's Q and K (dead after
+//                 S); then out = O / l, staged in the same bytes and stored a
+//                 row segment per lane
+//
+// Each row's arithmetic is the one-tile case of laya_attention_kernel step
+// for step (same MMAs, same partial sums in the same order), so a row gets
+// the same bits from either kernel.
+constexpr int LP_THREADS = 352;
+constexpr int LP_SMEM = 1024 + 4 * 3 * LA_CHUNK + 256;
+constexpr uint32_t LP_TMEM_COLS = 512;  // slot (g, s): columns 128 (2 g + s) .. + 128
+
+enum { LP_FULL = 0, LP_SFULL = 4, LP_PFULL = 8, LP_OFULL = 12, LP_TFREE = 16, LP_N = 20 };
+
+__global__ void __launch_bounds__(LP_THREADS, 1)
+    laya_attention_tile_kernel(const __grid_constant__ CUtensorMap tqkv, LayaAttnArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  auto chunk = [&](int slot, int c) { return sm + (slot * 3 + c) * LA_CHUNK; };  // Q, K, V
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + 4 * 3 * LA_CHUNK);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + LP_N);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int units = g.n_items * g.heads;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < LP_N; ++i)
+      mbar_init(&bars[i], (i >= LP_PFULL && i < LP_PFULL + 4) || i >= LP_TFREE ? 4 : 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tqkv);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, LP_TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  griddep_wait();
+  griddep_launch();
+
+  // Unit i of this CTA: group i & 1, its (i >> 1)-th unit, slot 2 (i & 1) +
+  // ((i >> 1) & 1), that slot's (i >> 2)-th use.
+  if (warp == 0) {
+    if (lane == 0) {
+      int i = 0;
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, ++i) {
+        const int slot = 2 * (i & 1) + ((i >> 1) & 1), use = i >> 2;
+        if (use > 0 && !mbar_wait(&bars[LP_TFREE + slot], (use - 1) & 1, abort_flag, g.status))
+          break;
+        const LayaAttnItem it = g.items[u / g.heads];
+        const int head = u % g.heads;
+        uint64_t* full = &bars[LP_FULL + slot];
+        mbar_arrive_expect_tx(full, 3 * LA_CHUNK);
+        tma_load_2d(chunk(slot, 0), &tqkv, full, head * kLayaHd, it.q0);
+        tma_load_2d(chunk(slot, 1), &tqkv, full, g.d + head * kLayaHd, it.k0);
+        tma_load_2d(chunk(slot, 2), &tqkv, full, 2 * g.d + head * kLayaHd, it.k0);
+      }
+    }
+  } else if (warp == 1 || warp == 2) {
+    if (lane == 0) {
+      const int grp = warp - 1;
+      constexpr uint32_t idesc_s = idesc_f16_f32(128, kLayaTile);
+      constexpr uint32_t idesc_o = idesc_f16_f32_bmn(128, kLayaHd);
+      int i = grp;
+      for (int u = blockIdx.x + grp * gridDim.x; u < units; u += 2 * gridDim.x, i += 2) {
+        const int slot = 2 * grp + ((i >> 1) & 1);
+        const uint32_t par = (i >> 2) & 1;
+        const uint32_t d = tmem + 128u * slot;
+        if (!mbar_wait(&bars[LP_FULL + slot], par, abort_flag, g.status)) break;
+        tc_fence_after();
+        const uint64_t da = sw128_desc(chunk(slot, 0)), db = sw128_desc(chunk(slot, 1));
+#pragma unroll
+        for (int k = 0; k < kLayaHd / 16; ++k) umma_f16(d, da + 2 * k, db + 2 * k, idesc_s, k);
+        umma_commit(&bars[LP_SFULL + slot]);
+        if (!mbar_wait(&bars[LP_PFULL + slot], par, abort_flag, g.status)) break;
+        tc_fence_after();
+        uint8_t* ps = chunk(slot, 0);  // P over Q and K
+#pragma unroll
+        for (int kk = 0; kk < kLayaTile / 16; ++kk) {
+          const uint64_t pa = sw128_desc(ps + (kk >> 2) * LA_CHUNK) + 2 * (kk & 3);
+          const uint64_t vb = sw128_mn_desc(chunk(slot, 2) + kk * 2048, LA_CHUNK);
+          umma_f16(d, pa, vb, idesc_o, kk ? 1u : 0u);
+        }
+        umma_commit(&bars[LP_OFULL + slot]);
+      }
+    }
+  } else {
+    const int grp = (warp - 3) >> 2;
+    const int q4 = warp & 3;
+    const int r = 32 * q4 + lane;
+    int i = grp;
+    for (int u = blockIdx.x + grp * gridDim.x; u < units; u += 2 * gridDim.x, i += 2) {
+      const int slot = 2 * grp + ((i >> 1) & 1);
+      const uint32_t par = (i >> 2) & 1;
+      const LayaAttnItem it = g.items[u / g.heads];
+      const int head = u % g.heads;
+      const bool valid = r < it.nq;
+      const int tok = it.q0 + r;
+      int vlo = 0, vhi = 0;
+      if (valid) {
+        const int2 sp = g.span[tok];
+        vlo = sp.x;
+        vhi = sp.y;
+        if (g.window > 0) {
+          vlo = max(vlo, tok - g.window);
+          vhi = min(vhi, tok + g.window + 1);
+        }
+      }
+      int c0 = min(max(vlo - it.k0, 0), kLayaTile), c1 = min(max(vhi - it.k0, 0), kLayaTile);
+      if (c1 < c0) c1 = c0;
+      if (!warp_wait(&bars[LP_SFULL + slot], par, abort_flag, g.status, lane)) break;
+      tc_fence_after();
+      const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q4) << 16) + 128u * slot;
+      // Pass 1: the masked row max.
+      float mt = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < kLayaTile / 32; ++c) {
+        float s[32];
+        tmem_ld32(trow + c * 32, s);
+        const int k0 = c * 32;
+        if (c1 <= k0 || c0 >= k0 + 32) continue;
+        if (c0 > k0 || c1 < k0 + 32) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (k0 + e < c0 || k0 + e >= c1) s[e] = -INFINITY;
+        }
+        float mx[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mx[e] = s[e];
+#pragma unroll
+        for (int e = 8; e < 32; ++e) mx[e & 7] = fmaxf(mx[e & 7], s[e]);
+        mt = fmaxf(mt, fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))));
+      }
+      const float m_new = mt;
+      const float alpha = m_new == -INFINITY ? 1.f : 0.f;  // exp2((-inf - m_new) log2e)
+      const float mb = m_new == -INFINITY ? 0.f : m_new * kLog2e;
+      // Pass 2: P = exp(s - m) on visible keys, 0 elsewhere, f16, K-major
+      // with the 128-byte swizzle, over the slot's Q and K.
+      uint8_t* ps = chunk(slot, 0);
+      float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+      for (int c = 0; c < kLayaTile / 32; ++c) {
+        float s[32];
+        tmem_ld32(trow + c * 32, s);
+        const int k0 = c * 32;
+        if (c1 <= k0 || c0 >= k0 + 32 || m_new == -INFINITY) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) s[e] = 0.f;
+        } else {
+          const bool split = c0 > k0 || c1 < k0 + 32;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            float p = exp2f(fmaf(s[e], kLog2e, -mb));
+            if (split && (k0 + e < c0 || k0 + e >= c1)) p = 0.f;
+            s[e] = p;
+            ps8[e & 7] += p;
+          }
+        }
+#pragma unroll
+        for (int pc = 0; pc < 4; ++pc) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const __half2 h = __floats2half2_rn(s[pc * 8 + 2 * e], s[pc * 8 + 2 * e + 1]);
+            w4[e] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          const int key0 = c * 32 + pc * 8;
+          const int kc = key0 >> 6, pw = (key0 & 63) >> 3;
+          *reinterpret_cast<uint4*>(ps + kc * LA_CHUNK + r * 128 + ((pw ^ (r & 7)) << 4)) =
+              make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+      }
+      const float sum = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
+      const float l = 0.f * alpha + sum;
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[LP_PFULL + slot]);
+      if (!warp_wait(&bars[LP_OFULL + slot], par, abort_flag, g.status, lane)) break;
+      tc_fence_after();
+      // out = O / l as f16, staged over P (the P.V that read it is done): row
+      // r at r * 128 bytes, piece p at p ^ (r & 7); each warp then stores
+      // its 32 rows, four 128-byte row segments per instruction.
+      const float inv = l > 0.f ? 1.0f / l : 0.f;
+#pragma unroll
+      for (int c = 0; c < kLayaHd / 32; ++c) {
+        float ov[32];
+        tmem_ld32(trow + c * 32, ov);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            // fmaf(0, alpha, O): the one-tile running output, exactly as the
+            // general kernel folds its only tile in.
+            const float o0 = fmaf(0.f, alpha, ov[8 * e + 2 * q]);
+            const float o1 = fmaf(0.f, alpha, ov[8 * e + 2 * q + 1]);
+            const __half2 h = __floats2half2_rn(o0 * inv, o1 * inv);
+            w4[q] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          const int piece = 4 * c + e;
+          *reinterpret_cast<uint4*>(ps + r * 128 + ((piece ^ (r & 7)) << 4)) =
+              make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+      }
+      __syncwarp();
+      {
+        const int p = lane & 7;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int row = 32 * q4 + 4 * k + (lane >> 3);
+          const uint4 v = *reinterpret_cast<const uint4*>(ps + row * 128 + ((p ^ (row & 7)) << 4));
+          if (row < it.nq)
+            *reinterpret_cast<uint4*>(g.out + static_cast<size_t>(it.q0 + row) * g.d +
+                                      head * kLayaHd + 8 * p) = v;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[LP_TFREE + slot]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, LP_TMEM_COLS);
+  }
+}
+
 }  // namespace
 
 void launch_laya_rope_table(float theta, int hd, int n_pos, float2* tab, cudaStream_t s) {
@@ -504,12 +748,21 @@ bool laya_attention_map(CUtensorMap* m, const void* qkv16, int rows_cap, int d, 
 
 void launch_laya_attention(const CUtensorMap& tqkv, const LayaAttnArgs& a, cudaStream_t s) {
   if (a.n_items <= 0) return;
+  if (a.single_tile) {
+    const int units = a.n_items * a.heads;
+    const int sms = a.num_sms > 0 ? a.num_sms : 148;
+    launch_pdl(laya_attention_tile_kernel, dim3(units < sms ? units : sms), dim3(LP_THREADS),
+               LP_SMEM, s, tqkv, a);
+    return;
+  }
   dim3 grid(a.n_items, a.heads);
   launch_pdl(laya_attention_kernel, grid, dim3(192), LA_SMEM, s, tqkv, a);
 }
 
 void laya_setup_device() {
   cudaFuncSetAttribute(laya_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LA_SMEM);
+  cudaFuncSetAttribute(laya_attention_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       LP_SMEM);
 }
 
 }  // namespace omg

@@ -74,6 +74,8 @@ struct LayaAttnArgs {
   __half* out;       // [t][heads * 64] f16
   uint32_t* status;
   int n_items, heads, d, window;
+  int single_tile;   // every item's keys fit one 128-key tile (nk <= 128)
+  int num_sms;       // persistent grid bound
 };
 
 // Items of a pass from the per-row spans (host).

@@ -406,7 +406,7 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
                    std::min(splits, S), err, sizeof err))
       fail("layer %d %s: %s", l, what, err);
     // Passes of many rows (a long state's prefill) take the CTA-pair kernel.
-    if (p->s.bn == 256 && epi != kEpiBiasF16 && epi != kEpiBiasReluF16 &&
+    if (p->s.bn == 256 &&
         !gemm_plan_pair(p, w, w_rows, false, err, sizeof err))
       fail("layer %d %s: %s", l, what, err);
   };

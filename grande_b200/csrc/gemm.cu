@@ -287,18 +287,32 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, int m_tile, int
         static_cast<__half*>(g.out) + static_cast<size_t>(row0 > 0 ? row0 : 0) * g.ldo;
 #pragma unroll 1
     for (int c = 0; c < BN / 32; c += 2) {
+      const int col0 = n_tile * BN + c * 32;
+      // The chunk pair's 64 bias values, the same for every row: 16-byte
+      // broadcast loads issued before the accumulator is read.
+      float bv[64];
+      if (col0 + 64 <= g.n_out && (reinterpret_cast<uintptr_t>(g.epi.bias) & 15) == 0) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float4 b4 = __ldg(reinterpret_cast<const float4*>(g.epi.bias + col0) + j);
+          bv[4 * j] = b4.x;
+          bv[4 * j + 1] = b4.y;
+          bv[4 * j + 2] = b4.z;
+          bv[4 * j + 3] = b4.w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 64; ++j) bv[j] = col0 + j < g.n_out ? g.epi.bias[col0 + j] : 0.f;
+      }
       float v[2][32];
       tmem_ld32(tbase + c * 32, v[0]);
       tmem_ld32(tbase + (c + 1) * 32, v[1]);
-      const int col0 = n_tile * BN + c * 32;
       if (nrows <= 0 || col0 >= g.n_out) continue;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const int col = col0 + 32 * h + j;
-          const float b = col < g.n_out ? g.epi.bias[col] : 0.f;
-          v[h][j] += b;
+          v[h][j] += bv[32 * h + j];
           if constexpr (EPI == kEpiBiasReluF16) v[h][j] = fmaxf(v[h][j], 0.f);
         }
       }
@@ -1442,6 +1456,8 @@ void gemm_setup_device() {
   set_smem_attr_pair<kEpiGeGluErf>();
   set_smem_attr_pair<kEpiRopeF16>();
   set_smem_attr_pair<kEpiResidF32>();
+  set_smem_attr_pair<kEpiBiasF16>();
+  set_smem_attr_pair<kEpiBiasReluF16>();
   set_smem_attr_pair<kEpiQkPrep>();
 }
 
@@ -1453,7 +1469,7 @@ bool gemm_plan_pair(GemmPlan* p, const void* w, int w_rows, bool always, char* e
   }
   switch (p->s.epi) {
     case kEpiF32: case kEpiF16: case kEpiGeGluTanh: case kEpiGeGluErf: case kEpiRopeF16:
-    case kEpiResidF32: case kEpiQkPrep:
+    case kEpiBiasF16: case kEpiBiasReluF16: case kEpiResidF32: case kEpiQkPrep:
       break;
     default:
       snprintf(err, errlen, "gemm: no CTA-pair kernel for epilogue %d", p->s.epi);
@@ -1608,6 +1624,8 @@ void gemm_run_epi(const GemmPlan& p, int m, void* out, int ldo, const GemmEpi& e
   if (use_pair(p, m)) {
     switch (p.s.epi) {
       case kEpiRopeF16: launch_pair<kEpiRopeF16>(p, a, stream); break;
+      case kEpiBiasF16: launch_pair<kEpiBiasF16>(p, a, stream); break;
+      case kEpiBiasReluF16: launch_pair<kEpiBiasReluF16>(p, a, stream); break;
       case kEpiResidF32: launch_pair<kEpiResidF32>(p, a, stream); break;
       case kEpiQkPrep: launch_pair<kEpiQkPrep>(p, a, stream); break;
       default: break;

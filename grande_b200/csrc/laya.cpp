@@ -408,7 +408,7 @@ LayaEngine::LayaEngine(LayaBuilder&& b, size_t capacity_, size_t max_rows_)
                    n_out % 256 == 0 || epi == kEpiGeGluErf ? 256 : 128, 1, err, sizeof err))
       fail("%s: %s", w.c_str(), err);
     // Batches of many rows take the CTA-pair kernel (same results).
-    if (p->s.bn == 256 && epi != kEpiBiasF16 && epi != kEpiBiasReluF16 &&
+    if (p->s.bn == 256 &&
         !gemm_plan_pair(p, W(w), w_rows, false, err, sizeof err))
       fail("%s: %s", w.c_str(), err);
   };

@@ -308,9 +308,12 @@ __device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
 }
 
 // Arrive on an mbarrier given by its shared::cluster address (the peer's).
+// Default (CTA-scope release) semantics: it signals that this warp's TMEM
+// reads are done, which tcgen05.fence::before_thread_sync orders; a
+// cluster-scope release would also hold the warp until its global stores
+// had completed, which nobody waits for.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
-               : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 
 // 2-D TMA tile load into this CTA's shared memory whose completion is

@@ -905,7 +905,8 @@ int Engine::launch_forward(const Packing& p, Want want) {
   if (want == Want::Logits) {
     k("logits");
     launch_logits(embed_.dtype, rows_.as<float>(), static_cast<int>(p.nwanted), embed_.codes.p,
-                  embed_.scales.p, c.vocab, d, c.softcap, logits_.as<float>(), num_sms_, stream_);
+                  embed_.scales.p, c.vocab, d, c.softcap, logits_.as<float>(), num_sms_, status,
+                  stream_);
   }
   if (profiling_) prof_mark(nullptr);
   CUDA_TRY(cudaGetLastError());

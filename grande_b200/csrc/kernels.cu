@@ -559,6 +559,310 @@ __global__ void __launch_bounds__(256, 1) logits_kernel(const float* __restrict_
   }
 }
 
+// ---- lm_head on the tensor cores ---------------------------------------------
+//
+// logits.wgsl in f32 on tcgen05: a CTA takes 128-row tiles of the packed
+// embedding table (M = 128 vocab rows) against up to 32 readout rows (N = 32)
+// over K = d in 64-wide steps. Eight warps dequantize the table's Q4_0 / Q8_0
+// / f16 blocks straight from HBM into 128-byte-swizzled f16 tiles in shared
+// memory (each thread half a row: one 32-element block), the MMA thread
+// multiplies. W = (q - 8) d has at most 15 significant bits and each readout
+// value 24, so both are split into f16 hi + lo and three products
+// W_hi X_hi + W_hi X_lo + W_lo X_hi (exact f16 x f16 products, f32
+// accumulation) keep the f32 dot product of logits.wgsl: the dropped
+// W_lo X_lo term is ~2^-22 of each product.
+//
+//   warp 0      MMA (lane 0)
+//   warp 1      TMEM allocation
+//   warps 2-9   dequant: row 32 (w & 3) + lane of the tile, block 2 kb + half
+//               of K step kb; then, for the previous tile, the epilogue:
+//               the thread owning a TMEM lane (vocab row) writes its logits
+//               for every readout row, softcapped (engine.rs:1901-1906)
+constexpr int LT_STAGES = 3;
+constexpr int LT_N = 32;                          // readout rows per pass
+constexpr int LT_W_BYTES = 128 * 128;             // 128 rows x 64 f16
+constexpr int LT_X_BYTES = LT_N * 128;            // 32 rows x 64 f16
+constexpr int LT_STAGE = 2 * LT_W_BYTES + 2 * LT_X_BYTES;  // W hi, W lo, X hi, X lo
+constexpr int LT_SMEM = 1024 + LT_STAGES * LT_STAGE + 256;
+constexpr int LT_THREADS = 320;
+
+__device__ __forceinline__ void split_store8(uint8_t* hi_row, uint8_t* lo_row, int piece, int r,
+                                             const float* v) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const __half2 a = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+    const float2 af = __half22float2(a);
+    const __half2 b = __floats2half2_rn(v[2 * e] - af.x, v[2 * e + 1] - af.y);
+    h[e] = *reinterpret_cast<const uint32_t*>(&a);
+    l[e] = *reinterpret_cast<const uint32_t*>(&b);
+  }
+  const int off = ((piece ^ (r & 7)) << 4);
+  *reinterpret_cast<uint4*>(hi_row + off) = make_uint4(h[0], h[1], h[2], h[3]);
+  *reinterpret_cast<uint4*>(lo_row + off) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// Elements 8 PC .. 8 PC + 7 of a table block as f16 hi + lo (W = hi + lo;
+// hi = f16(W)), computed in half2: a code pair is permuted into the two
+// 16-bit lanes as 1024 + q (the f16 0x6400 | q), one subtraction gives the
+// signed code exactly, hi = f16(code x d) is the f16 product, and
+// lo = code x d - hi (an f16 fma: the residual's <= 4 significant bits are
+// exact unless it falls below the f16 normal range).
+template <int DT, int PC>
+__device__ __forceinline__ void raw_piece_f16(const RawBlock<DT>& r, uint4& hi, uint4& lo) {
+  if constexpr (DT == kF16) {
+    // Each 16-byte chunk of an f16 block holds 8 values: piece PC is chunk PC.
+    hi = r.c[PC];
+    lo = make_uint4(0u, 0u, 0u, 0u);
+  } else {
+    const __half2 d2 = __float2half2_rn(r.scale);  // the block's f16 scale, exactly
+    uint32_t w0, w1;
+    __half2 bias;
+    uint32_t key;
+    if constexpr (DT == kQ8) {
+      const uint4 q = r.c[PC / 2];
+      w0 = (PC & 1) ? q.z : q.x;
+      w1 = (PC & 1) ? q.w : q.y;
+      bias = __float2half2_rn(1152.0f);  // 1024 + 128: codes stored as c + 128
+      key = 0x64806480u;                 // (c ^ 0x80) | 0x6400 per lane
+    } else {
+      const uint4 q = r.c[0];
+      // Low nibbles of bytes 0..15 are elements 0..15, high nibbles 16..31.
+      w0 = (PC & 1) ? q.z : q.x;
+      w1 = (PC & 1) ? q.w : q.y;
+      if (PC >= 2) {
+        w0 >>= 4;
+        w1 >>= 4;
+      }
+      bias = __float2half2_rn(1032.0f);  // 1024 + 8: w = (q - 8) d
+      key = 0x64006400u;
+    }
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t w = e < 2 ? w0 : w1;
+      uint32_t x = __byte_perm(w, 0u, (e & 1) ? 0x4342u : 0x4140u);  // bytes -> 16-bit lanes
+      x = DT == kQ8 ? (x ^ key) : ((x & 0x000F000Fu) | key);
+      const __half2 c = __hsub2(*reinterpret_cast<const __half2*>(&x), bias);
+      const __half2 hv = __hmul2(c, d2);
+      const __half2 lv = __hfma2(c, d2, __hneg2(hv));
+      h[e] = *reinterpret_cast<const uint32_t*>(&hv);
+      l[e] = *reinterpret_cast<const uint32_t*>(&lv);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+template <int DT>
+__global__ void __launch_bounds__(LT_THREADS, 1)
+    logits_tc_kernel(const float* __restrict__ rows, int nrows, const uint8_t* __restrict__ codes,
+                     const uint8_t* __restrict__ scales, int vocab, int d, float softcap,
+                     float* __restrict__ out, uint32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  auto stage = [&](int s) { return sm + s * LT_STAGE; };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + LT_STAGES * LT_STAGE);
+  uint64_t* full = bars;                    // [stages] 8 dequant warps
+  uint64_t* empty = full + LT_STAGES;       // [stages] MMA commit
+  uint64_t* tfull = empty + LT_STAGES;      // [2] MMA commit
+  uint64_t* tempty = tfull + 2;             // [2] 8 epilogue warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = d / 32, ksteps = d / 64;
+  const int tiles = (vocab + 127) / 128;
+  const int rgroups = (nrows + LT_N - 1) / LT_N;
+  const int units = tiles * rgroups;  // (vocab tile, group of 32 readout rows)
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < LT_STAGES; ++i) {
+      mbar_init(&full[i], 8);
+      mbar_init(&empty[i], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 64);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  griddep_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(128, LT_N);
+      int it = 0, local = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+        const int b = local & 1;
+        if (!mbar_wait(&tempty[b], ((local >> 1) & 1) ^ 1, abort_flag, status)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + 32u * b;
+        bool ok = true;
+        for (int kb = 0; kb < ksteps; ++kb, ++it) {
+          const int s = it % LT_STAGES;
+          if (!mbar_wait(&full[s], (it / LT_STAGES) & 1, abort_flag, status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint8_t* st = stage(s);
+          const uint64_t wh = sw128_desc(st), wl = sw128_desc(st + LT_W_BYTES);
+          const uint64_t xh = sw128_desc(st + 2 * LT_W_BYTES);
+          const uint64_t xl = sw128_desc(st + 2 * LT_W_BYTES + LT_X_BYTES);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            umma_f16(acc, wh + 2 * k, xh + 2 * k, idesc, (kb | k) ? 1u : 0u);
+            umma_f16(acc, wh + 2 * k, xl + 2 * k, idesc, 1u);
+            umma_f16(acc, wl + 2 * k, xh + 2 * k, idesc, 1u);
+          }
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&tfull[b]);
+      }
+    }
+  } else if (warp >= 2) {
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int r = 32 * q + lane;  // this thread's tile row (and TMEM lane)
+    const int t256 = threadIdx.x - 64;
+    auto epilogue = [&](int u, int local) -> bool {
+      const int b = local & 1;
+      int ok = 0;
+      if (lane == 0) ok = mbar_wait(&tfull[b], (local >> 1) & 1, abort_flag, status) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) return false;
+      tc_fence_after();
+      // Both halves read the row's 32 columns; each writes 16 readout rows.
+      float z[32];
+      tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + 32u * b, z);
+      const int v = (u / rgroups) * 128 + r;
+      const int r0 = (u % rgroups) * LT_N;
+      if (v < vocab) {
+        // Registers are indexed at compile time: one loop per half.
+        auto put = [&](int j, float x) {
+          const int rr = r0 + 16 * half + j;
+          if (rr < nrows) {
+            if (softcap > 0.f) x = softcap * tanhf(x / softcap);
+            out[static_cast<size_t>(rr) * vocab + v] = x;
+          }
+        };
+        if (half == 0) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) put(j, z[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) put(j, z[16 + j]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
+      return true;
+    };
+    // The steps of this CTA's units in order: step i is K step i % ksteps of
+    // local unit i / ksteps. Each thread keeps the packed block and readout
+    // values of the next four steps in flight in registers (a ring indexed
+    // at compile time), so a step's conversion never waits on HBM.
+    const int n_local = units > static_cast<int>(blockIdx.x)
+                            ? (units - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                            : 0;
+    const int steps = n_local * ksteps;
+    const int xr = t256 >> 3, xp = t256 & 7;
+    RawBlock<DT> rb[4];
+    float4 xa[4], xb[4];
+    auto fetch = [&](int i, RawBlock<DT>& dst, float4& a, float4& b) {
+      const int lu = i / ksteps, kb = i - lu * ksteps;
+      const int u = blockIdx.x + lu * gridDim.x;
+      const int v = (u / rgroups) * 128 + r;
+      const int rr = (u % rgroups) * LT_N + xr;
+      load_raw_block<DT>(codes, scales, static_cast<size_t>(v) * nb + 2 * kb + half,
+                         i < steps && v < vocab, dst);
+      if (i < steps && rr < nrows) {
+        const float4* src =
+            reinterpret_cast<const float4*>(rows + static_cast<size_t>(rr) * d + kb * 64 + 8 * xp);
+        a = __ldg(src);
+        b = __ldg(src + 1);
+      } else {
+        a = b = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    };
+#pragma unroll
+    for (int j = 0; j < 4; ++j) fetch(j, rb[j], xa[j], xb[j]);
+    int prev = -1;
+    bool ok = true;
+    for (int i0 = 0; i0 < steps && ok; i0 += 4) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = i0 + j;
+        if (i >= steps || !ok) break;
+        const int s = i % LT_STAGES;
+        if (i >= LT_STAGES) {
+          int w = 0;
+          if (lane == 0)
+            w = mbar_wait(&empty[s], ((i / LT_STAGES) & 1) ^ 1, abort_flag, status) ? 1 : 0;
+          if (!__shfl_sync(0xffffffffu, w, 0)) {
+            ok = false;
+            break;
+          }
+        }
+        uint8_t* st = stage(s);
+        // W: this thread's 32-element block of its row as f16 hi / lo, in
+        // pieces of 8 values.
+#define OMG_LT_PIECE(PC)                                                             \
+  {                                                                                  \
+    uint4 hv, lv;                                                                    \
+    raw_piece_f16<DT, PC>(rb[j], hv, lv);                                            \
+    const int off = r * 128 + (((4 * half + (PC)) ^ (r & 7)) << 4);                 \
+    *reinterpret_cast<uint4*>(st + off) = hv;                                        \
+    *reinterpret_cast<uint4*>(st + LT_W_BYTES + off) = lv;                           \
+  }
+        OMG_LT_PIECE(0)
+        OMG_LT_PIECE(1)
+        OMG_LT_PIECE(2)
+        OMG_LT_PIECE(3)
+#undef OMG_LT_PIECE
+        // X: 32 readout rows x 64 values of this K step, 8 per thread.
+        {
+          const float x8[8] = {xa[j].x, xa[j].y, xa[j].z, xa[j].w,
+                               xb[j].x, xb[j].y, xb[j].z, xb[j].w};
+          split_store8(st + 2 * LT_W_BYTES + xr * 128, st + 2 * LT_W_BYTES + LT_X_BYTES + xr * 128,
+                       xp, xr, x8);
+        }
+        // Every thread's stores to the async proxy, then one arrival per warp.
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[s]);
+        fetch(i + 4, rb[j], xa[j], xb[j]);
+        if ((i + 1) % ksteps == 0) {
+          // The previous unit's logits (its MMAs ran while this one was staged).
+          const int lu = i / ksteps;
+          if (prev >= 0 && !epilogue(prev, lu - 1)) {
+            ok = false;
+            break;
+          }
+          prev = blockIdx.x + lu * gridDim.x;
+        }
+      }
+    }
+    if (ok && prev >= 0) epilogue(prev, n_local - 1);
+  }
+  griddep_launch();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 64);
+  }
+}
+
 }  // namespace
 
 void launch_dequant_f16(int dtype, const void* codes, const void* scales, int rows, int k,
@@ -656,6 +960,9 @@ void launch_qk_prep(const QkArgs& a, cudaStream_t s) {
 }
 
 void logits_setup_device(int d) {
+  cudaFuncSetAttribute(logits_tc_kernel<kQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize, LT_SMEM);
+  cudaFuncSetAttribute(logits_tc_kernel<kQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize, LT_SMEM);
+  cudaFuncSetAttribute(logits_tc_kernel<kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, LT_SMEM);
   const int smem = kLogitsRows * d * 4;
   cudaFuncSetAttribute(logits_kernel<kQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   cudaFuncSetAttribute(logits_kernel<kQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -663,11 +970,27 @@ void logits_setup_device(int d) {
 }
 
 void launch_logits(int dtype, const float* rows, int nrows, const void* codes, const void* scales,
-                   int vocab, int d, float softcap, float* out, int num_sms, cudaStream_t s) {
+                   int vocab, int d, float softcap, float* out, int num_sms, uint32_t* status,
+                   cudaStream_t s) {
   if (nrows <= 0) return;
   const size_t smem = static_cast<size_t>(kLogitsRows) * d * 4;
   const auto* c = static_cast<const uint8_t*>(codes);
   const auto* sc = static_cast<const uint8_t*>(scales);
+  if (d % 64 == 0) {
+    const int units = ((vocab + 127) / 128) * ((nrows + LT_N - 1) / LT_N);
+    const int sms = num_sms > 0 ? num_sms : 148;
+    const dim3 grid(units < sms ? units : sms);
+    if (dtype == kQ4)
+      launch_pdl(logits_tc_kernel<kQ4>, grid, dim3(LT_THREADS), LT_SMEM, s, rows, nrows, c, sc, vocab,
+                 d, softcap, out, status);
+    else if (dtype == kQ8)
+      launch_pdl(logits_tc_kernel<kQ8>, grid, dim3(LT_THREADS), LT_SMEM, s, rows, nrows, c, sc, vocab,
+                 d, softcap, out, status);
+    else
+      launch_pdl(logits_tc_kernel<kF16>, grid, dim3(LT_THREADS), LT_SMEM, s, rows, nrows, c, sc,
+                 vocab, d, softcap, out, status);
+    return;
+  }
   // Persistent sweep of the table: one CTA per SM, staging the readout rows
   // once; 8 warps per CTA, a group of vocab rows per warp at a time.
   const int groups = (vocab + 1) / 2;  // an upper bound for every table type

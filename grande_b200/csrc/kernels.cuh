@@ -87,8 +87,13 @@ void launch_rope_table(float theta, int half, int n_pos, float2* tab, cudaStream
 // and width, before the first launch).
 void logits_setup_device(int d);
 
+// logits.wgsl: out[r, v] = rows[r] . W[v] (+ softcap). With d % 64 == 0 on
+// the tensor cores (logits_tc_kernel: the packed table dequantized into
+// shared memory, f16 hi + lo splits), otherwise on the CUDA cores. `status`
+// takes the tensor-core kernel's bounded-wait errors.
 void launch_logits(int dtype, const float* rows, int nrows, const void* codes, const void* scales,
-                   int vocab, int d, float softcap, float* out, int num_sms, cudaStream_t s);
+                   int vocab, int d, float softcap, float* out, int num_sms, uint32_t* status,
+                   cudaStream_t s);
 
 // Copy K/V cache rows for a state save / restore: contiguous f16 rows.
 // (Plain cudaMemcpyAsync; kept here for symmetry with the kernels.)

@@ -27,10 +27,11 @@ class OmgError(RuntimeError):
 
 
 class Branch(C.Structure):
+    # omg_branch: the pointers as plain addresses (set from numpy buffers).
     _fields_ = [
-        ("tokens", i32p),
+        ("tokens", C.c_void_p),
         ("n_tokens", C.c_size_t),
-        ("want", szp),
+        ("want", C.c_void_p),
         ("n_want", C.c_size_t),
     ]
 

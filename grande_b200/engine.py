@@ -170,15 +170,23 @@ class _Branches:
         for gi, g in enumerate(groups):
             prefix = np.ascontiguousarray(np.asarray(g.prefix, dtype=np.int64).astype(np.uint32))
             brs = (_lib.Branch * max(1, len(g.branches)))()
-            for bi, b in enumerate(g.branches):
-                toks = np.ascontiguousarray(np.asarray(b.tokens, dtype=np.int64).astype(np.int32))
-                want = np.ascontiguousarray(np.asarray(b.want, dtype=np.int64).astype(np.uint64))
-                self.keep += [toks, want]
-                brs[bi].tokens = _lib.ptr(toks, C.c_int32)
-                brs[bi].n_tokens = toks.size
-                brs[bi].want = want.ctypes.data_as(_lib.szp)
-                brs[bi].n_want = want.size
-            self.keep += [prefix, brs]
+            # One array for all branch tokens and one for all wanted rows; each
+            # branch points at its slice.
+            tok_all, want_all, spans = [], [], []
+            for b in g.branches:
+                spans.append((len(tok_all), len(b.tokens), len(want_all), len(b.want)))
+                tok_all.extend(b.tokens)
+                want_all.extend(b.want)
+            toks = np.asarray(tok_all, dtype=np.int64).astype(np.int32)
+            wants = np.asarray(want_all, dtype=np.int64).astype(np.uint64)
+            tb, wb = toks.ctypes.data, wants.ctypes.data
+            for bi, (to, tn, wo, wn) in enumerate(spans):
+                br = brs[bi]
+                br.tokens = tb + 4 * to
+                br.n_tokens = tn
+                br.want = wb + 8 * wo
+                br.n_want = wn
+            self.keep += [prefix, brs, toks, wants]
             self.groups[gi].prefix = _lib.ptr(prefix, C.c_uint32)
             self.groups[gi].n_prefix = prefix.size
             self.groups[gi].branches = brs
@@ -283,7 +291,8 @@ class Engine:
         for gi, grp in enumerate(groups):
             brs = []
             for b in grp.branches:
-                brs.append(BranchOutput(out[r:r + len(b.want)].copy()))
+                # Views into this call's own output array (no second copy).
+                brs.append(BranchOutput(out[r:r + len(b.want)]))
                 r += len(b.want)
             outs.append(GroupOutput(brs, _source(srcs[gi]) if rows is None else None))
         return outs

@@ -131,7 +131,7 @@ class LayaEngine:
         check(lib().omg_laya_hidden(self._h, req.arr, req.n, _lib.ptr(out, C.c_float), out.size))
         res, r = [], 0
         for s in seqs:
-            res.append(out[r:r + 1 + len(s.markers)].copy())
+            res.append(out[r:r + 1 + len(s.markers)])  # views into this call's array
             r += 1 + len(s.markers)
         return res
 
@@ -146,7 +146,7 @@ class LayaEngine:
         res, o = [], 0
         for i, s in enumerate(seqs):
             a = float(act[i])
-            res.append(Output(logits[o:o + len(s.markers)].copy(), None if np.isnan(a) else a))
+            res.append(Output(logits[o:o + len(s.markers)], None if np.isnan(a) else a))
             o += len(s.markers)
         return res
 

@@ -499,3 +499,17 @@ class B200Backend:
 
     def evict_resident(self):
         self.engine.evict_resident()
+
+    @staticmethod
+    def load(dir, capacity: int, max_rows: int, device: int = 0) -> "B200Backend":
+        """WgpuBackend::load (crates/omg-wgpu/src/backend.rs:25-63) without
+        the tokenizer: an exported directory or a Gemma 3 safetensors
+        checkpoint, warmed up."""
+        from .checkpoint import load_engine
+        return B200Backend(load_engine(dir, capacity, max_rows, device))
+
+    def set_state_cache(self, dir_path, nbytes: int, dir: Optional[str] = None):
+        """backend.rs:80-96: the model id is the checkpoint directory's name
+        and the byte size of its tensor files."""
+        from .checkpoint import model_id
+        self.engine.set_state_cache(nbytes, dir, model_id(dir_path))

@@ -75,6 +75,8 @@ PROTOTYPES: dict[str, tuple] = {
     "omg_last_error": (C.c_char_p, []),
     "omg_version": (C.c_char_p, []),
     "omg_device_count": (C.c_int, []),
+    "omg_host_alloc": (C.c_int, [C.c_int, sz, pp]),
+    "omg_host_free": (None, [vp]),
     "omg_config_check": (C.c_int, [cs, C.c_char_p, sz]),
     "omg_config_tensors": (C.c_int, [cs, C.c_char_p, sz, szp]),
     "omg_builder_new": (C.c_int, [cs, C.c_int, pp]),

@@ -57,6 +57,26 @@ int omg_device_count(void) {
   return n;
 }
 
+int omg_host_alloc(int device, size_t bytes, void** out) {
+  return guarded([&] {
+    if (!out) fail("null argument");
+    *out = nullptr;
+    CUDA_TRY(cudaSetDevice(device));
+    void* p = nullptr;
+    const cudaError_t e = cudaHostAlloc(&p, bytes ? bytes : 1, cudaHostAllocPortable);
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      fail("cudaHostAlloc of %zu bytes: %s", bytes, cudaGetErrorString(e));
+    }
+    *out = p;
+    return 0;
+  });
+}
+
+void omg_host_free(void* p) {
+  if (p) (void)cudaFreeHost(p);
+}
+
 int omg_config_check(const char* config_json, char* summary, size_t cap) {
   return guarded([&] {
     if (!config_json) fail("config is null");

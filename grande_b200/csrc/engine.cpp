@@ -1063,15 +1063,36 @@ void Engine::run(const GroupIn* groups, size_t n, size_t first,
   upload(p, per_layer_rows, rows_bytes);
   run_forward(p, want);
   const float* src = want == Want::Logits ? logits_.as<float>() : rows_.as<float>();
-  if (p.nwanted)
+  // A page-locked output buffer (omg_host_alloc) takes the rows straight from
+  // the device, one copy per run of consecutive rows; any other buffer gets
+  // them through the engine's own page-locked staging buffer.
+  cudaPointerAttributes attr{};
+  const bool pinned = out && cudaPointerGetAttributes(&attr, out) == cudaSuccess &&
+                      attr.type == cudaMemoryTypeHost;
+  if (!pinned) (void)cudaGetLastError();
+  if (pinned) {
+    for (size_t i = 0; i + 1 < p.out_index.size();) {
+      const size_t s0 = p.out_index[i], d0 = p.out_index[i + 1];
+      size_t run = 1;
+      while (i + 2 * run + 1 < p.out_index.size() && p.out_index[i + 2 * run] == s0 + run &&
+             p.out_index[i + 2 * run + 1] == d0 + run)
+        ++run;
+      CUDA_TRY(cudaMemcpyAsync(out + d0 * width, src + s0 * width, run * width * 4,
+                               cudaMemcpyDeviceToHost, stream_));
+      i += 2 * run;
+    }
+  } else if (p.nwanted) {
     CUDA_TRY(cudaMemcpyAsync(h_out_.p, src, p.nwanted * width * 4, cudaMemcpyDeviceToHost,
                              stream_));
+  }
   CUDA_TRY(cudaMemcpyAsync(h_status_.p, status_.p, 4, cudaMemcpyDeviceToHost, stream_));
   CUDA_TRY(cudaStreamSynchronize(stream_));
   check_status();
-  const float* h = h_out_.as<float>();
-  for (size_t i = 0; i + 1 < p.out_index.size(); i += 2)
-    std::memcpy(out + p.out_index[i + 1] * width, h + p.out_index[i] * width, width * 4);
+  if (!pinned) {
+    const float* h = h_out_.as<float>();
+    for (size_t i = 0; i + 1 < p.out_index.size(); i += 2)
+      std::memcpy(out + p.out_index[i + 1] * width, h + p.out_index[i] * width, width * 4);
+  }
   {
     std::lock_guard<std::mutex> g(mu_);
     resident_ = std::vector<uint32_t>(groups[first].prefix,

@@ -7,6 +7,7 @@ from __future__ import annotations
 
 import ctypes as C
 import json
+import threading
 from dataclasses import dataclass, field
 from enum import IntEnum
 from typing import Optional, Sequence
@@ -161,6 +162,73 @@ def _buf(b: bytes):
     return C.c_char_p(b) if b else None
 
 
+class _HostBlock:
+    """One page-locked block handed out as the base of an output array; it
+    goes back to its pool when the last view of the array is gone."""
+
+    __slots__ = ("pool", "addr", "size", "__array_interface__")
+
+    def __init__(self, pool: "_HostPool", addr: int, size: int, shape):
+        self.pool, self.addr, self.size = pool, addr, size
+        self.__array_interface__ = {"shape": tuple(shape), "typestr": "<f4",
+                                    "data": (addr, False), "version": 3}
+
+    def __del__(self):
+        try:
+            self.pool.put(self.addr, self.size)
+        except Exception:  # interpreter shutdown
+            pass
+
+
+class _HostPool:
+    """Page-locked output arrays (omg_host_alloc on the engine's device),
+    reused across calls: the engine copies the rows into them straight from
+    the device. Blocks are sized in 64 KiB steps; a few free blocks per size
+    are kept, the rest released."""
+
+    STEP = 1 << 16
+    KEEP = 4
+
+    def __init__(self, device: int):
+        self.device = device
+        self.free: dict = {}
+        self.lock = threading.Lock()
+
+    def array(self, shape) -> np.ndarray:
+        size = max(int(np.prod(shape)) * 4, 1)
+        size = (size + self.STEP - 1) // self.STEP * self.STEP
+        with self.lock:
+            blocks = self.free.get(size)
+            addr = blocks.pop() if blocks else None
+        if addr is None:
+            ptr = C.c_void_p()
+            if lib().omg_host_alloc(self.device, size, C.byref(ptr)) < 0:
+                # Out of page-locked memory: a pageable array (staged copy).
+                return np.empty(shape, dtype=np.float32)
+            addr = ptr.value
+        return np.asarray(_HostBlock(self, addr, size, shape))
+
+    def put(self, addr: int, size: int):
+        with self.lock:
+            blocks = self.free.setdefault(size, [])
+            if len(blocks) < self.KEEP:
+                blocks.append(addr)
+                return
+        lib().omg_host_free(addr)
+
+
+_POOLS: dict = {}
+_POOLS_LOCK = threading.Lock()
+
+
+def _host_pool(device: int) -> _HostPool:
+    """The page-locked output pool of one device, shared by its engines."""
+    with _POOLS_LOCK:
+        if device not in _POOLS:
+            _POOLS[device] = _HostPool(device)
+        return _POOLS[device]
+
+
 class _Branches:
     """Keeps the ctypes arrays of a request alive for one call."""
 
@@ -247,6 +315,7 @@ class Engine:
         self.device = info.device
         self.bos = info.bos
         self._embed_dtype = Dtype(info.embed_dtype)
+        self._pool = _host_pool(self.device)
 
     def close(self):
         h, self._h = getattr(self, "_h", None), None
@@ -276,7 +345,7 @@ class Engine:
         req = _Branches(groups)
         width = self.vocab if Want(want) == Want.LOGITS else self.d
         nrows = sum(g.rows() for g in groups)
-        out = np.empty((max(nrows, 1), width), dtype=np.float32)
+        out = self._pool.array((max(nrows, 1), width))
         srcs = (C.c_int32 * len(groups))()
         if rows is None:
             check(lib().omg_engine_evaluate_groups(self._h, req.groups, len(groups), int(want),

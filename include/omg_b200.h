@@ -90,6 +90,14 @@ const char* omg_version(void);
 /* Number of visible CUDA devices (0 when none). */
 int omg_device_count(void);
 
+/* Page-locked host memory for output buffers (no reference counterpart: a
+ * B200-side addition), allocated with `device` current so that no other
+ * device gets a context. The evaluate calls detect such a buffer and copy
+ * the rows into it straight from the device, skipping the staging copy that
+ * a pageable buffer needs. omg_host_free releases it (NULL is a no-op). */
+int omg_host_alloc(int device, size_t bytes, void** out);
+void omg_host_free(void* p);
+
 /* ---- model configuration -------------------------------------------------- */
 
 /* Config::from_json + Config::validate (model.rs:66-254). Writes a one-line

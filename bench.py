@@ -470,7 +470,7 @@ def run_laya(a, dist: Dist):
         "p50_latency_ms": round(statistics.median(lat), 3) if lat else None,
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                 "h2d_bytes_per_step": t * 4 * 4 + 8 * shape.markers * shape.seqs,
-                "d2h_bytes_per_step": shape.rows() * shape.d * 4,
+                "d2h_bytes_per_step": (shape.seqs * shape.markers + shape.seqs) * 4,
                 "ms_per_step": round(e2e_max / a.steps, 4)},
         "gpu_launches": launches * a.steps,
         "roofline": {"kernel": "gemm_wi (tcgen05, fused erf GeGLU)", "bound": "tensor",

@@ -54,10 +54,11 @@ class EngineInfo(C.Structure):
 
 
 class LayaSeqC(C.Structure):
+    # omg_laya_sequence: the pointers as plain addresses (set from numpy buffers).
     _fields_ = [
-        ("ids", u32p),
+        ("ids", C.c_void_p),
         ("n_ids", C.c_size_t),
-        ("markers", szp),
+        ("markers", C.c_void_p),
         ("n_markers", C.c_size_t),
         ("qtype", C.c_int),
     ]

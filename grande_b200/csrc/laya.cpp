@@ -344,7 +344,15 @@ LayaEngine::LayaEngine(LayaBuilder&& b, size_t capacity_, size_t max_rows_)
   b.stream_ = nullptr;
   lin_ = std::move(b.lin_);
   vec_ = std::move(b.vec_);
-  host_ = std::move(b.host_);
+  // The decision head's f32 weights (laya.rs:677-680 keeps them on the host
+  // in f32; here they run on the device in f32).
+  for (auto& kv : b.host_) {
+    DevBuffer& buf = headw_[kv.first];
+    buf.alloc(kv.second.size() * 4, false);
+    CUDA_TRY(cudaMemcpy(buf.p, kv.second.data(), kv.second.size() * 4, cudaMemcpyHostToDevice));
+  }
+  l2_bias_ = b.host_.at("scorer.l2_b").at(0);
+  b.host_.clear();
   embed_dtype_ = b.embed_dtype_;
   embed_codes_ = std::move(b.embed_codes_);
   embed_scales_ = std::move(b.embed_scales_);
@@ -371,6 +379,11 @@ LayaEngine::LayaEngine(LayaBuilder&& b, size_t capacity_, size_t max_rows_)
   attn16_.alloc(R * d * 2);
   act16_.alloc(R * act_stride_ * 2);
   rows_.alloc(std::max<size_t>(max_rows, 1) * d * 4);
+  // Head indices: max_rows int4 sequence entries, then max_rows marker rows;
+  // head outputs: max_rows logits, then max_rows act probabilities.
+  head_idx_.alloc(std::max<size_t>(max_rows, 1) * (sizeof(int4) + 4));
+  h_head_idx_.alloc(std::max<size_t>(max_rows, 1) * (sizeof(int4) + 4));
+  head_out_.alloc(std::max<size_t>(max_rows, 1) * 2 * 4);
   status_.alloc(16);
   h_ids_.alloc(R * 4);
   h_pos_.alloc(R * 4);
@@ -488,10 +501,14 @@ LayaEngine::Packing LayaEngine::pack(const LayaSequence* seqs, size_t n) const {
       p.qtype.push_back(s.qtype);
       p.span.push_back(make_int2(start, end));
     }
+    p.head_seq.push_back(make_int4(static_cast<int>(p.row_map.size()),
+                                   static_cast<int>(p.marker_row.size()),
+                                   static_cast<int>(s.n_markers), 0));
     p.row_map.push_back(start);
     for (size_t j = 0; j < s.n_markers; ++j) {
       const size_t m = s.markers[j];
       if (m >= s.n_ids) fail("sequence %zu: marker %zu past its %zu tokens", si, m, s.n_ids);
+      p.marker_row.push_back(static_cast<int32_t>(p.row_map.size()));
       p.row_map.push_back(start + static_cast<int32_t>(m));
     }
   }
@@ -516,6 +533,16 @@ void LayaEngine::upload(const Packing& p) {
   CUDA_TRY(cudaMemcpyAsync(span_.p, h_span_.p, t * sizeof(int2), cudaMemcpyHostToDevice, stream_));
   CUDA_TRY(cudaMemcpyAsync(row_map_.p, h_row_map_.p, p.row_map.size() * 4,
                            cudaMemcpyHostToDevice, stream_));
+  {
+    // Sequences and markers number at most the rows read back (<= max_rows).
+    const size_t cap = std::max<size_t>(max_rows, 1);
+    auto* hs = h_head_idx_.as<int4>();
+    std::memcpy(hs, p.head_seq.data(), p.head_seq.size() * sizeof(int4));
+    std::memcpy(reinterpret_cast<int32_t*>(hs + cap), p.marker_row.data(),
+                p.marker_row.size() * 4);
+    CUDA_TRY(cudaMemcpyAsync(head_idx_.p, h_head_idx_.p, cap * (sizeof(int4) + 4),
+                             cudaMemcpyHostToDevice, stream_));
+  }
   // Attention items of both windows in one staged block; the buffers grow
   // to the largest pass seen.
   const size_t ni = p.items[0].size() + p.items[1].size();
@@ -547,7 +574,7 @@ void LayaEngine::prof_mark(const char* name) {
 
 // laya.rs:1263-1345, one launch per step: the residual adds ride in the
 // projections' epilogues and each LayerNorm is one row sweep.
-int LayaEngine::launch_forward(const Packing& p) {
+int LayaEngine::launch_forward(const Packing& p, bool head) {
   const LayaConfig& c = config;
   const int t = static_cast<int>(p.t), d = c.d;
   uint32_t* status = status_.as<uint32_t>();
@@ -656,6 +683,47 @@ int LayaEngine::launch_forward(const Packing& p) {
   k("gather");
   launch_laya_gather(x, d, row_map_.as<int>(), static_cast<int>(p.row_map.size()), rows_.as<float>(),
                      stream_);
+  if (head) {
+    // laya.rs:1442-1486 on the device: scorer logits of every marker, then
+    // the act head of every sequence.
+    const size_t cap = std::max<size_t>(max_rows, 1);
+    const int4* hseq = head_idx_.as<int4>();
+    const int* mrow = reinterpret_cast<const int*>(hseq + cap);
+    float* logits = head_out_.as<float>();
+    auto H = [&](const char* n) { return headw_.at(n).as<float>(); };
+    LayaScoreArgs sa{};
+    sa.rows = rows_.as<float>();
+    sa.marker_row = mrow;
+    sa.k = static_cast<int>(p.marker_row.size());
+    sa.d = d;
+    sa.norm_w = H("scorer.norm_w");
+    sa.norm_b = H("scorer.norm_b");
+    sa.l1 = H("scorer.l1");
+    sa.l1_b = H("scorer.l1_b");
+    sa.l2 = H("scorer.l2");
+    sa.l2_b = l2_bias_;
+    sa.eps = c.eps;
+    sa.logits = logits;
+    k("head_score");
+    launch_laya_score(sa, stream_);
+    if (c.act_out > 0) {
+      LayaActArgs aa{};
+      aa.rows = rows_.as<float>();
+      aa.seq = hseq;
+      aa.n = static_cast<int>(p.head_seq.size());
+      aa.d = d;
+      aa.hidden = c.act_hidden;
+      aa.outs = c.act_out;
+      aa.l1 = H("act.l1");
+      aa.l1_b = H("act.l1_b");
+      aa.l2 = H("act.l2");
+      aa.l2_b = H("act.l2_b");
+      aa.logits = logits;
+      aa.act = logits + cap;
+      k("head_act");
+      launch_laya_act(aa, stream_);
+    }
+  }
   if (profiling_) prof_mark(nullptr);
   CUDA_TRY(cudaGetLastError());
   return launches;
@@ -682,42 +750,7 @@ void LayaEngine::hidden(const LayaSequence* seqs, size_t n, float* out, size_t o
   std::memcpy(out, h_out_.p, nrows * d * 4);
 }
 
-// laya.rs:1496-1523: the host helpers (the LayerNorm's sums in index order
-// as Rust's iterator sum; dot products below in eight partial sums).
-static std::vector<float> host_layer_norm(const float* x, const std::vector<float>& w,
-                                          const std::vector<float>& b, size_t n, float eps) {
-  float s = 0.f;
-  for (size_t i = 0; i < n; ++i) s += x[i];
-  const float mean = s / static_cast<float>(n);
-  float v = 0.f;
-  for (size_t i = 0; i < n; ++i) v += (x[i] - mean) * (x[i] - mean);
-  v /= static_cast<float>(n);
-  const float inv = 1.0f / std::sqrt(v + eps);
-  std::vector<float> out(n);
-  for (size_t i = 0; i < n; ++i) out[i] = (x[i] - mean) * inv * w[i] + b[i];
-  return out;
-}
-
-// Eight interleaved partial sums, added in a fixed order: the loop
-// vectorises, and the result differs from a sequential sum only by f32
-// reassociation.
-static float host_dot(const float* a, const float* b, size_t n) {
-  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  size_t i = 0;
-  for (; i + 8 <= n; i += 8)
-    for (int j = 0; j < 8; ++j) acc[j] += a[i + j] * b[i + j];
-  float s = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
-  for (; i < n; ++i) s += a[i] * b[i];
-  return s;
-}
-
-static std::vector<float> host_linear(const std::vector<float>& x, const std::vector<float>& w,
-                                      const std::vector<float>& b, size_t k) {
-  std::vector<float> y(b.size());
-  for (size_t r = 0; r < b.size(); ++r) y[r] = host_dot(w.data() + r * k, x.data(), k) + b[r];
-  return y;
-}
-
+// laya.rs:1489-1493's softmax for the calibrated probabilities.
 static std::vector<float> host_softmax(const std::vector<float>& z) {
   float m = -INFINITY;
   for (float v : z) m = std::max(m, v);
@@ -731,81 +764,32 @@ static std::vector<float> host_softmax(const std::vector<float>& z) {
   return e;
 }
 
-// laya.rs:1530-1543: erf to 1.5e-7 (Abramowitz & Stegun 7.1.26).
-static float host_erf(float x) {
-  const float s = x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f);
-  const float a = std::fabs(x);
-  const float t = 1.0f / (1.0f + 0.3275911f * a);
-  const float poly =
-      ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t +
-       0.254829592f) *
-      t;
-  return s * (1.0f - poly * std::exp(-a * a));
-}
-
-static float host_gelu_erf(float x) { return 0.5f * x * (1.0f + host_erf(x * 0.70710678118654752f)); }
-
-LayaOutput LayaEngine::score(const float* rows, size_t k) const {
-  const LayaConfig& c = config;
-  const size_t d = c.d;
-  const auto& H = host_;
-  LayaOutput out;
-  out.logits.resize(k);
-  for (size_t o = 0; o < k; ++o) {
-    std::vector<float> z = host_layer_norm(rows + (o + 1) * d, H.at("scorer.norm_w"),
-                                           H.at("scorer.norm_b"), d, c.eps);
-    z = host_linear(z, H.at("scorer.l1"), H.at("scorer.l1_b"), d);
-    for (float& v : z) v = host_gelu_erf(v);
-    out.logits[o] = host_dot(z.data(), H.at("scorer.l2").data(), d) + H.at("scorer.l2_b")[0];
-  }
-  if (c.act_out == 0) return out;
-  // Confidence features over the untempered softmax, a one-option question
-  // padded to two slots (laya.rs:1463-1475).
-  const size_t kk = std::max<size_t>(k, 2);
-  std::vector<float> padded = out.logits;
-  padded.resize(kk, -1e4f);
-  const std::vector<float> p = host_softmax(padded);
-  float ent = 0.f;
-  for (float v : p) ent += v * std::log(std::max(v, 1e-9f));
-  const float entropy = -ent / std::log(static_cast<float>(kk));
-  std::vector<float> sorted = p;
-  std::sort(sorted.begin(), sorted.end());
-  const float top1 = sorted[kk - 1], top2 = sorted[kk - 2];
-  std::vector<float> pooled(rows, rows + d);
-  pooled.push_back(top1);
-  pooled.push_back(top1 - top2);
-  pooled.push_back(entropy);
-  pooled.push_back(static_cast<float>(kk) / 255.0f);
-  std::vector<float> a = host_linear(pooled, H.at("act.l1"), H.at("act.l1_b"), d + 4);
-  for (float& v : a) v = host_gelu_erf(v);
-  const std::vector<float> act =
-      host_softmax(host_linear(a, H.at("act.l2"), H.at("act.l2_b"), c.act_hidden));
-  out.has_act = true;
-  out.act_probability = act[0];
-  return out;
-}
-
+// laya.rs:1435-1486: the pass, then the decision head on the device (the
+// reference reads the rows back and scores them on the host); only the
+// logits and act probabilities come back.
 std::vector<LayaOutput> LayaEngine::evaluate(const LayaSequence* seqs, size_t n) {
-  std::vector<size_t> first(n + 1, 0);
-  for (size_t i = 0; i < n; ++i) first[i + 1] = first[i] + 1 + seqs[i].n_markers;
-  std::vector<float> h(first[n] * config.d);
-  hidden(seqs, n, h.data(), h.size());
-  // The host half, sequences split over the host's cores (each sequence's
-  // score is independent and computed the same way on any thread).
+  std::lock_guard<std::mutex> g(mu_);
+  CUDA_TRY(cudaSetDevice(device_));
+  Packing p = pack(seqs, n);
+  upload(p);
+  launch_forward(p, true);
+  const size_t cap = std::max<size_t>(max_rows, 1), k = p.marker_row.size();
+  float* h = h_out_.as<float>();
+  if (k) CUDA_TRY(cudaMemcpyAsync(h, head_out_.p, k * 4, cudaMemcpyDeviceToHost, stream_));
+  if (config.act_out > 0)
+    CUDA_TRY(cudaMemcpyAsync(h + cap, head_out_.as<float>() + cap, n * 4, cudaMemcpyDeviceToHost,
+                             stream_));
+  CUDA_TRY(cudaMemcpyAsync(h_status_.p, status_.p, 4, cudaMemcpyDeviceToHost, stream_));
+  CUDA_TRY(cudaStreamSynchronize(stream_));
+  check_status();
   std::vector<LayaOutput> out(n);
-  const size_t nthreads =
-      std::min<size_t>(std::max(1u, std::thread::hardware_concurrency()), (n + 7) / 8);
-  auto work = [&](size_t w) {
-    for (size_t i = w; i < n; i += nthreads)
-      out[i] = score(h.data() + first[i] * config.d, seqs[i].n_markers);
-  };
-  if (nthreads <= 1) {
-    work(0);
-  } else {
-    std::vector<std::thread> pool;
-    for (size_t w = 1; w < nthreads; ++w) pool.emplace_back(work, w);
-    work(0);
-    for (auto& th : pool) th.join();
+  for (size_t i = 0; i < n; ++i) {
+    const int4 q = p.head_seq[i];
+    out[i].logits.assign(h + q.y, h + q.y + q.z);
+    if (config.act_out > 0) {
+      out[i].has_act = true;
+      out[i].act_probability = h[cap + i];
+    }
   }
   return out;
 }
@@ -823,8 +807,7 @@ void LayaEngine::warmup() {
   const uint32_t ids[3] = {config.cls, config.mask, config.sep};
   const size_t markers[1] = {1};
   LayaSequence s{ids, 3, markers, 1, 2};
-  std::vector<float> h(2 * static_cast<size_t>(config.d));
-  hidden(&s, 1, h.data(), h.size());
+  evaluate(&s, 1);
 }
 
 float LayaEngine::time_forward(const LayaSequence* seqs, size_t n, int iters, int* launches) {
@@ -835,7 +818,7 @@ float LayaEngine::time_forward(const LayaSequence* seqs, size_t n, int iters, in
   CUDA_TRY(cudaStreamSynchronize(stream_));
   int nl = 0;
   CUDA_TRY(cudaEventRecord(events_[6], stream_));
-  for (int i = 0; i < iters; ++i) nl = launch_forward(p);
+  for (int i = 0; i < iters; ++i) nl = launch_forward(p, true);
   CUDA_TRY(cudaEventRecord(events_[7], stream_));
   CUDA_TRY(cudaMemcpyAsync(h_status_.p, status_.p, 4, cudaMemcpyDeviceToHost, stream_));
   CUDA_TRY(cudaStreamSynchronize(stream_));
@@ -856,7 +839,7 @@ std::string LayaEngine::profile_forward(const LayaSequence* seqs, size_t n, int 
   // The profiled passes are the range an external profiler run with
   // --profile-from-start off captures.
   CUDA_TRY(cudaProfilerStart());
-  for (int i = 0; i < iters; ++i) launch_forward(p);
+  for (int i = 0; i < iters; ++i) launch_forward(p, true);
   CUDA_TRY(cudaProfilerStop());
   profiling_ = false;
   CUDA_TRY(cudaMemcpyAsync(h_status_.p, status_.p, 4, cudaMemcpyDeviceToHost, stream_));

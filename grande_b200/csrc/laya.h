@@ -118,8 +118,9 @@ class LayaEngine {
   // laya.rs:1126-1134.
   void warmup();
 
-  // Device-resident timing: pack and upload once, then `iters` passes
-  // between two CUDA events on the engine's stream; total milliseconds.
+  // Device-resident timing: pack and upload once, then `iters` decision
+  // passes (encoder, gather and head) between two CUDA events on the
+  // engine's stream; total milliseconds.
   float time_forward(const LayaSequence* seqs, size_t n, int iters, int* launches);
   // Per-kernel device time of `iters` passes: JSON {"kernel": [launches, ms]}.
   std::string profile_forward(const LayaSequence* seqs, size_t n, int iters);
@@ -137,6 +138,10 @@ class LayaEngine {
     std::vector<int2> span;
     std::vector<int32_t> row_map;
     std::vector<LayaAttnItem> items[2];  // [0] local window, [1] global
+    // Decision head: per sequence (its [CLS] row in the gathered rows, its
+    // first logit, its marker count, 0); the gathered row of each marker.
+    std::vector<int4> head_seq;
+    std::vector<int32_t> marker_row;
     size_t t = 0;
   };
   struct EncLayer {
@@ -151,8 +156,9 @@ class LayaEngine {
 
   Packing pack(const LayaSequence* seqs, size_t n) const;
   void upload(const Packing& p);
-  int launch_forward(const Packing& p);
-  LayaOutput score(const float* rows, size_t k) const;
+  // The encoder pass and the row gather; with `head`, also the decision
+  // head (scorer logits and act probabilities) on the device.
+  int launch_forward(const Packing& p, bool head = false);
   void check_status();
   void prof_mark(const char* name);
 
@@ -160,7 +166,8 @@ class LayaEngine {
   int num_sms_ = 148;
   cudaStream_t stream_ = nullptr;
   std::map<std::string, DevBuffer> lin_, vec_;
-  std::map<std::string, std::vector<float>> host_;
+  std::map<std::string, DevBuffer> headw_;  // scorer.* / act.* as f32
+  float l2_bias_ = 0.f;                      // scorer.l2_b
   int embed_dtype_ = 0;
   DevBuffer embed_codes_, embed_scales_;
   std::vector<EncLayer> enc_;
@@ -171,8 +178,9 @@ class LayaEngine {
 
   // Workspace.
   DevBuffer ids_, pos_, qtype_, span_, row_map_, items_, x_, h16_, qkv16_, attn16_, act16_,
-      rows_, rope_local_, rope_global_, status_;
-  PinnedBuffer h_ids_, h_pos_, h_qtype_, h_span_, h_row_map_, h_items_, h_out_, h_status_;
+      rows_, rope_local_, rope_global_, status_, head_idx_, head_out_;
+  PinnedBuffer h_ids_, h_pos_, h_qtype_, h_span_, h_row_map_, h_items_, h_out_, h_status_,
+      h_head_idx_;
   size_t items_cap_ = 0;
   CUtensorMap tqkv_;
 

@@ -765,4 +765,259 @@ void laya_setup_device() {
                        LP_SMEM);
 }
 
+
+// ---- the decision head on the device -------------------------------------------
+
+namespace {
+
+constexpr int kHeadThreads = 256;  // eight warps
+constexpr int kHeadWarps = kHeadThreads / 32;
+
+// erf by Abramowitz & Stegun 7.1.26 (|error| < 1.5e-7), the form laya.rs
+// uses for the host head.
+__device__ __forceinline__ float head_erf(float x) {
+  const float sgn = x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f);
+  const float a = fabsf(x);
+  const float t = 1.0f / (1.0f + 0.3275911f * a);
+  const float poly =
+      ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t +
+       0.254829592f) *
+      t;
+  return sgn * (1.0f - poly * expf(-a * a));
+}
+
+__device__ __forceinline__ float head_gelu(float x) {
+  return 0.5f * x * (1.0f + head_erf(x * 0.70710678118654752f));
+}
+
+__device__ __forceinline__ float warp_sum_all(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float dot4(float4 a, float4 b) {
+  return a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+}
+
+// The rows r = warp, warp + 8, ... < rows of W ([rows][n4] float4s) against
+// the MR inputs whose float4 slots lane + 32 j (j < NV) this lane holds in
+// `in` (zero past n4). The next row's slots are loaded while the current
+// row is summed, so each warp keeps NV loads in flight. consume(r, y) gets
+// the MR full sums (every lane holds them).
+template <int NV, int MR, class F>
+__device__ __forceinline__ void head_rows(const float4* __restrict__ W, int n4, int rows,
+                                          const float4 (&in)[MR][NV], F&& consume) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 wn[NV];
+  auto load = [&](int r) {
+    const float4* wr = W + static_cast<size_t>(r) * n4;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int i = lane + 32 * j;
+      wn[j] = i < n4 ? __ldg(wr + i) : zero;
+    }
+  };
+  if (warp < rows) load(warp);
+  for (int r = warp; r < rows; r += kHeadWarps) {
+    float4 w[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) w[j] = wn[j];
+    if (r + kHeadWarps < rows) load(r + kHeadWarps);
+    float y[MR];
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      y[m] = 0.f;
+#pragma unroll
+      for (int j = 0; j < NV; ++j) y[m] += dot4(w[j], in[m][j]);
+      y[m] = warp_sum_all(y[m]);
+    }
+    consume(r, y);
+  }
+}
+
+// Scorer: MR marker rows per CTA; NV = d / 128 float4 slots per lane.
+template <int NV, int MR>
+__global__ void __launch_bounds__(kHeadThreads) laya_score_kernel(LayaScoreArgs a) {
+  griddep_wait();
+  __shared__ float part[kHeadWarps][MR];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * MR;
+  const int d = a.d, n4 = d / 4;
+  // Every warp normalises the MR rows itself (each warp reduces the same
+  // values the same way, so all hold the same results) and keeps its lane's
+  // slots in registers.
+  float4 z[MR][NV];
+  const float4* nw = reinterpret_cast<const float4*>(a.norm_w);
+  const float4* nb = reinterpret_cast<const float4*>(a.norm_b);
+#pragma unroll
+  for (int m = 0; m < MR; ++m) {
+    const bool live = m0 + m < a.k;
+    const float4* x = reinterpret_cast<const float4*>(
+        a.rows + static_cast<size_t>(live ? a.marker_row[m0 + m] : 0) * d);
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      z[m][j] = x[lane + 32 * j];
+      s += (z[m][j].x + z[m][j].y) + (z[m][j].z + z[m][j].w);
+    }
+    const float mean = warp_sum_all(s) / static_cast<float>(d);
+    float v = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const float4 c = make_float4(z[m][j].x - mean, z[m][j].y - mean, z[m][j].z - mean,
+                                   z[m][j].w - mean);
+      v += dot4(c, c);
+    }
+    const float inv = 1.0f / sqrtf(warp_sum_all(v) / static_cast<float>(d) + a.eps);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const float4 w = __ldg(nw + lane + 32 * j), b = __ldg(nb + lane + 32 * j);
+      const float4 q = z[m][j];
+      z[m][j] = live ? make_float4((q.x - mean) * inv * w.x + b.x, (q.y - mean) * inv * w.y + b.y,
+                                   (q.z - mean) * inv * w.z + b.z, (q.w - mean) * inv * w.w + b.w)
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  float acc[MR];
+#pragma unroll
+  for (int m = 0; m < MR; ++m) acc[m] = 0.f;
+  head_rows<NV, MR>(reinterpret_cast<const float4*>(a.l1), n4, d, z,
+                    [&](int r, const float (&y)[MR]) {
+                      const float b = __ldg(a.l1_b + r), w2 = __ldg(a.l2 + r);
+#pragma unroll
+                      for (int m = 0; m < MR; ++m) acc[m] += head_gelu(y[m] + b) * w2;
+                    });
+  if (lane == 0) {
+#pragma unroll
+    for (int m = 0; m < MR; ++m) part[warp][m] = acc[m];
+  }
+  __syncthreads();
+  if (threadIdx.x < MR && m0 + static_cast<int>(threadIdx.x) < a.k) {
+    float s = 0.f;
+    for (int w = 0; w < kHeadWarps; ++w) s += part[w][threadIdx.x];
+    a.logits[m0 + threadIdx.x] = s + a.l2_b;
+  }
+}
+
+// Act head: MR sequences per CTA; the input u = [cls row (d), 4 features]
+// is NV = d / 128 full slots per lane plus one more slot that only lane 0
+// fills (the features).
+template <int NV, int MR>
+__global__ void __launch_bounds__(kHeadThreads) laya_act_kernel(LayaActArgs a) {
+  griddep_wait();
+  __shared__ float hid[MR][256];
+  __shared__ float4 feat[MR];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int s0 = blockIdx.x * MR;
+  const int d = a.d, n4 = d / 4 + 1;
+  // The confidence features of sequence m (laya.rs:1463-1475), by thread m.
+  if (threadIdx.x < MR) {
+    const int m = threadIdx.x;
+    float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (s0 + m < a.n) {
+      const int4 q = a.seq[s0 + m];
+      const float* lg = a.logits + q.y;
+      const int k = q.z, kk = k > 2 ? k : 2;
+      float mx = -INFINITY;
+      for (int j = 0; j < kk; ++j) mx = fmaxf(mx, j < k ? lg[j] : -1e4f);
+      float sum = 0.f;
+      for (int j = 0; j < kk; ++j) sum += expf((j < k ? lg[j] : -1e4f) - mx);
+      float ent = 0.f, top1 = -INFINITY, top2 = -INFINITY;
+      for (int j = 0; j < kk; ++j) {
+        const float p = expf((j < k ? lg[j] : -1e4f) - mx) / sum;
+        ent += p * logf(fmaxf(p, 1e-9f));
+        if (p > top1) {
+          top2 = top1;
+          top1 = p;
+        } else if (p > top2) {
+          top2 = p;
+        }
+      }
+      f = make_float4(top1, top1 - top2, -ent / logf(static_cast<float>(kk)),
+                      static_cast<float>(kk) / 255.0f);
+    }
+    feat[m] = f;
+  }
+  __syncthreads();
+  float4 u[MR][NV + 1];
+#pragma unroll
+  for (int m = 0; m < MR; ++m) {
+    const bool live = s0 + m < a.n;
+    const float4* x = reinterpret_cast<const float4*>(
+        a.rows + static_cast<size_t>(live ? a.seq[s0 + m].x : 0) * d);
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+      u[m][j] = live ? x[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+    u[m][NV] = lane == 0 ? feat[m] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  head_rows<NV + 1, MR>(reinterpret_cast<const float4*>(a.l1), n4, a.hidden, u,
+                        [&](int r, const float (&y)[MR]) {
+                          if (lane == 0) {
+                            const float b = __ldg(a.l1_b + r);
+#pragma unroll
+                            for (int m = 0; m < MR; ++m) hid[m][r] = head_gelu(y[m] + b);
+                          }
+                        });
+  __syncthreads();
+  // Output layer and softmax: warp m for sequence m, in two passes over the
+  // outputs (max, then the exponentials), each logit recomputed identically,
+  // so any number of outputs needs no storage.
+  for (int m = warp; m < MR; m += kHeadWarps) {
+    if (s0 + m >= a.n) break;
+    auto out_logit = [&](int o) {
+      const float* w = a.l2 + static_cast<size_t>(o) * a.hidden;
+      float s = 0.f;
+      for (int i = lane; i < a.hidden; i += 32) s += w[i] * hid[m][i];
+      return warp_sum_all(s) + a.l2_b[o];
+    };
+    float mx = -INFINITY;
+    for (int o = 0; o < a.outs; ++o) mx = fmaxf(mx, out_logit(o));
+    float sum = 0.f, e0 = 0.f;
+    for (int o = 0; o < a.outs; ++o) {
+      const float e = expf(out_logit(o) - mx);
+      if (o == 0) e0 = e;
+      sum += e;
+    }
+    if (lane == 0) a.act[s0 + m] = e0 / sum;
+  }
+}
+
+}  // namespace
+
+// Marker rows (sequences) per CTA by the registers a lane's slots take:
+// MR x NV float4s stay within 24. NV = hidden_size / 128 (1..16).
+#define OMG_HEAD_NV(X)                                                                    \
+  X(1, 8) X(2, 8) X(3, 8) X(4, 4) X(5, 4) X(6, 4) X(7, 2) X(8, 2) X(9, 2) X(10, 2) X(11, 2) \
+  X(12, 2) X(13, 1) X(14, 1) X(15, 1) X(16, 1)
+
+void launch_laya_score(const LayaScoreArgs& a, cudaStream_t s) {
+  if (a.k <= 0) return;
+  const int nv = a.d / 128;
+#define OMG_SCORE(NV, MR)                                                                     \
+  if (nv == NV) {                                                                             \
+    launch_pdl(laya_score_kernel<NV, MR>, dim3((a.k + MR - 1) / MR), dim3(kHeadThreads), 0, s, \
+               a);                                                                            \
+    return;                                                                                   \
+  }
+  OMG_HEAD_NV(OMG_SCORE)
+#undef OMG_SCORE
+}
+
+void launch_laya_act(const LayaActArgs& a, cudaStream_t s) {
+  if (a.n <= 0) return;
+  const int nv = a.d / 128;
+#define OMG_ACT(NV, MR)                                                                     \
+  if (nv == NV) {                                                                           \
+    launch_pdl(laya_act_kernel<NV, MR>, dim3((a.n + MR - 1) / MR), dim3(kHeadThreads), 0, s, \
+               a);                                                                          \
+    return;                                                                                 \
+  }
+  OMG_HEAD_NV(OMG_ACT)
+#undef OMG_ACT
+}
+#undef OMG_HEAD_NV
+
+
 }  // namespace omg

@@ -91,4 +91,39 @@ void launch_laya_attention(const CUtensorMap& tqkv, const LayaAttnArgs& a, cudaS
 // Shared-memory limits of the encoder kernels (once per device).
 void laya_setup_device();
 
+// ---- the decision head on the device (laya.rs:1442-1486) --------------------
+//
+// The scorer of every [MASK] row and the act head of every sequence, in f32
+// on the CUDA cores, over the gathered rows (per sequence its [CLS] row
+// then its marker rows). Same operations as the reference's host code; sums
+// run in another order (warp trees instead of index order), so results
+// agree with it to f32 reassociation.
+//
+// Scorer, per marker row x: z = LN(x; norm_w, norm_b) (biased variance,
+// 1 / sqrt(var + eps)), y = GELU_erf(l1 z + l1_b), logit = l2 . y + l2_b.
+struct LayaScoreArgs {
+  const float* rows;        // [*, d]
+  const int* marker_row;    // [k] row of each marker in `rows`
+  int k, d;
+  const float *norm_w, *norm_b, *l1, *l1_b, *l2;
+  float l2_b, eps;
+  float* logits;            // [k]
+};
+void launch_laya_score(const LayaScoreArgs& a, cudaStream_t s);
+
+// Act head, per sequence: the softmax of its marker logits padded to at
+// least two slots with -1e4 gives top1, top1 - top2 and the normalised
+// entropy; u = [cls row, top1, top1 - top2, entropy, slots / 255],
+// a = GELU_erf(l1 u + l1_b), p = softmax(l2 a + l2_b), act = p[0].
+// hidden <= 256 (the act head's width, laya.rs:1474-1486).
+struct LayaActArgs {
+  const float* rows;
+  const int4* seq;          // [n] (cls row, first logit, marker count, 0)
+  int n, d, hidden, outs;
+  const float *l1, *l1_b, *l2, *l2_b;
+  const float* logits;
+  float* act;               // [n]
+};
+void launch_laya_act(const LayaActArgs& a, cudaStream_t s);
+
 }  // namespace omg

@@ -13,6 +13,7 @@ There is no CPU fallback: without the native library every call raises.
 from __future__ import annotations
 
 import ctypes as C
+from itertools import chain
 import json
 from dataclasses import dataclass, field
 from typing import Optional, Sequence as Seq
@@ -47,17 +48,29 @@ class _Seqs:
     """Keeps the ctypes arrays of a request alive for one call."""
 
     def __init__(self, seqs: Seq[Sequence]):
-        self.keep = []
-        self.arr = (_lib.LayaSeqC * max(1, len(seqs)))()
+        n = len(seqs)
+        self.arr = (_lib.LayaSeqC * max(1, n))()
+        # One array for every sequence's ids and one for every marker; each
+        # sequence points at its slice (one conversion per field, not per
+        # sequence).
+        lens = [len(s.ids) for s in seqs]
+        nmk = [len(s.markers) for s in seqs]
+        ids = np.fromiter(chain.from_iterable(s.ids for s in seqs), dtype=np.int64,
+                          count=sum(lens)).astype(np.uint32)
+        mk = np.fromiter(chain.from_iterable(s.markers for s in seqs), dtype=np.int64,
+                         count=sum(nmk)).astype(np.uint64)
+        self.keep = [ids, mk]
+        ib, mb = ids.ctypes.data, mk.ctypes.data
+        io = mo = 0
         for i, s in enumerate(seqs):
-            ids = np.ascontiguousarray(np.asarray(s.ids, dtype=np.int64).astype(np.uint32))
-            mk = np.ascontiguousarray(np.asarray(s.markers, dtype=np.int64).astype(np.uint64))
-            self.keep += [ids, mk]
-            self.arr[i].ids = _lib.ptr(ids, C.c_uint32)
-            self.arr[i].n_ids = ids.size
-            self.arr[i].markers = mk.ctypes.data_as(_lib.szp)
-            self.arr[i].n_markers = mk.size
-            self.arr[i].qtype = int(s.qtype)
+            a = self.arr[i]
+            a.ids = ib + 4 * io
+            a.n_ids = lens[i]
+            a.markers = mb + 8 * mo
+            a.n_markers = nmk[i]
+            a.qtype = int(s.qtype)
+            io += lens[i]
+            mo += nmk[i]
         self.n = len(seqs)
 
 

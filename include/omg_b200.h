@@ -363,8 +363,9 @@ int omg_laya_warmup(omg_laya_engine* e);
 int omg_laya_hidden(omg_laya_engine* e, const omg_laya_sequence* seqs, size_t n, float* out_rows,
                     size_t out_floats);
 
-/* LayaEngine::evaluate (laya.rs:1435-1438) = hidden + the host scorer and
- * act head (laya.rs:1442-1486): out_logits gets each sequence's option
+/* LayaEngine::evaluate (laya.rs:1435-1438) = hidden + the scorer and act
+ * head (laya.rs:1442-1486; f32, run on the device here, so only the logits
+ * and act probabilities cross PCIe): out_logits gets each sequence's option
  * logits back to back (sum of n_markers floats), out_act (n floats, may be
  * NULL) the act probability, NaN without an act head. */
 int omg_laya_evaluate(omg_laya_engine* e, const omg_laya_sequence* seqs, size_t n,

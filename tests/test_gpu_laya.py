@@ -114,8 +114,9 @@ def test_sequences_are_isolated(long):
 
 
 def test_evaluate_scores_and_probabilities():
-    """evaluate() = hidden + the host scorer / act head (laya.rs:1442-1486);
-    probabilities() with the calibration temperature (laya.rs:1489-1493)."""
+    """evaluate() = hidden + the scorer / act head (laya.rs:1442-1486, run
+    on the device here); probabilities() with the calibration temperature
+    (laya.rs:1489-1493)."""
     by = {"choice:3-5": 0.7, "noul:2": 1.9}
     m = LayaModel(small(), 23, O.Q8, O.Q8, temperature=(1.3, 0.8, 1.1), by_options=by)
     eng = m.engine()
@@ -124,10 +125,12 @@ def test_evaluate_scores_and_probabilities():
     rows = eng.hidden(seqs)
     exp_rows = m.rows(seqs, m.hidden(seqs))
     for s, o, r, er in zip(seqs, outs, rows, exp_rows):
-        # The host half is exact on the engine's own rows ...
+        # The head agrees with the reference's host head on the engine's own
+        # rows to f32 reassociation (the device sums in warp trees, the host
+        # in index order) ...
         lg, act = O.laya_score(m.cfg, m.host, r)
-        np.testing.assert_allclose(o.logits, lg, rtol=1e-5, atol=1e-6)
-        assert o.act_probability is not None and abs(o.act_probability - act) < 1e-6
+        np.testing.assert_allclose(o.logits, lg, rtol=1e-4, atol=1e-5)
+        assert o.act_probability is not None and abs(o.act_probability - act) < 1e-5
         # ... and close to the oracle end to end.
         lg2, act2 = O.laya_score(m.cfg, m.host, er)
         assert np.abs(o.logits - lg2).max() < TOL
@@ -141,6 +144,32 @@ def test_evaluate_scores_and_probabilities():
         pe /= pe.sum()
         assert np.abs(p - pe).max() < 1e-3
         assert abs(p.sum() - 1.0) < 1e-6
+    eng.close()
+
+
+def test_device_head_many_sequences_and_markers():
+    """The device head over more sequences and markers than one CTA takes
+    (eight of each), one-marker sequences (the act head sees two slots, one
+    padded) and sequences of up to 20 markers, against the reference's host
+    head on the engine's own rows."""
+    m = LayaModel(small(), 37, O.Q8, O.Q8)
+    eng = m.engine(capacity=2048, max_rows=512)
+    rng = np.random.default_rng(11)
+    seqs = seqs_long()
+    for i in range(19):
+        n = int(rng.integers(2, 60))
+        ids = [1] + list(rng.integers(5, 96, n - 1))
+        k = 1 if i % 5 == 4 else int(rng.integers(1, min(n, 20) + 1))
+        markers = sorted(set(int(x) for x in rng.choice(np.arange(n), k, replace=False)))
+        seqs.append(Sequence(ids, markers, i % 3))
+    outs = eng.evaluate(seqs)
+    rows = eng.hidden(seqs)
+    assert sum(len(s.markers) for s in seqs) > 16 and len(seqs) > 16
+    for s, o, r in zip(seqs, outs, rows):
+        lg, act = O.laya_score(m.cfg, m.host, r)
+        assert len(o.logits) == len(s.markers)
+        np.testing.assert_allclose(o.logits, lg, rtol=1e-4, atol=1e-5)
+        assert abs(o.act_probability - act) < 1e-5
     eng.close()
 
 

@@ -147,28 +147,37 @@ __global__ void __launch_bounds__(kNormMaxThreads) residual_norm_kernel(
     const float* __restrict__ w1, float eps, float offset, float out_scale, float* __restrict__ x,
     __half* __restrict__ x16, const float* __restrict__ w2, __half* __restrict__ h16, int ldh,
     const int* __restrict__ row_map, float* __restrict__ rows_out) {
-  griddep_wait();
-  // Let the next kernel start its prologue; its CTAs wait for this grid.
-  griddep_launch();
   __shared__ float red[32];
   const int row = blockIdx.x;
-  if (row >= t) return;
   const int nthr = static_cast<int>(blockDim.x);
-  const float* ar = a + static_cast<size_t>(row) * lda;
-  float* xr = x + static_cast<size_t>(row) * d;
-  // Every load of the row up front (the slabs, the residual row and both
-  // norms' weights): only the two reductions order the work after them.
   float4 y[NV], xo[NV], wa[NV], wb[NV];
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  // The norms' weights are never written by a pass: load them while the
+  // previous kernel drains.
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     const int i = (threadIdx.x + j * nthr) * 4;
-    y[j] = xo[j] = wa[j] = wb[j] = zero;
+    wa[j] = wb[j] = zero;
+    if (i < d) {
+      wa[j] = __ldg(reinterpret_cast<const float4*>(w1 + i));
+      if (w2) wb[j] = __ldg(reinterpret_cast<const float4*>(w2 + i));
+    }
+  }
+  griddep_wait();
+  // Let the next kernel start its prologue; its CTAs wait for this grid.
+  griddep_launch();
+  if (row >= t) return;
+  const float* ar = a + static_cast<size_t>(row) * lda;
+  float* xr = x + static_cast<size_t>(row) * d;
+  // Every load of the row up front (the slabs and the residual row): only
+  // the two reductions order the work after them.
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = (threadIdx.x + j * nthr) * 4;
+    y[j] = xo[j] = zero;
     if (i < d) {
       y[j] = *reinterpret_cast<const float4*>(ar + i);
       xo[j] = *reinterpret_cast<const float4*>(xr + i);
-      wa[j] = *reinterpret_cast<const float4*>(w1 + i);
-      if (w2) wb[j] = *reinterpret_cast<const float4*>(w2 + i);
     }
   }
   for (int z = 1; z < splits; ++z) {

@@ -18,8 +18,11 @@
 //    is written before it is read. Calls whose work overlaps on the GPU (two
 //    host threads, or two streams, on one device) race on the array.
 //  * The first call on a device looks up the array's device address there
-//    (cudaGetSymbolAddress) and sets the kernels' shared-memory limits; make
-//    that first call before any stream capture on the device.
+//    (cudaGetSymbolAddress) and sets the kernels' shared-memory limits.
+//  * Every call reads the status word back and synchronises `stream` before
+//    it returns, so it must never be called while that stream (or, in the
+//    global capture mode, any stream) is being captured into a CUDA graph.
+//  * The caller's current device is restored before the call returns.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -66,6 +69,20 @@ __global__ void sum_slabs(const float* __restrict__ part, int splits, size_t sla
   }
 }
 
+// Makes `device` current for the scope of a call and puts the caller's
+// current device back on every exit path.
+struct DeviceScope {
+  int prev = -1;
+  explicit DeviceScope(int device) {
+    CUDA_TRY(cudaGetDevice(&prev));
+    if (prev != device) CUDA_TRY(cudaSetDevice(device));
+  }
+  ~DeviceScope() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
 }  // namespace
 }  // namespace omg
 
@@ -79,6 +96,7 @@ extern "C" int omg_gemm_splitk_noalloc(int device, const void* x_f16, int m, int
     if (m <= 0 || n <= 0 || k <= 0) fail("omg_gemm_splitk_noalloc: empty problem");
     if (device < 0 || device >= kMaxDevices) fail("omg_gemm_splitk_noalloc: device %d", device);
     if (ldo < n) fail("omg_gemm_splitk_noalloc: ldo %d < n %d", ldo, n);
+    if (lda < k) fail("omg_gemm_splitk_noalloc: lda %d < k %d", lda, k);
     const int kb = (k + 63) / 64;
     if (splits < 1 || splits > kb)
       fail("omg_gemm_splitk_noalloc: splits %d outside 1..%d for K %d", splits, kb, k);
@@ -88,7 +106,7 @@ extern "C" int omg_gemm_splitk_noalloc(int device, const void* x_f16, int m, int
       fail("omg_gemm_splitk_noalloc: %d x %d x %d f32 partials need %zu bytes; the static "
            "scratch holds %zu",
            splits, m, n, need, kNoAllocScratchBytes - kNoAllocHeader);
-    CUDA_TRY(cudaSetDevice(device));
+    DeviceScope on(device);
     uint8_t* scratch = scratch_on(device);
     auto* status = reinterpret_cast<uint32_t*>(scratch);
     auto* part = reinterpret_cast<float*>(scratch + kNoAllocHeader);

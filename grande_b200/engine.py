@@ -192,7 +192,10 @@ class _HostPool:
     def __init__(self, device: int):
         self.device = device
         self.free: dict = {}
-        self.lock = threading.Lock()
+        # Re-entrant: a _HostBlock finalised by the cyclic collector while
+        # this thread holds the lock (the collector may run on any
+        # allocation) calls put() on the same thread.
+        self.lock = threading.RLock()
 
     def array(self, shape) -> np.ndarray:
         size = max(int(np.prod(shape)) * 4, 1)

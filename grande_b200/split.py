@@ -65,6 +65,11 @@ def share_prefix(engine, prefix: Sequence[int], *, src: int = 0, group=None, dev
     if rank == src:
         if not engine.is_resident(prefix):
             engine.evaluate(prefix, [], want)
+        if dev.type == "cuda":
+            # The buffer comes from torch's caching allocator, which orders it
+            # only against torch's stream; the export writes it on the
+            # engine's own stream.
+            torch.cuda.current_stream(dev).synchronize()
         engine.export_state_device(prefix, buf.data_ptr(), nbytes)
     dist.broadcast(buf, src=dist.get_global_rank(group, src) if group is not None else src,
                    group=group)

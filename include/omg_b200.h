@@ -3,8 +3,8 @@
  *
  * This is the boundary a host-language shim binds: the reference's Rust
  * `omg_wgpu` crate would wrap it in an `extern "C"` block and keep its own
- * API (EngineBuilder / Engine / SavedState / WgpuBackend) on top; see
- * INTEGRATION.md. Every entry point takes plain pointers and sizes, returns
+ * API (EngineBuilder / Engine / SavedState / WgpuBackend) on top. Every
+ * entry point takes plain pointers and sizes, returns
  * 0 on success and -1 on error, and leaves a message for omg_last_error()
  * (thread-local, valid until the next call on the same thread). Outputs are
  * caller-allocated; nothing is written to them on error. Calls on one engine
@@ -398,8 +398,10 @@ void omg_laya_destroy(omg_laya_engine* e);
  * splits * m * round_up(n, 4) * 4 bytes must fit in 32 MiB - 256; larger
  * problems are rejected with an error. Calls that overlap on the GPU share
  * that array and race. The first call on a device looks the array up and
- * sets kernel attributes: make it before any stream capture there. Returns
- * after the work has finished (the status word is checked). */
+ * sets kernel attributes. Every call synchronises `stream` and checks the
+ * status word before it returns, so it must never be called while a stream
+ * capture is in progress. lda >= k and ldo >= n are required. The caller's
+ * current device is left as it was. */
 int omg_gemm_splitk_noalloc(int device, const void* x_f16, int m, int k, int lda,
                             const void* w_f16, int n, int splits, float* out, int ldo,
                             void* stream);

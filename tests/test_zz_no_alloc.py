@@ -5,8 +5,8 @@ allocate (their own memory pool, or code where a cudaMalloc would synchronise
 the device); its split-K partials live in a static device array instead.
 The test gives it device buffers (allocated here, by the test, with torch),
 calls it twice in a row through the C ABI with different inputs, and checks
-each result against the allocating entry point (omg_debug_gemm) at the GEMM
-tests' tolerance. This file is collected last so that a failure here cannot
+each result against an f64 product of the same f16 operands and against the
+allocating entry point (omg_debug_gemm), at the GEMM tests' tolerance. This file is collected last so that a failure here cannot
 stop the other GPU tests under `-x`.
 """
 import ctypes as C
@@ -47,6 +47,9 @@ def test_noalloc_gemm_matches_allocating_entry_point(device):
                                                 C.c_void_p(w_d.data_ptr()), n, splits,
                                                 C.c_void_p(out_d.data_ptr()), n, None))
         got = out_d.cpu().numpy()
+        f64 = x16.astype(np.float64) @ w16.astype(np.float64).T
+        err64 = float(np.max(np.abs(got - f64) / np.maximum(np.abs(f64), 1.0)))
+        assert err64 < TOL, (call, err64)
         exp = reference_gemm(device, x16, w16, splits)
         err = float(np.max(np.abs(got - exp) / np.maximum(np.abs(exp), 1.0)))
         assert err < TOL, (call, err)
@@ -60,3 +63,13 @@ def test_noalloc_rejects_oversized_problems(device):
                                          1024, None)
     assert rc == -1
     assert "static scratch holds" in L.lib().omg_last_error().decode()
+
+
+def test_noalloc_rejects_short_row_stride(device):
+    # An lda below k would make the operand rows overlap; it is refused before
+    # any device pointer is touched.
+    bogus = C.c_void_p(16)
+    rc = L.lib().omg_gemm_splitk_noalloc(device, bogus, 64, 256, 128, bogus, 64, 1, bogus, 64,
+                                         None)
+    assert rc == -1
+    assert "lda 128 < k 256" in L.lib().omg_last_error().decode()

@@ -19,12 +19,19 @@ collective on the data path). Rank 0 prints one JSON line.
   the engine's stream around the K calls.
 * ``roofline``: the largest kernel -- the fused FFN launch (gate+up with the
   GeGLU epilogue, then down) on the decoder, the erf-GeGLU Wi GEMM on the
-  encoder -- from per-launch CUDA events, against MEASURED_PEAKS.json, with
-  ``traffic`` from the committed ncu summary under profiles/.
+  encoder -- from per-launch CUDA events, against MEASURED_PEAKS.json's burst
+  tensor peak (the kernels are timed one launch at a time inside a pass of a
+  few ms), with ``traffic`` from the committed ncu summary under profiles/.
+* ``pass_roofline``: the whole pass's algorithmic FLOPs and bytes
+  (``pass_work``) against the measured ms per pass; ``kernels``: the same per
+  kernel class (projections and attention against the tensor peak, the
+  lm_head and the residual norms against HBM).
 * ``kv_broadcast`` (resident config, N > 1): one state's K/V handed from
   rank 0 to every rank with one NCCL broadcast (grande_b200/split.py).
 * ``cpu_baseline`` / ``--impl reference``: the reference's CPU forward
-  (tests/reference.rs), restated in oracle/, on the host cores.
+  (tests/reference.rs), restated in oracle/, on all host cores: whole
+  requests (every layer) on the same synthetic model, which oracle/ builds
+  itself (the product library is not loaded on that arm).
 
 ``--config mmbert-q8`` measures BASELINE.json's encoder configuration instead
 (not the headline metric): 256 sequences of 128 tokens through the Laya /
@@ -62,7 +69,6 @@ def args_():
     ap.add_argument("--config", default="e2b-q4")
     ap.add_argument("--profile-iters", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-sample-layers", type=int, default=2)
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layer count (small cases for ncu captures only)")
     return ap.parse_args()
@@ -189,44 +195,120 @@ def gpu_index(local: int) -> int:
 
 # ---- CPU side: the reference's CPU forward (oracle/) -------------------------------
 
-def cpu_sample(shape, layers: int, seed: int = 0) -> dict:
-    """One request of `shape` through the oracle with `layers` of the model's
-    layers (same shapes, same synthetic weights), timed on the host cores;
-    extrapolated linearly to the full depth (every layer has the same cost
-    at this length up to the window) plus the 12-row lm_head."""
-    import dataclasses
-
-    from grande_b200 import synth
+def oracle_model(shape, seed: int = 0):
+    """The synthetic model of `shape` as the oracle takes it: the same draws,
+    codes and scales as the GPU arm's model, generated, quantized and
+    dequantized by oracle/ alone (the product library is not loaded)."""
     from oracle import oracle as O
-    small = dataclasses.replace(shape, layers=layers)
-    cfgd = small.config()
-    sliding = [t == "sliding_attention" for t in cfgd["layer_types"]]
-    qs = 256 ** -0.5 if shape.gemma3_numerics else 1.0
-    ocfg = O.OracleConfig(vocab=shape.vocab, d=shape.d, layers=layers, heads=shape.heads,
-                          kv_heads=shape.kv_heads, head_dim=[256] * layers, ff=[shape.ff] * layers,
-                          sliding=sliding, kv_source=list(range(layers)), rope_dims=[256] * layers,
-                          window=512, query_scale=qs, norm_offset=0.0,
-                          v_norm=not shape.gemma3_numerics,
+    sliding = [t == "sliding_attention" for t in shape.config()["layer_types"]]
+    L = shape.layers
+    ocfg = O.OracleConfig(vocab=shape.vocab, d=shape.d, layers=L, heads=shape.heads,
+                          kv_heads=shape.kv_heads, head_dim=[256] * L, ff=[shape.ff] * L,
+                          sliding=sliding, kv_source=list(range(L)), rope_dims=[256] * L,
+                          window=512, query_scale=256 ** -0.5 if shape.gemma3_numerics else 1.0,
+                          norm_offset=0.0, v_norm=not shape.gemma3_numerics,
                           softcap=0.0 if shape.gemma3_numerics else 30.0)
-    tensors = []
-    for name, dims in ocfg.tensors():
-        qt = synth.tensor(seed, name, dims, shape.dtype)
-        tensors.append(O.dequantize(int(qt.dtype), qt.data, qt.scales, qt.numel()))
-    g = synth.request(shape, seed)
-    ids, pos, seq = O.pack(g.prefix, [(b.tokens, b.want) for b in g.branches])
-    threads = os.cpu_count() or 1
+    return ocfg, O.synth_tensors(ocfg.tensors(), seed, int(shape.dtype))
+
+
+def oracle_request(ocfg, tensors, req, threads: int) -> float:
+    """One request through the oracle (the reference's CPU forward,
+    tests/reference.rs:175-349, with the lm_head and softcap at the answer
+    rows, reference.rs:581-590): seconds of wall clock."""
+    from oracle import oracle as O
+    ids, pos, seq = O.pack(req.prefix, [(b.tokens, b.want) for b in req.branches])
+    rows, at = [], len(req.prefix)
+    for b in req.branches:
+        rows += [at + w for w in b.want]
+        at += len(b.tokens)
     t0 = time.perf_counter()
     hid = O.forward(ocfg, tensors, ids, pos, seq, O.ORACLE_EXACT, threads)
-    t_layers = time.perf_counter() - t0
-    rows = [len(g.prefix) + sum(len(x.tokens) for x in g.branches[:i]) + g.branches[i].want[0]
-            for i in range(len(g.branches))]
-    emb = tensors[0]
-    t1 = time.perf_counter()
     for r in rows:
-        O.logits(hid[r], emb, shape.vocab, shape.d, ocfg.softcap)
-    t_logits = time.perf_counter() - t1
-    per_request = t_layers * shape.layers / layers + t_logits
-    return {"per_request_s": per_request, "threads": threads, "sampled_s": t_layers + t_logits}
+        O.logits(hid[r], tensors[0], ocfg.vocab, ocfg.d, ocfg.softcap)
+    return time.perf_counter() - t0
+
+
+def cpu_sample(shape, seed: int = 0) -> dict:
+    """The GPU arm's CPU baseline: one whole request of `shape` (every layer,
+    the lm_head at its answer rows) through the oracle on all host cores."""
+    from grande_b200 import synth
+    threads = os.cpu_count() or 1
+    ocfg, tensors = oracle_model(shape, seed)
+    s = oracle_request(ocfg, tensors, synth.request(shape, seed=1000), threads)
+    return {"per_request_s": s, "threads": threads, "sampled_s": s}
+
+
+# ---- algorithmic work of one pass ------------------------------------------------
+
+def visible_pairs(prefix: int, branches: list, resident: bool, window: int) -> int:
+    """(query, key) pairs one pass's attention visits on a layer: the prefix
+    rows causally (when the prefix is decoded in this pass), each branch's
+    rows over the prefix and the branch's own earlier rows, keys within
+    `window` positions (0 = no window) -- the visibility rule of
+    attention.wgsl:70-76."""
+    import numpy as np
+    w = window or (1 << 30)
+    n = 0
+    if not resident:
+        i = np.arange(prefix)
+        n += int(np.minimum(i + 1, w).sum())
+    for bl in branches:
+        j = np.arange(bl)
+        qp = prefix + j
+        lo = np.maximum(qp - w + 1, 0)
+        n += int(np.maximum(prefix - lo, 0).sum() + np.minimum(j + 1, w).sum())
+    return n
+
+
+def pass_work(shape, req, resident: bool) -> dict:
+    """FLOPs and bytes one pass needs at the least, per kernel class: 2
+    FLOP per multiply-add of every linear over the pass's rows, 4 * head_dim
+    per visible (query, key) pair and head for attention (QK^T and P.V),
+    2 * rows * vocab * d for the lm_head; bytes = the packed weights read once
+    (Q4_0 18 B / Q8_0 34 B per 32 weights), the packed embedding table once
+    (the lm_head), and each layer's f16 K/V rows read once."""
+    bpw = 18 / 32 if shape.dtype.name == "Q4" else 34 / 32
+    d, ff, L, hd = shape.d, shape.ff, shape.layers, 256
+    qkv_w = (shape.heads + 2 * shape.kv_heads) * hd
+    t = (0 if resident else len(req.prefix)) + sum(len(b.tokens) for b in req.branches)
+    rows = sum(len(b.want) for b in req.branches)
+    blens = [len(b.tokens) for b in req.branches]
+    P = len(req.prefix)
+    kinds = ["sliding_attention" if (l + 1) % shape.global_every else "full_attention"
+             for l in range(L)]
+    pairs = {w: visible_pairs(P, blens, resident, w) for w in (0, 512)}
+    attn = sum(4 * hd * shape.heads * pairs[512 if k == "sliding_attention" else 0]
+               for k in kinds)
+    kv_rows = sum(min(P, 512) + sum(blens) if k == "sliding_attention" else P + sum(blens)
+                  for k in kinds)
+    f = {"gemm_qkv": 2.0 * t * d * qkv_w * L,
+         "gemm_o": 2.0 * t * shape.heads * hd * d * L,
+         "gemm_mlp": 2.0 * t * d * 3 * ff * L,
+         "attention": float(attn),
+         "logits": 2.0 * rows * shape.vocab * d}
+    w_bytes = (d * qkv_w + shape.heads * hd * d + 3 * ff * d) * L * bpw
+    b = {"weights": w_bytes, "embed_table": shape.vocab * d * bpw,
+         "kv": kv_rows * 2 * shape.kv_heads * hd * 2.0}
+    return {"tokens": t, "rows": rows, "flop": f, "bytes": b,
+            "flop_total": sum(f.values()), "bytes_total": sum(b.values()),
+            "visible_pairs": pairs}
+
+
+def workload_config(shape, resident: bool, n: int) -> dict:
+    """The `config` of both arms' JSON lines for a decoder shape."""
+    return {
+        "workload": f"{shape.name}: {'resident ' if resident else ''}{shape.state}-token "
+                    f"state + {shape.branches} branches x {shape.branch_len} tokens, one "
+                    f"block-causal pass, logits at {shape.branches} answer rows; "
+                    f"{shape.questions} questions per request, 1 request per GPU per step",
+        "model": f"{shape.name} shape, random init ({shape.layers} layers, d {shape.d}, "
+                 f"{shape.heads}q/{shape.kv_heads}kv heads x 256, ff {shape.ff}, "
+                 f"vocab {shape.vocab}, {shape.dtype.name}_0)",
+        "tokens_per_pass": (0 if resident else shape.state) + shape.branches * shape.branch_len,
+        "parallelism": f"replicas x{n} (independent requests)",
+        "l2": "inputs larger than L2: the f16 weights (3.6 GB at E2B) stream from HBM every "
+              "pass",
+    }
 
 
 # ---- the B200 arm -----------------------------------------------------------------------
@@ -306,7 +388,47 @@ def run_b200(a, dist: Dist):
     prof = eng.profile_forward([req], Want.LOGITS, a.profile_iters, resident=resident)
     kv_bcast = bench_kv_broadcast(eng, synth.request(shape, seed=1000).prefix, dist) \
         if resident and dist.world > 1 else None
-    t_pass = len(req.prefix) * (0 if resident else 1) + sum(len(b.tokens) for b in req.branches)
+    work = pass_work(shape, req, resident)
+    t_pass = work["tokens"]
+    pk, pk_kind = peaks()
+    # Kernels timed one launch at a time inside a pass of a few ms (well under
+    # a second of load): the burst tensor peak is their ceiling.
+    peak_tc = pk.get("bf16_tflops")
+    peak_hbm = pk.get("hbm_gbs")
+    n_pass = a.profile_iters
+    kernels = {}
+    for name, (launches_k, ms_k) in prof.items():
+        e = {"launches_per_pass": launches_k // n_pass, "ms_per_pass": round(ms_k / n_pass, 4)}
+        kernels[name] = e
+    # The FLOP-bound kernels against the tensor peak, the lm_head against HBM.
+    for name, key in (("gemm_qkv", "gemm_qkv"), ("gemm_o", "gemm_o"), ("gemm_mlp", "gemm_mlp")):
+        if name in kernels:
+            ms_k = kernels[name]["ms_per_pass"]
+            ach = work["flop"][key] / (ms_k * 1e-3) / 1e12
+            kernels[name].update(flop_per_pass=work["flop"][key], achieved_tflops=round(ach, 1),
+                                 frac=round(ach / peak_tc, 4), bound="tensor")
+    if "attention" in kernels:
+        ms_k = kernels["attention"]["ms_per_pass"] + kernels.get(
+            "attention_merge", {}).get("ms_per_pass", 0.0)
+        ach = work["flop"]["attention"] / (ms_k * 1e-3) / 1e12
+        kernels["attention"].update(flop_per_pass=work["flop"]["attention"],
+                                    achieved_tflops_with_merge=round(ach, 1),
+                                    frac=round(ach / peak_tc, 4), bound="tensor")
+    if "logits" in kernels:
+        ms_k = kernels["logits"]["ms_per_pass"]
+        lb = work["bytes"]["embed_table"] + work["rows"] * shape.d * 4 + \
+            work["rows"] * shape.vocab * 4
+        ach = lb / (ms_k * 1e-3) / 1e9
+        kernels["logits"].update(bytes_per_pass=lb, achieved_gbs=round(ach, 1),
+                                 frac=round(ach / peak_hbm, 4), bound="hbm")
+    if "residual_norm" in kernels:
+        ms_k = kernels["residual_norm"]["ms_per_pass"]
+        # Per launch: the f32 slabs (2 for the o and down projections), the
+        # residual stream read and written, the next norm's f16 rows.
+        rb = kernels["residual_norm"]["launches_per_pass"] * t_pass * shape.d * (2 * 4 + 8 + 2)
+        ach = rb / (ms_k * 1e-3) / 1e9
+        kernels["residual_norm"].update(bytes_per_pass=rb, achieved_gbs=round(ach, 1),
+                                        frac=round(ach / peak_hbm, 4), bound="hbm")
     # The dominant kernel: the FFN (gate+up with the fused GeGLU, and down) as
     # one launch where the engine fuses them, else the gate+up GEMM alone.
     if "gemm_mlp" in prof:
@@ -320,41 +442,46 @@ def run_b200(a, dist: Dist):
         top_flops = 2.0 * t_pass * shape.d * 2 * shape.ff
         traffic = read_traffic("gemm_gate_up", a.config)
     top_avg = top_ms / top_launches
-    pk, pk_kind = peaks()
-    peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
     achieved = top_flops / (top_avg * 1e-3) / 1e12
     n = dist.world
     value = n * q_per_step * a.steps / (ms_max * 1e-3)
     e2e_value = n * q_per_step * a.steps / (e2e_max * 1e-3)
+    ms_step = ms_max / a.steps
+    rl_tc = work["flop_total"] / (peak_tc * 1e12) * 1e3
+    rl_hbm = work["bytes_total"] / (peak_hbm * 1e9) * 1e3
     bytes_in = t_pass * (4 + 16 + 4) + 8 * (t_pass // 4 + 1)
     out = {
         "metric": metric_of(shape, resident), "value": round(value, 2), "unit": UNIT, "n_gpus": n,
-        "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_max / a.steps, 4),
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic: seeded N(0,0.02) weights quantized to "
                 f"{shape.dtype.name}_0, uniform token ids",
-        "config": {
-            "workload": f"{shape.name}: {'resident ' if resident else ''}{shape.state}-token "
-                        f"state + {shape.branches} branches x {shape.branch_len} tokens, one "
-                        f"block-causal pass, logits at {shape.branches} answer rows; "
-                        f"{q_per_step} questions per request, 1 request per GPU per step",
-            "model": f"{shape.name} shape, random init ({shape.layers} layers, d {shape.d}, "
-                     f"{shape.heads}q/{shape.kv_heads}kv heads x 256, ff {shape.ff}, "
-                     f"vocab {shape.vocab})",
-            "tokens_per_pass": t_pass, "parallelism": f"replicas x{n} (independent requests)",
-            "l2": "inputs larger than L2: 3.6 GB of f16 weights stream from HBM every pass",
-        },
+        "config": workload_config(shape, resident, n),
         "p50_latency_ms": round(statistics.median(lat), 3) if lat else None,
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                 "h2d_bytes_per_step": bytes_in, "d2h_bytes_per_step": shape.branches * width * 4,
                 "ms_per_step": round(e2e_max / a.steps, 4)},
         "gpu_launches": launches * a.steps,
         "roofline": {"kernel": top_kernel, "bound": "tensor",
-                     "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                     "frac": round(achieved / peak, 4), "peak_kind": f"{pk_kind} sustained",
+                     "achieved": round(achieved, 1), "peak": peak_tc, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak_tc, 4), "peak_kind": f"{pk_kind} burst",
                      "traffic": traffic, "avg_launch_ms": round(top_avg, 5),
                      "flop_per_launch": top_flops},
-        "kernels_ms_per_pass": {k: round(v[1] / a.profile_iters, 4) for k, v in prof.items()},
+        "pass_roofline": {
+            "flop": work["flop_total"], "bytes": work["bytes_total"],
+            "roofline_ms": round(max(rl_tc, rl_hbm), 4),
+            "bound": "tensor" if rl_tc >= rl_hbm else "hbm",
+            "tensor_ms": round(rl_tc, 4), "hbm_ms": round(rl_hbm, 4),
+            "measured_ms": round(ms_step, 4), "frac": round(max(rl_tc, rl_hbm) / ms_step, 4),
+            "hbm_frac": round(rl_hbm / ms_step, 4),
+            "peaks": {"tflops": peak_tc, "gbs": peak_hbm, "kind": f"{pk_kind} burst"},
+            "what": ("the whole pass: roofline time max(FLOP / tensor peak, bytes / HBM peak) "
+                     "over the measured ms per pass; hbm_frac = bytes / HBM peak over it"),
+        },
+        "kernels": kernels,
+        "kernels_note": "ms_per_pass from CUDA events between launches (serialised: the "
+                        "events break the programmatic-dependent-launch overlap, so they sum "
+                        "above ms_per_step); frac against the burst peaks",
         "clocks": clk,
         "build_s": round(t_build, 1),
     }
@@ -363,47 +490,65 @@ def run_b200(a, dist: Dist):
     if kv_bcast:
         out["kv_broadcast"] = kv_bcast
     if dist.world == 1 and not a.no_cpu_baseline:
-        cb = cpu_sample(shape, a.cpu_sample_layers)
+        cb = cpu_sample(shape)
         out["cpu_baseline"] = {
             "value": round(q_per_step / cb["per_request_s"], 4), "unit": UNIT,
             "cores": cb["threads"], "kind": "port",
-            "sample": f"one {shape.name} request through oracle/ (the reference's CPU forward, "
-                      f"tests/reference.rs:141-349, restated in C with OpenMP) with "
-                      f"{a.cpu_sample_layers} of {shape.layers} layers, extrapolated per layer, "
-                      f"+ the {shape.branches}-row lm_head; {cb['sampled_s']:.1f} s sampled",
+            "sample": f"one whole {shape.name} request ({shape.layers} layers, the "
+                      f"{shape.branches}-row lm_head) through oracle/ (the reference's CPU "
+                      f"forward, tests/reference.rs:175-349, restated in C with OpenMP), "
+                      f"{cb['sampled_s']:.1f} s"
+                      + ("; the oracle keeps no K/V between calls, so the resident prefix is "
+                         "recomputed" if resident else ""),
         }
     if dist.rank == 0:
         print(json.dumps(out), flush=True)
     eng.close()
 
 
-def laya_cpu_sample(shape, seqs: int, seed: int = 0) -> dict:
-    """`seqs` sequences of the encoder shape through oracle/ (the restated
-    GPU plan of laya.rs:1263-1345) with one encoder layer, then one encoder
-    layer + one head layer; per-layer times extrapolated to the full depth
-    and to the whole batch."""
-    import dataclasses
-
-    from grande_b200 import synth
+def laya_oracle_model(shape, seed: int = 0):
+    """The synthetic encoder of `shape` as the oracle takes it (the GPU arm's
+    model, generated by oracle/ alone)."""
     from oracle import oracle as O
+    ocfg = O.OracleLayaConfig(vocab=shape.vocab, d=shape.d, layers=shape.layers,
+                              heads=shape.heads, ff=shape.ff, sliding=[0] * shape.layers,
+                              window=64, head_layers=shape.head_layers,
+                              act_out=shape.act_costs + 1)
+    return ocfg, O.synth_tensors(ocfg.tensors(), seed, int(shape.dtype), laya=True)
+
+
+def laya_oracle_batch(ocfg, tensors, seqs, threads: int) -> float:
+    """`seqs` sequences through oracle/ (the GPU plan of laya.rs:1263-1345
+    restated, every encoder and head layer): seconds of wall clock."""
+    from oracle import oracle as O
+    ids, pos, seq, qt = O.laya_pack([(r.ids, r.qtype) for r in seqs])
+    t0 = time.perf_counter()
+    O.laya_hidden(ocfg, tensors, ids, pos, seq, qt, O.ORACLE_EXACT, threads)
+    return time.perf_counter() - t0
+
+
+def laya_cpu_sample(shape, seqs: int, seed: int = 0) -> dict:
+    """`seqs` of the batch's sequences at full depth through the oracle on all
+    host cores; the sequences are independent, so sequences/s over the sample
+    is the batch's rate."""
+    from grande_b200 import synth
     threads = os.cpu_count() or 1
-    reqs = synth.laya_request(shape, seed)[:seqs]
-    ids, pos, seq, qt = O.laya_pack([(r.ids, r.qtype) for r in reqs])
-    times = []
-    for head in (0, 1):
-        ocfg = O.OracleLayaConfig(vocab=shape.vocab, d=shape.d, layers=1, heads=shape.heads,
-                                  ff=shape.ff, sliding=[0], window=64, head_layers=head,
-                                  act_out=shape.act_costs + 1)
-        tensors = []
-        for name, dims in ocfg.tensors():
-            qt_ = synth.laya_tensor(seed, name, dims, shape.dtype)
-            tensors.append(O.dequantize(int(qt_.dtype), qt_.data, qt_.scales, qt_.numel()))
-        t0 = time.perf_counter()
-        O.laya_hidden(ocfg, tensors, ids, pos, seq, qt, O.ORACLE_EXACT, threads)
-        times.append(time.perf_counter() - t0)
-    t_enc, t_head = times[0], max(times[1] - times[0], 0.0)
-    per_batch = (t_enc * shape.layers + t_head * shape.head_layers) * shape.seqs / seqs
-    return {"per_batch_s": per_batch, "threads": threads, "sampled_s": sum(times)}
+    ocfg, tensors = laya_oracle_model(shape, seed)
+    s = laya_oracle_batch(ocfg, tensors, synth.laya_request(shape, 1000)[:seqs], threads)
+    return {"seqs_per_s": seqs / s, "threads": threads, "sampled_s": s}
+
+
+def laya_workload_config(shape, n: int) -> dict:
+    return {
+        "workload": f"{shape.name}: {shape.seqs} sequences x {shape.seq_len} tokens, full "
+                    f"bidirectional attention, [CLS] + {shape.markers} [MASK] row(s) per "
+                    f"sequence read back; 1 question per sequence",
+        "model": f"{shape.name} shape, random init ({shape.layers} layers, d {shape.d}, "
+                 f"{shape.heads} heads x 64, GeGLU ff {shape.ff}, vocab {shape.vocab}, "
+                 f"{shape.head_layers} decision-head layers)",
+        "tokens_per_pass": shape.tokens(), "parallelism": f"replicas x{n} (independent batches)",
+        "l2": "activations larger than L2 (32768 x 768 f32 residual stream per pass)",
+    }
 
 
 def run_laya(a, dist: Dist):
@@ -446,7 +591,7 @@ def run_laya(a, dist: Dist):
     wi_avg = wi_ms / wi_launches
     flops_wi = 2.0 * t * shape.d * 2 * shape.ff
     pk, pk_kind = peaks()
-    peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+    peak = pk.get("bf16_tflops")
     achieved = flops_wi / (wi_avg * 1e-3) / 1e12
     n = dist.world
     value = n * shape.seqs * a.steps / (ms_max * 1e-3)
@@ -457,16 +602,7 @@ def run_laya(a, dist: Dist):
         "warmup": a.warmup, "ms_per_step": round(ms_max / a.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic: seeded N(0,0.02) weights quantized to Q8_0, uniform token ids",
-        "config": {
-            "workload": f"{shape.name}: {shape.seqs} sequences x {shape.seq_len} tokens, full "
-                        f"bidirectional attention, [CLS] + {shape.markers} [MASK] row(s) per "
-                        f"sequence read back; 1 question per sequence",
-            "model": f"{shape.name} shape, random init ({shape.layers} layers, d {shape.d}, "
-                     f"{shape.heads} heads x 64, GeGLU ff {shape.ff}, vocab {shape.vocab}, "
-                     f"{shape.head_layers} decision-head layers)",
-            "tokens_per_pass": t, "parallelism": f"replicas x{n} (independent batches)",
-            "l2": "activations larger than L2 (32768 x 768 f32 residual stream per pass)",
-        },
+        "config": laya_workload_config(shape, n),
         "p50_latency_ms": round(statistics.median(lat), 3) if lat else None,
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                 "h2d_bytes_per_step": t * 4 * 4 + 8 * shape.markers * shape.seqs,
@@ -475,22 +611,22 @@ def run_laya(a, dist: Dist):
         "gpu_launches": launches * a.steps,
         "roofline": {"kernel": "gemm_wi (tcgen05, fused erf GeGLU)", "bound": "tensor",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                     "frac": round(achieved / peak, 4), "peak_kind": f"{pk_kind} sustained",
+                     "frac": round(achieved / peak, 4), "peak_kind": f"{pk_kind} burst",
                      "traffic": read_traffic("gemm_wi", a.config), "avg_launch_ms": round(wi_avg, 5),
                      "flop_per_launch": flops_wi},
         "kernels_ms_per_pass": {k: round(v[1] / a.profile_iters, 4) for k, v in prof.items()},
+        "kernels_note": "CUDA events between launches (serialised: they sum above ms_per_step)",
         "clocks": clk,
         "build_s": round(t_build, 1),
     }
     if dist.world == 1 and not a.no_cpu_baseline:
-        cb = laya_cpu_sample(shape, 8)
+        cb = laya_cpu_sample(shape, 32)
         out["cpu_baseline"] = {
-            "value": round(shape.seqs / cb["per_batch_s"], 4), "unit": UNIT,
+            "value": round(cb["seqs_per_s"], 4), "unit": UNIT,
             "cores": cb["threads"], "kind": "port",
-            "sample": f"8 of {shape.seqs} sequences through oracle/ (laya.rs:1263-1345 restated "
-                      f"in C with OpenMP), one encoder layer and one head layer, extrapolated "
-                      f"to {shape.layers} + {shape.head_layers} layers and the whole batch; "
-                      f"{cb['sampled_s']:.1f} s sampled",
+            "sample": f"32 of the batch's {shape.seqs} sequences through oracle/ "
+                      f"(laya.rs:1263-1345 restated in C with OpenMP), all {shape.layers} "
+                      f"encoder and {shape.head_layers} head layers; {cb['sampled_s']:.1f} s",
         }
     if dist.rank == 0:
         print(json.dumps(out), flush=True)
@@ -551,38 +687,49 @@ def read_traffic(kernel: str, config: str):
 
 def run_reference(a, dist: Dist):
     """The reference's CPU implementation of the path (its CPU forward,
-    restated in oracle/), on this host's cores, on the same workload."""
+    tests/reference.rs:175-349, restated in oracle/; the reference's own
+    llama.cpp CPU backend cannot be built here), on this host's cores, on the
+    GPU arm's workload: every step one whole request (all layers, the lm_head
+    at the answer rows) on the same synthetic model, built by oracle/ alone."""
     if dist.rank != 0:
         return
     from grande_b200 import synth
     if a.config in synth.LAYA_CONFIGS:
         return run_reference_laya(a)
     shape = synth.CONFIGS[a.config]
-    # Each step is a bounded sample (a.cpu_sample_layers layers of one request,
-    # extrapolated to the full depth) so K steps end within minutes.
-    per = []
+    resident = a.config.endswith("resident")
     threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    ocfg, tensors = oracle_model(shape)
+    setup_s = time.perf_counter() - t0
+    req = synth.request(shape, seed=1000)
+    per = []
     for i in range(a.warmup + a.steps):
-        cb = cpu_sample(shape, a.cpu_sample_layers, seed=i)
+        s = oracle_request(ocfg, tensors, req, threads)
         if i >= a.warmup:
-            per.append(cb["per_request_s"])
+            per.append(s)
     total = sum(per)
     value = shape.questions * len(per) / total
+    sample = (f"per step: one whole {shape.name} request ({shape.layers} layers + the "
+              f"{shape.branches}-row lm_head) through oracle/ (tests/reference.rs:175-349 "
+              f"restated in C, OpenMP over {threads} threads)"
+              + ("; the oracle keeps no K/V between calls, so the resident prefix is "
+                 "recomputed every step" if resident else ""))
     out = {
-        "impl": "reference", "metric": metric_of(shape, a.config.endswith("resident")),
+        "impl": "reference", "metric": metric_of(shape, resident),
         "value": round(value, 4), "unit": UNIT,
         "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": round(total / len(per) * 1e3, 2), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{shape.name}: {shape.state}-token state + {shape.branches} "
-                               f"branches x {shape.branch_len} tokens, logits at "
-                               f"{shape.branches} rows"},
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded N(0,0.02) weights quantized to "
+                f"{shape.dtype.name}_0, uniform token ids",
+        "config": workload_config(shape, resident, a.gpus),
+        "p50_latency_ms": round(statistics.median(per) * 1e3, 2),
         "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"per step: {a.cpu_sample_layers} of {shape.layers} layers "
-                                   "of one request through oracle/ (tests/reference.rs:141-349 "
-                                   "restated in C, OpenMP), extrapolated per layer, + lm_head"},
+                         "sample": sample},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
+        "setup_s": round(setup_s, 1),
     }
     print(json.dumps(out), flush=True)
 
@@ -590,27 +737,35 @@ def run_reference(a, dist: Dist):
 def run_reference_laya(a):
     from grande_b200 import synth
     shape = synth.LAYA_CONFIGS[a.config]
-    per = []
     threads = os.cpu_count() or 1
+    sample_seqs = 32
+    t0 = time.perf_counter()
+    ocfg, tensors = laya_oracle_model(shape)
+    setup_s = time.perf_counter() - t0
+    seqs = synth.laya_request(shape, 1000)[:sample_seqs]
+    per = []
     for i in range(a.warmup + a.steps):
-        cb = laya_cpu_sample(shape, 8, seed=i)
+        s = laya_oracle_batch(ocfg, tensors, seqs, threads)
         if i >= a.warmup:
-            per.append(cb["per_batch_s"])
+            per.append(s)
     total = sum(per)
-    value = shape.seqs * len(per) / total
+    value = sample_seqs * len(per) / total
     out = {
         "impl": "reference",
         "metric": "questions/s/GPU mmBERT-shape Q8_0 encoder (256 seqs x 128 tokens)",
         "value": round(value, 4), "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": round(total / len(per) * 1e3, 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic",
-        "config": {"workload": f"{shape.name}: {shape.seqs} sequences x {shape.seq_len} tokens"},
+        "data": "synthetic: seeded N(0,0.02) weights quantized to Q8_0, uniform token ids",
+        "config": laya_workload_config(shape, a.gpus),
         "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": "per step: 8 sequences, one encoder + one head layer through "
-                                   "oracle/, extrapolated to the full depth and batch"},
+                         "sample": f"per step: {sample_seqs} of the batch's {shape.seqs} "
+                                   f"sequences (independent, so sequences/s is the batch's "
+                                   f"rate) through oracle/, all {shape.layers} encoder and "
+                                   f"{shape.head_layers} head layers"},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
+        "setup_s": round(setup_s, 1),
     }
     print(json.dumps(out), flush=True)
 

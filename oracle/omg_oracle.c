@@ -99,6 +99,36 @@ void oracle_rng_values(uint64_t* state, float* out, size_t n, float scale) {
   *state = s;
 }
 
+/* ---- synthetic weights ------------------------------------------------------
+ * The benchmark's and the large-shape tests' random models: a normal draw per
+ * element from xorshift64 (seeded by FNV-1a(name) ^ seed; 53-bit uniforms in
+ * (0, 1)) through the Box-Muller transform in double precision, rounded to
+ * f32. The product library generates its models with the same definition;
+ * this copy lets CPU-only runs build the same weights without loading it. */
+void oracle_synth_normal(uint64_t seed, const char* name, float mean, float stddev, float* out,
+                         size_t n) {
+  uint64_t s = 0xcbf29ce484222325ull;
+  for (const char* p = name ? name : ""; *p; ++p) {
+    s ^= (uint8_t)*p;
+    s *= 0x00000100000001b3ull;
+  }
+  s ^= seed;
+  if (s == 0) s = 0x9e3779b97f4a7c15ull;
+  const double two_pi = 6.283185307179586;
+  for (size_t i = 0; i < n; i += 2) {
+    double u[2];
+    for (int j = 0; j < 2; ++j) {
+      s ^= s << 13;
+      s ^= s >> 7;
+      s ^= s << 17;
+      u[j] = ((double)(s >> 11) + 0.5) * (1.0 / 9007199254740992.0);
+    }
+    const double r = sqrt(-2.0 * log(u[0]));
+    out[i] = (float)(mean + stddev * r * cos(two_pi * u[1]));
+    if (i + 1 < n) out[i + 1] = (float)(mean + stddev * r * sin(two_pi * u[1]));
+  }
+}
+
 /* ---- quantizers (model.rs:409-466) --------------------------------------- */
 
 static void put_f16(uint8_t* p, float v) {
@@ -206,7 +236,50 @@ static void rmsnorm(const float* x, int n, const float* w, float eps, float offs
   for (int i = 0; i < n; ++i) out[i] = x[i] * inv * (w ? offset + w[i] : 1.0f);
 }
 
-/* reference.rs:151-157 for every row of X [t, k]: Y [t, n] = X W^T. */
+/* dot8 of four rows of X against two rows of W at once: eight independent
+ * 8-lane partial sums, each lane accumulating exactly as dot8 does (mul, then
+ * add, in k order) and reduced by the same tree, so every output has dot8's
+ * bits; the blocking only keeps more independent sums in flight. */
+typedef float v8f __attribute__((vector_size(32)));
+static inline v8f ld8(const float* p) {
+  v8f v;
+  memcpy(&v, p, sizeof v);
+  return v;
+}
+static inline float tree8(v8f a) {
+  return ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+}
+/* Partial dot8 sums of a 4 x 2 register tile over k in [k0, k1) (k1 - k0 a
+ * multiple of 8), carried in `acc` between calls. */
+static inline void dot8_4x2_part(const float* x, size_t ldx, const float* w, size_t ldw, int k0,
+                                 int k1, v8f acc[4][2]) {
+  v8f a00 = acc[0][0], a01 = acc[0][1], a10 = acc[1][0], a11 = acc[1][1];
+  v8f a20 = acc[2][0], a21 = acc[2][1], a30 = acc[3][0], a31 = acc[3][1];
+  for (int i = k0; i < k1; i += 8) {
+    const v8f b0 = ld8(w + i), b1 = ld8(w + ldw + i);
+    v8f a = ld8(x + i);
+    a00 += a * b0;
+    a01 += a * b1;
+    a = ld8(x + ldx + i);
+    a10 += a * b0;
+    a11 += a * b1;
+    a = ld8(x + 2 * ldx + i);
+    a20 += a * b0;
+    a21 += a * b1;
+    a = ld8(x + 3 * ldx + i);
+    a30 += a * b0;
+    a31 += a * b1;
+  }
+  acc[0][0] = a00, acc[0][1] = a01, acc[1][0] = a10, acc[1][1] = a11;
+  acc[2][0] = a20, acc[2][1] = a21, acc[3][0] = a30, acc[3][1] = a31;
+}
+
+/* reference.rs:151-157 for every row of X [t, k]: Y [t, n] = X W^T. Blocks of
+ * 32 rows x 32 outputs, walked in K chunks of 256 (a chunk of the block's
+ * operands stays in the core's L1) with 4 x 2 register tiles whose partial
+ * sums carry across chunks; every output keeps dot8's exact arithmetic (each
+ * of its 8 lanes accumulates mul-then-add in k order, reduced by dot8's
+ * tree, then the tail). dot8 itself for the ragged rows and outputs. */
 static void linear_rows(const float* x, int t, int k, const float* w, int n, int mode, float* y,
                         int threads) {
   const float* xs = x;
@@ -216,14 +289,43 @@ static void linear_rows(const float* x, int t, int k, const float* w, int n, int
   if (mode == ORACLE_KERNEL) {
     xr = (float*)malloc(sizeof(float) * (size_t)t * k);
     wr = (float*)malloc(sizeof(float) * (size_t)n * k);
+#pragma omp parallel for schedule(static) num_threads(threads)
     for (size_t i = 0; i < (size_t)t * k; ++i) xr[i] = round_f16(x[i]);
+#pragma omp parallel for schedule(static) num_threads(threads)
     for (size_t i = 0; i < (size_t)n * k; ++i) wr[i] = round_f16(w[i]);
     xs = xr;
     ws = wr;
   }
-#pragma omp parallel for schedule(static) num_threads(threads)
-  for (int r = 0; r < n; ++r)
-    for (int i = 0; i < t; ++i) y[(size_t)i * n + r] = dot8(xs + (size_t)i * k, ws + (size_t)r * k, k);
+  enum { BT = 32, BN = 32, KC = 256 };
+  const int tb = (t + BT - 1) / BT, nb = (n + BN - 1) / BN;
+  const int k8 = k / 8 * 8;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(threads)
+  for (int blk = 0; blk < tb * nb; ++blk) {
+    const int i0 = (blk % tb) * BT, r0 = (blk / tb) * BN;
+    const int i1 = i0 + BT < t ? i0 + BT : t, r1 = r0 + BN < n ? r0 + BN : n;
+    const int iq = i0 + (i1 - i0) / 4 * 4, rp = r0 + (r1 - r0) / 2 * 2;
+    v8f acc[BT / 4][BN / 2][4][2];
+    memset(acc, 0, sizeof acc);
+    for (int kc = 0; kc < k8; kc += KC) {
+      const int ke = kc + KC < k8 ? kc + KC : k8;
+      for (int r = r0; r < rp; r += 2)
+        for (int i = i0; i < iq; i += 4)
+          dot8_4x2_part(xs + (size_t)i * k, (size_t)k, ws + (size_t)r * k, (size_t)k, kc, ke,
+                        acc[(i - i0) / 4][(r - r0) / 2]);
+    }
+    for (int r = r0; r < rp; r += 2)
+      for (int i = i0; i < iq; i += 4)
+        for (int a = 0; a < 4; ++a)
+          for (int c = 0; c < 2; ++c) {
+            float s = tree8(acc[(i - i0) / 4][(r - r0) / 2][a][c]);
+            for (int j = k8; j < k; ++j)
+              s += xs[(size_t)(i + a) * k + j] * ws[(size_t)(r + c) * k + j];
+            y[(size_t)(i + a) * n + r + c] = s;
+          }
+    for (int r = r0; r < r1; ++r)
+      for (int i = (r < rp ? iq : i0); i < i1; ++i)
+        y[(size_t)i * n + r] = dot8(xs + (size_t)i * k, ws + (size_t)r * k, k);
+  }
   free(xr);
   free(wr);
 }
@@ -518,6 +620,7 @@ int oracle_forward(const oracle_config* cfg, const float* const* tensors, size_t
 
 void oracle_logits(const float* hidden, const float* embed, int vocab, int d, float softcap,
                    float* out) {
+#pragma omp parallel for schedule(static)
   for (int v = 0; v < vocab; ++v) {
     float z = 0.0f;
     for (int i = 0; i < d; ++i) z += hidden[i] * embed[(size_t)v * d + i];

@@ -36,6 +36,10 @@ void oracle_f16_to_f32_n(const uint16_t* in, size_t n, float* out);
 /* tests/reference.rs:17-26: xorshift64, uniform in [-1, 1). Fills n values
  * times `scale`, advancing *state. */
 void oracle_rng_values(uint64_t* state, float* out, size_t n, float scale);
+/* The synthetic models' normal draws (FNV-1a(name) ^ seed, xorshift64,
+ * Box-Muller in double). */
+void oracle_synth_normal(uint64_t seed, const char* name, float mean, float stddev, float* out,
+                         size_t n);
 
 /* model.rs:409-427 (Q8_0) and model.rs:431-466 (Q4_0). n is a multiple of 32;
  * codes get n (Q8) or n/2 (Q4) bytes, scales n/32 little-endian f16. */

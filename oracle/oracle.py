@@ -64,6 +64,8 @@ def lib():
         _lib.oracle_f32_to_f16_n.argtypes = [fp, C.c_size_t, C.POINTER(C.c_uint16)]
         _lib.oracle_f16_to_f32_n.argtypes = [C.POINTER(C.c_uint16), C.c_size_t, fp]
         _lib.oracle_rng_values.argtypes = [C.POINTER(C.c_uint64), fp, C.c_size_t, C.c_float]
+        _lib.oracle_synth_normal.argtypes = [C.c_uint64, C.c_char_p, C.c_float, C.c_float, fp,
+                                             C.c_size_t]
         _lib.oracle_quantize_q8.argtypes = [fp, C.c_size_t, u8, u8]
         _lib.oracle_quantize_q4.argtypes = [fp, C.c_size_t, u8, u8]
         _lib.oracle_dequant.argtypes = [C.c_int, u8, u8, C.c_size_t, fp]
@@ -142,6 +144,45 @@ def dequantize(dtype: int, data: bytes, scales: bytes, n: int) -> np.ndarray:
     if lib().oracle_dequant(dtype, _p(d, C.c_uint8), _p(s, C.c_uint8), n, _p(out, C.c_float)):
         raise ValueError("bad dtype")
     return out
+
+
+# ---- synthetic models (the benchmark's random checkpoints) -----------------------
+
+def synth_normal(seed: int, name: str, n: int, mean: float, std: float) -> np.ndarray:
+    """The synthetic models' draws: FNV-1a(name) ^ seed into xorshift64, Box-Muller."""
+    out = np.empty(n, dtype=np.float32)
+    lib().oracle_synth_normal(seed, name.encode(), mean, std, _p(out, C.c_float), n)
+    return out
+
+
+def synth_tensor(seed: int, name: str, shape, dtype: int, laya: bool = False) -> np.ndarray:
+    """One tensor of a synthetic model, quantized and dequantized by the
+    reference's rules (model.rs:395-525), as f32. Decoder: 2-D linears and
+    tables ~N(0, 0.02) in `dtype`, 1-D norm weights 1 + N(0, 0.02) in f16.
+    Encoder (`laya`): the same, except biases (names ending in `_b`) are
+    N(0, 0.02), and the type embedding and the host head (scorer.*, act.*)
+    stay f16."""
+    n = int(np.prod(shape))
+    last = name.rsplit(".", 1)[-1]
+    if len(shape) == 1:
+        mean = 0.0 if (laya and last.endswith("_b")) else 1.0
+        v, dt = synth_normal(seed, name, n, mean, 0.02), F16
+    else:
+        v, dt = synth_normal(seed, name, n, 0.0, 0.02), dtype
+        if laya and (name.startswith("scorer.") or name.startswith("act.") or name == "type_emb"):
+            dt = F16
+    data, scales = quantize(dt, v)
+    return dequantize(dt, data, scales, n)
+
+
+def synth_tensors(specs, seed: int, dtype: int, laya: bool = False, threads: int = 0) -> list:
+    """Every tensor of `specs` [(name, shape)] as f32, generated in a thread
+    pool (the C calls release the GIL)."""
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(max_workers=threads or os.cpu_count() or 1) as ex:
+        futs = [ex.submit(synth_tensor, seed, name, shape, dtype, laya) for name, shape in specs]
+        return [f.result() for f in futs]
 
 
 # ---- model description --------------------------------------------------------

@@ -149,3 +149,26 @@ def test_synth_normal_is_seeded_and_normal():
     L.check(L.lib().omg_synth_normal(0, b"blk.1.qkv", 0.0, 0.02, L.ptr(other, C.c_float),
                                      out.size))
     assert not np.array_equal(out, other)
+
+
+@pytest.mark.parametrize("name,shape,dtype,laya", [
+    ("blk.3.gate", [64, 128], Dtype.Q4, False),
+    ("blk.0.qkv", [96, 64], Dtype.Q8, False),
+    ("blk.1.ffn_norm", [256], Dtype.F16, False),
+    ("embed", [40, 64], Dtype.Q4, False),
+    ("blk.2.wi_b", [192], Dtype.F16, True),
+    ("scorer.l1", [64, 64], Dtype.Q8, True),
+    ("blk.0.wo", [64, 96], Dtype.Q8, True),
+])
+def test_oracle_synthetic_models_match_the_product_generator(name, shape, dtype, laya):
+    # The CPU baseline builds the benchmark's random models with oracle/ only;
+    # they must be the product's models bit for bit (draws, codes, scales).
+    from grande_b200 import synth
+    n = int(np.prod(shape))
+    for mean in (0.0, 1.0):
+        a = synth.normal(5, name, n, mean, 0.02)
+        b = O.synth_normal(5, name, n, mean, 0.02)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    qt = (synth.laya_tensor if laya else synth.tensor)(5, name, shape, dtype)
+    got = O.synth_tensor(5, name, shape, int(dtype), laya=laya)
+    assert np.array_equal(qt.to_f32().view(np.uint32), got.view(np.uint32))

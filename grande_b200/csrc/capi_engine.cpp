@@ -268,6 +268,16 @@ int omg_engine_gather_per_layer(omg_engine* e, const uint32_t* ids, size_t n, ui
   });
 }
 
+int omg_engine_weight_f16(omg_engine* e, const char* name, uint16_t* out, size_t n) {
+  return guarded([&] {
+    if (!name) fail("weight name is null");
+    auto w = eng(e).weight_f16(name);
+    if (n != w.size()) fail("weight_f16: %s has %zu values, the buffer %zu", name, w.size(), n);
+    std::memcpy(out, w.data(), w.size() * 2);
+    return 0;
+  });
+}
+
 int omg_engine_get_info(omg_engine* e, omg_engine_info* info) {
   return guarded([&] {
     Engine& x = eng(e);

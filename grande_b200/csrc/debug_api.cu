@@ -304,3 +304,33 @@ extern "C" int omg_debug_gemm_time(int device, int m, int n, int k, int epi, int
     return 0;
   });
 }
+
+extern "C" int omg_debug_dequant(int device, int dtype, const uint8_t* codes,
+                                 const uint8_t* scales, int rows, int k, int mode, uint16_t* hi,
+                                 uint16_t* lo) {
+  return guarded([&]() -> int {
+    if (rows <= 0 || k <= 0 || k % 32) fail("omg_debug_dequant: %d x %d is not whole blocks", rows, k);
+    if (dtype < 0 || dtype > 2) fail("omg_debug_dequant: dtype %d", dtype);
+    if (mode != 0 && mode != 1) fail("omg_debug_dequant: mode %d", mode);
+    if (mode == 1 && !lo) fail("omg_debug_dequant: mode 1 writes lo too");
+    CUDA_TRY(cudaSetDevice(device));
+    const size_t n = static_cast<size_t>(rows) * k;
+    const size_t cb = dtype == 0 ? n * 2 : (dtype == 1 ? n : n / 2);
+    const size_t sb = dtype == 0 ? 0 : n / 32 * 2;
+    DevBuf dc, ds, dh, dl;
+    if (!dc.alloc(cb) || !ds.alloc(sb) || !dh.alloc(n * 2) || !dl.alloc(n * 2))
+      return set_error("cudaMalloc failed");
+    CUDA_TRY(cudaMemcpy(dc.p, codes, cb, cudaMemcpyHostToDevice));
+    if (sb) CUDA_TRY(cudaMemcpy(ds.p, scales, sb, cudaMemcpyHostToDevice));
+    if (mode == 0)
+      launch_dequant_f16(dtype, dc.p, ds.p, rows, k, 0, static_cast<__half*>(dh.p), 0);
+    else
+      launch_table_hilo(dtype, dc.p, ds.p, n, static_cast<__half*>(dh.p),
+                        static_cast<__half*>(dl.p), 0);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaDeviceSynchronize());
+    CUDA_TRY(cudaMemcpy(hi, dh.p, n * 2, cudaMemcpyDeviceToHost));
+    if (mode == 1) CUDA_TRY(cudaMemcpy(lo, dl.p, n * 2, cudaMemcpyDeviceToHost));
+    return 0;
+  });
+}

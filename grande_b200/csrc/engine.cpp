@@ -529,6 +529,36 @@ std::vector<uint8_t> Engine::gather_per_layer(const uint32_t* ids, size_t n) con
   return out;
 }
 
+std::vector<uint16_t> Engine::weight_f16(const std::string& name) const {
+  CUDA_TRY(cudaSetDevice(device_));
+  std::vector<int64_t> shape;
+  for (const auto& t : config.tensors())
+    if (t.name == name) shape = t.shape;
+  if (shape.size() != 2 || name == "embed")
+    fail("weight_f16: %s is not a projection weight", name.c_str());
+  const size_t rows = static_cast<size_t>(shape[0]), k = static_cast<size_t>(shape[1]);
+  std::vector<uint16_t> out(rows * k);
+  const bool gate = ends_with(name, ".gate"), up = ends_with(name, ".up");
+  if (!gate && !up) {
+    auto it = lin_.find(name);
+    if (it == lin_.end()) fail("weight_f16: no device weight %s", name.c_str());
+    CUDA_TRY(cudaMemcpy(out.data(), it->second.p, out.size() * 2, cudaMemcpyDeviceToHost));
+    return out;
+  }
+  // Gate and up rows interleave in 256-row blocks [128 gate | 128 up].
+  const std::string key = name.substr(0, name.rfind('.')) + ".gate_up";
+  auto it = lin_.find(key);
+  if (it == lin_.end()) fail("weight_f16: no device weight %s", key.c_str());
+  const size_t blocks = (rows + 127) / 128;
+  std::vector<uint16_t> all(blocks * 256 * k);
+  CUDA_TRY(cudaMemcpy(all.data(), it->second.p, all.size() * 2, cudaMemcpyDeviceToHost));
+  for (size_t r = 0; r < rows; ++r) {
+    const size_t src = (r / 128) * 256 + (up ? 128 : 0) + r % 128;
+    std::memcpy(out.data() + r * k, all.data() + src * k, k * 2);
+  }
+  return out;
+}
+
 // engine.rs:1467-1477
 std::pair<size_t, std::optional<PrefixSource>> Engine::admit(const GroupIn* groups, size_t n) {
   for (size_t i = 0; i < n; ++i)

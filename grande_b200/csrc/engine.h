@@ -205,6 +205,11 @@ class Engine {
   // Events on the engine's stream for end-to-end timing around API calls.
   void record_event(int slot);
   float elapsed_ms(int a, int b);
+  // The f16 values the projection GEMMs multiply for the linear `name` (a
+  // catalogue name; blk.N.gate and blk.N.up read their rows of the
+  // interleaved gate/up weight), row-major [rows, k]: the device copy read
+  // back, for bit-exact checks of the device dequantization.
+  std::vector<uint16_t> weight_f16(const std::string& name) const;
   // Gather per-layer table rows for ids (engine.rs:1370-1381), f16 LE.
   std::vector<uint8_t> gather_per_layer(const uint32_t* ids, size_t n) const;
 

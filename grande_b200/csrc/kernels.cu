@@ -1,5 +1,7 @@
 // Row kernels of the decoder pass (see kernels.cuh). Reference shaders:
 // crates/omg-wgpu/src/shaders/{weight,embed,rmsnorm,qk_prep,logits}.wgsl.
+#include <algorithm>
+
 #include "kernels.cuh"
 #include "launch.cuh"
 #include "ptx.cuh"
@@ -872,7 +874,44 @@ __global__ void __launch_bounds__(LT_THREADS, 1)
   }
 }
 
+// The lm_head's block decoder (raw_piece_f16) over a whole table, row-major
+// hi and lo f16 outputs: the values logits_tc_kernel stages in shared memory.
+template <int DT>
+__global__ void table_hilo_kernel(const uint8_t* __restrict__ codes,
+                                  const uint8_t* __restrict__ scales, size_t nblk,
+                                  __half* __restrict__ hi, __half* __restrict__ lo) {
+  for (size_t b = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; b < nblk;
+       b += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    RawBlock<DT> rb;
+    load_raw_block<DT>(codes, scales, b, true, rb);
+    uint4 h[4], l[4];
+    raw_piece_f16<DT, 0>(rb, h[0], l[0]);
+    raw_piece_f16<DT, 1>(rb, h[1], l[1]);
+    raw_piece_f16<DT, 2>(rb, h[2], l[2]);
+    raw_piece_f16<DT, 3>(rb, h[3], l[3]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      reinterpret_cast<uint4*>(hi + b * 32)[i] = h[i];
+      reinterpret_cast<uint4*>(lo + b * 32)[i] = l[i];
+    }
+  }
+}
+
 }  // namespace
+
+void launch_table_hilo(int dtype, const void* codes, const void* scales, size_t n, __half* hi,
+                       __half* lo, cudaStream_t s) {
+  const size_t nblk = n / 32;
+  const int grid = static_cast<int>(std::min<size_t>((nblk + 255) / 256, 148 * 16));
+  const auto* c = static_cast<const uint8_t*>(codes);
+  const auto* sc = static_cast<const uint8_t*>(scales);
+  if (dtype == kQ4)
+    table_hilo_kernel<kQ4><<<grid, 256, 0, s>>>(c, sc, nblk, hi, lo);
+  else if (dtype == kQ8)
+    table_hilo_kernel<kQ8><<<grid, 256, 0, s>>>(c, sc, nblk, hi, lo);
+  else
+    table_hilo_kernel<kF16><<<grid, 256, 0, s>>>(c, sc, nblk, hi, lo);
+}
 
 void launch_dequant_f16(int dtype, const void* codes, const void* scales, int rows, int k,
                         int remap, __half* out, cudaStream_t s) {

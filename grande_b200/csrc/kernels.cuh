@@ -22,6 +22,10 @@ struct TokMeta {
 // remap 0 = identity; 1 / 2 = the gate / up half of the interleaved GeGLU
 // layout (256-row blocks: 128 gate rows, then the 128 up rows of the same
 // output columns).
+// The lm_head's in-shared-memory decoder over a whole table of n values:
+// hi = f16(w), lo = w - hi (f16), row-major (test entry point).
+void launch_table_hilo(int dtype, const void* codes, const void* scales, size_t n, __half* hi,
+                       __half* lo, cudaStream_t s);
 void launch_dequant_f16(int dtype, const void* codes, const void* scales, int rows, int k,
                         int remap, __half* out, cudaStream_t s);
 

@@ -438,6 +438,14 @@ class Engine:
                                                 _lib.ptr(out, C.c_uint8), n))
         return out.tobytes()
 
+    def weight_f16(self, name: str, shape) -> np.ndarray:
+        """The f16 bits the projection GEMMs multiply for linear `name`
+        ([rows, k] uint16), read back from the device."""
+        out = np.empty(tuple(shape), dtype=np.uint16)
+        check(lib().omg_engine_weight_f16(self._h, name.encode(), _lib.ptr(out, C.c_uint16),
+                                          out.size))
+        return out
+
     # ---- timing hooks (bench.py) --------------------------------------------
 
     def time_forward(self, groups: Sequence[Group], want: Want, iters: int,

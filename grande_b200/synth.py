@@ -83,25 +83,50 @@ def normal(seed: int, name: str, n: int, mean: float, std: float) -> np.ndarray:
     return out
 
 
-def tensor(seed: int, name: str, shape, dtype: Dtype) -> QTensor:
+def tensor(seed: int, name: str, shape, dtype: Dtype, qk_scale: float = 1.0) -> QTensor:
+    """One tensor of a synthetic model. `qk_scale` multiplies the q / k head
+    norm weights: with the Gemma-4 numerics (query scale 1) the attention
+    logits of the plain model spread with a standard deviation of ~16, so
+    the softmax picks near-single keys and any rounding difference flips
+    them; 0.25 gives logits of unit spread (a conditioned model for deep
+    parity checks)."""
     n = int(np.prod(shape))
     if len(shape) == 1:
-        return QTensor.from_f32(shape, normal(seed, name, n, 1.0, 0.02))
+        v = normal(seed, name, n, 1.0, 0.02)
+        if qk_scale != 1.0 and (name.endswith(".q_norm") or name.endswith(".k_norm")):
+            v = v * np.float32(qk_scale)
+        return QTensor.from_f32(shape, v)
     v = normal(seed, name, n, 0.0, 0.02)
     return QTensor._encode(dtype, shape, v)
 
 
 def build_engine(shape: Shape, capacity: int, max_rows: int, device: int = 0, seed: int = 0,
-                 threads: int = 8):
+                 threads: int = 8, qk_scale: float = 1.0, tensors: dict | None = None):
     """Generate, quantize and push every tensor (generation in a thread pool;
-    ctypes releases the GIL), then finish the engine."""
+    ctypes releases the GIL), then finish the engine. `tensors` (name ->
+    QTensor) supplies already generated tensors, e.g. a deeper model's, of
+    which this shape's catalogue takes its own."""
     b = EngineBuilder(shape.config_json(), device)
     specs = _lib_specs(shape.config_json())
+    if tensors is not None:
+        for name, _dims in specs:
+            b.push(name, tensors[name])
+        return b.finish(capacity, max_rows)
     with ThreadPoolExecutor(max_workers=threads) as ex:
-        futs = [(name, ex.submit(tensor, seed, name, dims, shape.dtype)) for name, dims in specs]
+        futs = [(name, ex.submit(tensor, seed, name, dims, shape.dtype, qk_scale))
+                for name, dims in specs]
         for name, f in futs:
             b.push(name, f.result())
     return b.finish(capacity, max_rows)
+
+
+def generate(shape: Shape, seed: int = 0, threads: int = 8, qk_scale: float = 1.0) -> dict:
+    """Every tensor of `shape`'s model, name -> QTensor."""
+    specs = _lib_specs(shape.config_json())
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        futs = [(name, ex.submit(tensor, seed, name, dims, shape.dtype, qk_scale))
+                for name, dims in specs]
+        return {name: f.result() for name, f in futs}
 
 
 def _lib_specs(config_json: str):

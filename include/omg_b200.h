@@ -300,6 +300,21 @@ int omg_debug_attention(int device, const uint16_t* q, const uint16_t* kv, const
                         int t, int base, int heads, int kv_heads, int hd, int window, int p_lo,
                         uint16_t* out);
 
+/* Bit-exact checks of the device dequantization (model.rs:508-525
+ * QTensor::get; weight.wgsl:29-54 decodes the same blocks per use). mode 0:
+ * the load-time decoder the engine runs on each pushed linear, hi [rows, k]
+ * = f16(QTensor::get); mode 1: the lm_head's in-shared-memory decoder
+ * (logits.wgsl:21-55 reads the table in f32), hi = f16(w) and lo = w - hi in
+ * f16, so hi + lo == w exactly. codes / scales as omg_builder_push takes them. */
+int omg_debug_dequant(int device, int dtype, const uint8_t* codes, const uint8_t* scales,
+                      int rows, int k, int mode, uint16_t* hi, uint16_t* lo);
+
+/* The f16 values an engine's projection GEMMs multiply for linear `name`
+ * (blk.N.qkv, .o, .gate, .up, .down, ...), [rows, k] row-major, read back
+ * from the device: the weight EngineBuilder::push received
+ * (crates/omg-wgpu/src/engine.rs:845-952), as the GEMM sees it. */
+int omg_engine_weight_f16(omg_engine* e, const char* name, uint16_t* out, size_t n);
+
 /* Kernel timing for tile sweeps (no reference counterpart; the reference
  * times dispatches with timestamp queries, crates/omg-wgpu/src/engine.rs:643-726):
  * `iters` launches of the GEMM on device-resident operands of the given shape

@@ -361,9 +361,10 @@ typedef struct {
   float out_scale;
 } layer_w;
 
-int oracle_forward(const oracle_config* cfg, const float* const* tensors, size_t n_tensors,
-                   const uint32_t* ids, const int32_t* pos, const int32_t* seq, size_t t_,
-                   int mode, int threads, float* hidden) {
+int oracle_forward_layers(const oracle_config* cfg, const float* const* tensors,
+                          size_t n_tensors, const uint32_t* ids, const int32_t* pos,
+                          const int32_t* seq, size_t t_, int mode, int threads, float* hidden,
+                          float* per_layer) {
   const int d = cfg->d, L = cfg->layers, heads = cfg->heads, kvh = cfg->kv_heads;
   const int pl = cfg->per_layer_dim;
   const int t = (int)t_;
@@ -592,6 +593,12 @@ int oracle_forward(const oracle_config* cfg, const float* const* tensors, size_t
       free(gated);
     }
     for (size_t k = 0; k < T * d; ++k) x[k] *= scale;
+    /* What a model cut after this layer would return: its final norm of
+     * the stream. */
+    if (per_layer)
+      for (int i = 0; i < t; ++i)
+        rmsnorm(x + (size_t)i * d, d, final_norm, cfg->eps, cfg->norm_offset,
+                per_layer + ((size_t)li * T + i) * d);
   }
   for (int i = 0; i < t; ++i)
     rmsnorm(x + (size_t)i * d, d, final_norm, cfg->eps, cfg->norm_offset, hidden + (size_t)i * d);
@@ -614,6 +621,13 @@ int oracle_forward(const oracle_config* cfg, const float* const* tensors, size_t
   free(pli);
   free(lw);
   return 0;
+}
+
+int oracle_forward(const oracle_config* cfg, const float* const* tensors, size_t n_tensors,
+                   const uint32_t* ids, const int32_t* pos, const int32_t* seq, size_t t,
+                   int mode, int threads, float* hidden) {
+  return oracle_forward_layers(cfg, tensors, n_tensors, ids, pos, seq, t, mode, threads, hidden,
+                               NULL);
 }
 
 /* ---- logits and readout --------------------------------------------------- */

@@ -86,6 +86,13 @@ enum {
 int oracle_forward(const oracle_config* cfg, const float* const* tensors, size_t n_tensors,
                    const uint32_t* ids, const int32_t* pos, const int32_t* seq, size_t t,
                    int mode, int threads, float* hidden);
+/* The same, and per_layer [layers][t][d] (or NULL) gets, after each layer
+ * l, the final norm of the residual stream: the hidden rows of the model cut
+ * after layer l. */
+int oracle_forward_layers(const oracle_config* cfg, const float* const* tensors,
+                          size_t n_tensors, const uint32_t* ids, const int32_t* pos,
+                          const int32_t* seq, size_t t, int mode, int threads, float* hidden,
+                          float* per_layer);
 
 /* The block-causal visibility rule (attention.wgsl:70-76): 1 if a query at
  * (qp, qs) sees a key at (kp, ks) on a layer with this window (0 = global). */

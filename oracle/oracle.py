@@ -72,6 +72,7 @@ def lib():
         _lib.oracle_forward.argtypes = [
             C.POINTER(_Cfg), C.POINTER(fp), C.c_size_t, C.POINTER(C.c_uint32),
             C.POINTER(C.c_int32), C.POINTER(C.c_int32), C.c_size_t, C.c_int, C.c_int, fp]
+        _lib.oracle_forward_layers.argtypes = _lib.oracle_forward.argtypes + [fp]
         _lib.oracle_visible.argtypes = [C.c_int32] * 4 + [C.c_int]
         _lib.oracle_logits.argtypes = [fp, fp, C.c_int, C.c_int, C.c_float, fp]
         _lib.oracle_softmax.argtypes = [fp, C.c_size_t, C.c_float, C.POINTER(C.c_double)]
@@ -155,18 +156,22 @@ def synth_normal(seed: int, name: str, n: int, mean: float, std: float) -> np.nd
     return out
 
 
-def synth_tensor(seed: int, name: str, shape, dtype: int, laya: bool = False) -> np.ndarray:
+def synth_tensor(seed: int, name: str, shape, dtype: int, laya: bool = False,
+                 qk_scale: float = 1.0) -> np.ndarray:
     """One tensor of a synthetic model, quantized and dequantized by the
     reference's rules (model.rs:395-525), as f32. Decoder: 2-D linears and
     tables ~N(0, 0.02) in `dtype`, 1-D norm weights 1 + N(0, 0.02) in f16.
     Encoder (`laya`): the same, except biases (names ending in `_b`) are
     N(0, 0.02), and the type embedding and the host head (scorer.*, act.*)
-    stay f16."""
+    stay f16. `qk_scale` multiplies the decoder's q / k head norm weights
+    (the conditioned variant of the model)."""
     n = int(np.prod(shape))
     last = name.rsplit(".", 1)[-1]
     if len(shape) == 1:
         mean = 0.0 if (laya and last.endswith("_b")) else 1.0
         v, dt = synth_normal(seed, name, n, mean, 0.02), F16
+        if qk_scale != 1.0 and (name.endswith(".q_norm") or name.endswith(".k_norm")):
+            v = v * np.float32(qk_scale)
     else:
         v, dt = synth_normal(seed, name, n, 0.0, 0.02), dtype
         if laya and (name.startswith("scorer.") or name.startswith("act.") or name == "type_emb"):
@@ -175,13 +180,15 @@ def synth_tensor(seed: int, name: str, shape, dtype: int, laya: bool = False) ->
     return dequantize(dt, data, scales, n)
 
 
-def synth_tensors(specs, seed: int, dtype: int, laya: bool = False, threads: int = 0) -> list:
+def synth_tensors(specs, seed: int, dtype: int, laya: bool = False, threads: int = 0,
+                  qk_scale: float = 1.0) -> list:
     """Every tensor of `specs` [(name, shape)] as f32, generated in a thread
     pool (the C calls release the GIL)."""
     import os
     from concurrent.futures import ThreadPoolExecutor
     with ThreadPoolExecutor(max_workers=threads or os.cpu_count() or 1) as ex:
-        futs = [ex.submit(synth_tensor, seed, name, shape, dtype, laya) for name, shape in specs]
+        futs = [ex.submit(synth_tensor, seed, name, shape, dtype, laya, qk_scale)
+                for name, shape in specs]
         return [f.result() for f in futs]
 
 
@@ -255,9 +262,11 @@ class OracleConfig:
 
 
 def forward(cfg: OracleConfig, tensors: list, ids, pos, seq, mode: int = ORACLE_EXACT,
-            threads: int = 0) -> np.ndarray:
+            threads: int = 0, per_layer: bool = False):
     """tests/reference.rs:175-349: final-norm hidden rows [t, d]. `tensors` are
-    dequantized f32 arrays in catalogue order (+ the per-layer table)."""
+    dequantized f32 arrays in catalogue order (+ the per-layer table). With
+    `per_layer`, also [layers, t, d]: after each layer l, the hidden rows the
+    model cut after layer l returns (the final norm of its stream)."""
     arrs = [np.ascontiguousarray(t, dtype=np.float32).ravel() for t in tensors]
     ptrs = (C.POINTER(C.c_float) * len(arrs))(*[_p(a, C.c_float) for a in arrs])
     ids = np.ascontiguousarray(ids, dtype=np.uint32)
@@ -265,13 +274,15 @@ def forward(cfg: OracleConfig, tensors: list, ids, pos, seq, mode: int = ORACLE_
     seq = np.ascontiguousarray(seq, dtype=np.int32)
     t = ids.size
     out = np.empty((t, cfg.d), dtype=np.float32)
+    layers = np.empty((cfg.layers, t, cfg.d), dtype=np.float32) if per_layer else None
     c = cfg._c()
-    rc = lib().oracle_forward(C.byref(c), ptrs, len(arrs), _p(ids, C.c_uint32),
-                              _p(pos, C.c_int32), _p(seq, C.c_int32), t, mode, threads,
-                              _p(out, C.c_float))
+    rc = lib().oracle_forward_layers(C.byref(c), ptrs, len(arrs), _p(ids, C.c_uint32),
+                                     _p(pos, C.c_int32), _p(seq, C.c_int32), t, mode, threads,
+                                     _p(out, C.c_float),
+                                     _p(layers, C.c_float) if per_layer else None)
     if rc != 0:
         raise ValueError(f"oracle_forward failed ({rc})")
-    return out
+    return (out, layers) if per_layer else out
 
 
 def visible(qp, qs, kp, ks, window) -> bool:

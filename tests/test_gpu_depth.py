@@ -1,0 +1,154 @@
+"""The E2B-shaped decoder at its production pass (
+d 2048, 8 q / 2 KV heads of 256, GeGLU 8192, Q4_0, vocab 25,000; a 500-token
+state + 12 branches of 24 tokens, 788 rows) through every depth up to the
+benchmarked 30 layers, against the reference's CPU forward
+(tests/reference.rs:175-349, restated in oracle/).
+
+Two models of that shape, each cut after 1, 2, 4, 8, 16 and 30 layers (a cut
+model is the first layers of the full one, then its final norm):
+
+* the benchmark's model (seeded N(0, 0.02) linears, norm weights around 1).
+  With query scale 1 its attention logits spread with a standard deviation
+  of ~16, so each softmax nearly picks one key and any rounding difference
+  can flip it: the reference's own two modes (f16 operand rounding as its
+  GPU shaders do, and exact f32) part ways within a few layers. Here the
+  engine's distance to the rounding mode is measured at every depth and
+  must stay within the reference's own distance between its modes (times
+  1.5) wherever that distance is still informative (below 0.1);
+* the same model with its q / k norm weights scaled by 0.25
+  (synth.tensor's qk_scale): attention logits of unit spread, so rounding
+  stays rounding through 30 layers. There the engine must stay within the
+  same bound at every depth, and at full depth its logits at the 12 answer
+  rows must be within 2e-2 max-abs of the reference's with the same argmax,
+  and the label probabilities of readout.rs:124-147 (3 seeded labels per
+  branch, temperature 1) within 1e-3.
+
+The measured drifts are printed (pytest -s) as a table and, with
+OMG_DEPTH_RECORD=<dir>, written there as depth_drift.json."""
+import dataclasses
+import json
+import os
+
+import numpy as np
+import pytest
+
+from grande_b200 import synth
+from grande_b200.engine import Want
+from grande_b200.readout import label_distribution
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DEPTHS = [1, 2, 4, 8, 16, 30]
+MARGIN = 1.5
+INFORMATIVE = 0.1
+QK_CONDITIONED = 0.25
+
+
+def rel(a, b):
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1.0))
+
+
+def oracle_cfg(shape):
+    sliding = [t == "sliding_attention" for t in shape.config()["layer_types"]]
+    L = shape.layers
+    return O.OracleConfig(vocab=shape.vocab, d=shape.d, layers=L, heads=shape.heads,
+                          kv_heads=shape.kv_heads, head_dim=[256] * L, ff=[shape.ff] * L,
+                          sliding=sliding, kv_source=list(range(L)), rope_dims=[256] * L,
+                          window=512, query_scale=1.0, norm_offset=0.0, v_norm=True,
+                          softcap=30.0)
+
+
+@pytest.fixture(scope="module")
+def sweep(device):
+    full = synth.CONFIGS["e2b-q4"]
+    req = synth.request(full, seed=3)
+    rows = []
+    at = len(req.prefix)
+    for b in req.branches:
+        rows.append(at + b.want[0])
+        at += len(b.tokens)
+    ids, pos, seq = O.pack(req.prefix, [(b.tokens, b.want) for b in req.branches])
+    ocfg = oracle_cfg(full)
+    specs = ocfg.tensors()
+    base = O.synth_tensors(specs, 0, int(full.dtype))
+    qt_base = synth.generate(full, seed=0)
+    out = {}
+    for label, qk in (("benchmark", 1.0), ("conditioned", QK_CONDITIONED)):
+        tensors = list(base)
+        qts = dict(qt_base)
+        if qk != 1.0:
+            for i, (name, shape) in enumerate(specs):
+                if name.endswith(".q_norm") or name.endswith(".k_norm"):
+                    tensors[i] = O.synth_tensor(0, name, shape, int(full.dtype), qk_scale=qk)
+                    qts[name] = synth.tensor(0, name, shape, full.dtype, qk_scale=qk)
+        _, kern = O.forward(ocfg, tensors, ids, pos, seq, O.ORACLE_KERNEL, 0, per_layer=True)
+        _, exact = O.forward(ocfg, tensors, ids, pos, seq, O.ORACLE_EXACT, 0, per_layer=True)
+        res = []
+        for depth in DEPTHS:
+            shape = dataclasses.replace(full, layers=depth)
+            eng = synth.build_engine(shape, full.tokens() + 64, full.branches, device=device,
+                                     tensors=qts)
+            hid = eng.evaluate(req.prefix, req.branches, Want.HIDDEN)
+            logits = None
+            if depth == DEPTHS[-1]:
+                eng.evict_resident()
+                logits = np.stack([o.rows[0] for o in
+                                   eng.evaluate(req.prefix, req.branches, Want.LOGITS)])
+            eng.close()
+            got = np.stack([o.rows[0] for o in hid])
+            k, e = kern[depth - 1][rows], exact[depth - 1][rows]
+            res.append({"depth": depth,
+                        "engine_vs_rounding": max(rel(g, x) for g, x in zip(got, k)),
+                        "engine_vs_exact": max(rel(g, x) for g, x in zip(got, e)),
+                        "reference_modes": max(rel(x, y) for x, y in zip(k, e)),
+                        "logits": logits, "kern": k, "exact": e})
+        out[label] = {"tensors": tensors, "res": res}
+    table = {lab: [{k: v for k, v in r.items() if k not in ("logits", "kern", "exact")}
+                   for r in out[lab]["res"]] for lab in out}
+    print("\n" + json.dumps(table, indent=1))
+    rec = os.environ.get("OMG_DEPTH_RECORD")
+    if rec:
+        os.makedirs(rec, exist_ok=True)
+        with open(os.path.join(rec, "depth_drift.json"), "w") as f:
+            json.dump(table, f, indent=1)
+    out["req"] = req
+    out["ocfg"] = ocfg
+    return out
+
+
+def test_benchmark_model_depth_sweep(sweep):
+    for r in sweep["benchmark"]["res"]:
+        if r["reference_modes"] < INFORMATIVE:
+            bound = MARGIN * max(r["reference_modes"], 1e-3)
+            assert r["engine_vs_rounding"] < bound, r
+
+
+def test_conditioned_model_depth_sweep(sweep):
+    for r in sweep["conditioned"]["res"]:
+        bound = MARGIN * max(r["reference_modes"], 1e-3)
+        assert r["engine_vs_rounding"] < bound, r
+        assert r["engine_vs_exact"] < 2e-2, r
+
+
+def test_conditioned_model_full_depth_logits_and_probabilities(sweep):
+    r = sweep["conditioned"]["res"][-1]
+    assert r["depth"] == 30
+    ocfg, embed = sweep["ocfg"], sweep["conditioned"]["tensors"][0]
+    rng = np.random.default_rng(12)
+    for i, got in enumerate(r["logits"]):
+        for ref_rows in (r["kern"], r["exact"]):
+            exp = O.logits(ref_rows[i], embed, ocfg.vocab, ocfg.d, ocfg.softcap)
+            err = float(np.abs(got - exp).max())
+            assert err < 2e-2, f"branch {i}: logits max-abs diff {err}"
+            top2 = np.sort(exp)[-2:]
+            if top2[1] - top2[0] > 2 * err:
+                assert int(np.argmax(got)) == int(np.argmax(exp)), f"branch {i}: argmax"
+            labels = rng.choice(ocfg.vocab, 3, replace=False)
+            dg = label_distribution(got, labels, 1.0)
+            probs = O.softmax(exp[labels], 1.0)
+            assert float(np.abs(dg.probs - probs).max()) < 1e-3, (i, dg.probs, probs)
+            mass = np.exp(O.log_sum_exp(exp[labels]) - O.log_sum_exp(exp))
+            # log(mass) is a difference of two log-sum-exps of logits, each
+            # within the logits' max-abs error.
+            assert abs(np.log(dg.candidate_mass) - np.log(mass)) <= 2 * err + 1e-6

@@ -172,3 +172,24 @@ def test_oracle_synthetic_models_match_the_product_generator(name, shape, dtype,
     qt = (synth.laya_tensor if laya else synth.tensor)(5, name, shape, dtype)
     got = O.synth_tensor(5, name, shape, int(dtype), laya=laya)
     assert np.array_equal(qt.to_f32().view(np.uint32), got.view(np.uint32))
+
+
+def test_label_readout_matches_the_oracle_math():
+    # readout.rs:130-147 on math.rs:5-17: the product's f64 softmax and
+    # log-sum-exp against the oracle's C restatement.
+    from grande_b200.readout import label_distribution, log_sum_exp, softmax
+    rng = np.random.default_rng(4)
+    row = (rng.standard_normal(25000) * 3).astype(np.float32)
+    ids = [17, 4000, 24999]
+    for temp in (1.0, 0.7, 0.0):
+        dist = label_distribution(row, ids, temp)
+        assert np.array_equal(dist.logits, row[ids])
+        exp = O.softmax(row[ids], temp)
+        assert np.allclose(dist.probs, exp, rtol=1e-12, atol=1e-15)
+        assert np.allclose(softmax(row[ids], temp), exp, rtol=1e-12, atol=1e-15)
+    lse = O.log_sum_exp(row)
+    assert abs(log_sum_exp(row) - lse) < 1e-9
+    mass = np.exp(O.log_sum_exp(row[ids]) - lse)
+    assert abs(dist.candidate_mass - mass) < 1e-12
+    with pytest.raises(ValueError):
+        label_distribution(row, [25000])

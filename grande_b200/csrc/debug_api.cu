@@ -11,6 +11,7 @@
 #include "capi_util.h"
 #include "attention.cuh"
 #include "gemm.cuh"
+#include "packed.cuh"
 #include "omg_b200.h"
 
 using namespace omg;
@@ -331,6 +332,130 @@ extern "C" int omg_debug_dequant(int device, int dtype, const uint8_t* codes,
     CUDA_TRY(cudaDeviceSynchronize());
     CUDA_TRY(cudaMemcpy(hi, dh.p, n * 2, cudaMemcpyDeviceToHost));
     if (mode == 1) CUDA_TRY(cudaMemcpy(lo, dl.p, n * 2, cudaMemcpyDeviceToHost));
+    return 0;
+  });
+}
+
+namespace {
+
+// A QTensor-layout weight [rows, k] (codes, f16 scales) packed on the device.
+bool upload_packed(int dtype, const uint8_t* codes, const uint8_t* scales, int rows, int k,
+                   DevBuf* out) {
+  const size_t n = static_cast<size_t>(rows) * k;
+  const size_t cb = dtype == kQ8 ? n : n / 2, sb = n / 32 * 2;
+  DevBuf dc, ds;
+  if (!dc.alloc(cb) || !ds.alloc(sb) || !out->alloc(packed_bytes(dtype, rows, k))) return false;
+  if (cudaMemcpy(dc.p, codes, cb, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(ds.p, scales, sb, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemset(out->p, 0, packed_bytes(dtype, rows, k)) != cudaSuccess)
+    return false;
+  launch_pack_weight(dtype, dc.p, ds.p, rows, k, 0, rows, static_cast<uint8_t*>(out->p), 0);
+  return cudaDeviceSynchronize() == cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" int omg_debug_gemm_q(int device, const uint16_t* x_f16, int m, int k, int lda,
+                                int wdtype, const uint8_t* w_codes, const uint8_t* w_scales,
+                                int w_rows, int n_out, int epi, int bn, int splits, void* out,
+                                int ldo) {
+  return guarded([&]() -> int {
+    if (wdtype != kQ4 && wdtype != kQ8) fail("omg_debug_gemm_q: dtype %d is not Q4_0 / Q8_0", wdtype);
+    if (k % 32) fail("omg_debug_gemm_q: K %d is not whole blocks", k);
+    CUDA_TRY(cudaSetDevice(device));
+    gemm_setup_device();
+    if (bn == 0) {
+      int sms = 148;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+      gemm_pick(n_out, k, sms, &bn, &splits);
+    }
+    DevBuf dx, dw, dout, dstat;
+    const size_t xb = static_cast<size_t>(m) * lda * 2;
+    const bool f32 = epi == kEpiF32;
+    if (!dx.alloc(xb) || !dstat.alloc(4)) return set_error("cudaMalloc failed");
+    if (!upload_packed(wdtype, w_codes, w_scales, w_rows, k, &dw))
+      return set_error("packing the weight failed");
+    CUDA_TRY(cudaMemcpy(dx.p, x_f16, xb, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemset(dstat.p, 0, 4));
+    GemmPlan plan;
+    char err[256];
+    if (!gemm_plan_packed(&plan, dx.p, m, lda, dw.p, wdtype, w_rows, n_out, k, epi, bn, splits,
+                          err, sizeof err))
+      return set_error(err);
+    const int sp = f32 ? plan.s.splits : 1;
+    const size_t slab = static_cast<size_t>(m) * ldo;
+    const size_t ob = slab * sp * (f32 ? 4 : 2);
+    if (!dout.alloc(ob)) return set_error("cudaMalloc failed");
+    CUDA_TRY(cudaMemset(dout.p, 0, ob));
+    gemm_run(plan, m, dout.p, ldo, slab, static_cast<uint32_t*>(dstat.p), 0);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaDeviceSynchronize());
+    uint32_t st = 0;
+    CUDA_TRY(cudaMemcpy(&st, dstat.p, 4, cudaMemcpyDeviceToHost));
+    if (st) return set_error("gemm kernel reported device status %u", st);
+    if (f32 && sp > 1) {
+      std::vector<float> h(slab * sp);
+      CUDA_TRY(cudaMemcpy(h.data(), dout.p, ob, cudaMemcpyDeviceToHost));
+      float* o = static_cast<float*>(out);
+      for (size_t i = 0; i < slab; ++i) {
+        float s = h[i];
+        for (int z = 1; z < sp; ++z) s += h[z * slab + i];
+        o[i] = s;
+      }
+    } else {
+      CUDA_TRY(cudaMemcpy(out, dout.p, ob, cudaMemcpyDeviceToHost));
+    }
+    return 0;
+  });
+}
+
+extern "C" int omg_debug_mlp_q(int device, const uint16_t* x, int m, int d, int wdtype,
+                               const uint8_t* up_codes, const uint8_t* up_scales, int ff,
+                               const uint8_t* down_codes, const uint8_t* down_scales,
+                               uint16_t* act_out, float* y_out) {
+  return guarded([&]() -> int {
+    if (wdtype != kQ4 && wdtype != kQ8) fail("omg_debug_mlp_q: dtype %d is not Q4_0 / Q8_0", wdtype);
+    CUDA_TRY(cudaSetDevice(device));
+    gemm_setup_device();
+    if (m <= 0 || d <= 0 || ff <= 0 || d % 128 != 0 || ff % d != 0)
+      return set_error("debug_mlp_q: needs d %% 128 == 0 and ff %% d == 0 (d %d, ff %d)", d, ff);
+    const int splits = ff / d;
+    DevBuf dx, dwu, dwd, dact, dslab, dready, dstat;
+    const size_t xb = static_cast<size_t>(m) * d * 2, actb = static_cast<size_t>(m) * ff * 2;
+    const size_t slab = static_cast<size_t>(m) * d;
+    const int m_tiles = (m + 127) / 128;
+    if (!dx.alloc(xb) || !dact.alloc(actb) || !dslab.alloc(slab * splits * 4) ||
+        !dready.alloc(static_cast<size_t>(m_tiles) * splits * 4) || !dstat.alloc(4))
+      return set_error("cudaMalloc failed");
+    if (!upload_packed(wdtype, up_codes, up_scales, 2 * ff, d, &dwu) ||
+        !upload_packed(wdtype, down_codes, down_scales, d, ff, &dwd))
+      return set_error("packing the weights failed");
+    CUDA_TRY(cudaMemcpy(dx.p, x, xb, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemset(dready.p, 0, static_cast<size_t>(m_tiles) * splits * 4));
+    CUDA_TRY(cudaMemset(dstat.p, 0, 4));
+    GemmPlan up, down;
+    char err[256];
+    if (!gemm_plan_packed(&up, dx.p, m, d, dwu.p, wdtype, 2 * ff, ff, d, kEpiGeGluTanh, 256, 1, err,
+                          sizeof err) ||
+        !gemm_plan_packed(&down, dact.p, m, ff, dwd.p, wdtype, d, d, ff, kEpiF32, 256, splits, err,
+                          sizeof err))
+      return set_error(err);
+    if (!gemm_mlp_ok(up, down)) return set_error("debug_mlp_q: shapes not fusable");
+    gemm_run_mlp(up, down, m, dact.p, ff, dslab.p, d, slab, static_cast<int*>(dready.p),
+                 4 * up.s.n_tiles / down.s.splits, static_cast<uint32_t*>(dstat.p), 0, 0);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaDeviceSynchronize());
+    uint32_t st = 0;
+    CUDA_TRY(cudaMemcpy(&st, dstat.p, 4, cudaMemcpyDeviceToHost));
+    if (st) return set_error("mlp kernel reported device status %u", st);
+    CUDA_TRY(cudaMemcpy(act_out, dact.p, actb, cudaMemcpyDeviceToHost));
+    std::vector<float> h(slab * splits);
+    CUDA_TRY(cudaMemcpy(h.data(), dslab.p, h.size() * 4, cudaMemcpyDeviceToHost));
+    for (size_t i = 0; i < slab; ++i) {
+      float v = h[i];
+      for (int z = 1; z < splits; ++z) v += h[z * slab + i];
+      y_out[i] = v;
+    }
     return 0;
   });
 }

@@ -1,5 +1,6 @@
 // The decoder engine (see engine.h). Reference: crates/omg-wgpu/src/engine.rs.
 #include "engine.h"
+#include "packed.cuh"
 
 #include <sys/stat.h>
 
@@ -262,8 +263,9 @@ void EngineBuilder::push(const std::string& name, const HostTensor& t) {
     pushed_[name] = true;
     return;
   }
-  // A linear: dequantize into its f16 layout (bit-exact QTensor::get rounded
-  // to f16, what weight.wgsl's dq*_pair decoders produce per use).
+  // A linear. Q4_0 / Q8_0: kept packed in the GEMMs' chunk layout, decoded
+  // per tile in shared memory (weight.wgsl decodes per use, too); f16: kept
+  // as f16 rows.
   const int rows = static_cast<int>(t.shape[0]), k = static_cast<int>(t.shape[1]);
   DevBuffer codes, scales;
   codes.alloc(t.data.size(), false);
@@ -280,6 +282,35 @@ void EngineBuilder::push(const std::string& name, const HostTensor& t) {
     remap = ends_with(name, ".gate") ? 1 : 2;
     out_rows = static_cast<size_t>((rows + 127) / 128) * 256;
   }
+  auto pit = pk_.find(key);
+  if (t.dtype != 0 && !lin_.count(key) && (pit == pk_.end() || pit->second.dtype == t.dtype)) {
+    if (pit == pk_.end()) {
+      PackedLinear w;
+      w.dtype = t.dtype;
+      w.rows = static_cast<int>(out_rows);
+      w.k = k;
+      w.chunks.alloc(packed_bytes(t.dtype, w.rows, k), true);
+      pit = pk_.emplace(key, std::move(w)).first;
+    }
+    launch_pack_weight(t.dtype, codes.p, scales.p, rows, k, remap, pit->second.rows,
+                       pit->second.chunks.as<uint8_t>(), stream_);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaStreamSynchronize(stream_));
+    pushed_[name] = true;
+    return;
+  }
+  if (pit != pk_.end()) {
+    // Gate and up of different dtypes: the pair is kept as f16 rows.
+    DevBuffer b;
+    b.alloc(out_rows * k * 2, true);
+    launch_unpack_weight(pit->second.dtype, pit->second.chunks.as<uint8_t>(), pit->second.rows, k,
+                         b.as<__half>(), stream_);
+    CUDA_TRY(cudaGetLastError());
+    lin_.emplace(key, std::move(b));
+    pk_.erase(pit);
+  }
+  // f16 rows: bit-exact QTensor::get rounded to f16, what weight.wgsl's
+  // dq*_pair decoders produce per use.
   auto lit = lin_.find(key);
   if (lit == lin_.end()) {
     DevBuffer b;
@@ -321,6 +352,7 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
   stream_ = b.stream_;
   b.stream_ = nullptr;
   lin_ = std::move(b.lin_);
+  pk_ = std::move(b.pk_);
   norms_ = std::move(b.norms_);
   embed_.dtype = b.embed_.dtype;
   embed_.codes = std::move(b.embed_.codes);
@@ -391,10 +423,10 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
   for (auto& e : events_) CUDA_TRY(cudaEventCreate(&e));
 
   auto norm = [&](const std::string& n) -> const float* { return norms_.at(n).as<float>(); };
-  auto lin = [&](const std::string& n) -> const __half* { return lin_.at(n).as<__half>(); };
+  auto lin = [&](const std::string& n) { return weight(n); };
   final_norm_ = norm("final_norm");
   char err[512];
-  auto plan = [&](GemmPlan* p, const void* a, int lda, const __half* w, int w_rows, int n_out,
+  auto plan = [&](GemmPlan* p, const void* a, int lda, const WeightRef& w, int w_rows, int n_out,
                   int k, int epi, const char* what, int l, int force_splits = 0) {
     int bn = 256, splits = 1;
     if (epi == kEpiF32) gemm_pick(n_out, k, num_sms_, &bn, &splits);
@@ -402,12 +434,19 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
       bn = 256;
       splits = force_splits;
     }
-    if (!gemm_plan(p, a, static_cast<int>(C), lda, w, w_rows, n_out, k, epi, bn,
+    if (w.pk != kF16) {
+      // Packed Q4_0 / Q8_0 weights: decoded per tile in shared memory.
+      if (!gemm_plan_packed(p, a, static_cast<int>(C), lda, w.p, w.pk, w_rows, n_out, k, epi, bn,
+                            std::min(splits, S), err, sizeof err))
+        fail("layer %d %s: %s", l, what, err);
+      return;
+    }
+    if (!gemm_plan(p, a, static_cast<int>(C), lda, w.p, w_rows, n_out, k, epi, bn,
                    std::min(splits, S), err, sizeof err))
       fail("layer %d %s: %s", l, what, err);
     // Passes of many rows (a long state's prefill) take the CTA-pair kernel.
     if (p->s.bn == 256 &&
-        !gemm_plan_pair(p, w, w_rows, false, err, sizeof err))
+        !gemm_plan_pair(p, w.p, w_rows, false, err, sizeof err))
       fail("layer %d %s: %s", l, what, err);
   };
   layers_.resize(L);
@@ -429,17 +468,15 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
     ly.next_norm = l + 1 == L ? final_norm_ : norm("blk." + std::to_string(l + 1) + ".attn_norm");
     auto sc = b.scalars_.find(n("out_scale"));
     ly.out_scale = sc == b.scalars_.end() ? 1.f : sc->second;
-    ly.w_qkv = lin(n("qkv"));
-    ly.w_o = lin(n("o"));
-    ly.w_gu = lin(n("gate_up"));
-    ly.w_down = lin(n("down"));
+    const WeightRef w_qkv = lin(n("qkv")), w_o = lin(n("o")), w_gu = lin(n("gate_up")),
+                    w_down = lin(n("down"));
     const int attn_w = c.heads * ly.hd;
     // 256-dim heads: q/k norm, RoPE and the K/V-cache write ride in the
     // projection's epilogue (one 256-column tile per head).
-    plan(&ly.qkv, h16_.p, d, ly.w_qkv, ly.qkv_w, ly.qkv_w, d,
+    plan(&ly.qkv, h16_.p, d, w_qkv, ly.qkv_w, ly.qkv_w, d,
          ly.hd == 256 ? kEpiQkPrep : kEpiF32, "qkv", l);
-    plan(&ly.o, attn16_.p, attn_w, ly.w_o, d, d, attn_w, kEpiF32, "o", l);
-    plan(&ly.gate_up, h16_.p, d, ly.w_gu, (ly.ff + 127) / 128 * 256, ly.ff, d, kEpiGeGluTanh,
+    plan(&ly.o, attn16_.p, attn_w, w_o, d, d, attn_w, kEpiF32, "o", l);
+    plan(&ly.gate_up, h16_.p, d, w_gu, (ly.ff + 127) / 128 * 256, ly.ff, d, kEpiGeGluTanh,
          "gate_up", l);
     // The down projection joins gate_up's launch when its split-K units run
     // as many K blocks as a gate_up tile (a split count that depends on the
@@ -447,11 +484,11 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
     const int kb_up = (d + 63) / 64, kb_dn = (ly.ff + 63) / 64;
     const int fuse_splits = kb_dn % kb_up == 0 ? kb_dn / kb_up : 0;
     if (fuse_splits >= 1 && fuse_splits <= S) {
-      plan(&ly.down, act16_.p, ly.ff, ly.w_down, d, d, ly.ff, kEpiF32, "down", l, fuse_splits);
+      plan(&ly.down, act16_.p, ly.ff, w_down, d, d, ly.ff, kEpiF32, "down", l, fuse_splits);
       ly.fused_mlp = gemm_mlp_ok(ly.gate_up, ly.down);
     }
     if (!ly.fused_mlp)
-      plan(&ly.down, act16_.p, ly.ff, ly.w_down, d, d, ly.ff, kEpiF32, "down", l);
+      plan(&ly.down, act16_.p, ly.ff, w_down, d, d, ly.ff, kEpiF32, "down", l);
     if (P > 0) {
       ly.pl_norm = norm(n("pl_norm"));
       plan(&ly.pl_gate, x16_.p, d, lin(n("pl_gate")), P, P, d, kEpiF32, "pl_gate", l);
@@ -529,6 +566,14 @@ std::vector<uint8_t> Engine::gather_per_layer(const uint32_t* ids, size_t n) con
   return out;
 }
 
+Engine::WeightRef Engine::weight(const std::string& name) const {
+  auto pit = pk_.find(name);
+  if (pit != pk_.end()) return {pit->second.dtype, pit->second.chunks.p};
+  auto it = lin_.find(name);
+  if (it == lin_.end()) fail("no device weight %s", name.c_str());
+  return {kF16, it->second.p};
+}
+
 std::vector<uint16_t> Engine::weight_f16(const std::string& name) const {
   CUDA_TRY(cudaSetDevice(device_));
   std::vector<int64_t> shape;
@@ -539,19 +584,27 @@ std::vector<uint16_t> Engine::weight_f16(const std::string& name) const {
   const size_t rows = static_cast<size_t>(shape[0]), k = static_cast<size_t>(shape[1]);
   std::vector<uint16_t> out(rows * k);
   const bool gate = ends_with(name, ".gate"), up = ends_with(name, ".up");
-  if (!gate && !up) {
-    auto it = lin_.find(name);
-    if (it == lin_.end()) fail("weight_f16: no device weight %s", name.c_str());
-    CUDA_TRY(cudaMemcpy(out.data(), it->second.p, out.size() * 2, cudaMemcpyDeviceToHost));
-    return out;
+  const std::string key = gate || up ? name.substr(0, name.rfind('.')) + ".gate_up" : name;
+  const size_t stored_rows = gate || up ? (rows + 127) / 128 * 256 : rows;
+  std::vector<uint16_t> all(stored_rows * k);
+  auto pit = pk_.find(key);
+  if (pit != pk_.end()) {
+    // Packed: decoded by the GEMMs' tile decoder (unpack_block).
+    DevBuffer tmp;
+    tmp.alloc(all.size() * 2, false);
+    launch_unpack_weight(pit->second.dtype, pit->second.chunks.as<uint8_t>(),
+                         static_cast<int>(stored_rows), static_cast<int>(k), tmp.as<__half>(),
+                         stream_);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaStreamSynchronize(stream_));
+    CUDA_TRY(cudaMemcpy(all.data(), tmp.p, all.size() * 2, cudaMemcpyDeviceToHost));
+  } else {
+    auto it = lin_.find(key);
+    if (it == lin_.end()) fail("weight_f16: no device weight %s", key.c_str());
+    CUDA_TRY(cudaMemcpy(all.data(), it->second.p, all.size() * 2, cudaMemcpyDeviceToHost));
   }
+  if (!gate && !up) return all;
   // Gate and up rows interleave in 256-row blocks [128 gate | 128 up].
-  const std::string key = name.substr(0, name.rfind('.')) + ".gate_up";
-  auto it = lin_.find(key);
-  if (it == lin_.end()) fail("weight_f16: no device weight %s", key.c_str());
-  const size_t blocks = (rows + 127) / 128;
-  std::vector<uint16_t> all(blocks * 256 * k);
-  CUDA_TRY(cudaMemcpy(all.data(), it->second.p, all.size() * 2, cudaMemcpyDeviceToHost));
   for (size_t r = 0; r < rows; ++r) {
     const size_t src = (r / 128) * 256 + (up ? 128 : 0) + r % 128;
     std::memcpy(out.data() + r * k, all.data() + src * k, k * 2);

@@ -146,12 +146,20 @@ class EngineBuilder {
     int dtype = 0;
     DevBuffer codes, scales;
   };
+  // A Q4_0 / Q8_0 linear kept packed in the GEMMs' chunk layout (packed.cuh).
+  struct PackedLinear {
+    int dtype = 0;
+    int rows = 0;  // rows as stored (gate_up: interleaved, padded to 256-row blocks)
+    int k = 0;
+    DevBuffer chunks;
+  };
   Config cfg_;
   int device_;
   cudaStream_t stream_ = nullptr;
   std::map<std::string, std::vector<int64_t>> expected_;
   std::map<std::string, bool> pushed_;
-  std::map<std::string, DevBuffer> lin_;    // f16 dequantized linears (gate+up interleaved as "blk.N.gate_up")
+  std::map<std::string, DevBuffer> lin_;    // f16 linears (gate+up interleaved as "blk.N.gate_up")
+  std::map<std::string, PackedLinear> pk_;  // Q4_0 / Q8_0 linears, packed
   std::map<std::string, DevBuffer> norms_;  // f32 norm weights
   std::map<std::string, float> scalars_;
   Packed embed_;
@@ -217,9 +225,14 @@ class Engine {
   friend class EngineBuilder;
   Engine(EngineBuilder&& b, size_t capacity, size_t max_rows);
 
+  // A linear's device weight: f16 rows (pk kF16) or packed chunks.
+  struct WeightRef {
+    int pk = 0;
+    const void* p = nullptr;
+  };
+  WeightRef weight(const std::string& name) const;
   struct Layer {
     GemmPlan qkv, o, gate_up, down, pl_gate, pl_proj;
-    const __half *w_qkv = nullptr, *w_o = nullptr, *w_gu = nullptr, *w_down = nullptr;
     const float *attn_norm, *q_norm, *k_norm, *post_attn_norm, *ffn_norm, *post_ffn_norm;
     const float *pl_norm = nullptr;
     const float* next_norm;  // the norm that reads the stream after this layer
@@ -304,6 +317,7 @@ class Engine {
   int num_sms_ = 148;
   cudaStream_t stream_ = nullptr;
   std::map<std::string, DevBuffer> lin_, norms_;
+  std::map<std::string, EngineBuilder::PackedLinear> pk_;
   EngineBuilder::Packed embed_;
   std::optional<HostTensor> per_layer_table_;
   std::vector<Layer> layers_;

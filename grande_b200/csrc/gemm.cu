@@ -7,6 +7,7 @@
 // grid covers the 148 SMs.
 #include "gemm.cuh"
 #include "launch.cuh"
+#include "packed.cuh"
 #include "ptx.cuh"
 #include <cudaTypedefs.h>
 #include <cstdio>
@@ -34,6 +35,7 @@ struct GemmArgs {
   size_t split_stride;
   uint32_t* status;
   GemmEpi epi;
+  const uint8_t* wpack;  // packed weight chunks (packed kernels only)
 };
 
 // Tile t of a launch: split-major, then (m fastest) or (n fastest).
@@ -54,18 +56,118 @@ __device__ __forceinline__ TileId decode_tile(const GemmArgs& g, int t) {
   return x;
 }
 
-template <int BN>
+// PK: where the weight tile comes from. kF16: a TMA load of row-major f16
+// weights. kQ4 / kQ8: packed chunks (packed.cuh) fetched by a bulk copy into
+// a raw ring and decoded into the swizzled f16 tile by four converter warps.
+template <int BN, int PK = kF16>
 struct Cfg {
-  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr bool PACKED = PK != kF16;
+  static constexpr int STAGES = PACKED ? (BN == 256 ? 3 : 4) : (BN == 256 ? 4 : 6);
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int CHUNK = PK == kQ4 ? PackChunk<kQ4>::BYTES
+                                         : (PK == kQ8 ? PackChunk<kQ8>::BYTES : 0);
+  static constexpr int RAW_BYTES = (BN / 128) * CHUNK;
+  static constexpr int RAW_STAGES = !PACKED ? 0 : (PK == kQ8 && BN == 256 ? 3 : 6);
+  static constexpr int RING = STAGES * STAGE_BYTES + RAW_STAGES * RAW_BYTES;
   // Ring + alignment slack + barriers, 2 KB the epilogue may stage its
   // per-column constants in (the q / k norm weights of kEpiQkPrep), and a
   // 4 KB row-staging slot per epilogue warp.
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + 2048 + 4 * 4096;
+  static constexpr int SMEM = RING + 1024 + 256 + 2048 + 4 * 4096;
   // Two accumulators: the epilogue drains one while the MMAs fill the other.
   static constexpr uint32_t TMEM_COLS = 2 * BN;
+  // Warps: 0 TMA (A, and B when f16), 1 MMA, 2-5 epilogue; packed: 6 bulk
+  // copies of the raw chunks, 7-10 converters.
+  static constexpr int THREADS = PACKED ? 352 : 192;
+  static_assert(SMEM <= 232448, "shared memory");
+  static_assert(2 * STAGES + 4 + 2 * RAW_STAGES <= 30, "barrier area");
+};
+
+// Shared-memory carve-up of the one-CTA kernels.
+template <int BN, int PK>
+struct Smem {
+  using C = Cfg<BN, PK>;
+  uint8_t *sa, *sb, *raw;
+  uint64_t *full, *empty, *tfull, *tempty, *raw_full, *raw_empty;
+  uint32_t* tmem_slot;
+  volatile int* abort_flag;
+  float* epi_consts;
+  uint8_t* slots;
+  __device__ explicit Smem(uint8_t* smem) {
+    sa = smem;
+    sb = smem + C::STAGES * C::A_BYTES;
+    raw = sb + C::STAGES * C::B_BYTES;
+    uint8_t* bars = smem + C::RING;
+    full = reinterpret_cast<uint64_t*>(bars);
+    empty = full + C::STAGES;
+    tfull = empty + C::STAGES;  // [2] accumulator ready
+    tempty = tfull + 2;         // [2] accumulator drained
+    raw_full = tempty + 2;
+    raw_empty = raw_full + C::RAW_STAGES;
+    tmem_slot = reinterpret_cast<uint32_t*>(raw_empty + C::RAW_STAGES);
+    abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    epi_consts = reinterpret_cast<float*>(bars + 256);
+    slots = bars + 256 + 2048;
+  }
+};
+
+// The packed-weight side of a one-CTA kernel's pipeline, shared by its raw
+// producer warp and its converter warps. K step `it` of the CTA (counted over
+// all its tiles) uses ring slot it % STAGES and raw slot it % RAW_STAGES.
+template <int BN, int PK>
+struct PackedPipe {
+  using C = Cfg<BN, PK>;
+  // Producer (one thread): the BN / 128 chunks of weight rows
+  // [n_tile * BN, n_tile * BN + BN) at K step kb into raw slot it.
+  __device__ static bool load(const Smem<BN, PK>& sm, const uint8_t* wpack, int kb_total,
+                              int n_tile, int kb, int it, uint32_t* status) {
+    const int r = it % C::RAW_STAGES;
+    if (!mbar_wait(&sm.raw_empty[r], ((it / C::RAW_STAGES) & 1) ^ 1, sm.abort_flag, status))
+      return false;
+    mbar_arrive_expect_tx(&sm.raw_full[r], C::RAW_BYTES);
+#pragma unroll
+    for (int c = 0; c < BN / 128; ++c)
+      bulk_load(sm.raw + r * C::RAW_BYTES + c * C::CHUNK,
+                wpack + (static_cast<size_t>(n_tile * (BN / 128) + c) * kb_total + kb) * C::CHUNK,
+                C::CHUNK, &sm.raw_full[r]);
+    return true;
+  }
+  // Producer, after its last load: see the copies land before the CTA exits
+  // (they have unless the CTA gave up).
+  __device__ static void drain(const Smem<BN, PK>& sm, int issued) {
+    for (int j = issued - C::RAW_STAGES > 0 ? issued - C::RAW_STAGES : 0; j < issued; ++j)
+      if (!mbar_drain(&sm.raw_full[j % C::RAW_STAGES], (j / C::RAW_STAGES) & 1, 1ll << 24)) break;
+  }
+  // Converter warps (t = 0..127 over the four): K step `it` from its raw slot
+  // into ring slot it % STAGES (free once the MMAs of step it - STAGES are
+  // done), then arrive on full[s] and hand the raw slot back.
+  __device__ static bool convert(const Smem<BN, PK>& sm, int it, int t, uint32_t* status) {
+    const int r = it % C::RAW_STAGES, s = it % C::STAGES;
+    const uint32_t pr = (it / C::RAW_STAGES) & 1, pe = ((it / C::STAGES) & 1) ^ 1;
+    int ok = 1;
+    if ((t & 31) == 0)
+      ok = mbar_wait(&sm.raw_full[r], pr, sm.abort_flag, status) &&
+           mbar_wait(&sm.empty[s], pe, sm.abort_flag, status);
+    if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
+    // Both phases are complete (neither barrier can move on before this warp
+    // arrives): every lane observes them, acquiring the raw slot's bytes.
+    mbar_try_wait(&sm.raw_full[r], pr);
+    mbar_try_wait(&sm.empty[s], pe);
+    const uint8_t* raw = sm.raw + r * C::RAW_BYTES;
+    uint8_t* tile = sm.sb + s * C::B_BYTES;
+#pragma unroll
+    for (int c = 0; c < BN / 128; ++c) unpack_row_to_tile<PK>(raw + c * C::CHUNK, t, tile, c * 128 + t);
+    // The tile's stores to the async proxy (the MMA reads it), then one
+    // arrival per warp on each barrier.
+    fence_proxy_async();
+    __syncwarp();
+    if ((t & 31) == 0) {
+      mbar_arrive(&sm.full[s]);
+      mbar_arrive(&sm.raw_empty[r]);
+    }
+    return true;
+  }
 };
 
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -577,23 +679,24 @@ __device__ __forceinline__ void residual_prefetch(const GemmArgs& g, int tile, i
 
 // Persistent: CTA b handles tiles b, b + gridDim.x, ... in decode_tile's
 // order.
-template <int BN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+template <int BN, int EPI, int PK>
+__global__ void __launch_bounds__(Cfg<BN, PK>::THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
                 GemmArgs g) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, PK>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sa = smem;
-  uint8_t* sb = smem + C::STAGES * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sb + C::STAGES * C::B_BYTES);
-  uint64_t* empty = full + C::STAGES;
-  uint64_t* tfull = empty + C::STAGES;   // [2] accumulator ready
-  uint64_t* tempty = tfull + 2;          // [2] accumulator drained
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* epi_consts = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);
+  const Smem<BN, PK> sm(smem);
+  uint8_t* sa = sm.sa;
+  uint8_t* sb = sm.sb;
+  uint64_t* full = sm.full;
+  uint64_t* empty = sm.empty;
+  uint64_t* tfull = sm.tfull;
+  uint64_t* tempty = sm.tempty;
+  uint32_t* tmem_slot = sm.tmem_slot;
+  volatile int* abort_flag = sm.abort_flag;
+  float* epi_consts = sm.epi_consts;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -601,17 +704,22 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(&full[s], 1);
+      // Packed: the TMA bytes of A plus one arrival per converter warp.
+      mbar_init(&full[s], C::PACKED ? 5 : 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 4);
     }
+    for (int r = 0; r < C::RAW_STAGES; ++r) {
+      mbar_init(&sm.raw_full[r], 1);
+      mbar_init(&sm.raw_empty[r], 4);
+    }
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&tma);
-    prefetch_tmap(&tmb);
+    if constexpr (!C::PACKED) prefetch_tmap(&tmb);
   }
   if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
   tc_fence_before();
@@ -619,9 +727,10 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   // Operands and residual rows come from earlier kernels (programmatic
-  // dependent launch: the prologue above may overlap their tail). The grid
-  // is persistent (one wave), so the next kernel may begin launching now.
-  griddep_wait();
+  // dependent launch: the prologue above may overlap their tail); the packed
+  // weights never change during a pass, so their copies start at once. The
+  // grid is persistent (one wave), so the next kernel may begin launching now.
+  if (!(C::PACKED && warp == 6)) griddep_wait();
   griddep_launch();
 
   if (warp == 0) {
@@ -640,9 +749,14 @@ __global__ void __launch_bounds__(192, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-          tma_load_2d(sa + s * C::A_BYTES, &tma, &full[s], kb * BK, m_tile * BM);
-          tma_load_2d(sb + s * C::B_BYTES, &tmb, &full[s], kb * BK, n_tile * BN);
+          if constexpr (C::PACKED) {
+            mbar_arrive_expect_tx(&full[s], C::A_BYTES);
+            tma_load_2d(sa + s * C::A_BYTES, &tma, &full[s], kb * BK, m_tile * BM);
+          } else {
+            mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+            tma_load_2d(sa + s * C::A_BYTES, &tma, &full[s], kb * BK, m_tile * BM);
+            tma_load_2d(sb + s * C::B_BYTES, &tmb, &full[s], kb * BK, n_tile * BN);
+          }
         }
         if (!ok) break;
       }
@@ -679,7 +793,7 @@ __global__ void __launch_bounds__(192, 1)
         umma_commit(&tfull[b]);
       }
     }
-  } else {
+  } else if (warp < 6) {
     // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +32, one row per thread.
     const int q = warp & 3;
     if constexpr (EPI == kEpiQkPrep) {
@@ -703,7 +817,7 @@ __global__ void __launch_bounds__(192, 1)
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-      uint8_t* slot = reinterpret_cast<uint8_t*>(full) + 256 + 2048 + q * 4096;
+      uint8_t* slot = sm.slots + q * 4096;
       const uint32_t tbase =
           tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BN);
       epilogue_tile<BN, EPI>(g, m_tile, n_tile, split, tbase, q, lane, slot, epi_consts);
@@ -711,6 +825,34 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
+    }
+  } else if constexpr (C::PACKED) {
+    if (warp == 6) {
+      // Bulk copies of the packed weight chunks, up to RAW_STAGES K steps ahead.
+      if (lane == 0) {
+        int it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < total && ok && !*abort_flag; tile += gridDim.x) {
+          const TileId id = decode_tile(g, tile);
+          const int kb0 = id.split * g.kb_per_split;
+          const int kb1 = min(g.kb_total, kb0 + g.kb_per_split);
+          for (int kb = kb0; kb < kb1 && ok; ++kb, ++it)
+            ok = PackedPipe<BN, PK>::load(sm, g.wpack, g.kb_total, id.n, kb, it, g.status);
+        }
+        PackedPipe<BN, PK>::drain(sm, it);
+      }
+    } else {
+      // Converters: chunk row t of each K step into the swizzled f16 tile.
+      const int t = threadIdx.x - 224;
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        const TileId id = decode_tile(g, tile);
+        const int kb0 = id.split * g.kb_per_split;
+        const int kb1 = min(g.kb_total, kb0 + g.kb_per_split);
+        for (int kb = kb0; kb < kb1 && ok; ++kb, ++it)
+          ok = PackedPipe<BN, PK>::convert(sm, it, t, g.status);
+      }
     }
   }
   tc_fence_before();
@@ -953,26 +1095,27 @@ struct MlpArgs {
   int band;  // up column tiles per down split
 };
 
-template <int EPI_UP>
-__global__ void __launch_bounds__(192, 1)
+template <int EPI_UP, int PK>
+__global__ void __launch_bounds__(Cfg<256, PK>::THREADS, 1)
     gemm_mlp_kernel(const __grid_constant__ CUtensorMap ta_up,
                     const __grid_constant__ CUtensorMap tb_up,
                     const __grid_constant__ CUtensorMap ta_dn,
                     const __grid_constant__ CUtensorMap tb_dn, MlpArgs g) {
   constexpr int BN = 256;
-  using C = Cfg<BN>;
+  using C = Cfg<BN, PK>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sa = smem;
-  uint8_t* sb = smem + C::STAGES * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sb + C::STAGES * C::B_BYTES);
-  uint64_t* empty = full + C::STAGES;
-  uint64_t* tfull = empty + C::STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* epi_consts = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);
+  const Smem<BN, PK> sm(smem);
+  uint8_t* sa = sm.sa;
+  uint8_t* sb = sm.sb;
+  uint64_t* full = sm.full;
+  uint64_t* empty = sm.empty;
+  uint64_t* tfull = sm.tfull;
+  uint64_t* tempty = sm.tempty;
+  uint32_t* tmem_slot = sm.tmem_slot;
+  volatile int* abort_flag = sm.abort_flag;
+  float* epi_consts = sm.epi_consts;
   uint32_t* status = g.up.status;
 
   const int warp = threadIdx.x >> 5;
@@ -1008,26 +1151,32 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], C::PACKED ? 5 : 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 4);
     }
+    for (int r = 0; r < C::RAW_STAGES; ++r) {
+      mbar_init(&sm.raw_full[r], 1);
+      mbar_init(&sm.raw_empty[r], 4);
+    }
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&ta_up);
-    prefetch_tmap(&tb_up);
     prefetch_tmap(&ta_dn);
-    prefetch_tmap(&tb_dn);
+    if constexpr (!C::PACKED) {
+      prefetch_tmap(&tb_up);
+      prefetch_tmap(&tb_dn);
+    }
   }
   if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  griddep_wait();
+  if (!(C::PACKED && warp == 6)) griddep_wait();
   griddep_launch();
 
   if (warp == 0) {
@@ -1067,9 +1216,14 @@ __global__ void __launch_bounds__(192, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-          tma_load_2d(sa + s * C::A_BYTES, ta, &full[s], kb * BK, x.m * BM);
-          tma_load_2d(sb + s * C::B_BYTES, tb, &full[s], kb * BK, x.n * BN);
+          if constexpr (C::PACKED) {
+            mbar_arrive_expect_tx(&full[s], C::A_BYTES);
+            tma_load_2d(sa + s * C::A_BYTES, ta, &full[s], kb * BK, x.m * BM);
+          } else {
+            mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+            tma_load_2d(sa + s * C::A_BYTES, ta, &full[s], kb * BK, x.m * BM);
+            tma_load_2d(sb + s * C::B_BYTES, tb, &full[s], kb * BK, x.n * BN);
+          }
         }
         if (!ok) break;
       }
@@ -1104,7 +1258,7 @@ __global__ void __launch_bounds__(192, 1)
         umma_commit(&tfull[b]);
       }
     }
-  } else {
+  } else if (warp < 6) {
     const int q = warp & 3;
     int local = 0;
     for (int u = blockIdx.x; u < total; u += gridDim.x, ++local) {
@@ -1115,7 +1269,7 @@ __global__ void __launch_bounds__(192, 1)
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-      uint8_t* slot = reinterpret_cast<uint8_t*>(full) + 256 + 2048 + q * 4096;
+      uint8_t* slot = sm.slots + q * 4096;
       const uint32_t tbase =
           tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BN);
       if (x.up) {
@@ -1132,6 +1286,31 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
+    }
+  } else if constexpr (C::PACKED) {
+    if (warp == 6) {
+      // The weight chunks of every unit (they do not wait for the
+      // activations: a down unit's weights arrive while its band finishes).
+      if (lane == 0) {
+        int it = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < total && ok && !*abort_flag; u += gridDim.x) {
+          const Unit x = decode(u);
+          const GemmArgs& ga = x.up ? g.up : g.down;
+          for (int kb = x.kb0; kb < x.kb1 && ok; ++kb, ++it)
+            ok = PackedPipe<BN, PK>::load(sm, ga.wpack, ga.kb_total, x.n, kb, it, status);
+        }
+        PackedPipe<BN, PK>::drain(sm, it);
+      }
+    } else {
+      const int t = threadIdx.x - 224;
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        const Unit x = decode(u);
+        for (int kb = x.kb0; kb < x.kb1 && ok; ++kb, ++it)
+          ok = PackedPipe<BN, PK>::convert(sm, it, t, status);
+      }
     }
   }
   tc_fence_before();
@@ -1370,10 +1549,22 @@ bool make_tmap_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t out
 // N-fastest tile order when the A rows outweigh the weight rows four to one.
 int n_fast_order(int m, int n) { return static_cast<int64_t>(m) > 4 * static_cast<int64_t>(n) ? 1 : 0; }
 
+// The epilogues that have packed-weight kernels.
+constexpr bool packed_epi(int epi) {
+  return epi == kEpiF32 || epi == kEpiF16 || epi == kEpiGeGluTanh || epi == kEpiGeGluErf ||
+         epi == kEpiQkPrep;
+}
+
 template <int BN, int EPI>
 void set_smem_attr() {
-  cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaFuncSetAttribute(gemm_kernel<BN, EPI, kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        Cfg<BN>::SMEM);
+  if constexpr (packed_epi(EPI)) {
+    cudaFuncSetAttribute(gemm_kernel<BN, EPI, kQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         Cfg<BN, kQ4>::SMEM);
+    cudaFuncSetAttribute(gemm_kernel<BN, EPI, kQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         Cfg<BN, kQ8>::SMEM);
+  }
 }
 
 template <int EPI>
@@ -1389,11 +1580,23 @@ void launch_pair(const GemmPlan& p, const GemmArgs& a, cudaStream_t stream) {
   launch_pdl(gemm2_kernel<EPI>, dim3(grid), dim3(192), Cfg2::SMEM, stream, p.a, p.b_half, a);
 }
 
+template <int BN, int EPI, int PK>
+void launch_pk(const GemmPlan& p, const GemmArgs& a, int grid, cudaStream_t stream) {
+  using C = Cfg<BN, PK>;
+  launch_pdl(gemm_kernel<BN, EPI, PK>, dim3(grid), dim3(C::THREADS), C::SMEM, stream, p.a, p.b, a);
+}
+
 template <int BN, int EPI>
-void launch(const GemmPlan& p, const GemmArgs& a, cudaStream_t stream) {
+void launch(const GemmPlan& p, const GemmArgs& a0, cudaStream_t stream) {
+  GemmArgs a = a0;
+  a.wpack = p.wpack;
   const int total = a.m_tiles * a.n_tiles * a.splits;
   const int grid = total < p.num_sms ? total : p.num_sms;
-  launch_pdl(gemm_kernel<BN, EPI>, dim3(grid), dim3(192), Cfg<BN>::SMEM, stream, p.a, p.b, a);
+  if constexpr (packed_epi(EPI)) {
+    if (p.pk == kQ4) return launch_pk<BN, EPI, kQ4>(p, a, grid, stream);
+    if (p.pk == kQ8) return launch_pk<BN, EPI, kQ8>(p, a, grid, stream);
+  }
+  launch_pk<BN, EPI, kF16>(p, a, grid, stream);
 }
 
 }  // namespace
@@ -1427,10 +1630,18 @@ bool make_tmap_f16(CUtensorMap* m, const void* base, int rank, const uint64_t* d
 }
 
 void gemm_setup_device() {
-  cudaFuncSetAttribute(gemm_mlp_kernel<kEpiGeGluTanh>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       Cfg<256>::SMEM);
-  cudaFuncSetAttribute(gemm_mlp_kernel<kEpiGeGluErf>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       Cfg<256>::SMEM);
+  cudaFuncSetAttribute(gemm_mlp_kernel<kEpiGeGluTanh, kF16>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<256>::SMEM);
+  cudaFuncSetAttribute(gemm_mlp_kernel<kEpiGeGluErf, kF16>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<256>::SMEM);
+  cudaFuncSetAttribute(gemm_mlp_kernel<kEpiGeGluTanh, kQ4>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<256, kQ4>::SMEM);
+  cudaFuncSetAttribute(gemm_mlp_kernel<kEpiGeGluTanh, kQ8>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<256, kQ8>::SMEM);
+  cudaFuncSetAttribute(gemm_mlp_kernel<kEpiGeGluErf, kQ4>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<256, kQ4>::SMEM);
+  cudaFuncSetAttribute(gemm_mlp_kernel<kEpiGeGluErf, kQ8>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<256, kQ8>::SMEM);
   set_smem_attr<128, kEpiF32>();
   set_smem_attr<256, kEpiF32>();
   set_smem_attr<128, kEpiF16>();
@@ -1463,6 +1674,10 @@ void gemm_setup_device() {
 
 bool gemm_plan_pair(GemmPlan* p, const void* w, int w_rows, bool always, char* err,
                     size_t errlen) {
+  if (p->pk != kF16) {
+    snprintf(err, errlen, "gemm: the CTA-pair kernel takes f16 weights");
+    return false;
+  }
   if (p->s.bn != 256) {
     snprintf(err, errlen, "gemm: the CTA-pair kernel needs BN 256 (got %d)", p->s.bn);
     return false;
@@ -1512,9 +1727,32 @@ void gemm_pick(int n, int k, int num_sms, int* bn, int* splits) {
   *splits = best;
 }
 
+bool gemm_plan_packed(GemmPlan* p, const void* a, int a_rows_cap, int lda, const void* wpack,
+                      int dtype, int w_rows, int n_out, int k, int epi, int bn, int splits,
+                      char* err, size_t errlen) {
+  if (dtype != kQ4 && dtype != kQ8) {
+    snprintf(err, errlen, "gemm: packed weights are Q4_0 or Q8_0 (dtype %d)", dtype);
+    return false;
+  }
+  if (!packed_epi(epi)) {
+    snprintf(err, errlen, "gemm: no packed-weight kernel for epilogue %d", epi);
+    return false;
+  }
+  if (k % 32 != 0) {
+    snprintf(err, errlen, "gemm: packed weights need K %% 32 == 0 (K %d)", k);
+    return false;
+  }
+  if (!gemm_plan(p, a, a_rows_cap, lda, nullptr, w_rows, n_out, k, epi, bn, splits, err, errlen))
+    return false;
+  p->pk = dtype;
+  p->wpack = static_cast<const uint8_t*>(wpack);
+  return true;
+}
+
 bool gemm_plan(GemmPlan* p, const void* a, int a_rows_cap, int lda, const void* w, int w_rows,
                int n_out, int k, int epi, int bn, int splits, char* err, size_t errlen) {
   memset(p, 0, sizeof(*p));
+  p->pk = kF16;
   if (k % 8 != 0 || lda % 8 != 0) {
     snprintf(err, errlen, "gemm: K %d and lda %d must be multiples of 8", k, lda);
     return false;
@@ -1548,7 +1786,8 @@ bool gemm_plan(GemmPlan* p, const void* a, int a_rows_cap, int lda, const void* 
     p->s.n_tiles = (n_out + bn - 1) / bn;
   if (!make_tmap_2d(&p->a, a, k, a_rows_cap, static_cast<uint64_t>(lda) * 2, BK, BM, err, errlen))
     return false;
-  if (!make_tmap_2d(&p->b, w, k, w_rows, static_cast<uint64_t>(k) * 2, BK, bn, err, errlen))
+  // A packed plan (w null) reads its weight through bulk copies instead.
+  if (w && !make_tmap_2d(&p->b, w, k, w_rows, static_cast<uint64_t>(k) * 2, BK, bn, err, errlen))
     return false;
   return true;
 }
@@ -1662,7 +1901,8 @@ bool gemm_mlp_ok(const GemmPlan& up, const GemmPlan& down) {
   // Down split s must read exactly the columns of up column tiles
   // [s * band, (s + 1) * band) (an up tile stores 128 activation columns).
   const int kb_split = (kb_dn + down.s.splits - 1) / down.s.splits;
-  return (up.s.epi == kEpiGeGluTanh || up.s.epi == kEpiGeGluErf) && up.s.bn == 256 &&
+  return up.pk == down.pk && (up.s.epi == kEpiGeGluTanh || up.s.epi == kEpiGeGluErf) &&
+         up.s.bn == 256 &&
          down.s.epi == kEpiF32 && down.s.bn == 256 && kb_split == kb_up &&
          kb_dn == kb_split * down.s.splits && kb_split % 2 == 0 &&
          up.s.n_tiles == down.s.splits * (kb_split / 2) && up.s.n_out == down.s.k;
@@ -1710,12 +1950,21 @@ void gemm_run_mlp(const GemmPlan& up, const GemmPlan& down, int m, void* act, in
   }
   const int total = a.up.m_tiles * a.up.n_tiles + a.down.m_tiles * a.down.n_tiles * a.down.splits;
   const int grid = total < up.num_sms ? total : up.num_sms;
-  if (up.s.epi == kEpiGeGluTanh)
-    launch_pdl(gemm_mlp_kernel<kEpiGeGluTanh>, dim3(grid), dim3(192), Cfg<256>::SMEM, stream, up.a,
-               up.b, down.a, down.b, a);
+  a.up.wpack = up.wpack;
+  a.down.wpack = down.wpack;
+  auto go = [&](auto kernel, int threads, int smem) {
+    launch_pdl(kernel, dim3(grid), dim3(threads), smem, stream, up.a, up.b, down.a, down.b, a);
+  };
+  const bool tanh_ = up.s.epi == kEpiGeGluTanh;
+  if (up.pk == kQ4)
+    tanh_ ? go(gemm_mlp_kernel<kEpiGeGluTanh, kQ4>, Cfg<256, kQ4>::THREADS, Cfg<256, kQ4>::SMEM)
+          : go(gemm_mlp_kernel<kEpiGeGluErf, kQ4>, Cfg<256, kQ4>::THREADS, Cfg<256, kQ4>::SMEM);
+  else if (up.pk == kQ8)
+    tanh_ ? go(gemm_mlp_kernel<kEpiGeGluTanh, kQ8>, Cfg<256, kQ8>::THREADS, Cfg<256, kQ8>::SMEM)
+          : go(gemm_mlp_kernel<kEpiGeGluErf, kQ8>, Cfg<256, kQ8>::THREADS, Cfg<256, kQ8>::SMEM);
   else
-    launch_pdl(gemm_mlp_kernel<kEpiGeGluErf>, dim3(grid), dim3(192), Cfg<256>::SMEM, stream, up.a,
-               up.b, down.a, down.b, a);
+    tanh_ ? go(gemm_mlp_kernel<kEpiGeGluTanh, kF16>, 192, Cfg<256>::SMEM)
+          : go(gemm_mlp_kernel<kEpiGeGluErf, kF16>, 192, Cfg<256>::SMEM);
 }
 
 }  // namespace omg

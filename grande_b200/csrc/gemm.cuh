@@ -75,11 +75,13 @@ struct GemmShape {
 // built once when the engine wires its layers.
 struct GemmPlan {
   CUtensorMap a;  // activations [rows_cap, K] f16, box 64 x 128
-  CUtensorMap b;  // weights [N_rows, K] f16, box 64 x bn
+  CUtensorMap b;  // weights [N_rows, K] f16, box 64 x bn (f16 weights)
   CUtensorMap b_half;  // the same, box 64 x 128 (each CTA of a pair loads half a tile)
   GemmShape s;
   int rows_cap;
   int num_sms;  // persistent grid size (CTAs = min(tiles, SMs))
+  int pk;       // kF16: TMA-loaded f16 weights; kQ4 / kQ8: packed chunks (packed.cuh)
+  const uint8_t* wpack;  // the packed weight (pk != kF16)
 };
 
 // Build the plan. `a_rows_cap` bounds the activation rows the tensor map
@@ -87,6 +89,16 @@ struct GemmPlan {
 // stored (for GeGLU: 2 x padded width).
 bool gemm_plan(GemmPlan* p, const void* a, int a_rows_cap, int lda, const void* w, int w_rows,
                int n_out, int k, int epi, int bn, int splits, char* err, size_t errlen);
+
+// The same over a weight kept packed as Q4_0 / Q8_0 chunks (packed.cuh;
+// `dtype` kQ4 or kQ8, `w_rows` the weight's rows, padded to whole chunks in
+// memory): the kernels fetch each K step's chunks with a bulk copy and
+// decode them into the f16 tile in shared memory, so the product is the one
+// the f16 weight gives, bit for bit. Epilogues kEpiF32, kEpiF16, the GeGLUs
+// and kEpiQkPrep; one-CTA kernels.
+bool gemm_plan_packed(GemmPlan* p, const void* a, int a_rows_cap, int lda, const void* wpack,
+                      int dtype, int w_rows, int n_out, int k, int epi, int bn, int splits,
+                      char* err, size_t errlen);
 
 // Switch a BN-256 plan to the CTA-pair kernel: two CTAs on one TPC share a
 // 256 x 256 tile, each staging its own 128 rows of A and 128 of the 256

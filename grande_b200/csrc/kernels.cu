@@ -3,6 +3,7 @@
 #include <algorithm>
 
 #include "kernels.cuh"
+#include "packed.cuh"
 #include "launch.cuh"
 #include "ptx.cuh"
 #include "quant.cuh"
@@ -897,7 +898,74 @@ __global__ void table_hilo_kernel(const uint8_t* __restrict__ codes,
   }
 }
 
+// One thread per (row, 32-element block) of the pushed weight: its codes
+// and scale into the chunk layout of packed.cuh.
+template <int DT>
+__global__ void pack_weight_kernel(const uint8_t* __restrict__ codes,
+                                   const uint8_t* __restrict__ scales, int rows, int k, int remap,
+                                   uint8_t* __restrict__ out) {
+  using P = PackChunk<DT>;
+  const int kb32 = k / 32, ksteps = (k + 63) / 64;
+  const size_t nblk = static_cast<size_t>(rows) * kb32;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < nblk;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / kb32), blk = static_cast<int>(i % kb32);
+    const int dr = remap_row(r, remap);
+    uint8_t* chunk = out + (static_cast<size_t>(dr / 128) * ksteps + blk / 2) * P::BYTES;
+    const int b = blk & 1, cr = dr % 128;
+    const uint4* src = reinterpret_cast<const uint4*>(codes + i * P::CODE_BYTES);
+    uint4* dst = reinterpret_cast<uint4*>(chunk + (b * 128 + cr) * P::CODE_BYTES);
+    dst[0] = src[0];
+    if constexpr (DT == kQ8) dst[1] = src[1];
+    *reinterpret_cast<uint16_t*>(chunk + P::CODES + (b * 128 + cr) * 2) =
+        static_cast<uint16_t>(scales[2 * i]) | (static_cast<uint16_t>(scales[2 * i + 1]) << 8);
+  }
+}
+
+// One thread per (row, 32-element block): the GEMM's tile decoder, written
+// row-major.
+template <int DT>
+__global__ void unpack_weight_kernel(const uint8_t* __restrict__ packed, int rows, int k,
+                                     __half* __restrict__ out) {
+  using P = PackChunk<DT>;
+  const int kb32 = k / 32, ksteps = (k + 63) / 64;
+  const size_t nblk = static_cast<size_t>(rows) * kb32;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < nblk;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / kb32), blk = static_cast<int>(i % kb32);
+    const uint8_t* chunk = packed + (static_cast<size_t>(r / 128) * ksteps + blk / 2) * P::BYTES;
+    uint4 pc[4];
+    unpack_block<DT>(chunk, r % 128, blk & 1, pc);
+    uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(r) * k + blk * 32);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j] = pc[j];
+  }
+}
+
 }  // namespace
+
+void launch_pack_weight(int dtype, const void* codes, const void* scales, int rows, int k,
+                        int remap, int out_rows, uint8_t* out, cudaStream_t s) {
+  (void)out_rows;
+  const size_t nblk = static_cast<size_t>(rows) * (k / 32);
+  const int grid = static_cast<int>(std::min<size_t>((nblk + 255) / 256, 148 * 16));
+  const auto* c = static_cast<const uint8_t*>(codes);
+  const auto* sc = static_cast<const uint8_t*>(scales);
+  if (dtype == kQ4)
+    pack_weight_kernel<kQ4><<<grid, 256, 0, s>>>(c, sc, rows, k, remap, out);
+  else
+    pack_weight_kernel<kQ8><<<grid, 256, 0, s>>>(c, sc, rows, k, remap, out);
+}
+
+void launch_unpack_weight(int dtype, const uint8_t* packed, int rows, int k, __half* out,
+                          cudaStream_t s) {
+  const size_t nblk = static_cast<size_t>(rows) * (k / 32);
+  const int grid = static_cast<int>(std::min<size_t>((nblk + 255) / 256, 148 * 16));
+  if (dtype == kQ4)
+    unpack_weight_kernel<kQ4><<<grid, 256, 0, s>>>(packed, rows, k, out);
+  else
+    unpack_weight_kernel<kQ8><<<grid, 256, 0, s>>>(packed, rows, k, out);
+}
 
 void launch_table_hilo(int dtype, const void* codes, const void* scales, size_t n, __half* hi,
                        __half* lo, cudaStream_t s) {

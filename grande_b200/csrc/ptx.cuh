@@ -110,6 +110,27 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* tmap, ui
       : "memory");
 }
 
+// Contiguous bulk copy global -> this CTA's shared memory (16-byte aligned
+// addresses, a multiple of 16 bytes), completing on `bar`'s transaction count.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Wait for phase `parity` of `bar` whatever the CTA's abort flag says, for at
+// most `limit` clocks: a CTA that gave up waits this way for copies it issued
+// into its own shared memory to land before it exits.
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity, long long limit) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity))
+    if (clock64() - t0 > limit) return false;
+  return true;
+}
+
 // Programmatic dependent launch: wait until the grids this one depends on
 // have completed and their writes are visible (a no-op when the launch had no
 // such dependency), and let the next grid in the stream start launching.

@@ -341,11 +341,12 @@ int omg_state_to_bytes(const omg_state* s, const char* model_id, uint8_t* buf, s
                        size_t* needed) {
   return guarded([&] {
     if (!s) fail("state is null");
-    auto b = s->s.to_bytes(model_id ? model_id : "");
-    if (needed) *needed = b.size();
+    const std::string id = model_id ? model_id : "";
+    const size_t len = s->s.file_len(id);
+    if (needed) *needed = len;
     if (buf) {
-      if (cap < b.size()) fail("buffer holds %zu bytes, the state needs %zu", cap, b.size());
-      std::memcpy(buf, b.data(), b.size());
+      if (cap < len) fail("buffer holds %zu bytes, the state needs %zu", cap, len);
+      s->s.write_bytes(id, buf);
     }
     return 0;
   });

@@ -9,6 +9,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <sstream>
@@ -64,34 +65,132 @@ float HostTensor::get(size_t i) const {
   return blk[i % 32];
 }
 
+// ---- page-locked host blocks --------------------------------------------------
+
+namespace {
+
+// Page-locked blocks for saved states, reused across saves: pinning fresh
+// memory costs more than copying 50 MB over the host link, so freed blocks
+// (sizes rounded up to 1 MiB) go back to a pool that keeps up to 1 GiB idle.
+// The pool is never destroyed (blocks may be freed after the CUDA runtime
+// has begun to shut down at exit).
+class HostBlocks {
+ public:
+  static HostBlocks& get() {
+    static HostBlocks* pool = new HostBlocks();
+    return *pool;
+  }
+  std::shared_ptr<uint8_t> take(size_t n) {
+    const size_t size = (std::max<size_t>(n, 1) + kStep - 1) / kStep * kStep;
+    uint8_t* p = nullptr;
+    size_t got = size;
+    {
+      std::lock_guard<std::mutex> g(mu_);
+      // The smallest idle block that holds `size` without wasting half of it.
+      auto best = free_.end();
+      for (auto it = free_.begin(); it != free_.end(); ++it)
+        if (it->second >= size && it->second <= 2 * size &&
+            (best == free_.end() || it->second < best->second))
+          best = it;
+      if (best != free_.end()) {
+        p = best->first;
+        got = best->second;
+        idle_ -= got;
+        free_.erase(best);
+      }
+    }
+    bool pinned = true;
+    if (!p && cudaHostAlloc(reinterpret_cast<void**>(&p), size, cudaHostAllocPortable) !=
+                  cudaSuccess) {
+      // Out of page-locked memory: pageable memory still works (slower copies).
+      (void)cudaGetLastError();
+      p = static_cast<uint8_t*>(std::malloc(size));
+      pinned = false;
+      if (!p) fail("out of host memory for a %zu-byte state", size);
+    }
+    return std::shared_ptr<uint8_t>(p, [this, got, pinned](uint8_t* q) { give(q, got, pinned); });
+  }
+
+ private:
+  static constexpr size_t kStep = size_t(1) << 20;
+  static constexpr size_t kKeepIdle = size_t(1) << 30;
+  void give(uint8_t* p, size_t size, bool pinned) {
+    if (!pinned) {
+      std::free(p);
+      return;
+    }
+    {
+      std::lock_guard<std::mutex> g(mu_);
+      if (idle_ + size <= kKeepIdle) {
+        free_.emplace_back(p, size);
+        idle_ += size;
+        return;
+      }
+    }
+    cudaFreeHost(p);
+  }
+  std::mutex mu_;
+  std::vector<std::pair<uint8_t*, size_t>> free_;
+  size_t idle_ = 0;
+};
+
+void put_u32(uint8_t* out, uint32_t v) {
+  for (int i = 0; i < 4; ++i) out[i] = static_cast<uint8_t>(v >> (8 * i));
+}
+
+}  // namespace
+
 // ---- SavedState (engine.rs:503-580) ----------------------------------------
 
 size_t SavedState::byte_len() const {
   size_t n = prefix.size() * 4;
-  for (const auto& l : layers) n += l.bytes.size();
+  for (const auto& l : layers) n += l.len;
   return n;
 }
 
-static void put_u32(std::vector<uint8_t>& out, uint32_t v) {
-  for (int i = 0; i < 4; ++i) out.push_back(static_cast<uint8_t>(v >> (8 * i)));
+size_t SavedState::file_len(const std::string& model_id) const {
+  return 6 + 4 + model_id.size() + body_len;
+}
+
+SavedState SavedState::make(const uint32_t* prefix, size_t n,
+                            const std::vector<std::array<size_t, 3>>& layers) {
+  SavedState s;
+  s.prefix.assign(prefix, prefix + n);
+  size_t len = 4 + 4 * n + 4;
+  for (const auto& l : layers) len += 12 + l[2];
+  s.body = HostBlocks::get().take(len);
+  s.body_len = len;
+  uint8_t* b = s.body.get();
+  put_u32(b, static_cast<uint32_t>(n));
+  for (size_t i = 0; i < n; ++i) put_u32(b + 4 + 4 * i, prefix[i]);
+  size_t at = 4 + 4 * n;
+  put_u32(b + at, static_cast<uint32_t>(layers.size()));
+  at += 4;
+  for (const auto& l : layers) {
+    put_u32(b + at, static_cast<uint32_t>(l[0]));
+    put_u32(b + at + 4, static_cast<uint32_t>(l[1]));
+    put_u32(b + at + 8, static_cast<uint32_t>(l[2]));
+    Layer ly;
+    ly.layer = static_cast<int>(l[0]);
+    ly.row0 = static_cast<int>(l[1]);
+    ly.off = at + 12;
+    ly.len = l[2];
+    s.layers.push_back(ly);
+    at += 12 + l[2];
+  }
+  return s;
+}
+
+void SavedState::write_bytes(const std::string& model_id, uint8_t* out) const {
+  std::memcpy(out, "GRWS1\0", 6);
+  put_u32(out + 6, static_cast<uint32_t>(model_id.size()));
+  std::memcpy(out + 10, model_id.data(), model_id.size());
+  if (body_len) std::memcpy(out + 10 + model_id.size(), body.get(), body_len);
 }
 
 std::vector<uint8_t> SavedState::to_bytes(const std::string& model_id) const {
-  std::vector<uint8_t> out;
-  out.reserve(byte_len() + 64 + model_id.size());
-  const char magic[6] = {'G', 'R', 'W', 'S', '1', '\0'};
-  out.insert(out.end(), magic, magic + 6);
-  put_u32(out, static_cast<uint32_t>(model_id.size()));
-  out.insert(out.end(), model_id.begin(), model_id.end());
-  put_u32(out, static_cast<uint32_t>(prefix.size()));
-  for (uint32_t t : prefix) put_u32(out, t);
-  put_u32(out, static_cast<uint32_t>(layers.size()));
-  for (const auto& l : layers) {
-    put_u32(out, static_cast<uint32_t>(l.layer));
-    put_u32(out, static_cast<uint32_t>(l.row0));
-    put_u32(out, static_cast<uint32_t>(l.bytes.size()));
-    out.insert(out.end(), l.bytes.begin(), l.bytes.end());
-  }
+  std::vector<uint8_t> out(file_len(model_id));
+  write_bytes(model_id, out.data());
   return out;
 }
 
@@ -114,24 +213,24 @@ SavedState SavedState::from_bytes(const uint8_t* b, size_t n, const std::string&
   const uint8_t* id = take(idn);
   if (idn != model_id.size() || std::memcmp(id, model_id.data(), idn) != 0)
     fail("state file is for a different model");
-  SavedState s;
+  const size_t body0 = at;
   const size_t np = u32();
   const uint8_t* pp = take(np * 4);
-  s.prefix.resize(np);
+  std::vector<uint32_t> prefix(np);
   for (size_t i = 0; i < np; ++i)
-    s.prefix[i] = static_cast<uint32_t>(pp[4 * i]) | (static_cast<uint32_t>(pp[4 * i + 1]) << 8) |
-                  (static_cast<uint32_t>(pp[4 * i + 2]) << 16) |
-                  (static_cast<uint32_t>(pp[4 * i + 3]) << 24);
+    prefix[i] = static_cast<uint32_t>(pp[4 * i]) | (static_cast<uint32_t>(pp[4 * i + 1]) << 8) |
+                (static_cast<uint32_t>(pp[4 * i + 2]) << 16) |
+                (static_cast<uint32_t>(pp[4 * i + 3]) << 24);
   const size_t nl = u32();
+  std::vector<std::array<size_t, 3>> specs;
   for (size_t i = 0; i < nl; ++i) {
-    Layer l;
-    l.layer = static_cast<int>(u32());
-    l.row0 = static_cast<int>(u32());
-    const size_t len = u32();
-    const uint8_t* d = take(len);
-    l.bytes.assign(d, d + len);
-    s.layers.push_back(std::move(l));
+    const size_t layer = u32(), row0 = u32(), len = u32();
+    take(len);
+    specs.push_back({layer, row0, len});
   }
+  SavedState s = make(prefix.data(), np, specs);
+  // The body as read: the same bytes make() laid out, rows included.
+  std::memcpy(s.body.get(), b + body0, s.body_len);
   return s;
 }
 
@@ -1251,20 +1350,21 @@ SavedState Engine::save_state(const uint32_t* prefix, size_t n) {
 
 SavedState Engine::save_state_at(const uint32_t* prefix, size_t n, size_t row0) {
   CUDA_TRY(cudaSetDevice(device_));
-  SavedState s;
-  s.prefix.assign(prefix, prefix + n);
+  std::vector<std::array<size_t, 3>> specs;
   for (int l = 0; l < config.layers; ++l) {
     if (!config.has_kv(l)) continue;
     auto [r0, r1] = state_rows(l, n);
     const size_t row_bytes = static_cast<size_t>(2) * config.kv_heads * config.head_dim[l] * 2;
-    SavedState::Layer ly;
-    ly.layer = l;
-    ly.row0 = static_cast<int>(r0);
-    ly.bytes.resize((r1 - r0) * row_bytes);
-    if (!ly.bytes.empty())
-      CUDA_TRY(cudaMemcpyAsync(ly.bytes.data(), kv_[l].as<uint8_t>() + (row0 + r0) * row_bytes,
-                               ly.bytes.size(), cudaMemcpyDeviceToHost, stream_));
-    s.layers.push_back(std::move(ly));
+    specs.push_back({static_cast<size_t>(l), r0, (r1 - r0) * row_bytes});
+  }
+  // One device-to-host copy per layer, straight into the page-locked file body.
+  SavedState s = SavedState::make(prefix, n, specs);
+  for (const auto& ly : s.layers) {
+    const size_t row_bytes =
+        static_cast<size_t>(2) * config.kv_heads * config.head_dim[ly.layer] * 2;
+    if (ly.len)
+      CUDA_TRY(cudaMemcpyAsync(s.data(ly), kv_[ly.layer].as<uint8_t>() + (row0 + ly.row0) * row_bytes,
+                               ly.len, cudaMemcpyDeviceToHost, stream_));
   }
   CUDA_TRY(cudaStreamSynchronize(stream_));
   return s;
@@ -1279,15 +1379,15 @@ void Engine::restore_state(const SavedState& s) {
       fail("state has K/V for layer %d, which owns none", ly.layer);
     const size_t row = static_cast<size_t>(2) * config.kv_heads * config.head_dim[ly.layer];
     auto [r0, r1] = state_rows(ly.layer, p);
-    if (static_cast<size_t>(ly.row0) != r0 || ly.bytes.size() != (r1 - r0) * row * 2)
-      fail("state layer %d: %zu bytes at row %d, expected %zu at %zu", ly.layer, ly.bytes.size(),
+    if (static_cast<size_t>(ly.row0) != r0 || ly.len != (r1 - r0) * row * 2)
+      fail("state layer %d: %zu bytes at row %d, expected %zu at %zu", ly.layer, ly.len,
            ly.row0, (r1 - r0) * row * 2, r0);
   }
   for (const auto& ly : s.layers) {
     const size_t row_bytes = static_cast<size_t>(2) * config.kv_heads * config.head_dim[ly.layer] * 2;
-    if (!ly.bytes.empty())
-      CUDA_TRY(cudaMemcpyAsync(kv_[ly.layer].as<uint8_t>() + ly.row0 * row_bytes, ly.bytes.data(),
-                               ly.bytes.size(), cudaMemcpyHostToDevice, stream_));
+    if (ly.len)
+      CUDA_TRY(cudaMemcpyAsync(kv_[ly.layer].as<uint8_t>() + ly.row0 * row_bytes, s.data(ly),
+                               ly.len, cudaMemcpyHostToDevice, stream_));
   }
   std::vector<TokMeta> meta(p);
   for (size_t i = 0; i < p; ++i)
@@ -1431,8 +1531,12 @@ void Engine::remember(const uint32_t* prefix, size_t n, size_t row0) {
   if (!path.empty()) {
     mkdir(state_dir_.c_str(), 0755);
     std::ofstream f(path, std::ios::binary);
-    const auto bytes = s.to_bytes(model_id_);
-    f.write(reinterpret_cast<const char*>(bytes.data()), static_cast<std::streamsize>(bytes.size()));
+    uint8_t head[10];
+    std::memcpy(head, "GRWS1\0", 6);
+    put_u32(head + 6, static_cast<uint32_t>(model_id_.size()));
+    f.write(reinterpret_cast<const char*>(head), 10);
+    f.write(model_id_.data(), static_cast<std::streamsize>(model_id_.size()));
+    f.write(reinterpret_cast<const char*>(s.body.get()), static_cast<std::streamsize>(s.body_len));
     if (!f) fail("writing %s", path.c_str());
   }
   std::lock_guard<std::mutex> g(mu_);

@@ -10,6 +10,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <array>
 #include <cstdint>
 #include <map>
 #include <memory>
@@ -66,19 +67,34 @@ struct GroupIn {
 };
 
 // engine.rs:503-580: a prefix's K/V rows as f16 per layer that owns K/V;
-// sliding layers keep only the last `window` rows.
+// sliding layers keep only the last `window` rows. The rows live in one
+// page-locked host block laid out as the GRWS1 file from the prefix count
+// on (prefix, layer count, per layer its header and rows), so the device
+// copies land straight in the file's bytes and a save or restore moves at
+// the host link's speed.
 struct SavedState {
   std::vector<uint32_t> prefix;
   struct Layer {
     int layer = 0;
     int row0 = 0;
-    std::vector<uint8_t> bytes;  // f16 LE rows of [kv_heads * hd K | kv_heads * hd V]
+    size_t off = 0;  // f16 LE rows of [kv_heads * hd K | kv_heads * hd V] at body + off
+    size_t len = 0;
   };
   std::vector<Layer> layers;
+  std::shared_ptr<uint8_t> body;
+  size_t body_len = 0;
 
+  const uint8_t* data(const Layer& l) const { return body.get() + l.off; }
+  uint8_t* data(const Layer& l) { return body.get() + l.off; }
   size_t byte_len() const;
+  size_t file_len(const std::string& model_id) const;
+  // The GRWS1 file (engine.rs:510-579) into `out` (file_len bytes).
+  void write_bytes(const std::string& model_id, uint8_t* out) const;
   std::vector<uint8_t> to_bytes(const std::string& model_id) const;
   static SavedState from_bytes(const uint8_t* b, size_t n, const std::string& model_id);
+  // A state for `prefix` with layers (layer, row0, bytes); rows unset.
+  static SavedState make(const uint32_t* prefix, size_t n,
+                         const std::vector<std::array<size_t, 3>>& layers);
 };
 
 // engine.rs:584-620: LRU of saved states keyed by the exact prefix, most

@@ -278,6 +278,13 @@ int omg_engine_weight_f16(omg_engine* e, const char* name, uint16_t* out, size_t
   });
 }
 
+int omg_engine_arm_wait_timeout(omg_engine* e, long long clocks) {
+  return guarded([&] {
+    eng(e).arm_wait_timeout(clocks);
+    return 0;
+  });
+}
+
 int omg_engine_get_info(omg_engine* e, omg_engine_info* info) {
   return guarded([&] {
     Engine& x = eng(e);

@@ -1049,8 +1049,12 @@ int Engine::launch_forward(const Packing& p, Want want) {
     if (ly.fused_mlp) {
       k("gemm_mlp");
       mlp_target += 4 * ly.gate_up.s.n_tiles / ly.down.s.splits;
+      // arm_wait_timeout: one band more than the up tiles deliver, a short limit.
+      const long long stall = stall_clocks_;
+      stall_clocks_ = 0;
       gemm_run_mlp(ly.gate_up, ly.down, t, act16_.p, ly.ff, a32_.p, d, slab_a,
-                   mlp_ready_.as<int>(), mlp_target, status, stream_);
+                   mlp_ready_.as<int>(), mlp_target + (stall ? 1 : 0), status, stream_, -1,
+                   stall);
     } else {
       k("gemm_gate_up");
       gemm_run(ly.gate_up, t, act16_.p, ly.ff, 0, status, stream_);
@@ -1225,6 +1229,14 @@ std::string Engine::profile_forward(const GroupIn* groups, size_t n, Want want, 
   return js;
 }
 
+void Engine::arm_wait_timeout(long long clocks) {
+  if (clocks <= 0) fail("arm_wait_timeout: the limit must be positive");
+  bool fused = false;
+  for (const auto& ly : layers_) fused = fused || ly.fused_mlp;
+  if (!fused) fail("arm_wait_timeout: this engine has no fused FFN launch");
+  stall_clocks_ = clocks;
+}
+
 void Engine::check_status() {
   const uint32_t st = *h_status_.as<uint32_t>();
   if (st != 0)
@@ -1243,7 +1255,10 @@ void Engine::run(const GroupIn* groups, size_t n, size_t first,
     fail("output buffer holds %zu floats, the request returns %zu", out_floats,
          total_rows * width);
   upload(p, per_layer_rows, rows_bytes);
-  run_forward(p, want);
+  if (stall_clocks_)
+    launch_forward(p, want);  // a test pass that must fail: never captured
+  else
+    run_forward(p, want);
   const float* src = want == Want::Logits ? logits_.as<float>() : rows_.as<float>();
   // A page-locked output buffer (omg_host_alloc) takes the rows straight from
   // the device, one copy per run of consecutive rows; any other buffer gets

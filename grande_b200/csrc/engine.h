@@ -226,6 +226,11 @@ class Engine {
   // engine.rs:643-726): JSON {"kernel": [launches, total_ms], ...}.
   std::string profile_forward(const GroupIn* groups, size_t n, Want want, bool resident,
                               int iters);
+  // Test hook for the bounded device waits: the next pass's first fused FFN
+  // launch waits for an activation band that never completes and gives up
+  // after `clocks` SM clocks, so the pass fails with the wait-timeout error
+  // (the pass runs outside the graph cache; the hook disarms itself).
+  void arm_wait_timeout(long long clocks);
   // Events on the engine's stream for end-to-end timing around API calls.
   void record_event(int slot);
   float elapsed_ms(int a, int b);
@@ -320,6 +325,7 @@ class Engine {
   void check_status();
   void prof_mark(const char* name);
   bool profiling_ = false;
+  long long stall_clocks_ = 0;  // arm_wait_timeout
   std::vector<cudaEvent_t> prof_events_;
   std::vector<const char*> prof_names_;
   size_t prof_used_ = 0;

@@ -1093,6 +1093,7 @@ struct MlpArgs {
   int* ready;
   int ready_target;
   int band;  // up column tiles per down split
+  long long wait_limit;  // SM clocks a down unit waits for its band before giving up
 };
 
 template <int EPI_UP, int PK>
@@ -1195,7 +1196,7 @@ __global__ void __launch_bounds__(Cfg<256, PK>::THREADS, 1)
               ok = false;
               break;
             }
-            if (clock64() - t0 > kWaitLimitClocks) {
+            if (clock64() - t0 > g.wait_limit) {
               *abort_flag = 1;
               atomicCAS(status, 0u, static_cast<uint32_t>(kDevWaitTimeout));
               ok = false;
@@ -1423,7 +1424,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
               ok = false;
               break;
             }
-            if (clock64() - t0 > kWaitLimitClocks) {
+            if (clock64() - t0 > g.wait_limit) {
               *abort_flag = 1;
               atomicCAS(status, 0u, static_cast<uint32_t>(kDevWaitTimeout));
               ok = false;
@@ -1910,7 +1911,7 @@ bool gemm_mlp_ok(const GemmPlan& up, const GemmPlan& down) {
 
 void gemm_run_mlp(const GemmPlan& up, const GemmPlan& down, int m, void* act, int ld_act,
                   void* slabs, int ld_slab, size_t split_stride, int* ready, int ready_target,
-                  uint32_t* status, cudaStream_t stream, int force_pair) {
+                  uint32_t* status, cudaStream_t stream, int force_pair, long long wait_limit) {
   if (m <= 0) return;
   // force_pair: -1 by row tiles, 0 one-CTA tiles, 1 CTA pairs (kernel tests).
   const bool pair = up.s.pair && down.s.pair &&
@@ -1934,6 +1935,7 @@ void gemm_run_mlp(const GemmPlan& up, const GemmPlan& down, int m, void* act, in
   a.up.splits = 1;
   a.ready = ready;
   a.ready_target = ready_target;
+  a.wait_limit = wait_limit > 0 ? wait_limit : kWaitLimitClocks;
   a.band = a.down.kb_per_split / 2;
   if (pair) {
     const int m_pairs = (a.up.m_tiles + 1) / 2;

@@ -136,11 +136,14 @@ void gemm_run_epi(const GemmPlan& p, int m, void* out, int ldo, const GemmEpi& e
 // split's K blocks equal to the up projection's (gemm_mlp_ok). `ready` holds
 // one counter per (128-row tile, down split), zeroed at the start of a pass;
 // `ready_target` is the running sum over the pass's fused launches of
-// 4 x (up column tiles / down splits).
+// 4 x (up column tiles / down splits). A down unit waits at most
+// `wait_limit` SM clocks (0: about a second) for its band, then records
+// kDevWaitTimeout in `status` and its CTA stops.
 bool gemm_mlp_ok(const GemmPlan& up, const GemmPlan& down);
 void gemm_run_mlp(const GemmPlan& up, const GemmPlan& down, int m, void* act, int ld_act,
                   void* slabs, int ld_slab, size_t split_stride, int* ready, int ready_target,
-                  uint32_t* status, cudaStream_t stream, int force_pair = -1);
+                  uint32_t* status, cudaStream_t stream, int force_pair = -1,
+                  long long wait_limit = 0);
 
 // Encode a TMA tensor map over f16 data with the 128-byte swizzle: `rank`
 // dimensions innermost first, byte strides of dimensions 1..rank-1, box

@@ -438,6 +438,12 @@ class Engine:
                                                 _lib.ptr(out, C.c_uint8), n))
         return out.tobytes()
 
+    def arm_wait_timeout(self, clocks: int):
+        """Test hook: the next pass's first fused FFN launch waits for a band
+        that never completes and gives up after `clocks` SM clocks, so that
+        pass raises the engine's wait-timeout error."""
+        check(lib().omg_engine_arm_wait_timeout(self._h, int(clocks)))
+
     def weight_f16(self, name: str, shape) -> np.ndarray:
         """The f16 bits the projection GEMMs multiply for linear `name`
         ([rows, k] uint16), read back from the device."""

@@ -329,6 +329,13 @@ int omg_debug_dequant(int device, int dtype, const uint8_t* codes, const uint8_t
  * (crates/omg-wgpu/src/engine.rs:845-952), as the GEMM sees it. */
 int omg_engine_weight_f16(omg_engine* e, const char* name, uint16_t* out, size_t n);
 
+/* Test hook for the bounded device waits (no counterpart in the reference,
+ * whose GPU path has no waits of its own): the engine's next pass arms its
+ * first fused FFN launch to wait for an activation band that never
+ * completes, so that wait gives up after `clocks` SM clocks; the pass then
+ * fails with "a kernel gave up waiting" and the engine keeps working. */
+int omg_engine_arm_wait_timeout(omg_engine* e, long long clocks);
+
 /* Kernel timing for tile sweeps (no reference counterpart; the reference
  * times dispatches with timestamp queries, crates/omg-wgpu/src/engine.rs:643-726):
  * `iters` launches of the GEMM on device-resident operands of the given shape

@@ -69,6 +69,8 @@ def args_():
     ap.add_argument("--config", default="e2b-q4")
     ap.add_argument("--profile-iters", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--weights", choices=["packed", "f16"], default="packed",
+                    help="Q4_0/Q8_0 linears kept packed (decoded per tile) or as f16 rows")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layer count (small cases for ncu captures only)")
     return ap.parse_args()
@@ -323,7 +325,8 @@ def run_b200(a, dist: Dist):
     resident = a.config.endswith("resident")
     cap = shape.tokens() + 64
     t_build = time.perf_counter()
-    eng = synth.build_engine(shape, cap, shape.branches, device=dist.local, seed=0)
+    eng = synth.build_engine(shape, cap, shape.branches, device=dist.local, seed=0,
+                             packed=a.weights == "packed")
     t_build = time.perf_counter() - t_build
     req = synth.request(shape, seed=1000 + dist.rank)
     if resident:
@@ -456,7 +459,7 @@ def run_b200(a, dist: Dist):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic: seeded N(0,0.02) weights quantized to "
                 f"{shape.dtype.name}_0, uniform token ids",
-        "config": workload_config(shape, resident, n),
+        "config": {**workload_config(shape, resident, n), "weights": a.weights},
         "p50_latency_ms": round(statistics.median(lat), 3) if lat else None,
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                 "h2d_bytes_per_step": bytes_in, "d2h_bytes_per_step": shape.branches * width * 4,

@@ -129,6 +129,7 @@ PROTOTYPES: dict[str, tuple] = {
                                      u16p]),
     "omg_engine_weight_f16": (C.c_int, [vp, C.c_char_p, u16p, sz]),
     "omg_engine_arm_wait_timeout": (C.c_int, [vp, C.c_longlong]),
+    "omg_builder_set_weight_layout": (C.c_int, [vp, C.c_int]),
     "omg_debug_gemm": (
         C.c_int,
         [C.c_int, u16p, C.c_int, C.c_int, C.c_int, u16p, C.c_int, C.c_int, C.c_int, C.c_int,

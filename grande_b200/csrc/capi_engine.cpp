@@ -134,6 +134,16 @@ int omg_builder_set_per_layer_table(omg_builder* b, int dtype, const int64_t* sh
   });
 }
 
+int omg_builder_set_weight_layout(omg_builder* b, int layout) {
+  return guarded([&] {
+    if (!b || !b->b) fail("builder is null");
+    if (layout != OMG_WEIGHTS_PACKED && layout != OMG_WEIGHTS_F16)
+      fail("weight layout must be OMG_WEIGHTS_PACKED or OMG_WEIGHTS_F16 (got %d)", layout);
+    b->b->set_packed(layout == OMG_WEIGHTS_PACKED);
+    return 0;
+  });
+}
+
 int omg_builder_missing(omg_builder* b, char* buf, size_t cap, size_t* needed) {
   return guarded([&] {
     if (!b || !b->b) fail("builder is null");

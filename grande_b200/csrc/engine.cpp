@@ -382,7 +382,8 @@ void EngineBuilder::push(const std::string& name, const HostTensor& t) {
     out_rows = static_cast<size_t>((rows + 127) / 128) * 256;
   }
   auto pit = pk_.find(key);
-  if (t.dtype != 0 && !lin_.count(key) && (pit == pk_.end() || pit->second.dtype == t.dtype)) {
+  if (t.dtype != 0 && (packed_ || pit != pk_.end()) && !lin_.count(key) &&
+      (pit == pk_.end() || pit->second.dtype == t.dtype)) {
     if (pit == pk_.end()) {
       PackedLinear w;
       w.dtype = t.dtype;

@@ -394,6 +394,7 @@ template <int DT>
 struct RawBlock {
   uint4 c[DT == kF16 ? 4 : (DT == kQ8 ? 2 : 1)];
   float scale;
+  uint32_t scale2;  // the f16 scale in both halves of a half2
 };
 
 template <int DT>
@@ -405,6 +406,7 @@ __device__ __forceinline__ void load_raw_block(const uint8_t* __restrict__ codes
 #pragma unroll
     for (int i = 0; i < NC; ++i) r.c[i] = make_uint4(0u, 0u, 0u, 0u);
     r.scale = 0.f;
+    r.scale2 = 0u;
     return;
   }
   const uint4* src = reinterpret_cast<const uint4*>(codes + gb * (NC * 16));
@@ -412,9 +414,11 @@ __device__ __forceinline__ void load_raw_block(const uint8_t* __restrict__ codes
   for (int i = 0; i < NC; ++i) r.c[i] = src[i];
   if constexpr (DT == kF16) {
     r.scale = 1.f;
+    r.scale2 = 0x3C003C00u;
   } else {
     const uint16_t sb = *reinterpret_cast<const uint16_t*>(scales + 2 * gb);
     r.scale = half_bits_to_float(sb);
+    r.scale2 = static_cast<uint32_t>(sb) * 0x00010001u;
   }
 }
 
@@ -627,7 +631,7 @@ __device__ __forceinline__ void raw_piece_f16(const RawBlock<DT>& r, uint4& hi, 
     hi = r.c[PC];
     lo = make_uint4(0u, 0u, 0u, 0u);
   } else {
-    const __half2 d2 = __float2half2_rn(r.scale);  // the block's f16 scale, exactly
+    const __half2 d2 = bits_half2(r.scale2);  // the block's f16 scale
     uint32_t w0, w1;
     __half2 bias;
     uint32_t key;
@@ -635,7 +639,7 @@ __device__ __forceinline__ void raw_piece_f16(const RawBlock<DT>& r, uint4& hi, 
       const uint4 q = r.c[PC / 2];
       w0 = (PC & 1) ? q.z : q.x;
       w1 = (PC & 1) ? q.w : q.y;
-      bias = __float2half2_rn(1152.0f);  // 1024 + 128: codes stored as c + 128
+      bias = bits_half2(0x64806480u);  // 1152 = 1024 + 128: codes stored as c + 128
       key = 0x64806480u;                 // (c ^ 0x80) | 0x6400 per lane
     } else {
       const uint4 q = r.c[0];
@@ -646,7 +650,7 @@ __device__ __forceinline__ void raw_piece_f16(const RawBlock<DT>& r, uint4& hi, 
         w0 >>= 4;
         w1 >>= 4;
       }
-      bias = __float2half2_rn(1032.0f);  // 1024 + 8: w = (q - 8) d
+      bias = bits_half2(0x64086408u);  // 1032 = 1024 + 8: w = (q - 8) d
       key = 0x64006400u;
     }
     uint32_t h[4], l[4];

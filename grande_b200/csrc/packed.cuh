@@ -51,6 +51,12 @@ inline size_t packed_bytes(int dtype, int rows, int k) {
 }
 
 #if defined(__CUDACC__)
+// A half2 from its bit pattern (no conversion instruction: constants built
+// with __float2half2_rn are converted at run time).
+__device__ __forceinline__ __half2 bits_half2(uint32_t b) {
+  return *reinterpret_cast<const __half2*>(&b);
+}
+
 // Values 8 PC .. 8 PC + 7 of a block (its codes `c`, its scale `d2` in both
 // halves) as eight f16, one 16-byte piece of an f16 row.
 template <int DT, int PC>
@@ -61,7 +67,7 @@ __device__ __forceinline__ uint4 unpack_piece(const uint4* c, __half2 d2) {
     const uint4 q = c[PC / 2];
     w0 = (PC & 1) ? q.z : q.x;
     w1 = (PC & 1) ? q.w : q.y;
-    bias = __float2half2_rn(1152.0f);  // 1024 + 128: (int8 ^ 0x80) is the code + 128
+    bias = bits_half2(0x64806480u);  // 1152 = 1024 + 128: (int8 ^ 0x80) is the code + 128
   } else {
     const uint4 q = c[0];
     w0 = (PC & 1) ? q.z : q.x;
@@ -70,7 +76,7 @@ __device__ __forceinline__ uint4 unpack_piece(const uint4* c, __half2 d2) {
       w0 >>= 4;
       w1 >>= 4;
     }
-    bias = __float2half2_rn(1032.0f);  // 1024 + 8: w = (q - 8) d
+    bias = bits_half2(0x64086408u);  // 1032 = 1024 + 8: w = (q - 8) d
   }
   uint32_t h[4];
 #pragma unroll

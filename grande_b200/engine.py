@@ -502,6 +502,12 @@ class EngineBuilder:
     def catalogue(self) -> list:
         return [n for n, _ in config_tensors(self.config_json)]
 
+    def set_weight_layout(self, packed: bool):
+        """Q4_0 / Q8_0 linears pushed from now on: kept packed and decoded
+        per tile in shared memory by the GEMMs (True, the default), or
+        decoded once into f16 rows (False; 3.6x the memory, same results)."""
+        check(lib().omg_builder_set_weight_layout(self._h, 0 if packed else 1))
+
     def push(self, name: str, t: QTensor):
         shape = _shape(t.shape)
         check(lib().omg_builder_push(self._h, name.encode(), int(t.dtype), shape, len(t.shape),

@@ -101,12 +101,14 @@ def tensor(seed: int, name: str, shape, dtype: Dtype, qk_scale: float = 1.0) -> 
 
 
 def build_engine(shape: Shape, capacity: int, max_rows: int, device: int = 0, seed: int = 0,
-                 threads: int = 8, qk_scale: float = 1.0, tensors: dict | None = None):
+                 threads: int = 8, qk_scale: float = 1.0, tensors: dict | None = None,
+                 packed: bool = True):
     """Generate, quantize and push every tensor (generation in a thread pool;
     ctypes releases the GIL), then finish the engine. `tensors` (name ->
     QTensor) supplies already generated tensors, e.g. a deeper model's, of
     which this shape's catalogue takes its own."""
     b = EngineBuilder(shape.config_json(), device)
+    b.set_weight_layout(packed)
     specs = _lib_specs(shape.config_json())
     if tensors is not None:
         for name, _dims in specs:

@@ -91,3 +91,28 @@ def test_packed_fused_mlp_equals_f16(device, dtype, m, d, ff):
         L.ptr(act.view(np.uint16), L.C.c_uint16), L.ptr(y, L.C.c_float)))
     assert np.array_equal(act, a1)
     assert np.array_equal(y, y1)
+
+
+@pytest.mark.parametrize("config", ["e2b-q4", "gemma3-270m-q8"])
+def test_packed_engine_equals_f16_engine(device, config):
+    """Whole passes (QKV with the fused qk_prep, o, the fused FFN, logits) of
+    an engine keeping its Q4_0 / Q8_0 linears packed and of one decoding them
+    once into f16 rows: the same bits."""
+    import dataclasses
+
+    from grande_b200 import synth
+    from grande_b200.engine import Want
+    shape = dataclasses.replace(synth.CONFIGS[config], layers=2)
+    req = synth.request(shape, seed=9)
+    tensors = synth.generate(shape, seed=0)
+    rows = {}
+    for packed in (True, False):
+        eng = synth.build_engine(shape, shape.tokens() + 64, shape.branches, device=device,
+                                 tensors=tensors, packed=packed)
+        hid = eng.evaluate(req.prefix, req.branches, Want.HIDDEN)
+        eng.evict_resident()
+        lg = eng.evaluate(req.prefix, req.branches, Want.LOGITS)
+        rows[packed] = [o.rows for o in hid] + [o.rows for o in lg]
+        eng.close()
+    for a, b in zip(rows[True], rows[False]):
+        assert np.array_equal(a, b)

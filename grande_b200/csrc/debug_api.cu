@@ -379,9 +379,12 @@ extern "C" int omg_debug_gemm_q(int device, const uint16_t* x_f16, int m, int k,
     CUDA_TRY(cudaMemset(dstat.p, 0, 4));
     GemmPlan plan;
     char err[256];
-    if (!gemm_plan_packed(&plan, dx.p, m, lda, dw.p, wdtype, w_rows, n_out, k, epi, bn, splits,
-                          err, sizeof err))
+    // bn 512 asks for the CTA-pair kernel (256 x 256 tiles over two SMs).
+    const bool pair = bn == 512;
+    if (!gemm_plan_packed(&plan, dx.p, m, lda, dw.p, wdtype, w_rows, n_out, k, epi,
+                          pair ? 256 : bn, splits, err, sizeof err))
       return set_error(err);
+    if (pair && !gemm_plan_pair(&plan, nullptr, w_rows, true, err, sizeof err)) return set_error(err);
     const int sp = f32 ? plan.s.splits : 1;
     const size_t slab = static_cast<size_t>(m) * ldo;
     const size_t ob = slab * sp * (f32 ? 4 : 2);
@@ -411,7 +414,7 @@ extern "C" int omg_debug_gemm_q(int device, const uint16_t* x_f16, int m, int k,
 
 extern "C" int omg_debug_mlp_q(int device, const uint16_t* x, int m, int d, int wdtype,
                                const uint8_t* up_codes, const uint8_t* up_scales, int ff,
-                               const uint8_t* down_codes, const uint8_t* down_scales,
+                               const uint8_t* down_codes, const uint8_t* down_scales, int pair,
                                uint16_t* act_out, float* y_out) {
   return guarded([&]() -> int {
     if (wdtype != kQ4 && wdtype != kQ8) fail("omg_debug_mlp_q: dtype %d is not Q4_0 / Q8_0", wdtype);
@@ -438,11 +441,14 @@ extern "C" int omg_debug_mlp_q(int device, const uint16_t* x, int m, int d, int 
     if (!gemm_plan_packed(&up, dx.p, m, d, dwu.p, wdtype, 2 * ff, ff, d, kEpiGeGluTanh, 256, 1, err,
                           sizeof err) ||
         !gemm_plan_packed(&down, dact.p, m, ff, dwd.p, wdtype, d, d, ff, kEpiF32, 256, splits, err,
-                          sizeof err))
+                          sizeof err) ||
+        !gemm_plan_pair(&up, nullptr, 2 * ff, false, err, sizeof err) ||
+        !gemm_plan_pair(&down, nullptr, d, false, err, sizeof err))
       return set_error(err);
     if (!gemm_mlp_ok(up, down)) return set_error("debug_mlp_q: shapes not fusable");
     gemm_run_mlp(up, down, m, dact.p, ff, dslab.p, d, slab, static_cast<int*>(dready.p),
-                 4 * up.s.n_tiles / down.s.splits, static_cast<uint32_t*>(dstat.p), 0, 0);
+                 4 * up.s.n_tiles / down.s.splits, static_cast<uint32_t*>(dstat.p), 0,
+                 pair ? 1 : 0);
     CUDA_TRY(cudaGetLastError());
     CUDA_TRY(cudaDeviceSynchronize());
     uint32_t st = 0;

@@ -539,6 +539,8 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
       if (!gemm_plan_packed(p, a, static_cast<int>(C), lda, w.p, w.pk, w_rows, n_out, k, epi, bn,
                             std::min(splits, S), err, sizeof err))
         fail("layer %d %s: %s", l, what, err);
+      if (p->s.bn == 256 && !gemm_plan_pair(p, nullptr, w_rows, false, err, sizeof err))
+        fail("layer %d %s: %s", l, what, err);
       return;
     }
     if (!gemm_plan(p, a, static_cast<int>(C), lda, w.p, w_rows, n_out, k, epi, bn,

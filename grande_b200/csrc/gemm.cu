@@ -84,10 +84,10 @@ struct Cfg {
   static_assert(2 * STAGES + 4 + 2 * RAW_STAGES <= 30, "barrier area");
 };
 
-// Shared-memory carve-up of the one-CTA kernels.
-template <int BN, int PK>
+// Shared-memory carve-up: A ring, B ring, raw ring, then barriers, epilogue
+// constants and row-staging slots (one-CTA and CTA-pair configs alike).
+template <class C>
 struct Smem {
-  using C = Cfg<BN, PK>;
   uint8_t *sa, *sb, *raw;
   uint64_t *full, *empty, *tfull, *tempty, *raw_full, *raw_empty;
   uint32_t* tmem_slot;
@@ -118,9 +118,10 @@ struct Smem {
 template <int BN, int PK>
 struct PackedPipe {
   using C = Cfg<BN, PK>;
+  using S = Smem<C>;
   // Producer (one thread): the BN / 128 chunks of weight rows
   // [n_tile * BN, n_tile * BN + BN) at K step kb into raw slot it.
-  __device__ static bool load(const Smem<BN, PK>& sm, const uint8_t* wpack, int kb_total,
+  __device__ static bool load(const S& sm, const uint8_t* wpack, int kb_total,
                               int n_tile, int kb, int it, uint32_t* status) {
     const int r = it % C::RAW_STAGES;
     if (!mbar_wait(&sm.raw_empty[r], ((it / C::RAW_STAGES) & 1) ^ 1, sm.abort_flag, status))
@@ -135,14 +136,14 @@ struct PackedPipe {
   }
   // Producer, after its last load: see the copies land before the CTA exits
   // (they have unless the CTA gave up).
-  __device__ static void drain(const Smem<BN, PK>& sm, int issued) {
+  __device__ static void drain(const S& sm, int issued) {
     for (int j = issued - C::RAW_STAGES > 0 ? issued - C::RAW_STAGES : 0; j < issued; ++j)
       if (!mbar_drain(&sm.raw_full[j % C::RAW_STAGES], (j / C::RAW_STAGES) & 1, 1ll << 24)) break;
   }
   // Converter warps (t = 0..127 over the four): K step `it` from its raw slot
   // into ring slot it % STAGES (free once the MMAs of step it - STAGES are
   // done), then arrive on full[s] and hand the raw slot back.
-  __device__ static bool convert(const Smem<BN, PK>& sm, int it, int t, uint32_t* status) {
+  __device__ static bool convert(const S& sm, int it, int t, uint32_t* status) {
     const int r = it % C::RAW_STAGES, s = it % C::STAGES;
     const uint32_t pr = (it / C::RAW_STAGES) & 1, pe = ((it / C::STAGES) & 1) ^ 1;
     int ok = 1;
@@ -687,7 +688,7 @@ __global__ void __launch_bounds__(Cfg<BN, PK>::THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  const Smem<BN, PK> sm(smem);
+  const Smem<C> sm(smem);
   uint8_t* sa = sm.sa;
   uint8_t* sb = sm.sb;
   uint64_t* full = sm.full;
@@ -878,13 +879,68 @@ __global__ void __launch_bounds__(Cfg<BN, PK>::THREADS, 1)
 // complete on the leader's barrier); empty[s] and tfull[b] are signalled in
 // both CTAs by the leader's commits; tempty[b] on the leader counts the
 // epilogue warps of both CTAs (the peer's arrive remotely).
+template <int PK = kF16>
 struct Cfg2 {
-  static constexpr int STAGES = 6;
+  static constexpr bool PACKED = PK != kF16;
+  static constexpr int STAGES = PACKED ? 5 : 6;
   static constexpr int A_BYTES = BM * BK * 2;       // 128 rows of A
   static constexpr int B_BYTES = 128 * BK * 2;      // this CTA's 128 weight rows
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + 2048 + 4 * 4096;
+  static constexpr int CHUNK = PK == kQ4 ? PackChunk<kQ4>::BYTES
+                                         : (PK == kQ8 ? PackChunk<kQ8>::BYTES : 0);
+  static constexpr int RAW_BYTES = CHUNK;           // this CTA's 128 weight rows, packed
+  static constexpr int RAW_STAGES = !PACKED ? 0 : (PK == kQ4 ? 6 : 4);
+  static constexpr int RING = STAGES * STAGE_BYTES + RAW_STAGES * RAW_BYTES;
+  static constexpr int SMEM = RING + 1024 + 256 + 2048 + 4 * 4096;
   static constexpr uint32_t TMEM_COLS = 512;        // two 256-column accumulators
+  static constexpr int THREADS = PACKED ? 352 : 192;
+  static_assert(SMEM <= 232448, "shared memory");
+  static_assert(2 * STAGES + 4 + 2 * RAW_STAGES <= 30, "barrier area");
+};
+
+// The packed-weight side of the CTA-pair kernels: each CTA fetches and
+// decodes its own 128 weight rows of the tile (chunk 2 n + rank) into its
+// half of the B operand; both CTAs' converter warps arrive on the leader's
+// full barrier (releasing their stores at cluster scope), which the
+// leader's MMA thread waits on with cluster-scope acquire.
+template <int PK>
+struct PackedPipe2 {
+  using C = Cfg2<PK>;
+  using S = Smem<C>;
+  __device__ static bool load(const S& sm, const uint8_t* wpack, int kb_total, int chunk_row,
+                              int kb, int it, uint32_t* status) {
+    const int r = it % C::RAW_STAGES;
+    if (!mbar_wait(&sm.raw_empty[r], ((it / C::RAW_STAGES) & 1) ^ 1, sm.abort_flag, status))
+      return false;
+    mbar_arrive_expect_tx(&sm.raw_full[r], C::RAW_BYTES);
+    bulk_load(sm.raw + r * C::RAW_BYTES,
+              wpack + (static_cast<size_t>(chunk_row) * kb_total + kb) * C::CHUNK, C::CHUNK,
+              &sm.raw_full[r]);
+    return true;
+  }
+  __device__ static void drain(const S& sm, int issued) {
+    for (int j = issued - C::RAW_STAGES > 0 ? issued - C::RAW_STAGES : 0; j < issued; ++j)
+      if (!mbar_drain(&sm.raw_full[j % C::RAW_STAGES], (j / C::RAW_STAGES) & 1, 1ll << 24)) break;
+  }
+  __device__ static bool convert(const S& sm, int it, int t, uint32_t* status) {
+    const int r = it % C::RAW_STAGES, s = it % C::STAGES;
+    const uint32_t pr = (it / C::RAW_STAGES) & 1, pe = ((it / C::STAGES) & 1) ^ 1;
+    int ok = 1;
+    if ((t & 31) == 0)
+      ok = mbar_wait(&sm.raw_full[r], pr, sm.abort_flag, status) &&
+           mbar_wait(&sm.empty[s], pe, sm.abort_flag, status);
+    if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
+    mbar_try_wait(&sm.raw_full[r], pr);
+    mbar_try_wait(&sm.empty[s], pe);
+    unpack_row_to_tile<PK>(sm.raw + r * C::RAW_BYTES, t, sm.sb + s * C::B_BYTES, t);
+    fence_proxy_async();
+    __syncwarp();
+    if ((t & 31) == 0) {
+      mbar_arrive_release_cluster(cluster_addr(&sm.full[s], 0));
+      mbar_arrive(&sm.raw_empty[r]);
+    }
+    return true;
+  }
 };
 
 // Pair tile t: split-major, then (M pair fastest) or (N fastest).
@@ -898,24 +954,25 @@ __device__ __forceinline__ TileId decode_pair_tile(const GemmArgs& g, int m_pair
   return x;
 }
 
-template <int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+template <int EPI, int PK>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg2<PK>::THREADS, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
                  GemmArgs g) {
   constexpr int BN = 256;
-  using C = Cfg2;
+  using C = Cfg2<PK>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sa = smem;
-  uint8_t* sb = smem + C::STAGES * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sb + C::STAGES * C::B_BYTES);
-  uint64_t* empty = full + C::STAGES;
-  uint64_t* tfull = empty + C::STAGES;   // [2] accumulator ready (both CTAs)
-  uint64_t* tempty = tfull + 2;          // [2] accumulator drained (leader: 8 warps)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* epi_consts = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);
+  const Smem<C> sm(smem);
+  uint8_t* sa = sm.sa;
+  uint8_t* sb = sm.sb;
+  uint64_t* full = sm.full;
+  uint64_t* empty = sm.empty;
+  uint64_t* tfull = sm.tfull;    // [2] accumulator ready (both CTAs)
+  uint64_t* tempty = sm.tempty;  // [2] accumulator drained (leader: 8 warps)
+  uint32_t* tmem_slot = sm.tmem_slot;
+  volatile int* abort_flag = sm.abort_flag;
+  float* epi_consts = sm.epi_consts;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -927,24 +984,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(&full[s], 1);
+      // Packed: the leader's also counts both CTAs' converter warps.
+      mbar_init(&full[s], C::PACKED ? 9 : 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 8);
     }
+    for (int r = 0; r < C::RAW_STAGES; ++r) {
+      mbar_init(&sm.raw_full[r], 1);
+      mbar_init(&sm.raw_empty[r], 4);
+    }
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&tma);
-    prefetch_tmap(&tmb);
+    if constexpr (!C::PACKED) prefetch_tmap(&tmb);
   }
   if (warp == 1) tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
   tc_fence_before();
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  griddep_wait();
+  if (!(C::PACKED && warp == 6)) griddep_wait();
   griddep_launch();
 
   if (warp == 0) {
@@ -963,11 +1025,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
             ok = false;
             break;
           }
-          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * C::STAGE_BYTES);
           const uint32_t bar = cluster_addr(&full[s], 0);
-          tma_load_2d_pair(sa + s * C::A_BYTES, &tma, bar, kb * BK, m_tile * BM);
-          tma_load_2d_pair(sb + s * C::B_BYTES, &tmb, bar, kb * BK,
-                           id.n * BN + 128 * static_cast<int>(rank));
+          if constexpr (C::PACKED) {
+            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * C::A_BYTES);
+            tma_load_2d_pair(sa + s * C::A_BYTES, &tma, bar, kb * BK, m_tile * BM);
+          } else {
+            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * C::STAGE_BYTES);
+            tma_load_2d_pair(sa + s * C::A_BYTES, &tma, bar, kb * BK, m_tile * BM);
+            tma_load_2d_pair(sb + s * C::B_BYTES, &tmb, bar, kb * BK,
+                             id.n * BN + 128 * static_cast<int>(rank));
+          }
         }
         if (!ok) break;
       }
@@ -992,7 +1059,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
-          if (!mbar_wait(&full[s], ph, abort_flag, g.status)) {
+          if (!mbar_wait_cluster(&full[s], ph, abort_flag, g.status)) {
             ok = false;
             break;
           }
@@ -1008,7 +1075,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         umma_commit_pair(&tfull[b]);
       }
     }
-  } else {
+  } else if (warp < 6) {
     const int q = warp & 3;
     if constexpr (EPI == kEpiQkPrep) {
       for (int i = threadIdx.x - 64; i < 512; i += 128) {
@@ -1041,7 +1108,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-      uint8_t* slot = reinterpret_cast<uint8_t*>(full) + 256 + 2048 + q * 4096;
+      uint8_t* slot = sm.slots + q * 4096;
       const uint32_t tbase =
           tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BN);
       epilogue_tile<BN, EPI>(g, 2 * id.m + static_cast<int>(rank), id.n, id.split, tbase, q, lane,
@@ -1049,6 +1116,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[b], 0));
+    }
+  } else if constexpr (C::PACKED) {
+    if (warp == 6) {
+      // This CTA's 128 weight rows of each tile, packed, RAW_STAGES K steps ahead.
+      if (lane == 0) {
+        int it = 0;
+        bool ok = true;
+        for (int tile = pair; tile < total && ok && !*abort_flag; tile += npairs) {
+          const TileId id = decode_pair_tile(g, m_pairs, tile);
+          const int kb0 = id.split * g.kb_per_split;
+          const int kb1 = min(g.kb_total, kb0 + g.kb_per_split);
+          for (int kb = kb0; kb < kb1 && ok; ++kb, ++it)
+            ok = PackedPipe2<PK>::load(sm, g.wpack, g.kb_total, 2 * id.n + static_cast<int>(rank),
+                                       kb, it, g.status);
+        }
+        PackedPipe2<PK>::drain(sm, it);
+      }
+    } else {
+      const int t = threadIdx.x - 224;
+      int it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < total && ok; tile += npairs) {
+        const TileId id = decode_pair_tile(g, m_pairs, tile);
+        const int kb0 = id.split * g.kb_per_split;
+        const int kb1 = min(g.kb_total, kb0 + g.kb_per_split);
+        for (int kb = kb0; kb < kb1 && ok; ++kb, ++it)
+          ok = PackedPipe2<PK>::convert(sm, it, t, g.status);
+      }
     }
   }
   tc_fence_before();
@@ -1107,7 +1202,7 @@ __global__ void __launch_bounds__(Cfg<256, PK>::THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  const Smem<BN, PK> sm(smem);
+  const Smem<C> sm(smem);
   uint8_t* sa = sm.sa;
   uint8_t* sb = sm.sb;
   uint64_t* full = sm.full;
@@ -1328,26 +1423,27 @@ __global__ void __launch_bounds__(Cfg<256, PK>::THREADS, 1)
 // its own M tile's activation band (a CTA whose half lies past the last M
 // tile has no rows and waits for nothing); the leader's full barrier then
 // holds the MMA until both halves are loaded.
-template <int EPI_UP>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+template <int EPI_UP, int PK>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg2<PK>::THREADS, 1)
     gemm_mlp2_kernel(const __grid_constant__ CUtensorMap ta_up,
                      const __grid_constant__ CUtensorMap tb_up,
                      const __grid_constant__ CUtensorMap ta_dn,
                      const __grid_constant__ CUtensorMap tb_dn, MlpArgs g) {
   constexpr int BN = 256;
-  using C = Cfg2;
+  using C = Cfg2<PK>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sa = smem;
-  uint8_t* sb = smem + C::STAGES * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sb + C::STAGES * C::B_BYTES);
-  uint64_t* empty = full + C::STAGES;
-  uint64_t* tfull = empty + C::STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* epi_consts = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);
+  const Smem<C> sm(smem);
+  uint8_t* sa = sm.sa;
+  uint8_t* sb = sm.sb;
+  uint64_t* full = sm.full;
+  uint64_t* empty = sm.empty;
+  uint64_t* tfull = sm.tfull;
+  uint64_t* tempty = sm.tempty;
+  uint32_t* tmem_slot = sm.tmem_slot;
+  volatile int* abort_flag = sm.abort_flag;
+  float* epi_consts = sm.epi_consts;
   uint32_t* status = g.up.status;
 
   const int warp = threadIdx.x >> 5;
@@ -1388,26 +1484,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], C::PACKED ? 9 : 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 8);
     }
+    for (int r = 0; r < C::RAW_STAGES; ++r) {
+      mbar_init(&sm.raw_full[r], 1);
+      mbar_init(&sm.raw_empty[r], 4);
+    }
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&ta_up);
-    prefetch_tmap(&tb_up);
     prefetch_tmap(&ta_dn);
-    prefetch_tmap(&tb_dn);
+    if constexpr (!C::PACKED) {
+      prefetch_tmap(&tb_up);
+      prefetch_tmap(&tb_dn);
+    }
   }
   if (warp == 1) tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
   tc_fence_before();
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  griddep_wait();
+  if (!(C::PACKED && warp == 6)) griddep_wait();
   griddep_launch();
 
   if (warp == 0) {
@@ -1445,11 +1547,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
             ok = false;
             break;
           }
-          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * C::STAGE_BYTES);
           const uint32_t bar = cluster_addr(&full[s], 0);
-          tma_load_2d_pair(sa + s * C::A_BYTES, ta, bar, kb * BK, x.m * BM);
-          tma_load_2d_pair(sb + s * C::B_BYTES, tb, bar, kb * BK,
-                           x.n * BN + 128 * static_cast<int>(rank));
+          if constexpr (C::PACKED) {
+            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * C::A_BYTES);
+            tma_load_2d_pair(sa + s * C::A_BYTES, ta, bar, kb * BK, x.m * BM);
+          } else {
+            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * C::STAGE_BYTES);
+            tma_load_2d_pair(sa + s * C::A_BYTES, ta, bar, kb * BK, x.m * BM);
+            tma_load_2d_pair(sb + s * C::B_BYTES, tb, bar, kb * BK,
+                             x.n * BN + 128 * static_cast<int>(rank));
+          }
         }
         if (!ok) break;
       }
@@ -1470,7 +1577,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         for (int kb = x.kb0; kb < x.kb1; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
-          if (!mbar_wait(&full[s], ph, abort_flag, status)) {
+          if (!mbar_wait_cluster(&full[s], ph, abort_flag, status)) {
             ok = false;
             break;
           }
@@ -1486,7 +1593,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         umma_commit_pair(&tfull[b]);
       }
     }
-  } else {
+  } else if (warp < 6) {
     const int q = warp & 3;
     int local = 0;
     for (int u = pair; u < total; u += npairs, ++local) {
@@ -1497,7 +1604,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-      uint8_t* slot = reinterpret_cast<uint8_t*>(full) + 256 + 2048 + q * 4096;
+      uint8_t* slot = sm.slots + q * 4096;
       const uint32_t tbase =
           tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BN);
       if (x.up) {
@@ -1514,6 +1621,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[b], 0));
+    }
+  } else if constexpr (C::PACKED) {
+    if (warp == 6) {
+      if (lane == 0) {
+        int it = 0;
+        bool ok = true;
+        for (int u = pair; u < total && ok && !*abort_flag; u += npairs) {
+          const Unit x = decode(u);
+          const GemmArgs& ga = x.up ? g.up : g.down;
+          for (int kb = x.kb0; kb < x.kb1 && ok; ++kb, ++it)
+            ok = PackedPipe2<PK>::load(sm, ga.wpack, ga.kb_total, 2 * x.n + static_cast<int>(rank),
+                                       kb, it, status);
+        }
+        PackedPipe2<PK>::drain(sm, it);
+      }
+    } else {
+      const int t = threadIdx.x - 224;
+      int it = 0;
+      bool ok = true;
+      for (int u = pair; u < total && ok; u += npairs) {
+        const Unit x = decode(u);
+        for (int kb = x.kb0; kb < x.kb1 && ok; ++kb, ++it)
+          ok = PackedPipe2<PK>::convert(sm, it, t, status);
+      }
     }
   }
   tc_fence_before();
@@ -1570,15 +1701,35 @@ void set_smem_attr() {
 
 template <int EPI>
 void set_smem_attr_pair() {
-  cudaFuncSetAttribute(gemm2_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg2::SMEM);
+  cudaFuncSetAttribute(gemm2_kernel<EPI, kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       Cfg2<>::SMEM);
+  if constexpr (packed_epi(EPI)) {
+    cudaFuncSetAttribute(gemm2_kernel<EPI, kQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         Cfg2<kQ4>::SMEM);
+    cudaFuncSetAttribute(gemm2_kernel<EPI, kQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         Cfg2<kQ8>::SMEM);
+  }
+}
+
+template <int EPI, int PK>
+void launch_pair_pk(const GemmPlan& p, const GemmArgs& a, int grid, cudaStream_t stream) {
+  using C = Cfg2<PK>;
+  launch_pdl(gemm2_kernel<EPI, PK>, dim3(grid), dim3(C::THREADS), C::SMEM, stream, p.a, p.b_half,
+             a);
 }
 
 template <int EPI>
-void launch_pair(const GemmPlan& p, const GemmArgs& a, cudaStream_t stream) {
+void launch_pair(const GemmPlan& p, const GemmArgs& a0, cudaStream_t stream) {
+  GemmArgs a = a0;
+  a.wpack = p.wpack;
   const int pairs = ((a.m_tiles + 1) / 2) * a.n_tiles * a.splits;
   const int max_pairs = p.num_sms / 2;
   const int grid = 2 * (pairs < max_pairs ? pairs : max_pairs);
-  launch_pdl(gemm2_kernel<EPI>, dim3(grid), dim3(192), Cfg2::SMEM, stream, p.a, p.b_half, a);
+  if constexpr (packed_epi(EPI)) {
+    if (p.pk == kQ4) return launch_pair_pk<EPI, kQ4>(p, a, grid, stream);
+    if (p.pk == kQ8) return launch_pair_pk<EPI, kQ8>(p, a, grid, stream);
+  }
+  launch_pair_pk<EPI, kF16>(p, a, grid, stream);
 }
 
 template <int BN, int EPI, int PK>
@@ -1658,10 +1809,18 @@ void gemm_setup_device() {
   set_smem_attr<128, kEpiResidF32>();
   set_smem_attr<256, kEpiResidF32>();
   set_smem_attr<256, kEpiQkPrep>();
-  cudaFuncSetAttribute(gemm_mlp2_kernel<kEpiGeGluTanh>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       Cfg2::SMEM);
-  cudaFuncSetAttribute(gemm_mlp2_kernel<kEpiGeGluErf>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       Cfg2::SMEM);
+  cudaFuncSetAttribute(gemm_mlp2_kernel<kEpiGeGluTanh, kF16>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg2<>::SMEM);
+  cudaFuncSetAttribute(gemm_mlp2_kernel<kEpiGeGluErf, kF16>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg2<>::SMEM);
+  cudaFuncSetAttribute(gemm_mlp2_kernel<kEpiGeGluTanh, kQ4>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg2<kQ4>::SMEM);
+  cudaFuncSetAttribute(gemm_mlp2_kernel<kEpiGeGluTanh, kQ8>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg2<kQ8>::SMEM);
+  cudaFuncSetAttribute(gemm_mlp2_kernel<kEpiGeGluErf, kQ4>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg2<kQ4>::SMEM);
+  cudaFuncSetAttribute(gemm_mlp2_kernel<kEpiGeGluErf, kQ8>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg2<kQ8>::SMEM);
   set_smem_attr_pair<kEpiF32>();
   set_smem_attr_pair<kEpiF16>();
   set_smem_attr_pair<kEpiGeGluTanh>();
@@ -1675,10 +1834,6 @@ void gemm_setup_device() {
 
 bool gemm_plan_pair(GemmPlan* p, const void* w, int w_rows, bool always, char* err,
                     size_t errlen) {
-  if (p->pk != kF16) {
-    snprintf(err, errlen, "gemm: the CTA-pair kernel takes f16 weights");
-    return false;
-  }
   if (p->s.bn != 256) {
     snprintf(err, errlen, "gemm: the CTA-pair kernel needs BN 256 (got %d)", p->s.bn);
     return false;
@@ -1691,7 +1846,9 @@ bool gemm_plan_pair(GemmPlan* p, const void* w, int w_rows, bool always, char* e
       snprintf(err, errlen, "gemm: no CTA-pair kernel for epilogue %d", p->s.epi);
       return false;
   }
-  if (!make_tmap_2d(&p->b_half, w, p->s.k, w_rows, static_cast<uint64_t>(p->s.k) * 2, BK, 128, err,
+  // Packed weights: each CTA bulk-copies its own chunks instead.
+  if (p->pk == kF16 &&
+      !make_tmap_2d(&p->b_half, w, p->s.k, w_rows, static_cast<uint64_t>(p->s.k) * 2, BK, 128, err,
                     errlen))
     return false;
   p->s.pair = always ? 2 : 1;
@@ -1700,7 +1857,8 @@ bool gemm_plan_pair(GemmPlan* p, const void* w, int w_rows, bool always, char* e
 
 // Whether a launch over `m` rows takes the CTA-pair kernel.
 bool use_pair(const GemmPlan& p, int m) {
-  return p.s.pair == 2 || (p.s.pair == 1 && (m + BM - 1) / BM >= kPairMinTiles);
+  const int min_tiles = p.pk == kF16 ? kPairMinTiles : kPairMinTilesPacked;
+  return p.s.pair == 2 || (p.s.pair == 1 && (m + BM - 1) / BM >= min_tiles);
 }
 
 void gemm_pick(int n, int k, int num_sms, int* bn, int* splits) {
@@ -1914,8 +2072,9 @@ void gemm_run_mlp(const GemmPlan& up, const GemmPlan& down, int m, void* act, in
                   uint32_t* status, cudaStream_t stream, int force_pair, long long wait_limit) {
   if (m <= 0) return;
   // force_pair: -1 by row tiles, 0 one-CTA tiles, 1 CTA pairs (kernel tests).
+  const int min_tiles = up.pk == kF16 ? kPairMlpMinTiles : kPairMinTilesPacked;
   const bool pair = up.s.pair && down.s.pair &&
-                    (force_pair >= 0 ? force_pair == 1 : (m + BM - 1) / BM >= kPairMlpMinTiles);
+                    (force_pair >= 0 ? force_pair == 1 : (m + BM - 1) / BM >= min_tiles);
   MlpArgs a{};
   auto fill = [&](GemmArgs& x, const GemmPlan& p, void* out, int ldo, size_t stride) {
     x.m = m;
@@ -1937,27 +2096,34 @@ void gemm_run_mlp(const GemmPlan& up, const GemmPlan& down, int m, void* act, in
   a.ready_target = ready_target;
   a.wait_limit = wait_limit > 0 ? wait_limit : kWaitLimitClocks;
   a.band = a.down.kb_per_split / 2;
+  a.up.wpack = up.wpack;
+  a.down.wpack = down.wpack;
+  const bool tanh_ = up.s.epi == kEpiGeGluTanh;
   if (pair) {
     const int m_pairs = (a.up.m_tiles + 1) / 2;
     const int units = m_pairs * (a.up.n_tiles + a.down.n_tiles * a.down.splits);
     const int max_pairs = up.num_sms / 2;
     const int grid = 2 * (units < max_pairs ? units : max_pairs);
-    if (up.s.epi == kEpiGeGluTanh)
-      launch_pdl(gemm_mlp2_kernel<kEpiGeGluTanh>, dim3(grid), dim3(192), Cfg2::SMEM, stream, up.a,
-                 up.b_half, down.a, down.b_half, a);
+    auto go = [&](auto kernel, int threads, int smem) {
+      launch_pdl(kernel, dim3(grid), dim3(threads), smem, stream, up.a, up.b_half, down.a,
+                 down.b_half, a);
+    };
+    if (up.pk == kQ4)
+      tanh_ ? go(gemm_mlp2_kernel<kEpiGeGluTanh, kQ4>, Cfg2<kQ4>::THREADS, Cfg2<kQ4>::SMEM)
+            : go(gemm_mlp2_kernel<kEpiGeGluErf, kQ4>, Cfg2<kQ4>::THREADS, Cfg2<kQ4>::SMEM);
+    else if (up.pk == kQ8)
+      tanh_ ? go(gemm_mlp2_kernel<kEpiGeGluTanh, kQ8>, Cfg2<kQ8>::THREADS, Cfg2<kQ8>::SMEM)
+            : go(gemm_mlp2_kernel<kEpiGeGluErf, kQ8>, Cfg2<kQ8>::THREADS, Cfg2<kQ8>::SMEM);
     else
-      launch_pdl(gemm_mlp2_kernel<kEpiGeGluErf>, dim3(grid), dim3(192), Cfg2::SMEM, stream, up.a,
-                 up.b_half, down.a, down.b_half, a);
+      tanh_ ? go(gemm_mlp2_kernel<kEpiGeGluTanh, kF16>, 192, Cfg2<>::SMEM)
+            : go(gemm_mlp2_kernel<kEpiGeGluErf, kF16>, 192, Cfg2<>::SMEM);
     return;
   }
   const int total = a.up.m_tiles * a.up.n_tiles + a.down.m_tiles * a.down.n_tiles * a.down.splits;
   const int grid = total < up.num_sms ? total : up.num_sms;
-  a.up.wpack = up.wpack;
-  a.down.wpack = down.wpack;
   auto go = [&](auto kernel, int threads, int smem) {
     launch_pdl(kernel, dim3(grid), dim3(threads), smem, stream, up.a, up.b, down.a, down.b, a);
   };
-  const bool tanh_ = up.s.epi == kEpiGeGluTanh;
   if (up.pk == kQ4)
     tanh_ ? go(gemm_mlp_kernel<kEpiGeGluTanh, kQ4>, Cfg<256, kQ4>::THREADS, Cfg<256, kQ4>::SMEM)
           : go(gemm_mlp_kernel<kEpiGeGluErf, kQ4>, Cfg<256, kQ4>::THREADS, Cfg<256, kQ4>::SMEM);

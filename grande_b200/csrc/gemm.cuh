@@ -95,7 +95,7 @@ bool gemm_plan(GemmPlan* p, const void* a, int a_rows_cap, int lda, const void* 
 // memory): the kernels fetch each K step's chunks with a bulk copy and
 // decode them into the f16 tile in shared memory, so the product is the one
 // the f16 weight gives, bit for bit. Epilogues kEpiF32, kEpiF16, the GeGLUs
-// and kEpiQkPrep; one-CTA kernels.
+// and kEpiQkPrep; one-CTA and CTA-pair kernels (gemm_plan_pair).
 bool gemm_plan_packed(GemmPlan* p, const void* a, int a_rows_cap, int lda, const void* wpack,
                       int dtype, int w_rows, int n_out, int k, int epi, int bn, int splits,
                       char* err, size_t errlen);
@@ -115,6 +115,10 @@ constexpr int kPairMinTiles = 16;
 // pass's 7 tiles, run as 4 pairs, the deeper pipeline only pays for the
 // empty half: 2.48 vs 2.40-2.44 ms per pass on one-CTA tiles.)
 constexpr int kPairMlpMinTiles = 16;
+
+// Packed weights take CTA pairs from 2 row tiles: each SM of a pair decodes
+// only its half of the weight tile, which halves the per-SM decode work.
+constexpr int kPairMinTilesPacked = 2;
 
 // Whether a launch of this plan over `m` rows takes the CTA-pair kernel.
 bool use_pair(const GemmPlan& p, int m);

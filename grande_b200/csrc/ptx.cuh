@@ -337,6 +337,43 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 
+// Arrive on a barrier of either CTA of the pair (shared::cluster address)
+// releasing this thread's prior shared-memory writes at cluster scope: a
+// thread of the other CTA that waits with cluster-scope acquire
+// (mbar_wait_cluster), and the MMAs it then issues, see them.
+__device__ __forceinline__ void mbar_arrive_release_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait with cluster-scope acquire (arrivals from the peer CTA).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  volatile int* abort_flag, uint32_t* status) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitLimitClocks) {
+      *abort_flag = 1;
+      if (status) atomicCAS(status, 0u, static_cast<uint32_t>(kDevWaitTimeout));
+      return false;
+    }
+  }
+}
+
 // 2-D TMA tile load into this CTA's shared memory whose completion is
 // counted on an mbarrier of either CTA of the pair (`cluster_bar`, a
 // shared::cluster address): both CTAs' halves complete on the leader's.

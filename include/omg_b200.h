@@ -315,14 +315,15 @@ int omg_debug_attention(int device, const uint16_t* q, const uint16_t* kv, const
  * as the f16 entry points take them): the kernels decode each K step's
  * blocks into the f16 tile in shared memory, as weight.wgsl:29-54 decodes
  * per use, so the results equal the f16 entry points' on f16(QTensor::get)
- * bit for bit. One-CTA kernels. */
+ * bit for bit. bn = 512 (and pair = 1) run the CTA-pair kernels, each CTA
+ * decoding its half of the weight tile. */
 int omg_debug_gemm_q(int device, const uint16_t* x_f16, int m, int k, int lda, int wdtype,
                      const uint8_t* w_codes, const uint8_t* w_scales, int w_rows, int n_out,
                      int epi, int bn, int splits, void* out, int ldo);
 int omg_debug_mlp_q(int device, const uint16_t* x, int m, int d, int wdtype,
                     const uint8_t* up_codes, const uint8_t* up_scales, int ff,
-                    const uint8_t* down_codes, const uint8_t* down_scales, uint16_t* act_out,
-                    float* y_out);
+                    const uint8_t* down_codes, const uint8_t* down_scales, int pair,
+                    uint16_t* act_out, float* y_out);
 
 /* Bit-exact checks of the device dequantization (model.rs:508-525
  * QTensor::get; weight.wgsl:29-54 decodes the same blocks per use). mode 0:

@@ -42,17 +42,18 @@ def run_gemm_q(device, x16, dtype, codes, sc, w_rows, n_out, epi, bn=0, splits=1
 @pytest.mark.parametrize("m,n,k,bn,splits", [
     (23, 96, 64, 128, 1), (130, 200, 96, 256, 1), (300, 520, 2080, 256, 2), (1, 128, 32, 128, 1),
     (788, 2048, 2048, 256, 2), (788, 3072, 2048, 256, 1), (150, 640, 2048, 256, 1),
+    (300, 520, 2080, 512, 2), (788, 2048, 2048, 512, 2), (130, 200, 96, 512, 1),
 ])
 def test_packed_gemm_equals_f16_gemm(device, dtype, m, n, k, bn, splits):
     rng = np.random.default_rng(m + n + k + dtype)
     x16 = (rng.uniform(-1, 1, (m, k)) * 2).astype(np.float16)
     w32 = (rng.standard_normal((n, k)) * 0.05).astype(np.float32)
     codes, sc, w16 = quantized(dtype, w32)
-    exp = run_gemm(device, x16, w16, n, 0, bn=bn, splits=splits)
+    exp = run_gemm(device, x16, w16, n, 0, bn=min(bn, 256), splits=splits)
     got = run_gemm_q(device, x16, dtype, codes, sc, n, n, 0, bn=bn, splits=splits)
     assert np.array_equal(got, exp)
     # f16 epilogue too
-    exp16 = run_gemm(device, x16, w16, n, 3, bn=bn)
+    exp16 = run_gemm(device, x16, w16, n, 3, bn=min(bn, 256))
     got16 = run_gemm_q(device, x16, dtype, codes, sc, n, n, 3, bn=bn)
     assert np.array_equal(got16, exp16)
 
@@ -71,10 +72,12 @@ def test_packed_gated_equals_f16_gated(device, dtype, m, n, k):
 
 
 @pytest.mark.parametrize("dtype", [O.Q4, O.Q8])
-@pytest.mark.parametrize("m,d,ff", [(700, 256, 1024), (788, 2048, 8192)])
-def test_packed_fused_mlp_equals_f16(device, dtype, m, d, ff):
+@pytest.mark.parametrize("pair", [0, 1])
+@pytest.mark.parametrize("m,d,ff", [(700, 256, 1024), (788, 2048, 8192), (130, 256, 512)])
+def test_packed_fused_mlp_equals_f16(device, dtype, m, d, ff, pair):
     """The fused FFN launch (gate+up, GeGLU, split-K down units gated on the
-    activation bands) on packed weights: the f16 launch's bits."""
+    activation bands) on packed weights, one-CTA tiles and CTA pairs: the
+    f16 launch's bits."""
     rng = np.random.default_rng(m + d + dtype)
     x16 = rng.uniform(-1, 1, (m, d)).astype(np.float16)
     w_up32 = interleave_gate_up((rng.standard_normal((ff, d)) * 0.05).astype(np.float32),
@@ -87,7 +90,7 @@ def test_packed_fused_mlp_equals_f16(device, dtype, m, d, ff):
     y = np.zeros((m, d), np.float32)
     L.check(L.lib().omg_debug_mlp_q(
         device, L.ptr(x16.view(np.uint16), L.C.c_uint16), m, d, dtype, L.ptr(uc, L.C.c_uint8),
-        L.ptr(us, L.C.c_uint8), ff, L.ptr(dc, L.C.c_uint8), L.ptr(ds, L.C.c_uint8),
+        L.ptr(us, L.C.c_uint8), ff, L.ptr(dc, L.C.c_uint8), L.ptr(ds, L.C.c_uint8), pair,
         L.ptr(act.view(np.uint16), L.C.c_uint16), L.ptr(y, L.C.c_float)))
     assert np.array_equal(act, a1)
     assert np.array_equal(y, y1)

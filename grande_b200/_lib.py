@@ -125,6 +125,8 @@ PROTOTYPES: dict[str, tuple] = {
                                     C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp, C.c_int]),
     "omg_debug_mlp_q": (C.c_int, [C.c_int, u16p, C.c_int, C.c_int, C.c_int, u8p, u8p, C.c_int,
                                    u8p, u8p, C.c_int, u16p, f32p]),
+    "omg_debug_gemm_time_q": (C.c_int, [C.c_int] * 9 + [f32p]),
+    "omg_debug_mlp_time": (C.c_int, [C.c_int] * 7 + [f32p]),
     "omg_debug_dequant": (C.c_int, [C.c_int, C.c_int, u8p, u8p, C.c_int, C.c_int, C.c_int, u16p,
                                      u16p]),
     "omg_engine_weight_f16": (C.c_int, [vp, C.c_char_p, u16p, sz]),

@@ -465,3 +465,114 @@ extern "C" int omg_debug_mlp_q(int device, const uint16_t* x, int m, int d, int 
     return 0;
   });
 }
+
+extern "C" int omg_debug_gemm_time_q(int device, int m, int n, int k, int epi, int bn, int splits,
+                                     int wdtype, int iters, float* ms) {
+  return guarded([&]() -> int {
+    if (wdtype != kQ4 && wdtype != kQ8) fail("omg_debug_gemm_time_q: dtype %d", wdtype);
+    CUDA_TRY(cudaSetDevice(device));
+    gemm_setup_device();
+    if (bn == 0) {
+      int sms = 148;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+      gemm_pick(n, k, sms, &bn, &splits);
+    }
+    const bool gated = epi == kEpiGeGluTanh || epi == kEpiGeGluErf;
+    const int w_rows = gated ? (n + 127) / 128 * 256 : n;
+    const size_t wb = packed_bytes(wdtype, w_rows, k);
+    DevBuf dx, dw, dout, dstat;
+    if (!dx.alloc(static_cast<size_t>(m) * k * 2) || !dw.alloc(wb) ||
+        !dout.alloc(static_cast<size_t>(m) * n * 4 * std::max(splits, 1)) || !dstat.alloc(4))
+      return set_error("cudaMalloc failed");
+    CUDA_TRY(cudaMemset(dx.p, 0x3c, static_cast<size_t>(m) * k * 2));
+    CUDA_TRY(cudaMemset(dw.p, 0x21, wb));
+    CUDA_TRY(cudaMemset(dstat.p, 0, 4));
+    GemmPlan plan;
+    char err[256];
+    const bool pair = bn == 512;
+    if (!gemm_plan_packed(&plan, dx.p, m, k, dw.p, wdtype, w_rows, n, k, epi, pair ? 256 : bn,
+                          splits, err, sizeof err))
+      return set_error(err);
+    if (pair && !gemm_plan_pair(&plan, nullptr, w_rows, true, err, sizeof err)) return set_error(err);
+    cudaEvent_t a, b;
+    CUDA_TRY(cudaEventCreate(&a));
+    CUDA_TRY(cudaEventCreate(&b));
+    for (int i = 0; i < 3; ++i)
+      gemm_run(plan, m, dout.p, n, static_cast<size_t>(m) * n, static_cast<uint32_t*>(dstat.p), 0);
+    CUDA_TRY(cudaEventRecord(a, 0));
+    for (int i = 0; i < iters; ++i)
+      gemm_run(plan, m, dout.p, n, static_cast<size_t>(m) * n, static_cast<uint32_t*>(dstat.p), 0);
+    CUDA_TRY(cudaEventRecord(b, 0));
+    CUDA_TRY(cudaEventSynchronize(b));
+    float t = 0;
+    CUDA_TRY(cudaEventElapsedTime(&t, a, b));
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    uint32_t st = 0;
+    CUDA_TRY(cudaMemcpy(&st, dstat.p, 4, cudaMemcpyDeviceToHost));
+    if (st) return set_error("gemm kernel reported device status %u", st);
+    *ms = t / iters;
+    return 0;
+  });
+}
+
+extern "C" int omg_debug_mlp_time(int device, int m, int d, int ff, int wdtype, int pair, int iters,
+                                  float* ms) {
+  return guarded([&]() -> int {
+    CUDA_TRY(cudaSetDevice(device));
+    gemm_setup_device();
+    if (m <= 0 || d % 128 != 0 || ff % d != 0) fail("omg_debug_mlp_time: shapes");
+    const int splits = ff / d;
+    const bool pk = wdtype == kQ4 || wdtype == kQ8;
+    const size_t wub = pk ? packed_bytes(wdtype, 2 * ff, d) : static_cast<size_t>(2) * ff * d * 2;
+    const size_t wdb = pk ? packed_bytes(wdtype, d, ff) : static_cast<size_t>(d) * ff * 2;
+    const size_t slab = static_cast<size_t>(m) * d;
+    const int m_tiles = (m + 127) / 128;
+    DevBuf dx, dwu, dwd, dact, dslab, dready, dstat;
+    if (!dx.alloc(slab * 2) || !dwu.alloc(wub) || !dwd.alloc(wdb) ||
+        !dact.alloc(static_cast<size_t>(m) * ff * 2) || !dslab.alloc(slab * splits * 4) ||
+        !dready.alloc(static_cast<size_t>(m_tiles) * splits * 4) || !dstat.alloc(4))
+      return set_error("cudaMalloc failed");
+    CUDA_TRY(cudaMemset(dx.p, 0x3c, slab * 2));
+    CUDA_TRY(cudaMemset(dwu.p, pk ? 0x21 : 0x20, wub));
+    CUDA_TRY(cudaMemset(dwd.p, pk ? 0x21 : 0x20, wdb));
+    CUDA_TRY(cudaMemset(dstat.p, 0, 4));
+    GemmPlan up, down;
+    char err[256];
+    bool ok = pk ? gemm_plan_packed(&up, dx.p, m, d, dwu.p, wdtype, 2 * ff, ff, d, kEpiGeGluTanh,
+                                    256, 1, err, sizeof err) &&
+                       gemm_plan_packed(&down, dact.p, m, ff, dwd.p, wdtype, d, d, ff, kEpiF32,
+                                        256, splits, err, sizeof err)
+                 : gemm_plan(&up, dx.p, m, d, dwu.p, 2 * ff, ff, d, kEpiGeGluTanh, 256, 1, err,
+                             sizeof err) &&
+                       gemm_plan(&down, dact.p, m, ff, dwd.p, d, d, ff, kEpiF32, 256, splits, err,
+                                 sizeof err);
+    ok = ok && gemm_plan_pair(&up, pk ? nullptr : dwu.p, 2 * ff, false, err, sizeof err) &&
+         gemm_plan_pair(&down, pk ? nullptr : dwd.p, d, false, err, sizeof err);
+    if (!ok) return set_error(err);
+    if (!gemm_mlp_ok(up, down)) return set_error("omg_debug_mlp_time: shapes not fusable");
+    const int target_step = 4 * up.s.n_tiles / down.s.splits;
+    cudaEvent_t a, b;
+    CUDA_TRY(cudaEventCreate(&a));
+    CUDA_TRY(cudaEventCreate(&b));
+    auto once = [&]() {
+      cudaMemsetAsync(dready.p, 0, static_cast<size_t>(m_tiles) * splits * 4, 0);
+      gemm_run_mlp(up, down, m, dact.p, ff, dslab.p, d, slab, static_cast<int*>(dready.p),
+                   target_step, static_cast<uint32_t*>(dstat.p), 0, pair ? 1 : 0);
+    };
+    for (int i = 0; i < 3; ++i) once();
+    CUDA_TRY(cudaEventRecord(a, 0));
+    for (int i = 0; i < iters; ++i) once();
+    CUDA_TRY(cudaEventRecord(b, 0));
+    CUDA_TRY(cudaEventSynchronize(b));
+    float t = 0;
+    CUDA_TRY(cudaEventElapsedTime(&t, a, b));
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    uint32_t st = 0;
+    CUDA_TRY(cudaMemcpy(&st, dstat.p, 4, cudaMemcpyDeviceToHost));
+    if (st) return set_error("mlp kernel reported device status %u", st);
+    *ms = t / iters;
+    return 0;
+  });
+}

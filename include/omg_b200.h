@@ -354,6 +354,13 @@ int omg_engine_arm_wait_timeout(omg_engine* e, long long clocks);
  * average per launch. */
 int omg_debug_gemm_time(int device, int m, int n, int k, int epi, int bn, int splits, int iters,
                         float* ms);
+/* The same over packed Q4_0 / Q8_0 weights (wdtype 2 / 1), and the fused FFN
+ * launch of an [m, d] x ff layer (wdtype 0: f16 weights; pair 1: CTA pairs):
+ * average ms per launch. */
+int omg_debug_gemm_time_q(int device, int m, int n, int k, int epi, int bn, int splits,
+                          int wdtype, int iters, float* ms);
+int omg_debug_mlp_time(int device, int m, int d, int ff, int wdtype, int pair, int iters,
+                       float* ms);
 
 /* ---- Laya / ModernBERT encoder (crates/omg-wgpu/src/laya.rs) ---------------
  * The encoder behind omg_core::Decider (crates/omg-core/src/engine.rs:70-93,

@@ -69,7 +69,7 @@ def args_():
     ap.add_argument("--config", default="e2b-q4")
     ap.add_argument("--profile-iters", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--weights", choices=["packed", "f16"], default="packed",
+    ap.add_argument("--weights", choices=["packed", "f16"], default="f16",
                     help="Q4_0/Q8_0 linears kept packed (decoded per tile) or as f16 rows")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layer count (small cases for ncu captures only)")

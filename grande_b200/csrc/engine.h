@@ -155,7 +155,7 @@ class EngineBuilder {
   void push(const std::string& name, const HostTensor& t);
   void set_per_layer_table(HostTensor t);
   // Q4_0 / Q8_0 linears pushed from now on: packed chunks decoded per tile
-  // (true, the default) or f16 rows decoded once here.
+  // (true) or f16 rows decoded once here (false, the default: faster).
   void set_packed(bool on) { packed_ = on; }
   std::unique_ptr<Engine> finish(size_t capacity, size_t max_rows);
 
@@ -179,7 +179,7 @@ class EngineBuilder {
   std::map<std::string, bool> pushed_;
   std::map<std::string, DevBuffer> lin_;    // f16 linears (gate+up interleaved as "blk.N.gate_up")
   std::map<std::string, PackedLinear> pk_;  // Q4_0 / Q8_0 linears, packed
-  bool packed_ = true;
+  bool packed_ = false;
   std::map<std::string, DevBuffer> norms_;  // f32 norm weights
   std::map<std::string, float> scalars_;
   Packed embed_;

@@ -504,8 +504,9 @@ class EngineBuilder:
 
     def set_weight_layout(self, packed: bool):
         """Q4_0 / Q8_0 linears pushed from now on: kept packed and decoded
-        per tile in shared memory by the GEMMs (True, the default), or
-        decoded once into f16 rows (False; 3.6x the memory, same results)."""
+        per tile in shared memory by the GEMMs (True; 18 bytes per 32 Q4_0
+        weights), or decoded once into f16 rows (False, the default: faster,
+        3.6x the memory). Same results either way."""
         check(lib().omg_builder_set_weight_layout(self._h, 0 if packed else 1))
 
     def push(self, name: str, t: QTensor):

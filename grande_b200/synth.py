@@ -102,7 +102,7 @@ def tensor(seed: int, name: str, shape, dtype: Dtype, qk_scale: float = 1.0) -> 
 
 def build_engine(shape: Shape, capacity: int, max_rows: int, device: int = 0, seed: int = 0,
                  threads: int = 8, qk_scale: float = 1.0, tensors: dict | None = None,
-                 packed: bool = True):
+                 packed: bool = False):
     """Generate, quantize and push every tensor (generation in a thread pool;
     ctypes releases the GIL), then finish the engine. `tensors` (name ->
     QTensor) supplies already generated tensors, e.g. a deeper model's, of

@@ -120,10 +120,11 @@ int omg_builder_push(omg_builder* b, const char* name, int dtype, const int64_t*
 
 /* How Q4_0 / Q8_0 linears pushed after this call are kept on the device
  * (the reference keeps them packed and decodes per use, weight.wgsl:29-54):
- * OMG_WEIGHTS_PACKED (the default) keeps the packed blocks and decodes them
- * per tile in shared memory inside the tensor-core GEMMs; OMG_WEIGHTS_F16
- * decodes each once at push into f16 rows (3.6x the memory, no per-tile
- * decode). Both give the same results bit for bit. */
+ * OMG_WEIGHTS_PACKED keeps the packed blocks (18 / 34 bytes per 32 weights)
+ * and decodes them per tile in shared memory inside the tensor-core GEMMs;
+ * OMG_WEIGHTS_F16 (the default) decodes each once at push into f16 rows
+ * (3.6x / 1.9x the memory, no per-tile decode, faster). Both give the same
+ * results bit for bit. */
 #define OMG_WEIGHTS_PACKED 0
 #define OMG_WEIGHTS_F16 1
 int omg_builder_set_weight_layout(omg_builder* b, int layout);

@@ -56,10 +56,13 @@ def test_load_time_and_lm_head_decoders_are_exact(device, dtype):
             assert np.array_equal(recon[fin].astype(np.float32), ref[fin])
 
 
+@pytest.mark.parametrize("packed", [False, True])
 @pytest.mark.parametrize("config,layer", [("e2b-q4", 4), ("gemma3-270m-q8", 5)])
-def test_engine_weights_are_f16_of_the_reference_dequant(device, config, layer):
+def test_engine_weights_are_f16_of_the_reference_dequant(device, config, layer, packed):
+    # f16 rows: the load-time decoder's output; packed: the chunks decoded by
+    # the GEMMs' own tile decoder.
     shape = dataclasses.replace(synth.CONFIGS[config], layers=layer + 1)
-    eng = synth.build_engine(shape, 64, 4, device=device)
+    eng = synth.build_engine(shape, 64, 4, device=device, packed=packed)
     try:
         d, ff = shape.d, shape.ff
         qkv = (shape.heads + 2 * shape.kv_heads) * 256

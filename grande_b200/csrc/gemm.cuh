@@ -116,9 +116,11 @@ constexpr int kPairMinTiles = 16;
 // empty half: 2.48 vs 2.40-2.44 ms per pass on one-CTA tiles.)
 constexpr int kPairMlpMinTiles = 16;
 
-// Packed weights take CTA pairs from 2 row tiles: each SM of a pair decodes
-// only its half of the weight tile, which halves the per-SM decode work.
-constexpr int kPairMinTilesPacked = 2;
+// Packed weights take CTA pairs from as many row tiles as f16 weights do
+// (each SM of a pair decodes only its half of the weight tile, but at the
+// decoder's ~4 instructions per weight the pair kernels measured slower
+// than one-CTA tiles on the E2B FFN: 214 vs 148 us).
+constexpr int kPairMinTilesPacked = kPairMinTiles;
 
 // Whether a launch of this plan over `m` rows takes the CTA-pair kernel.
 bool use_pair(const GemmPlan& p, int m);

@@ -731,11 +731,28 @@ __global__ void __launch_bounds__(Cfg<BN, PK>::THREADS, 1)
   // dependent launch: the prologue above may overlap their tail); the packed
   // weights never change during a pass, so their copies start at once. The
   // grid is persistent (one wave), so the next kernel may begin launching now.
-  if (!(C::PACKED && warp == 6)) griddep_wait();
+  if (!(C::PACKED && warp == 6) && warp != 0) griddep_wait();
   griddep_launch();
 
   if (warp == 0) {
     if (lane == 0) {
+      // f16 weights never change during a pass: the first tile's first ring
+      // of weight tiles is requested before the wait for the previous
+      // kernel, which produces only the activations.
+      int pre = 0;
+      if constexpr (!C::PACKED) {
+        if (static_cast<int>(blockIdx.x) < total) {
+          const TileId id = decode_tile(g, blockIdx.x);
+          const int kb0 = id.split * g.kb_per_split;
+          const int kb1 = min(g.kb_total, kb0 + g.kb_per_split);
+          pre = min(C::STAGES, kb1 - kb0);
+          for (int j = 0; j < pre; ++j) {
+            mbar_expect_tx(&full[j], C::B_BYTES);
+            tma_load_2d(sb + j * C::B_BYTES, &tmb, &full[j], (kb0 + j) * BK, id.n * BN);
+          }
+        }
+      }
+      griddep_wait();
       int it = 0;
       for (int tile = blockIdx.x; tile < total && !*abort_flag; tile += gridDim.x) {
         const TileId id = decode_tile(g, tile);
@@ -753,6 +770,9 @@ __global__ void __launch_bounds__(Cfg<BN, PK>::THREADS, 1)
           if constexpr (C::PACKED) {
             mbar_arrive_expect_tx(&full[s], C::A_BYTES);
             tma_load_2d(sa + s * C::A_BYTES, &tma, &full[s], kb * BK, m_tile * BM);
+          } else if (it < pre) {
+            mbar_arrive_expect_tx(&full[s], C::A_BYTES);
+            tma_load_2d(sa + s * C::A_BYTES, &tma, &full[s], kb * BK, m_tile * BM);
           } else {
             mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
             tma_load_2d(sa + s * C::A_BYTES, &tma, &full[s], kb * BK, m_tile * BM);
@@ -761,6 +781,8 @@ __global__ void __launch_bounds__(Cfg<BN, PK>::THREADS, 1)
         }
         if (!ok) break;
       }
+    } else {
+      griddep_wait();
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -1272,11 +1294,26 @@ __global__ void __launch_bounds__(Cfg<256, PK>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (!(C::PACKED && warp == 6)) griddep_wait();
+  if (!(C::PACKED && warp == 6) && warp != 0) griddep_wait();
   griddep_launch();
 
   if (warp == 0) {
     if (lane == 0) {
+      // The first unit's first ring of weight tiles before the wait for the
+      // previous kernel (f16 weights never change during a pass).
+      int pre = 0;
+      if constexpr (!C::PACKED) {
+        if (static_cast<int>(blockIdx.x) < total) {
+          const Unit x = decode(blockIdx.x);
+          pre = min(C::STAGES, x.kb1 - x.kb0);
+          for (int j = 0; j < pre; ++j) {
+            mbar_expect_tx(&full[j], C::B_BYTES);
+            tma_load_2d(sb + j * C::B_BYTES, x.up ? &tb_up : &tb_dn, &full[j], (x.kb0 + j) * BK,
+                        x.n * BN);
+          }
+        }
+      }
+      griddep_wait();
       int it = 0;
       for (int u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
         const Unit x = decode(u);
@@ -1315,6 +1352,9 @@ __global__ void __launch_bounds__(Cfg<256, PK>::THREADS, 1)
           if constexpr (C::PACKED) {
             mbar_arrive_expect_tx(&full[s], C::A_BYTES);
             tma_load_2d(sa + s * C::A_BYTES, ta, &full[s], kb * BK, x.m * BM);
+          } else if (it < pre) {
+            mbar_arrive_expect_tx(&full[s], C::A_BYTES);
+            tma_load_2d(sa + s * C::A_BYTES, ta, &full[s], kb * BK, x.m * BM);
           } else {
             mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
             tma_load_2d(sa + s * C::A_BYTES, ta, &full[s], kb * BK, x.m * BM);
@@ -1323,6 +1363,8 @@ __global__ void __launch_bounds__(Cfg<256, PK>::THREADS, 1)
         }
         if (!ok) break;
       }
+    } else {
+      griddep_wait();
     }
   } else if (warp == 1) {
     if (lane == 0) {

@@ -8,6 +8,7 @@ from __future__ import annotations
 import ctypes as C
 import json
 import threading
+from itertools import chain
 from dataclasses import dataclass, field
 from enum import IntEnum
 from typing import Optional, Sequence
@@ -239,29 +240,32 @@ class _Branches:
         self.keep = []
         self.groups = (_lib.GroupC * len(groups))()
         for gi, g in enumerate(groups):
-            prefix = np.ascontiguousarray(np.asarray(g.prefix, dtype=np.int64).astype(np.uint32))
-            brs = (_lib.Branch * max(1, len(g.branches)))()
+            prefix = np.fromiter(g.prefix, dtype=np.uint32, count=len(g.prefix))
+            nb = len(g.branches)
+            brs = (_lib.Branch * max(1, nb))()
             # One array for all branch tokens and one for all wanted rows; each
             # branch points at its slice.
-            tok_all, want_all, spans = [], [], []
-            for b in g.branches:
-                spans.append((len(tok_all), len(b.tokens), len(want_all), len(b.want)))
-                tok_all.extend(b.tokens)
-                want_all.extend(b.want)
-            toks = np.asarray(tok_all, dtype=np.int64).astype(np.int32)
-            wants = np.asarray(want_all, dtype=np.int64).astype(np.uint64)
+            ntok = [len(b.tokens) for b in g.branches]
+            nwant = [len(b.want) for b in g.branches]
+            toks = np.fromiter(chain.from_iterable(b.tokens for b in g.branches),
+                               dtype=np.int32, count=sum(ntok))
+            wants = np.fromiter(chain.from_iterable(b.want for b in g.branches),
+                                dtype=np.uint64, count=sum(nwant))
             tb, wb = toks.ctypes.data, wants.ctypes.data
-            for bi, (to, tn, wo, wn) in enumerate(spans):
+            to = wo = 0
+            for bi in range(nb):
                 br = brs[bi]
                 br.tokens = tb + 4 * to
-                br.n_tokens = tn
+                br.n_tokens = ntok[bi]
                 br.want = wb + 8 * wo
-                br.n_want = wn
+                br.n_want = nwant[bi]
+                to += ntok[bi]
+                wo += nwant[bi]
             self.keep += [prefix, brs, toks, wants]
             self.groups[gi].prefix = _lib.ptr(prefix, C.c_uint32)
             self.groups[gi].n_prefix = prefix.size
             self.groups[gi].branches = brs
-            self.groups[gi].n_branches = len(g.branches)
+            self.groups[gi].n_branches = nb
 
 
 class SavedState:

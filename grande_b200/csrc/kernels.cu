@@ -794,36 +794,50 @@ __global__ void __launch_bounds__(LT_THREADS, 1)
     const int xr = t256 >> 3, xp = t256 & 7;
     RawBlock<DT> rb[4];
     float4 xa[4], xb[4];
-    auto fetch = [&](int i, RawBlock<DT>& dst, float4& a, float4& b) {
-      const int lu = i / ksteps, kb = i - lu * ksteps;
-      const int u = blockIdx.x + lu * gridDim.x;
-      const int v = (u / rgroups) * 128 + r;
-      const int rr = (u % rgroups) * LT_N + xr;
-      load_raw_block<DT>(codes, scales, static_cast<size_t>(v) * nb + 2 * kb + half,
-                         i < steps && v < vocab, dst);
-      if (i < steps && rr < nrows) {
+    // The fetch position (step fi: K step f_kb of local unit f_lu) advances
+    // one step per call, in step order, so the unit's table row and readout
+    // row are recomputed once per unit instead of dividing per step.
+    int fi = 0, f_lu = 0, f_kb = 0;
+    int f_v = 0, f_rr = 0;
+    auto unit_rows = [&]() {
+      const int u = static_cast<int>(blockIdx.x) + f_lu * static_cast<int>(gridDim.x);
+      f_v = (u / rgroups) * 128 + r;
+      f_rr = (u % rgroups) * LT_N + xr;
+    };
+    unit_rows();
+    auto fetch = [&](RawBlock<DT>& dst, float4& a, float4& b) {
+      const bool live = fi < steps;
+      load_raw_block<DT>(codes, scales, static_cast<size_t>(f_v) * nb + 2 * f_kb + half,
+                         live && f_v < vocab, dst);
+      if (live && f_rr < nrows) {
         const float4* src =
-            reinterpret_cast<const float4*>(rows + static_cast<size_t>(rr) * d + kb * 64 + 8 * xp);
+            reinterpret_cast<const float4*>(rows + static_cast<size_t>(f_rr) * d + f_kb * 64 + 8 * xp);
         a = __ldg(src);
         b = __ldg(src + 1);
       } else {
         a = b = make_float4(0.f, 0.f, 0.f, 0.f);
       }
+      ++fi;
+      if (++f_kb == ksteps) {
+        f_kb = 0;
+        ++f_lu;
+        unit_rows();
+      }
     };
 #pragma unroll
-    for (int j = 0; j < 4; ++j) fetch(j, rb[j], xa[j], xb[j]);
+    for (int j = 0; j < 4; ++j) fetch(rb[j], xa[j], xb[j]);
     int prev = -1;
     bool ok = true;
+    int s = 0, sph = 0;     // ring slot of step i and its wrap count
+    int kb_i = 0, lu_i = 0; // K step and local unit of step i
     for (int i0 = 0; i0 < steps && ok; i0 += 4) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int i = i0 + j;
         if (i >= steps || !ok) break;
-        const int s = i % LT_STAGES;
         if (i >= LT_STAGES) {
           int w = 0;
-          if (lane == 0)
-            w = mbar_wait(&empty[s], ((i / LT_STAGES) & 1) ^ 1, abort_flag, status) ? 1 : 0;
+          if (lane == 0) w = mbar_wait(&empty[s], (sph & 1) ^ 1, abort_flag, status) ? 1 : 0;
           if (!__shfl_sync(0xffffffffu, w, 0)) {
             ok = false;
             break;
@@ -856,15 +870,20 @@ __global__ void __launch_bounds__(LT_THREADS, 1)
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) mbar_arrive(&full[s]);
-        fetch(i + 4, rb[j], xa[j], xb[j]);
-        if ((i + 1) % ksteps == 0) {
+        fetch(rb[j], xa[j], xb[j]);
+        if (++s == LT_STAGES) {
+          s = 0;
+          ++sph;
+        }
+        if (++kb_i == ksteps) {
+          kb_i = 0;
           // The previous unit's logits (its MMAs ran while this one was staged).
-          const int lu = i / ksteps;
-          if (prev >= 0 && !epilogue(prev, lu - 1)) {
+          if (prev >= 0 && !epilogue(prev, lu_i - 1)) {
             ok = false;
             break;
           }
-          prev = blockIdx.x + lu * gridDim.x;
+          prev = static_cast<int>(blockIdx.x) + lu_i * static_cast<int>(gridDim.x);
+          ++lu_i;
         }
       }
     }

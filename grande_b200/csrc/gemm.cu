@@ -172,10 +172,15 @@ struct PackedPipe {
 };
 
 __device__ __forceinline__ float gelu_tanh(float x) {
-  // Gemma's tanh GELU with the argument clamped to +-15 (matmul_gated.wgsl:126-134).
+  // Gemma's tanh GELU with the argument clamped to +-15
+  // (matmul_gated.wgsl:126-134), in its logistic form:
+  // 0.5 x (1 + tanh z) = x / (1 + e^(-2 z)), with the fast hardware
+  // exponential and division (relative error ~1e-6, far below the f16
+  // rounding of the stored activation; WGSL's tanh is not correctly rounded
+  // either). 1-1.5 us less per E2B / E4B FFN launch than tanhf.
   float z = 0.7978845608028654f * (x + 0.044715f * x * x * x);
   z = fminf(fmaxf(z, -15.0f), 15.0f);
-  return 0.5f * x * (1.0f + tanhf(z));
+  return __fdividef(x, 1.0f + __expf(-2.0f * z));
 }
 
 __device__ __forceinline__ float erf_as(float x) {

@@ -107,6 +107,9 @@ PROTOTYPES: dict[str, tuple] = {
                                              C.c_char_p, sz, szp]),
     "omg_debug_attention": (C.c_int, [C.c_int, u16p, u16p, i32p, C.c_int, C.c_int, C.c_int,
                                       C.c_int, C.c_int, C.c_int, C.c_int, u16p]),
+    "omg_debug_attention_time": (C.c_int, [C.c_int, u16p, u16p, i32p, C.c_int, C.c_int, C.c_int,
+                                           C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                           C.POINTER(C.c_float)]),
     "omg_gemm_splitk_noalloc": (C.c_int, [C.c_int, vp, C.c_int, C.c_int, C.c_int, vp, C.c_int,
                                           C.c_int, vp, C.c_int, vp]),
     "omg_engine_record_event": (C.c_int, [vp, C.c_int]),

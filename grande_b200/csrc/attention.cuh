@@ -23,30 +23,12 @@ __host__ __device__ inline bool attn_visible(int qp, int qs, int kp, int ks, int
          (window == 0 || static_cast<unsigned>(qp - kp) < static_cast<unsigned>(window));
 }
 
-// ---- head_dim 512: mma.sync kernel ------------------------------------------
-
-struct AttnArgs {
-  const __half* q;      // [t, heads * hd]: workspace rows 0..t = cache rows base..base+t
-  const __half* kv;     // [rows, 2 * kv_heads * hd]: K heads then V heads per cache row
-  const TokMeta* meta;  // cache-row order
-  __half* out;          // [t, heads * hd]
-  const int2* ctas;     // per CTA: first workspace token, token count (attention_schedule)
-  int n_ctas;
-  int t, base, heads, kv_heads, hd, window;
-};
-
-// Split the t tokens of a pass (their metadata, workspace order) into CTA
-// runs of at most 64 / (heads per KV head) tokens that never cross a request
-// group (groups differ in row_lo).
-void attention_schedule(const TokMeta* meta, int t, int hpg, std::vector<int2>* out);
-
-void launch_attention(const AttnArgs& a, cudaStream_t s);
-
-// ---- head_dim 256: tensor-core (tcgen05) kernel -----------------------------
+// ---- tensor-core (tcgen05) kernel, head_dim 256 and 512 ---------------------
 //
 // A run is up to 128 / (heads per KV head) consecutive query tokens of one
 // request group: 128 query rows (the tokens x the query heads sharing one KV
-// head). One CTA per (run, KV head) visits, with an online softmax, every
+// head). One CTA per (run, KV head; head_dim 512: and 256-dim half of V)
+// visits, with an online softmax, every
 // 64-key tile that any of its rows sees; tiles sit on a grid anchored at the
 // group's first cache row, so a token meets its keys in the same tiles
 // whatever else shares the pass.
@@ -95,11 +77,12 @@ struct AttnFlashArgs {
   int n_items;
   const AttnFlashMerge* merges;
   int n_merges;
-  float* part_o;         // [slot x kv_heads][128 rows][256] unnormalised O
+  float* part_o;         // [slot x kv_heads][128 rows][hd] unnormalised O
   float2* part_ml;       // [slot x kv_heads][128 rows] (reference max, row sum)
-  __half* out;           // [t, heads * 256] f16
+  __half* out;           // [t, heads * hd] f16
   uint32_t* status;      // device status word (bounded waits)
   int t, base, heads, kv_heads, hpg, window;
+  int hd = 256;          // head_dim: 256 or 512
 };
 
 // Per workspace token (metadata `meta_ws` = cache rows base..base+t) the
@@ -120,12 +103,13 @@ int attention_flash_runs(const TokMeta* meta_ws, const int4* vis, int t, int hpg
                          std::vector<AttnFlashRun>* runs, std::vector<int>* tiles,
                          std::vector<AttnFlashItem>* items, std::vector<AttnFlashMerge>* merges);
 
-// Tensor maps of the tensor-core kernel: q16 [t_cap][heads * 256] f16 and one
-// layer's K/V cache [rows_cap][2 * kv_heads * 256] f16 (64-key boxes).
-bool attention_map_q(CUtensorMap* m, const void* q16, int t_cap, int heads, int kv_heads,
+// Tensor maps of the tensor-core kernel: q16 [t_cap][heads * hd] f16 and one
+// layer's K/V cache [rows_cap][2 * kv_heads * hd] f16 (64-key boxes); hd 256
+// or 512.
+bool attention_map_q(CUtensorMap* m, const void* q16, int t_cap, int heads, int kv_heads, int hd,
                      char* err, size_t errlen);
-bool attention_map_kv(CUtensorMap* m, const void* kv, int rows_cap, int kv_heads, char* err,
-                      size_t errlen);
+bool attention_map_kv(CUtensorMap* m, const void* kv, int rows_cap, int kv_heads, int hd,
+                      char* err, size_t errlen);
 
 // `p_lo`: also feed what f16 rounding dropped from P (a second P.V product),
 // so P carries ~22 bits instead of f16's 11.
@@ -138,7 +122,7 @@ void launch_attention_flash(const CUtensorMap& tq, const CUtensorMap& tkv,
 void launch_attention_merge(const AttnFlashArgs& a, cudaStream_t s);
 
 // Dynamic shared memory the attention kernels need (set once per device).
+// Shared-memory limits of the attention kernels on the current device.
 void attention_setup_device();
-void attention_flash_setup_device();
 
 }  // namespace omg

@@ -1,6 +1,6 @@
-// Block-causal GQA attention on the 5th-generation tensor cores, head_dim 256
-// (see attention.cuh). Replaces crates/omg-wgpu/src/shaders/attention.wgsl
-// for the decoder's head_dim-256 layers.
+// Block-causal GQA attention on the 5th-generation tensor cores, head_dim
+// 256 and 512 (see attention.cuh). Replaces
+// crates/omg-wgpu/src/shaders/attention.wgsl for the decoder's layers.
 //
 // One CTA = one run (up to 128 query rows: a run's tokens x the query heads of
 // one KV head) against every 64-key tile any of its rows sees, with an online
@@ -23,6 +23,14 @@
 // zeros, so a row's result depends only on its own visible keys and the
 // key grid anchored at its group's first row: a group's rows are the same
 // bits wherever it sits in the pass, and whether its prefix is resident.
+//
+// head_dim 512 (Gemma 4's global layers): a 128 x 512 f32 O would fill all
+// 512 TMEM columns, so two CTAs (grid.z) share a run, each accumulating the
+// O of one 256-dim half of V; both compute the whole S = Q K^T (K = 512)
+// and so the same softmax, bit for bit. Q (8 x [128 rows][64 dims], 128 KB)
+// stays resident; K streams through a ring of four [64 keys][64 dims]
+// chunks, the S MMAs of a tile consuming them as they land; the V half is
+// one buffer of 4 chunks.
 #include <algorithm>
 #include <climits>
 #include <cstdio>
@@ -36,7 +44,7 @@ namespace omg {
 
 namespace {
 
-constexpr int FA_HD = 256;
+constexpr int FA_HD = 256;                              // dims of O per CTA
 constexpr int FA_KEYS = kAttnTileKeys;                  // 64 keys per tile
 constexpr int FA_QCH = 128 * 128;                       // [128 rows][128 bytes]
 constexpr int FA_KVCH = FA_KEYS * 128;                  // [64 keys][128 bytes]
@@ -58,19 +66,35 @@ template <bool PLO>
 constexpr int fa_p_slot_bytes() {
   return (PLO ? 2 : 1) * FA_P_BYTES;
 }
-template <bool PLO>
-constexpr int fa_smem() {
-  return 1024 + FA_Q_BYTES + 4 * FA_KV_BYTES + fa_p_slots<PLO>() * fa_p_slot_bytes<PLO>() + 256;
+// head_dim 512: the K ring's chunks.
+constexpr int FA_KRING = 4;
+// Q, then K/V: head_dim 256 two K and two V tiles; 512 the K ring and one V
+// half.
+template <int HD>
+constexpr int fa_q_bytes() {
+  return (HD / 64) * FA_QCH;
 }
-static_assert(fa_smem<false>() <= 227 * 1024 && fa_smem<true>() <= 227 * 1024,
+template <int HD>
+constexpr int fa_kv_area() {
+  return HD == 256 ? 4 * FA_KV_BYTES : FA_KRING * FA_KVCH + FA_KV_BYTES;
+}
+template <int HD, bool PLO>
+constexpr int fa_smem() {
+  return 1024 + fa_q_bytes<HD>() + fa_kv_area<HD>() + fa_p_slots<PLO>() * fa_p_slot_bytes<PLO>() +
+         256;
+}
+static_assert(fa_smem<256, false>() <= 227 * 1024 && fa_smem<256, true>() <= 227 * 1024 &&
+                  fa_smem<512, false>() <= 227 * 1024 && fa_smem<512, true>() <= 227 * 1024,
               "attention shared memory above the per-CTA limit");
 
 // B_P*: P of the slot written (4 softmax warps arrive); B_O*: the P.V of the
-// tiles of that parity done.
+// tiles of that parity done. head_dim 512: B_R* / B_E* the K ring's chunks
+// landed / consumed, B_V0 / B_VF0 the one V buffer.
 enum {
   B_Q = 0, B_K0, B_K1, B_V0, B_V1, B_S0, B_S1, B_P0, B_P1, B_O0, B_O1, B_KF0, B_KF1, B_VF0,
-  B_VF1, B_N
+  B_VF1, B_R0, B_R1, B_R2, B_R3, B_E0, B_E1, B_E2, B_E3, B_N
 };
+static_assert(B_R0 + FA_KRING == B_E0 && B_E0 + FA_KRING == B_N, "K ring barriers");
 
 // Bits [a, b) of a 64-bit set, 0 <= a <= b <= 64.
 __device__ __forceinline__ uint64_t key_bits(int a, int b) {
@@ -94,17 +118,23 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-template <bool PLO>
+template <int HD, bool PLO>
 __global__ void __launch_bounds__(192, 1)
     attention_flash_kernel(const __grid_constant__ CUtensorMap tq,
                            const __grid_constant__ CUtensorMap tkv, AttnFlashArgs g) {
+  static_assert(HD == 256 || HD == 512, "head_dim 256 or 512");
+  constexpr int QB = fa_q_bytes<HD>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* qs = sm;
-  auto ks = [&](int b) { return qs + FA_Q_BYTES + b * FA_KV_BYTES; };        // K buffer b
-  auto vs = [&](int b) { return qs + FA_Q_BYTES + (2 + b) * FA_KV_BYTES; };  // V buffer b
-  uint8_t* ps = qs + FA_Q_BYTES + 4 * FA_KV_BYTES;  // P hi, then (PLO) P lo
+  auto ks = [&](int b) { return qs + QB + b * FA_KV_BYTES; };  // K buffer b (head_dim 256)
+  // V buffer b (head_dim 512: the one buffer after the K ring).
+  auto vs = [&](int b) {
+    return HD == 256 ? qs + QB + (2 + b) * FA_KV_BYTES : qs + QB + FA_KRING * FA_KVCH;
+  };
+  auto kr = [&](int c) { return qs + QB + c * FA_KVCH; };  // K ring chunk c (head_dim 512)
+  uint8_t* ps = qs + QB + fa_kv_area<HD>();  // P hi, then (PLO) P lo
   constexpr int NPS = fa_p_slots<PLO>(), PSB = fa_p_slot_bytes<PLO>();
   uint64_t* bars = reinterpret_cast<uint64_t*>(ps + NPS * PSB);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B_N);
@@ -114,6 +144,7 @@ __global__ void __launch_bounds__(192, 1)
   const AttnFlashItem item = g.items[blockIdx.x];
   const AttnFlashRun run = g.runs[item.run];
   const int kvh = blockIdx.y;
+  const int vhalf = HD == 512 ? static_cast<int>(blockIdx.z) : 0;  // this CTA's 256 dims of V
   const int tok_per_tile = kAttnTileRows / g.hpg;
   const int* tiles = g.tiles + run.tile0 + item.t0;
   const int nt = item.nt;
@@ -135,12 +166,37 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint32_t qbytes = 4u * 64u * 2u * static_cast<uint32_t>(g.hpg * tok_per_tile);
+      constexpr int QC = HD / 64;
+      const uint32_t qbytes = QC * 64u * 2u * static_cast<uint32_t>(g.hpg * tok_per_tile);
       mbar_arrive_expect_tx(&bars[B_Q], qbytes);
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int c = 0; c < QC; ++c)
         tma_load_4d(qs + c * FA_QCH, &tq, &bars[B_Q], c * 64, 0, kvh, run.tok0);
-      for (int j = 0; j < nt; ++j) {
+      if constexpr (HD == 512) {
+        // K of each tile in 8 ring chunks; then its V half, once P_{j-1} V_{j-1}
+        // freed the buffer.
+        int it = 0;
+        bool ok = true;
+        for (int j = 0; j < nt && ok; ++j) {
+          for (int c = 0; c < 8 && ok; ++c, ++it) {
+            const int s = it % FA_KRING, n = it / FA_KRING;
+            if (n > 0 && !mbar_wait(&bars[B_E0 + s], (n - 1) & 1, abort_flag, g.status)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&bars[B_R0 + s], FA_KVCH);
+            tma_load_2d(kr(s), &tkv, &bars[B_R0 + s], kvh * HD + c * 64, tiles[j]);
+          }
+          if (!ok) break;
+          if (j > 0 && !mbar_wait(&bars[B_VF0], (j - 1) & 1, abort_flag, g.status)) break;
+          mbar_arrive_expect_tx(&bars[B_V0], FA_KV_BYTES);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            tma_load_2d(vs(0) + c * FA_KVCH, &tkv, &bars[B_V0],
+                        (g.kv_heads + kvh) * HD + vhalf * 256 + c * 64, tiles[j]);
+        }
+      }
+      for (int j = 0; HD == 256 && j < nt; ++j) {
         const int b = j & 1, u = j >> 1;
         if (u > 0 && !mbar_wait(&bars[B_KF0 + b], (u - 1) & 1, abort_flag, g.status)) break;
         mbar_arrive_expect_tx(&bars[B_K0 + b], FA_KV_BYTES);
@@ -159,9 +215,26 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16_f32(128, FA_KEYS);
       constexpr uint32_t idesc_o = idesc_f16_f32_bmn(128, FA_HD);
+      int kit = 0;  // K ring chunks consumed (head_dim 512)
       // S_j = Q K_j^T into score buffer j & 1.
       auto issue_s = [&](int j) -> bool {
         const int b = j & 1;
+        if constexpr (HD == 512) {
+          for (int c = 0; c < 8; ++c, ++kit) {
+            const int s = kit % FA_KRING;
+            if (!mbar_wait(&bars[B_R0 + s], (kit / FA_KRING) & 1, abort_flag, g.status))
+              return false;
+            tc_fence_after();
+            const uint64_t da = sw128_desc(qs + c * FA_QCH);
+            const uint64_t db = sw128_desc(kr(s));
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              umma_f16(tmem + b * FA_KEYS, da + 2 * k, db + 2 * k, idesc_s, (c | k) ? 1u : 0u);
+            umma_commit(&bars[B_E0 + s]);
+          }
+          umma_commit(&bars[B_S0 + b]);
+          return true;
+        }
         if (!mbar_wait(&bars[B_K0 + b], (j >> 1) & 1, abort_flag, g.status)) return false;
         tc_fence_after();
 #pragma unroll
@@ -186,27 +259,30 @@ __global__ void __launch_bounds__(192, 1)
         // P_j sits in slot j & 1 (the only slot with PLO).
         const int slot = NPS == 2 ? b : 0;
         const uint32_t p_par = NPS == 2 ? (j >> 1) & 1 : j & 1;
+        // V_j: buffer j & 1 (head_dim 256), the one buffer (512).
+        const int vb_i = HD == 256 ? b : 0;
+        const uint32_t v_par = HD == 256 ? (j >> 1) & 1 : j & 1;
         if (!mbar_wait(&bars[B_P0 + slot], p_par, abort_flag, g.status) ||
-            !mbar_wait(&bars[B_V0 + b], (j >> 1) & 1, abort_flag, g.status))
+            !mbar_wait(&bars[B_V0 + vb_i], v_par, abort_flag, g.status))
           break;
         tc_fence_after();
         const uint8_t* pj = ps + slot * PSB;
 #pragma unroll
         for (int kk = 0; kk < FA_KEYS / 16; ++kk) {
           const uint64_t pa = sw128_desc(pj) + 2 * kk;
-          const uint64_t vb = sw128_mn_desc(vs(b) + kk * 2048, FA_KVCH);
+          const uint64_t vb = sw128_mn_desc(vs(vb_i) + kk * 2048, FA_KVCH);
           umma_f16(tmem + FA_TMEM_O, pa, vb, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
         if constexpr (PLO) {
 #pragma unroll
           for (int kk = 0; kk < FA_KEYS / 16; ++kk) {
             const uint64_t pa = sw128_desc(pj + FA_P_BYTES) + 2 * kk;
-            const uint64_t vb = sw128_mn_desc(vs(b) + kk * 2048, FA_KVCH);
+            const uint64_t vb = sw128_mn_desc(vs(vb_i) + kk * 2048, FA_KVCH);
             umma_f16(tmem + FA_TMEM_O, pa, vb, idesc_o, 1u);
           }
         }
         umma_commit(&bars[B_O0 + b]);
-        umma_commit(&bars[B_VF0 + b]);
+        umma_commit(&bars[B_VF0 + vb_i]);
       }
     }
   } else {
@@ -374,8 +450,8 @@ __global__ void __launch_bounds__(192, 1)
       // buffer like the f16 output below (512 bytes per row) and stored a
       // row per warp instruction.
       const size_t ps = static_cast<size_t>(item.slot) * g.kv_heads + kvh;
-      g.part_ml[ps * kAttnTileRows + r] = make_float2(m_ref, l);
-      float* po = g.part_o + ps * kAttnTileRows * FA_HD;
+      if (vhalf == 0) g.part_ml[ps * kAttnTileRows + r] = make_float2(m_ref, l);
+      float* po = g.part_o + ps * kAttnTileRows * HD + vhalf * FA_HD;
       uint8_t* stage = qs;
 #pragma unroll 1
       for (int half = 0; half < 2; ++half) {
@@ -396,7 +472,7 @@ __global__ void __launch_bounds__(192, 1)
           const int row = 32 * q4 + i;
           const uint4 v =
               *reinterpret_cast<const uint4*>(stage + row * 512 + ((lane ^ (row & 7)) << 4));
-          *reinterpret_cast<uint4*>(po + static_cast<size_t>(row) * FA_HD + 128 * half + 4 * lane) = v;
+          *reinterpret_cast<uint4*>(po + static_cast<size_t>(row) * HD + 128 * half + 4 * lane) = v;
         }
         __syncwarp();
       }
@@ -435,8 +511,9 @@ __global__ void __launch_bounds__(192, 1)
         if (rt >= run.ntok || rt >= tok_per_tile) break;  // later rows are past the run too
         const int row = 32 * q4 + i;
         const uint4 v = *reinterpret_cast<const uint4*>(stage + row * 512 + ((lane ^ (row & 7)) << 4));
-        __half* orow =
-            g.out + (static_cast<size_t>(run.tok0 + rt) * g.heads + kvh * g.hpg + hh) * FA_HD;
+        __half* orow = g.out +
+                       (static_cast<size_t>(run.tok0 + rt) * g.heads + kvh * g.hpg + hh) * HD +
+                       vhalf * FA_HD;
         *reinterpret_cast<uint4*>(orow + lane * 8) = v;
         if (++hh == g.hpg) {
           hh = 0;
@@ -462,6 +539,7 @@ __global__ void __launch_bounds__(192, 1)
 // at a time with all their loads issued first.
 constexpr int kMergeRows = 8;
 
+template <int HD>
 __global__ void __launch_bounds__(32 * kMergeRows) attention_merge_kernel(AttnFlashArgs g) {
   griddep_wait();
   constexpr int groups = kAttnTileRows / kMergeRows;
@@ -481,6 +559,10 @@ __global__ void __launch_bounds__(32 * kMergeRows) attention_merge_kernel(AttnFl
     for (int c = lane; c < mg.nchunks; c += 32) mmax = fmaxf(mmax, g.part_ml[slot_row(c)].x);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, o));
+    // head_dim 512: the two 256-dim halves one after the other (the same
+    // chunk weights and sum).
+#pragma unroll 1
+    for (int dh = 0; dh < HD / FA_HD; ++dh) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     float lsum = 0.f;
     for (int c0 = 0; c0 < mg.nchunks; c0 += 4) {
@@ -491,7 +573,8 @@ __global__ void __launch_bounds__(32 * kMergeRows) attention_merge_kernel(AttnFl
         if (c0 + k < mg.nchunks) {
           const size_t sr = slot_row(c0 + k);
           ml[k] = g.part_ml[sr];
-          const float4* src = reinterpret_cast<const float4*>(g.part_o + sr * FA_HD + 8 * lane);
+          const float4* src =
+              reinterpret_cast<const float4*>(g.part_o + sr * HD + dh * FA_HD + 8 * lane);
           a[k] = src[0];
           b[k] = src[1];
         }
@@ -515,7 +598,8 @@ __global__ void __launch_bounds__(32 * kMergeRows) attention_merge_kernel(AttnFl
     const float inv = lsum > 0.f ? 1.0f / lsum : 0.f;
     const int tl = r / g.hpg, hh = r - tl * g.hpg;
     __half* orow = g.out +
-                   (static_cast<size_t>(run.tok0 + tl) * g.heads + kvh * g.hpg + hh) * FA_HD + 8 * lane;
+                   (static_cast<size_t>(run.tok0 + tl) * g.heads + kvh * g.hpg + hh) * HD +
+                   dh * FA_HD + 8 * lane;
     uint32_t w4[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -523,6 +607,7 @@ __global__ void __launch_bounds__(32 * kMergeRows) attention_merge_kernel(AttnFl
       w4[q] = *reinterpret_cast<const uint32_t*>(&h);
     }
     *reinterpret_cast<uint4*>(orow) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    }
   }
   griddep_launch();
 }
@@ -635,52 +720,79 @@ int attention_flash_runs(const TokMeta* m, const int4* vis, int t, int hpg, int 
   return slots;
 }
 
-bool attention_map_q(CUtensorMap* mp, const void* q16, int t_cap, int heads, int kv_heads,
+bool attention_map_q(CUtensorMap* mp, const void* q16, int t_cap, int heads, int kv_heads, int hd,
                      char* err, size_t errlen) {
   const int hpg = heads / kv_heads;
   if (hpg < 1 || hpg > kAttnTileRows || heads % kv_heads != 0) {
     snprintf(err, errlen, "attention: %d query heads over %d KV heads", heads, kv_heads);
     return false;
   }
-  const uint64_t dims[4] = {static_cast<uint64_t>(FA_HD), static_cast<uint64_t>(hpg),
+  if (hd != 256 && hd != 512) {
+    snprintf(err, errlen, "attention: head_dim %d (256 or 512)", hd);
+    return false;
+  }
+  const uint64_t dims[4] = {static_cast<uint64_t>(hd), static_cast<uint64_t>(hpg),
                             static_cast<uint64_t>(kv_heads), static_cast<uint64_t>(t_cap)};
-  const uint64_t strides[3] = {FA_HD * 2ull, static_cast<uint64_t>(hpg) * FA_HD * 2,
-                               static_cast<uint64_t>(heads) * FA_HD * 2};
+  const uint64_t strides[3] = {hd * 2ull, static_cast<uint64_t>(hpg) * hd * 2,
+                               static_cast<uint64_t>(heads) * hd * 2};
   const uint32_t box[4] = {64, static_cast<uint32_t>(hpg), 1,
                            static_cast<uint32_t>(kAttnTileRows / hpg)};
   return make_tmap_f16(mp, q16, 4, dims, strides, box, err, errlen);
 }
 
-bool attention_map_kv(CUtensorMap* mp, const void* kv, int rows_cap, int kv_heads, char* err,
-                      size_t errlen) {
-  const uint64_t dims[2] = {static_cast<uint64_t>(2 * kv_heads * FA_HD),
+bool attention_map_kv(CUtensorMap* mp, const void* kv, int rows_cap, int kv_heads, int hd,
+                      char* err, size_t errlen) {
+  if (hd != 256 && hd != 512) {
+    snprintf(err, errlen, "attention: head_dim %d (256 or 512)", hd);
+    return false;
+  }
+  const uint64_t dims[2] = {static_cast<uint64_t>(2 * kv_heads * hd),
                             static_cast<uint64_t>(rows_cap)};
-  const uint64_t strides[1] = {static_cast<uint64_t>(2 * kv_heads * FA_HD) * 2};
+  const uint64_t strides[1] = {static_cast<uint64_t>(2 * kv_heads * hd) * 2};
   const uint32_t box[2] = {64, static_cast<uint32_t>(FA_KEYS)};
   return make_tmap_f16(mp, kv, 2, dims, strides, box, err, errlen);
 }
 
-void attention_flash_setup_device() {
-  cudaFuncSetAttribute(attention_flash_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       fa_smem<true>());
-  cudaFuncSetAttribute(attention_flash_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       fa_smem<false>());
+void attention_setup_device() {
+  cudaFuncSetAttribute(attention_flash_kernel<256, true>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, fa_smem<256, true>());
+  cudaFuncSetAttribute(attention_flash_kernel<256, false>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, fa_smem<256, false>());
+  cudaFuncSetAttribute(attention_flash_kernel<512, true>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, fa_smem<512, true>());
+  cudaFuncSetAttribute(attention_flash_kernel<512, false>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, fa_smem<512, false>());
 }
 
 void launch_attention_flash(const CUtensorMap& tq, const CUtensorMap& tkv,
                             const AttnFlashArgs& a, bool p_lo, cudaStream_t s) {
   if (a.n_items <= 0) return;
+  if (a.hd == 512) {
+    dim3 grid(a.n_items, a.kv_heads, 2);  // z: the V half
+    if (p_lo)
+      launch_pdl(attention_flash_kernel<512, true>, grid, dim3(192), fa_smem<512, true>(), s, tq,
+                 tkv, a);
+    else
+      launch_pdl(attention_flash_kernel<512, false>, grid, dim3(192), fa_smem<512, false>(), s, tq,
+                 tkv, a);
+    return;
+  }
   dim3 grid(a.n_items, a.kv_heads);
   if (p_lo)
-    launch_pdl(attention_flash_kernel<true>, grid, dim3(192), fa_smem<true>(), s, tq, tkv, a);
+    launch_pdl(attention_flash_kernel<256, true>, grid, dim3(192), fa_smem<256, true>(), s, tq, tkv,
+               a);
   else
-    launch_pdl(attention_flash_kernel<false>, grid, dim3(192), fa_smem<false>(), s, tq, tkv, a);
+    launch_pdl(attention_flash_kernel<256, false>, grid, dim3(192), fa_smem<256, false>(), s, tq,
+               tkv, a);
 }
 
 void launch_attention_merge(const AttnFlashArgs& a, cudaStream_t s) {
   if (a.n_merges <= 0) return;
-  launch_pdl(attention_merge_kernel, dim3(a.n_merges * (kAttnTileRows / kMergeRows), a.kv_heads),
-             dim3(32 * kMergeRows), 0, s, a);
+  const dim3 grid(a.n_merges * (kAttnTileRows / kMergeRows), a.kv_heads);
+  if (a.hd == 512)
+    launch_pdl(attention_merge_kernel<512>, grid, dim3(32 * kMergeRows), 0, s, a);
+  else
+    launch_pdl(attention_merge_kernel<256>, grid, dim3(32 * kMergeRows), 0, s, a);
 }
 
 }  // namespace omg

@@ -141,9 +141,11 @@ extern "C" int omg_debug_mlp(int device, const uint16_t* x, int m, int d, const 
 // Block-causal attention on host buffers: q [t, heads * hd] f16 (cache rows
 // base..base+t), kv [rows, 2 * kv_heads * hd] f16, meta 4 ints per cache row
 // (pos, seq, row_lo, row_hi), out [t, heads * hd] f16.
-extern "C" int omg_debug_attention(int device, const uint16_t* q, const uint16_t* kv,
-                                   const int32_t* meta, int t, int base, int heads, int kv_heads,
-                                   int hd, int window, int p_lo, uint16_t* out) {
+// iters > 0: time that many launches (and merges) with CUDA events after
+// one untimed run; *ms gets the average.
+static int debug_attention(int device, const uint16_t* q, const uint16_t* kv, const int32_t* meta,
+                           int t, int base, int heads, int kv_heads, int hd, int window, int p_lo,
+                           uint16_t* out, int iters, float* ms) {
   return guarded([&]() -> int {
     CUDA_TRY(cudaSetDevice(device));
     omg::attention_setup_device();
@@ -161,7 +163,8 @@ extern "C" int omg_debug_attention(int device, const uint16_t* q, const uint16_t
                         cudaMemcpyHostToDevice));
     CUDA_TRY(cudaMemcpy(dm.p, meta, static_cast<size_t>(rows) * 16, cudaMemcpyHostToDevice));
     const omg::TokMeta* hm = reinterpret_cast<const omg::TokMeta*>(meta);
-    if (hd == 256) {
+    if (hd != 256 && hd != 512) return set_error("attention: head_dim %d (256 or 512)", hd);
+    {
       // Tensor-core path: the engine's schedule, with the interval form of
       // the visibility rule checked against the rule itself on every pair.
       std::vector<int4> vis;
@@ -181,7 +184,7 @@ extern "C" int omg_debug_attention(int device, const uint16_t* q, const uint16_t
           !dti.alloc(std::max<size_t>(tiles.size(), 1) * sizeof(int)) || !dst.alloc(4) ||
           !dit.alloc(items.size() * sizeof(omg::AttnFlashItem)) ||
           !dmg.alloc(std::max<size_t>(merges.size(), 1) * sizeof(omg::AttnFlashMerge)) ||
-          !dpo.alloc(prow * 256 * sizeof(float)) || !dpml.alloc(prow * sizeof(float2)))
+          !dpo.alloc(prow * hd * sizeof(float)) || !dpml.alloc(prow * sizeof(float2)))
         return set_error("cudaMalloc failed");
       CUDA_TRY(cudaMemcpy(dit.p, items.data(), items.size() * sizeof(omg::AttnFlashItem),
                           cudaMemcpyHostToDevice));
@@ -195,8 +198,8 @@ extern "C" int omg_debug_attention(int device, const uint16_t* q, const uint16_t
       CUDA_TRY(cudaMemset(dst.p, 0, 4));
       CUtensorMap tq, tkv;
       char err[256];
-      if (!omg::attention_map_q(&tq, dq.p, t, heads, kv_heads, err, sizeof err) ||
-          !omg::attention_map_kv(&tkv, dkv.p, rows_pad, kv_heads, err, sizeof err))
+      if (!omg::attention_map_q(&tq, dq.p, t, heads, kv_heads, hd, err, sizeof err) ||
+          !omg::attention_map_kv(&tkv, dkv.p, rows_pad, kv_heads, hd, err, sizeof err))
         return set_error("%s", err);
       omg::AttnFlashArgs a{};
       a.vis = static_cast<const int4*>(dv.p);
@@ -218,40 +221,51 @@ extern "C" int omg_debug_attention(int device, const uint16_t* q, const uint16_t
       a.kv_heads = kv_heads;
       a.hpg = heads / kv_heads;
       a.window = window;
-      omg::launch_attention_flash(tq, tkv, a, p_lo != 0, 0);
-      if (a.n_merges > 0) omg::launch_attention_merge(a, 0);
+      a.hd = hd;
+      auto once = [&]() {
+        omg::launch_attention_flash(tq, tkv, a, p_lo != 0, 0);
+        if (a.n_merges > 0) omg::launch_attention_merge(a, 0);
+      };
+      once();
       CUDA_TRY(cudaGetLastError());
       CUDA_TRY(cudaDeviceSynchronize());
+      if (iters > 0) {
+        cudaEvent_t e0, e1;
+        CUDA_TRY(cudaEventCreate(&e0));
+        CUDA_TRY(cudaEventCreate(&e1));
+        CUDA_TRY(cudaEventRecord(e0, 0));
+        for (int i = 0; i < iters; ++i) once();
+        CUDA_TRY(cudaEventRecord(e1, 0));
+        CUDA_TRY(cudaEventSynchronize(e1));
+        float tms = 0.f;
+        CUDA_TRY(cudaEventElapsedTime(&tms, e0, e1));
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        *ms = tms / iters;
+      }
       uint32_t st = 0;
       CUDA_TRY(cudaMemcpy(&st, dst.p, 4, cudaMemcpyDeviceToHost));
       if (st) return set_error("attention kernel reported device status %u", st);
-      CUDA_TRY(cudaMemcpy(out, dout.p, qb, cudaMemcpyDeviceToHost));
+      if (out) CUDA_TRY(cudaMemcpy(out, dout.p, qb, cudaMemcpyDeviceToHost));
       return 0;
     }
-    std::vector<int2> ctas;
-    omg::attention_schedule(hm + base, t, heads / kv_heads, &ctas);
-    DevBuf dc;
-    if (!dc.alloc(ctas.size() * sizeof(int2))) return set_error("cudaMalloc failed");
-    CUDA_TRY(cudaMemcpy(dc.p, ctas.data(), ctas.size() * sizeof(int2), cudaMemcpyHostToDevice));
-    omg::AttnArgs a{};
-    a.ctas = static_cast<const int2*>(dc.p);
-    a.n_ctas = static_cast<int>(ctas.size());
-    a.q = static_cast<const __half*>(dq.p);
-    a.kv = static_cast<const __half*>(dkv.p);
-    a.meta = static_cast<const omg::TokMeta*>(dm.p);
-    a.out = static_cast<__half*>(dout.p);
-    a.t = t;
-    a.base = base;
-    a.heads = heads;
-    a.kv_heads = kv_heads;
-    a.hd = hd;
-    a.window = window;
-    omg::launch_attention(a, 0);
-    CUDA_TRY(cudaGetLastError());
-    CUDA_TRY(cudaDeviceSynchronize());
-    CUDA_TRY(cudaMemcpy(out, dout.p, qb, cudaMemcpyDeviceToHost));
-    return 0;
   });
+}
+
+extern "C" int omg_debug_attention(int device, const uint16_t* q, const uint16_t* kv,
+                                   const int32_t* meta, int t, int base, int heads, int kv_heads,
+                                   int hd, int window, int p_lo, uint16_t* out) {
+  return debug_attention(device, q, kv, meta, t, base, heads, kv_heads, hd, window, p_lo, out, 0,
+                         nullptr);
+}
+
+extern "C" int omg_debug_attention_time(int device, const uint16_t* q, const uint16_t* kv,
+                                        const int32_t* meta, int t, int base, int heads,
+                                        int kv_heads, int hd, int window, int p_lo, int iters,
+                                        float* ms) {
+  if (iters <= 0 || !ms) return set_error("omg_debug_attention_time: iters > 0 and ms needed");
+  return debug_attention(device, q, kv, meta, t, base, heads, kv_heads, hd, window, p_lo, nullptr,
+                         iters, ms);
 }
 
 // Time `iters` launches of the GEMM on device-resident random operands

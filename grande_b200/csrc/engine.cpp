@@ -500,21 +500,21 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
   kv_.resize(L);
   for (int l = 0; l < L; ++l)
     if (c.has_kv(l)) kv_[l].alloc(Cpad * 2 * c.kv_heads * c.head_dim[l] * 2);
-  attn_ctas_.alloc(Cpad * sizeof(int2));
   mlp_ready_.alloc((Cpad + 127) / 128 * S * sizeof(int));
   {
     char err[256];
-    if (!attention_map_q(&attn_tq_, q16_.p, static_cast<int>(Cpad), c.heads, c.kv_heads, err,
-                            sizeof err))
-      fail("%s", err);
+    // q16 holds a layer's rows as [t][heads * head_dim]: one map per width.
+    for (int hi = 0; hi < 2; ++hi)
+      if (!attention_map_q(&attn_tq_[hi], q16_.p, static_cast<int>(Cpad), c.heads, c.kv_heads,
+                           256 << hi, err, sizeof err))
+        fail("%s", err);
     attn_tkv_.resize(L);
     for (int l = 0; l < L; ++l)
-      if (c.has_kv(l) && c.head_dim[l] == 256 &&
-          !attention_map_kv(&attn_tkv_[l], kv_[l].p, static_cast<int>(Cpad), c.kv_heads, err,
-                               sizeof err))
+      if (c.has_kv(l) &&
+          !attention_map_kv(&attn_tkv_[l], kv_[l].p, static_cast<int>(Cpad), c.kv_heads,
+                            c.head_dim[l], err, sizeof err))
         fail("layer %d: %s", l, err);
   }
-  h_attn_ctas_.alloc(Cpad * sizeof(int2));
   h_ids_.alloc(Cpad * 4);
   h_meta_.alloc(Cpad * sizeof(TokMeta));
   h_row_map_.alloc(Cpad * 4);
@@ -806,8 +806,6 @@ Engine::Packing Engine::pack(const GroupIn* groups, size_t n, size_t first,
     }
     // out_index[device row order] is filled below
   }
-  attention_schedule(p.meta.data(), static_cast<int>(p.t), config.heads / config.kv_heads,
-                     &p.attn_ctas);
   {
     const int t = static_cast<int>(p.t), base = static_cast<int>(p.base);
     const int hpg = config.heads / config.kv_heads;
@@ -879,13 +877,12 @@ void Engine::upload(const Packing& p, const uint8_t* per_layer_rows, size_t rows
     if (attn_part_ml_.bytes < rows * sizeof(float2)) {
       CUDA_TRY(cudaStreamSynchronize(stream_));
       const size_t cap = std::max<size_t>(rows * 2, 8 * kAttnTileRows);
-      attn_part_o_.alloc(cap * 256 * sizeof(float), false);
+      int hd_max = 256;
+      for (int hd : config.head_dim) hd_max = std::max(hd_max, hd);
+      attn_part_o_.alloc(cap * hd_max * sizeof(float), false);
       attn_part_ml_.alloc(cap * sizeof(float2), false);
     }
   }
-  std::memcpy(h_attn_ctas_.p, p.attn_ctas.data(), p.attn_ctas.size() * sizeof(int2));
-  CUDA_TRY(cudaMemcpyAsync(attn_ctas_.p, h_attn_ctas_.p, p.attn_ctas.size() * sizeof(int2),
-                           cudaMemcpyHostToDevice, stream_));
   const int P = config.per_layer_dim;
   if (P > 0) {
     if (!per_layer_rows) fail("per-layer embedding rows required");
@@ -992,8 +989,8 @@ int Engine::launch_forward(const Packing& p, Want want) {
       k("qk_prep");
       launch_qk_prep(qa, stream_);
     }
-    // Block-causal attention over the cache.
-    if (ly.hd == 256) {
+    // Block-causal attention over the cache (head_dim 256 or 512).
+    {
       const int w = ly.sliding ? 0 : 1;
       const uint8_t* sched = attn_sched_.as<uint8_t>();
       AttnFlashArgs ta{};
@@ -1016,28 +1013,14 @@ int Engine::launch_forward(const Packing& p, Want want) {
       ta.kv_heads = c.kv_heads;
       ta.hpg = c.heads / c.kv_heads;
       ta.window = ly.sliding ? c.window : 0;
+      ta.hd = ly.hd;
       k("attention");
-      launch_attention_flash(attn_tq_, attn_tkv_[ly.kv_src], ta, kAttnPLo, stream_);
+      launch_attention_flash(attn_tq_[ly.hd == 512 ? 1 : 0], attn_tkv_[ly.kv_src], ta, kAttnPLo,
+                             stream_);
       if (ta.n_merges > 0) {
         k("attention_merge");
         launch_attention_merge(ta, stream_);
       }
-    } else {
-      AttnArgs aa{};
-      aa.q = q16_.as<__half>();
-      aa.kv = kv_[ly.kv_src].as<__half>();
-      aa.meta = meta_.as<TokMeta>();
-      aa.out = attn16_.as<__half>();
-      aa.ctas = attn_ctas_.as<int2>();
-      aa.n_ctas = static_cast<int>(p.attn_ctas.size());
-      aa.t = t;
-      aa.base = static_cast<int>(p.base);
-      aa.heads = c.heads;
-      aa.kv_heads = c.kv_heads;
-      aa.hd = ly.hd;
-      aa.window = ly.sliding ? c.window : 0;
-      k("attention");
-      launch_attention(aa, stream_);
     }
     // Output projection, then x += norm(a); h = ffn_norm(x).
     k("gemm_o");
@@ -1103,7 +1086,7 @@ int Engine::launch_forward(const Packing& p, Want want) {
 }
 
 bool Engine::GraphKey::operator==(const GraphKey& o) const {
-  return t == o.t && base == o.base && nwanted == o.nwanted && ctas == o.ctas &&
+  return t == o.t && base == o.base && nwanted == o.nwanted &&
          sched_bytes == o.sched_bytes && want == o.want && sched == o.sched &&
          std::equal(attn_off, attn_off + kAttnSchedParts, o.attn_off) && runs[0] == o.runs[0] &&
          runs[1] == o.runs[1] && tiles[0] == o.tiles[0] && tiles[1] == o.tiles[1] &&
@@ -1116,7 +1099,6 @@ Engine::GraphKey Engine::graph_key(const Packing& p, Want want) const {
   k.t = p.t;
   k.base = p.base;
   k.nwanted = p.nwanted;
-  k.ctas = p.attn_ctas.size();
   k.sched_bytes = p.attn_bytes;
   std::copy(p.attn_off, p.attn_off + kAttnSchedParts, k.attn_off);
   for (int w = 0; w < 2; ++w) {

@@ -275,7 +275,6 @@ class Engine {
     // (group, branch, slot) -> flat output row
     std::vector<size_t> out_index;
     std::vector<std::pair<size_t, size_t>> decoded;  // (group, cache row of its prefix)
-    std::vector<int2> attn_ctas;                     // attention CTA runs (head_dim 512)
     // Tensor-core attention schedule (head_dim 256): per-token visible rows,
     // then items and multi-item runs for sliding [0] and global [1] layers,
     // staged as one block: vis | items[0] | runs[0] | items[1] | runs[1].
@@ -295,7 +294,7 @@ class Engine {
   // the schedule's offsets); everything else it reads lives at fixed device
   // addresses and is uploaded before each pass.
   struct GraphKey {
-    size_t t = 0, base = 0, nwanted = 0, ctas = 0, sched_bytes = 0;
+    size_t t = 0, base = 0, nwanted = 0, sched_bytes = 0;
     size_t attn_off[kAttnSchedParts] = {};
     size_t items[2] = {}, merges[2] = {};
     const void* part = nullptr;
@@ -352,13 +351,13 @@ class Engine {
   int max_qkv_ = 0, max_attn_ = 0, max_ff_ = 0;
 
   // Workspace.
-  DevBuffer attn_ctas_, attn_sched_, mlp_ready_;
+  DevBuffer attn_sched_, mlp_ready_;
   // Chunk-split attention partials: O [slots x kv_heads][128][256] f32 and
   // (max, sum) [slots x kv_heads][128], grown to the largest pass seen.
   DevBuffer attn_part_o_, attn_part_ml_;
-  PinnedBuffer h_attn_ctas_, h_attn_sched_;
-  CUtensorMap attn_tq_;
-  std::vector<CUtensorMap> attn_tkv_;  // per layer owning head_dim-256 K/V
+  PinnedBuffer h_attn_sched_;
+  CUtensorMap attn_tq_[2];             // q16 as head_dim 256 / 512 rows
+  std::vector<CUtensorMap> attn_tkv_;  // per layer owning K/V
   DevBuffer ids_, meta_, row_map_, x_, x16_, h16_, qkv_, q16_, attn16_, a32_, act16_, rows_,
       logits_, status_, pl_rows16_, pli_, plp_;
   std::vector<DevBuffer> kv_;  // per layer that owns K/V: [cap_rows, 2 * kv_heads * hd] f16

@@ -305,11 +305,17 @@ int omg_debug_mlp(int device, const uint16_t* x, int m, int d, const uint16_t* w
  * q [t, heads * hd] f16 for cache rows base..base+t, kv [base + t, 2 * kv_heads * hd]
  * f16 (K heads then V heads per row), meta 4 ints per cache row (position,
  * sequence id, first key row of its group, own row + 1; engine.rs:1519-1571),
- * window 0 = global. p_lo (head_dim 256): also feed P's f16 rounding residue
- * into P.V. Writes out [t, heads * hd] f16. */
+ * window 0 = global, hd 256 or 512 (the tcgen05 kernel either way). p_lo:
+ * also feed P's f16 rounding residue into P.V. Writes out [t, heads * hd]
+ * f16. */
 int omg_debug_attention(int device, const uint16_t* q, const uint16_t* kv, const int32_t* meta,
                         int t, int base, int heads, int kv_heads, int hd, int window, int p_lo,
                         uint16_t* out);
+/* The same launch (and merge) timed: `iters` runs after one untimed run,
+ * *ms the average per run (CUDA events). */
+int omg_debug_attention_time(int device, const uint16_t* q, const uint16_t* kv,
+                             const int32_t* meta, int t, int base, int heads, int kv_heads, int hd,
+                             int window, int p_lo, int iters, float* ms);
 
 /* omg_debug_gemm and omg_debug_mlp over weights kept packed as Q4_0 / Q8_0
  * (wdtype 2 / 1; codes and f16 scales as omg_builder_push takes them, W rows

@@ -19,11 +19,11 @@
 
 namespace omg {
 
-// The attention's P enters P.V as f16 only (the reference rounds Q, K and V
-// to f16; P's own f16 rounding adds ~2^-12 relative error, below the f16
-// rounding of the attention output that follows). Set to feed P's rounding
-// residue too, for ~22-bit P.
-constexpr bool kAttnPLo = false;
+// The attention's P enters P.V as f16 hi + lo (~22 bits), as close to
+// attention.wgsl's f32 p (multiplied by f16 V) as f16 MMA operands get; the
+// reference rounds only Q, K and V. (f16 P alone: ~2^-12 relative error per
+// probability, 0.03-0.06 ms less per E2B pass.)
+constexpr bool kAttnPLo = true;
 
 // ---- buffers ----------------------------------------------------------------
 

@@ -580,11 +580,17 @@ Engine::Engine(EngineBuilder&& b, size_t capacity_, size_t max_rows_)
     plan(&ly.o, attn16_.p, attn_w, w_o, d, d, attn_w, kEpiF32, "o", l);
     plan(&ly.gate_up, h16_.p, d, w_gu, (ly.ff + 127) / 128 * 256, ly.ff, d, kEpiGeGluTanh,
          "gate_up", l);
-    // The down projection joins gate_up's launch when its split-K units run
-    // as many K blocks as a gate_up tile (a split count that depends on the
-    // layer's shape only).
+    // The down projection joins gate_up's launch, split so that each split
+    // reads whole gate_up column tiles: into units as long as a gate_up tile
+    // where that divides (E2B, E4B), else into the most splits (up to S)
+    // that do, for the shortest up -> down chain (a split count that
+    // depends on the layer's shape only).
     const int kb_up = (d + 63) / 64, kb_dn = (ly.ff + 63) / 64;
-    const int fuse_splits = kb_dn % kb_up == 0 ? kb_dn / kb_up : 0;
+    const int up_tiles = (ly.ff + 127) / 128;
+    int fuse_splits = kb_dn % kb_up == 0 ? kb_dn / kb_up : 0;
+    for (int sp = S; fuse_splits == 0 && sp >= 1; --sp)
+      if (kb_dn % sp == 0 && (kb_dn / sp) % 2 == 0 && up_tiles == sp * (kb_dn / sp / 2))
+        fuse_splits = sp;
     if (fuse_splits >= 1 && fuse_splits <= S) {
       plan(&ly.down, act16_.p, ly.ff, w_down, d, d, ly.ff, kEpiF32, "down", l, fuse_splits);
       ly.fused_mlp = gemm_mlp_ok(ly.gate_up, ly.down);

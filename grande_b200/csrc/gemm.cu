@@ -2106,10 +2106,11 @@ bool gemm_mlp_ok(const GemmPlan& up, const GemmPlan& down) {
   const int kb_dn = (down.s.k + BK - 1) / BK;
   // Down split s must read exactly the columns of up column tiles
   // [s * band, (s + 1) * band) (an up tile stores 128 activation columns).
+  // Up and down units may differ in length (kb_up vs kb_split K blocks).
   const int kb_split = (kb_dn + down.s.splits - 1) / down.s.splits;
   return up.pk == down.pk && (up.s.epi == kEpiGeGluTanh || up.s.epi == kEpiGeGluErf) &&
-         up.s.bn == 256 &&
-         down.s.epi == kEpiF32 && down.s.bn == 256 && kb_split == kb_up &&
+         up.s.bn == 256 && kb_up >= 1 &&
+         down.s.epi == kEpiF32 && down.s.bn == 256 &&
          kb_dn == kb_split * down.s.splits && kb_split % 2 == 0 &&
          up.s.n_tiles == down.s.splits * (kb_split / 2) && up.s.n_out == down.s.k;
 }

@@ -138,8 +138,8 @@ void gemm_run_epi(const GemmPlan& p, int m, void* out, int ldo, const GemmEpi& e
 
 // Gate+up (GeGLU epilogue into `act`) and down (f32 split slabs) of one FFN
 // as one persistent launch whose down units start as soon as the up tiles
-// of their columns are stored. Needs both plans at BN 256 and the down
-// split's K blocks equal to the up projection's (gemm_mlp_ok). `ready` holds
+// of their columns are stored. Needs both plans at BN 256 and each down
+// split reading whole up column tiles (gemm_mlp_ok). `ready` holds
 // one counter per (128-row tile, down split), zeroed at the start of a pass;
 // `ready_target` is the running sum over the pass's fused launches of
 // 4 x (up column tiles / down splits). A down unit waits at most

@@ -37,6 +37,10 @@ class Shape:
     branches: int
     branch_len: int
     questions: int      # questions per request (branches / option orders)
+    # Gemma 4's global layers: their head_dim and the RoPE share of it
+    # (partial_rotary_factor); 256 / 1.0 keeps every layer at 256 fully rotated.
+    global_head_dim: int = 256
+    global_rotary: float = 1.0
 
     def config(self) -> dict:
         types = ["full_attention" if (l + 1) % self.global_every == 0 else "sliding_attention"
@@ -56,6 +60,10 @@ class Shape:
             c["query_pre_attn_scalar"] = 256
         else:
             c["final_logit_softcapping"] = 30.0
+        if self.global_head_dim != 256:
+            c["global_head_dim"] = self.global_head_dim
+        if self.global_rotary != 1.0:
+            c["rope_parameters"]["full_attention"]["partial_rotary_factor"] = self.global_rotary
         return c
 
     def config_json(self) -> str:

@@ -11,6 +11,8 @@ production widths, against the reference's CPU forward (oracle/):
   norms of test_gpu_depth): the cold pass against the reference, the
   resident pass and a pass after a save / restore of the state equal to it
   bit for bit (reference.rs:509,520);
+* Gemma 4's real layer layout at E2B widths (a 256-dim sliding layer, a
+  512-dim global layer with partial RoPE) on the headline request;
 * configs[3], E4B widths (d 2560, GeGLU 10240) with a 2,000-token state and
   20 branches of 32 tokens (2,640 rows, the CTA-pair kernels), 2 layers;
 * configs[4], mmBERT widths at the full 22 encoder layers + 2 decision-head
@@ -101,6 +103,24 @@ def test_e2b_resident_state_two_layers(device):
     again = eng.evaluate(req.prefix, req.branches, Want.HIDDEN)
     assert eng.prefix_source() == PrefixSource.RESIDENT
     for a, b in zip(cold, again):
+        assert np.array_equal(a.rows, b.rows)
+    eng.close()
+
+
+def test_gemma4_global_head_dim_512_e2b_widths(device):
+    """Gemma 4's real layer layout at E2B widths (model.rs:110-148): a
+    sliding layer with 256-dim heads, then a global layer with 512-dim heads
+    rotated over a quarter of their dims, on the headline request (500-token
+    state, 12 branches of 24): the tcgen05 head_dim-512 attention and the
+    512-dim q / k / v norms and partial RoPE against the reference."""
+    shape = dataclasses.replace(synth.CONFIGS["e2b-q4"], layers=2, global_every=2,
+                                global_head_dim=512, global_rotary=0.25)
+    eng, req = check_pass(shape, 0.25, device)
+    eng.evict_resident()
+    cold = eng.evaluate(req.prefix, req.branches, Want.HIDDEN)
+    warm = eng.evaluate(req.prefix, req.branches, Want.HIDDEN)
+    assert eng.prefix_source() == PrefixSource.RESIDENT
+    for a, b in zip(cold, warm):
         assert np.array_equal(a.rows, b.rows)
     eng.close()
 

@@ -52,9 +52,11 @@ def rel(a, b):
 def oracle_cfg(shape):
     sliding = [t == "sliding_attention" for t in shape.config()["layer_types"]]
     L = shape.layers
+    hd = [256 if s else shape.global_head_dim for s in sliding]
+    rope = [256 if s else int(shape.global_head_dim * shape.global_rotary) for s in sliding]
     return O.OracleConfig(vocab=shape.vocab, d=shape.d, layers=L, heads=shape.heads,
-                          kv_heads=shape.kv_heads, head_dim=[256] * L, ff=[shape.ff] * L,
-                          sliding=sliding, kv_source=list(range(L)), rope_dims=[256] * L,
+                          kv_heads=shape.kv_heads, head_dim=hd, ff=[shape.ff] * L,
+                          sliding=sliding, kv_source=list(range(L)), rope_dims=rope,
                           window=512, query_scale=1.0, norm_offset=0.0, v_norm=True,
                           softcap=30.0)
 

@@ -11,8 +11,8 @@ production widths, against the reference's CPU forward (oracle/):
   norms of test_gpu_depth): the cold pass against the reference, the
   resident pass and a pass after a save / restore of the state equal to it
   bit for bit (reference.rs:509,520);
-* Gemma 4's real layer layout at E2B widths (a 256-dim sliding layer, a
-  512-dim global layer with partial RoPE) on the headline request;
+* Gemma 4's real layer layout at E2B and E4B widths (a 256-dim sliding
+  layer, a 512-dim global layer with partial RoPE) on their requests;
 * configs[3], E4B widths (d 2560, GeGLU 10240) with a 2,000-token state and
   20 branches of 32 tokens (2,640 rows, the CTA-pair kernels), 2 layers;
 * configs[4], mmBERT widths at the full 22 encoder layers + 2 decision-head
@@ -107,13 +107,16 @@ def test_e2b_resident_state_two_layers(device):
     eng.close()
 
 
-def test_gemma4_global_head_dim_512_e2b_widths(device):
-    """Gemma 4's real layer layout at E2B widths (model.rs:110-148): a
-    sliding layer with 256-dim heads, then a global layer with 512-dim heads
-    rotated over a quarter of their dims, on the headline request (500-token
-    state, 12 branches of 24): the tcgen05 head_dim-512 attention and the
-    512-dim q / k / v norms and partial RoPE against the reference."""
-    shape = dataclasses.replace(synth.CONFIGS["e2b-q4"], layers=2, global_every=2,
+@pytest.mark.parametrize("base", ["e2b-q4", "e4b-q4"])
+def test_gemma4_global_head_dim_512(device, base):
+    """Gemma 4's real layer layout (model.rs:110-148) at E2B and E4B widths:
+    a sliding layer with 256-dim heads, then a global layer with 512-dim
+    heads rotated over a quarter of their dims, on the config's request (E2B:
+    500-token state, 12 branches of 24; E4B: 2,000-token state, 20 branches
+    of 32, chunk-split runs and their merges): the tcgen05 head_dim-512
+    attention and the 512-dim q / k / v norms and partial RoPE against the
+    reference."""
+    shape = dataclasses.replace(synth.CONFIGS[base], layers=2, global_every=2,
                                 global_head_dim=512, global_rotary=0.25)
     eng, req = check_pass(shape, 0.25, device)
     eng.evict_resident()
